@@ -1,0 +1,418 @@
+#!/usr/bin/env python
+"""Benchmark: decode tok/s of the Qwen3-30B-A3B MoE stack on B200.
+
+Workload (BASELINE.json configs[1] shape, stacked to the 48 layers of
+configs[2]): hidden 2048, 128 experts, top-8, expert FFN 768; gate/up q4_K,
+down q6_K, N(0, 0.02) weights quantised per block; every expert resident in
+HBM (48 x 128 x 3.06 MB = 18.8 GB per GPU).  Router rows carry a Zipf(1.1)
+popularity bias.  One step = one decode token through the 48 MoE blocks
+(RMSNorm -> router -> top-k -> gate/up+SiLU -> down -> combine), i.e. the
+north-star path; attention is not on the path.  Synthetic data, generated on
+the device.
+
+`value`: tokens/s over all ranks with inputs resident (device-timed CUDA
+graph replays, CUDA events).  `e2e`: the same through the C ABI with host
+buffers (upload token, replay, download hidden state + ids every step).
+`roofline`: one MoE block (3 kernels) = 25,550,848 algorithmic bytes against
+the measured HBM copy bandwidth.  Multi-GPU: independent replicas (the
+30B shape fits one GPU), weak scaling.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s (30B-A3B shape, q4_K) at 1/2/4/8 B200; MoE-layer % of HBM peak"
+H, F, E, K_TOP, N_LAYERS = 2048, 768, 128, 8, 48
+Q4_K, Q6_K = 12, 14
+SG = (H // 256) * 144 * F          # gate / up slab bytes per expert
+SD = (F // 256) * 210 * H          # down slab bytes per expert
+ALG_BYTES_LAYER = K_TOP * (2 * SG + SD) + E * H * 4 + 3 * H * 4   # 25,550,848
+ZIPF_S, ZIPF_TAU, ZIPF_KAPPA = 1.1, 0.25, 4.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def zipf_bias(layer: int) -> np.ndarray:
+    """a_e = tau * ln p_pi(e), p_j ~ j^-s, pi a seeded permutation."""
+    rng = np.random.default_rng(9000 + layer)
+    p = np.arange(1, E + 1, dtype=np.float64) ** -ZIPF_S
+    p /= p.sum()
+    perm = rng.permutation(E)
+    return (ZIPF_TAU * np.log(p[perm])).astype(np.float32)
+
+
+def zipf_dir() -> np.ndarray:
+    m = np.random.default_rng(8999).normal(0, 1, H)
+    return (m / np.linalg.norm(m)).astype(np.float32)
+
+
+def token_bank(n: int) -> np.ndarray:
+    rng = np.random.default_rng(102)
+    return (rng.normal(0, 1, (n, H)) + ZIPF_KAPPA * zipf_dir()[None, :]).astype(np.float32)
+
+
+def router_host(layer: int) -> np.ndarray:
+    rng = np.random.default_rng(5000 + layer)
+    r = rng.normal(0, 0.02, (E, H)).astype(np.float32)
+    return r + zipf_bias(layer)[:, None] * zipf_dir()[None, :]
+
+
+# -------------------------------------------------------------- clocks
+class Clocks:
+    """nvidia-smi sampled during the timed region."""
+
+    def __init__(self, dev: int):
+        self.dev = dev
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,utilization.gpu")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p:
+            time.sleep(0.2)
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        rows = []
+        try:
+            with open(self.f.name) as f:
+                for line in f:
+                    parts = [x.strip() for x in line.split(",")]
+                    if len(parts) >= 7:
+                        rows.append(parts)
+        except Exception:
+            pass
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        busy = [r for r in rows if r[6].isdigit() and int(r[6]) > 0] or rows
+        sm = [float(r[0]) for r in busy if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in busy if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in busy for i in range(4) if r[2 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(busy)}
+
+
+# ---------------------------------------------------------- CPU legs
+def cpu_layer(seed: int = 0):
+    """One 30B-shaped MoE layer on the host (same shapes and value
+    distribution as the device workload), quantised by the oracle."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(7000 + seed)
+    gate = np.empty(E * SG, np.uint8)
+    up = np.empty(E * SG, np.uint8)
+    down = np.empty(E * SD, np.uint8)
+    for e in range(E):
+        gate[e * SG:(e + 1) * SG] = O.quantize(Q4_K, rng.standard_normal((F, H), np.float32) * np.float32(0.02)).reshape(-1)
+        up[e * SG:(e + 1) * SG] = O.quantize(Q4_K, rng.standard_normal((F, H), np.float32) * np.float32(0.02)).reshape(-1)
+        down[e * SD:(e + 1) * SD] = O.quantize(Q6_K, rng.standard_normal((H, F), np.float32) * np.float32(0.02)).reshape(-1)
+    return router_host(0), np.ones(H, np.float32), gate, up, down
+
+
+def time_cpu(budget_s: float, nthreads: int):
+    """Times the oracle MoE block (C, OpenMP over rows) for ~budget_s.
+    Returns (tok/s for the 48-layer stack, seconds per layer, reps)."""
+    from oracle import oracle as O
+    router, norm, gate, up, down = cpu_layer()
+    toks = token_bank(16)
+    O.moe_block_mt(toks[0], norm, 1e-6, router, K_TOP, True, (Q4_K, Q4_K, Q6_K), gate, up, down, F, nthreads)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        O.moe_block_mt(toks[reps % 16], norm, 1e-6, router, K_TOP, True, (Q4_K, Q4_K, Q6_K), gate, up, down, F,
+                       nthreads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or reps >= 2000:
+            break
+    per_layer = el / reps
+    return 1.0 / (N_LAYERS * per_layer), per_layer, reps
+
+
+def run_reference(args, rank: int) -> int:
+    """--impl reference: the reference's CPU implementation of the path (the
+    C restatement in oracle/, all host threads) on the same workload."""
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    O.build()
+    nth = os.cpu_count() or 1
+    router, norm, gate, up, down = cpu_layer()
+    toks = token_bank(16)
+    qts = (Q4_K, Q4_K, Q6_K)
+    layers_per_step = 2
+    for i in range(args.warmup):
+        O.moe_block_mt(toks[i % 16], norm, 1e-6, router, K_TOP, True, qts, gate, up, down, F, nth)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        for j in range(layers_per_step):
+            O.moe_block_mt(toks[(i + j) % 16], norm, 1e-6, router, K_TOP, True, qts, gate, up, down, F, nth)
+    el = time.perf_counter() - t0
+    per_layer = el / (args.steps * layers_per_step)
+    v = 1.0 / (N_LAYERS * per_layer)
+    sample = (f"{layers_per_step} of the 48 MoE layers per step (one 30B-shaped layer re-run), "
+              f"scaled to the 48-layer token; {per_layer * 1e3:.2f} ms per layer")
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * N_LAYERS * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(args.gpus),
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": nth, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference = C restatement of the reference CPU path (oracle/); the reference itself is "
+                    "Rust+Vulkan and cannot run here (no Rust toolchain, no graphics stack)"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(n: int):
+    return {"workload": "cfg2 MoE layer (H2048 E128 top8 F768, gate/up q4_K, down q6_K) stacked x48 "
+                        "(cfg3 MoE path), batch-1 decode, all experts resident",
+            "n_layers": N_LAYERS, "n_embd": H, "n_expert": E, "n_expert_used": K_TOP, "n_ff": F,
+            "global_batch": n, "parallelism": f"replicas x{n}" if n > 1 else "single",
+            "l2": "inputs larger than L2 (1.2 GB of expert slabs per token vs 126 MB L2)",
+            "router": "Zipf(1.1) popularity bias"}
+
+
+# ------------------------------------------------------------- GPU arm
+def build_model(dev: int, n_layers: int, unique: int = 4):
+    import torch
+
+    from styx_b200 import ops
+    torch.cuda.set_device(dev)
+    d = f"cuda:{dev}"
+    base = []
+    for u in range(min(unique, n_layers)):
+        g = ops.synth_quant(Q4_K, E * F, H, 1000 + 3 * u, 0.02, device=dev)
+        up = ops.synth_quant(Q4_K, E * F, H, 1001 + 3 * u, 0.02, device=dev)
+        dn = ops.synth_quant(Q6_K, E * H, F, 1002 + 3 * u, 0.02, device=dev)
+        base.append((g, up, dn))
+    torch.cuda.synchronize()
+    layers = []
+    norm = torch.ones(H, dtype=torch.float32, device=d)
+    for layer in range(n_layers):
+        if layer < len(base):
+            g, up, dn = base[layer]
+        else:   # distinct copies: every layer streams its own bytes
+            g, up, dn = (t.clone() for t in base[layer % len(base)])
+        router = torch.from_numpy(router_host(layer)).to(d)
+        layers.append(ops.LayerWeights(norm, router, ops.Experts(Q4_K, g, SG), ops.Experts(Q4_K, up, SG),
+                                       ops.Experts(Q6_K, dn, SD)))
+    torch.cuda.synchronize()
+    return layers
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="styx", choices=["styx", "reference"])
+    ap.add_argument("--layers", type=int, default=N_LAYERS)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import ctypes as C
+
+    import torch
+
+    from styx_b200 import _lib, ops
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device(dev))
+        pg = dist
+
+    L = args.layers
+    layers = build_model(local, L)
+    blk = ops.MoeBlock(ops.Dims(H, F, E, K_TOP), local)
+    lib, cx = _lib.lib(), blk.ctx.handle
+    bank = torch.from_numpy(token_bank(64)).to(dev)
+    x = torch.empty(H, dtype=torch.float32, device=dev)
+    ids = torch.zeros(L * 64, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def token(i):
+        x.copy_(bank[i % bank.shape[0]])
+        for layer in range(L):
+            blk.forward(x, layers[layer], layer, ids)
+
+    with torch.cuda.stream(stream):
+        token(0)
+    stream.synchronize()
+    blk.ctx.check_device_error(stream)
+
+    # record one token (48 x 3 kernels) through the C ABI's graph API
+    graph = C.c_void_p()
+    sp = C.c_void_p(stream.cuda_stream)
+    _lib.check(lib.styx_graph_begin(cx, sp))
+    with torch.cuda.stream(stream):
+        for layer in range(L):
+            blk.forward(x, layers[layer], layer, ids)
+    _lib.check(lib.styx_graph_end(cx, sp, C.byref(graph)))
+
+    def replay(i):
+        with torch.cuda.stream(stream):
+            x.copy_(bank[i % bank.shape[0]])
+        _lib.check(lib.styx_graph_launch(cx, graph, sp))
+
+    for i in range(args.warmup):
+        replay(i)
+    stream.synchronize()
+    blk.ctx.check_device_error(stream)
+
+    def barrier():
+        if pg:
+            pg.barrier()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            replay(i)
+        ev1.record(stream)
+        stream.synchronize()
+    barrier()
+    el_ms = ev0.elapsed_time(ev1)
+    blk.ctx.check_device_error(stream)
+    if pg:
+        t = torch.tensor([el_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        el_ms = float(t.item())
+    clocks = clk.summary()
+    ms_step = el_ms / args.steps
+    value = world * args.steps / (el_ms / 1e3)
+
+    # e2e: C ABI with host buffers -- upload the token, replay, download the
+    # hidden state and the ids every step
+    n_e2e = args.e2e_steps or args.steps
+    hx = ops.HostBuffer(H * 4, local)
+    hout = ops.HostBuffer(H * 4 + L * 256, local)
+    hbank = token_bank(64)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    xp, idp = C.c_void_p(x.data_ptr()), C.c_void_p(ids.data_ptr())
+    barrier()
+    torch.cuda.synchronize()
+    t_wall = time.perf_counter()
+    e0.record(stream)
+    for i in range(n_e2e):
+        hx.tensor.view(torch.float32).copy_(torch.from_numpy(hbank[i % 64]))
+        _lib.check(lib.styx_upload(cx, xp, 0, C.c_void_p(hx.ptr), H * 4, sp))
+        _lib.check(lib.styx_graph_launch(cx, graph, sp))
+        _lib.check(lib.styx_download(cx, C.c_void_p(hout.ptr), xp, 0, H * 4, sp))
+        _lib.check(lib.styx_download(cx, C.c_void_p(hout.ptr + H * 4), idp, 0, L * 256, sp))
+    e1.record(stream)
+    stream.synchronize()
+    t_wall = time.perf_counter() - t_wall
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if pg:
+        t = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = world * n_e2e / (e2e_ms / 1e3)
+
+    peak, peak_kind = peaks()
+    t_layer = ms_step / L * 1e-3
+    achieved = ALG_BYTES_LAYER / t_layer / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "moe_layer_traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get("dram_bytes_per_layer")
+        except Exception:
+            traffic = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            from oracle import oracle as O
+            O.build()
+            nth = os.cpu_count() or 1
+            v, per_layer, reps = time_cpu(args.cpu_seconds, nth)
+            cpu = {"value": v, "unit": "tok/s", "cores": nth, "kind": "port",
+                   "sample": f"{reps} runs of one 30B-shaped MoE layer (C oracle, OpenMP), "
+                             f"{per_layer * 1e3:.2f} ms/layer, scaled to 48 layers"}
+        except Exception as e:  # the CPU leg must not sink the GPU number
+            cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "port", "sample": f"failed: {e}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8-dp4a/f32 (q4_K,q6_K weights)", "data": "synthetic",
+            "config": workload_config(world),
+            "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": H * 4,
+                    "d2h_bytes_per_step": H * 4 + L * 256, "wall_s": t_wall},
+            "gpu_launches": args.steps * L * 3,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "unit_of_work": "one MoE block (route + gate/up + down kernels)",
+                         "alg_bytes": ALG_BYTES_LAYER, "peak_kind": peak_kind,
+                         "us_per_layer": t_layer * 1e6},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    _lib.check(lib.styx_graph_destroy(cx, graph))
+    hx.free()
+    hout.free()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,278 @@
+/*
+ * styx_moe.h -- C ABI of libstyx_moe.so: the Qwen3-MoE MoE block of
+ * aDirtyScoundrel/styx on NVIDIA B200 (sm_100a).
+ *
+ * The library replaces, for the MoE-block hot path, the operator layer that
+ * crates/model's MoeModel drives through crates/vk-backend (ash/Vulkan +
+ * SPIR-V).  Each entry point below names the reference interface it takes
+ * the place of (path:line inside the reference project).
+ *
+ * Conventions
+ *   - Every function returns 0 (STYX_OK) or a negative STYX_E* code and, on
+ *     error, leaves a message for styx_last_error() (thread-local).  The
+ *     reference returns Result<_, String> (crates/vk-backend/src/lib.rs).
+ *   - Pointers are device pointers (or STYX_MEM_HOST pinned, device-mapped
+ *     host pointers where stated); sizes are in bytes unless stated.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default).
+ *     Every op is stream-ordered and asynchronous; nothing here waits for the
+ *     device unless stated (styx_stream_sync, styx_download to pageable).
+ *   - No function allocates device memory during a hot-path op: the MoE
+ *     block uses a caller-provided workspace (styx_moe_workspace_bytes).
+ *   - A ctx is not thread-safe; use one ctx per host thread.  Calls made on
+ *     different streams with the same workspace race.
+ */
+#ifndef STYX_MOE_H
+#define STYX_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define STYX_OK 0
+#define STYX_EINVAL (-1)      /* bad argument / unsupported shape */
+#define STYX_ECUDA (-2)       /* CUDA runtime error */
+#define STYX_ENOMEM (-3)      /* allocation failed */
+#define STYX_ETIMEOUT (-4)    /* a device-side bounded wait gave up */
+#define STYX_EUNSUPPORTED (-5)
+
+/* expert id meaning "no expert" in the id rows (topk_softmax_f32.comp:27) */
+#define STYX_SKIP 0xFFFFFFFFu
+/* i32 per layer in the ids buffer: rows [0,16) original ids, [16,32) hot
+ * index, [32,48) arena slot, [48,64) full-tensor id (moe.rs:1158-1162,
+ * topk_softmax_f32.comp:5-11).  256 bytes, as bids is laid out there. */
+#define STYX_IDS_PER_LAYER 64
+#define STYX_MAX_TOPK 16      /* moe.rs:587 */
+#define STYX_MAX_EXPERTS 512  /* topk_softmax_f32.comp:3, onboard.rs:24 */
+
+/* ggml quantisation types accepted for expert matrices (moe.rs:24-40) */
+typedef enum {
+    STYX_F32 = 0,
+    STYX_Q8_0 = 8,
+    STYX_Q4_K = 12,
+    STYX_Q5_K = 13,
+    STYX_Q6_K = 14
+} styx_qtype;
+
+/* memory kinds for styx_alloc */
+typedef enum {
+    STYX_MEM_DEVICE = 0,      /* HBM (create_buffer, lib.rs:568) */
+    STYX_MEM_HOST = 1         /* pinned + device-mapped host memory, the GTT
+                                 tier (create_buffer_host[_shared],
+                                 lib.rs:756, 802) */
+} styx_mem_kind;
+
+typedef struct styx_ctx styx_ctx;
+typedef void *styx_stream;
+typedef void *styx_event;
+
+/* ------------------------------------------------------------ device */
+const char *styx_last_error(void);
+/* Gpu::new (crates/vk-backend/src/lib.rs:356): bind CUDA device `device`. */
+int styx_init(int device, styx_ctx **out);
+/* Drop for Gpu (lib.rs:1602-1612). */
+void styx_destroy(styx_ctx *ctx);
+/* Gpu::vram_bytes (lib.rs:534-554): total device memory. */
+int styx_vram_bytes(styx_ctx *ctx, uint64_t *out);
+/* SM count and name of the bound device (Gpu::device_name). */
+int styx_device_info(styx_ctx *ctx, int *sm_count, char *name, int name_len);
+/* Reads and clears the device-side error word that bounded waits set
+ * (returns STYX_ETIMEOUT if one fired since the last call).  Synchronises
+ * the stream. */
+int styx_check_device_error(styx_ctx *ctx, styx_stream stream);
+
+/* ------------------------------------------------------------ memory */
+/* create_buffer / create_buffer_host / create_buffer_host_shared
+ * (lib.rs:568, 756, 802).  Returned pointers are 256-byte aligned. */
+int styx_alloc(styx_ctx *ctx, uint64_t bytes, int kind, void **out);
+/* destroy_buffer (lib.rs:1517) */
+int styx_free(styx_ctx *ctx, void *ptr);
+/* upload (lib.rs:1033): dst[dst_off..+n] = src[0..n] (host -> device). */
+int styx_upload(styx_ctx *ctx, void *dst, uint64_t dst_off, const void *src,
+                uint64_t n, styx_stream stream);
+/* download (lib.rs:1175): dst[0..n] = src[src_off..+n] (device -> host). */
+int styx_download(styx_ctx *ctx, void *dst, const void *src, uint64_t src_off,
+                  uint64_t n, styx_stream stream);
+/* copy_region (lib.rs:1192-1217), any direction the pointers allow. */
+int styx_copy(styx_ctx *ctx, const void *src, uint64_t src_off, void *dst,
+              uint64_t dst_off, uint64_t n, styx_stream stream);
+int styx_memset(styx_ctx *ctx, void *dst, int value, uint64_t n,
+                styx_stream stream);
+
+/* ----------------------------------------------------- streams / events
+ * Replace Batch submit / submit_async / timeline semaphores
+ * (lib.rs:200-333, 700-712). */
+int styx_stream_create(styx_ctx *ctx, styx_stream *out);
+int styx_stream_destroy(styx_ctx *ctx, styx_stream stream);
+int styx_stream_sync(styx_ctx *ctx, styx_stream stream);
+int styx_event_create(styx_ctx *ctx, styx_event *out);
+int styx_event_destroy(styx_ctx *ctx, styx_event ev);
+int styx_event_record(styx_ctx *ctx, styx_event ev, styx_stream stream);
+int styx_stream_wait_event(styx_ctx *ctx, styx_stream stream, styx_event ev);
+
+/* Recorded per-token work (Batch::begin / submit, lib.rs:56-231): ops issued
+ * on `stream` between styx_graph_begin and styx_graph_end are recorded, not
+ * run; styx_graph_launch replays them on any stream.  The recording keeps
+ * the pointers it was given: the buffers must outlive the graph. */
+typedef void *styx_graph;
+int styx_graph_begin(styx_ctx *ctx, styx_stream stream);
+int styx_graph_end(styx_ctx *ctx, styx_stream stream, styx_graph *out);
+int styx_graph_launch(styx_ctx *ctx, styx_graph graph, styx_stream stream);
+int styx_graph_destroy(styx_ctx *ctx, styx_graph graph);
+
+/* ------------------------------------------------------- single ops
+ * One entry point per dispatch that MoeModel::forward_token records for the
+ * MoE block (crates/model/src/moe.rs:1974-2062). */
+
+/* rms_norm_f32 with weight multiply (moe.rs:1975-1982; semantics
+ * kernels.rs:58-67): out[r][c] = x[r][c] * 1/sqrt(mean_c(x^2)+eps) * w[c].
+ * w may be NULL (no multiply). */
+int styx_rms_norm(styx_ctx *ctx, styx_stream stream, const float *x,
+                  const float *w, float eps, int ncols, int nrows, float *out);
+
+/* matvec_strided_f32 (shaders/matvec_strided_f32.comp, moe.rs:1984-1996):
+ * d[r] = sum_c a[r*stride_a + c] * x[c]. */
+int styx_matvec_f32(styx_ctx *ctx, styx_stream stream, const float *a,
+                    int nrows, int ncols, int stride_a, const float *x,
+                    float *d);
+
+/* topk_softmax_f32 (shaders/topk_softmax_f32.comp, moe.rs:1998-2016).
+ * remap / pmap may be NULL (all SKIP).  ids64: the layer's 64-int block. */
+int styx_topk_softmax(styx_ctx *ctx, styx_stream stream, const float *logits,
+                      int n, int k, int renorm, const uint32_t *remap,
+                      const uint32_t *pmap, float *weights, int32_t *ids64);
+
+/* mul_mat_vec_id_<type>_f32_f32 with the MatVecIdPush meaning
+ * (crates/vk-backend/src/ops.rs:120-147, moe.rs:1561-1606; offsets per
+ * kernels.rs:124-131), for slot s < n_ids with ids[s] != SKIP:
+ *   y[s*stride_d + r] = sum_c deq(A_e)[r][c] * x[(s % ne11)*stride_b + c]
+ *   A_e = a + e * expert_bytes, e = ids[s], rows of row_bytes(qtype, ncols).
+ * SKIP slots leave y untouched (the patched SKIP early-out).  Ids >= n_expert
+ * are skipped too and reported through styx_check_device_error. */
+int styx_mul_mat_vec_id(styx_ctx *ctx, styx_stream stream, int qtype,
+                        const void *a, uint64_t expert_bytes, int n_expert,
+                        int nrows, int ncols, const int32_t *ids, int n_ids,
+                        const float *x, int stride_b, int ne11, float *y,
+                        int stride_d);
+
+/* swiglu_f32 split mode (ops.rs:337-370, moe.rs:2025-2038; CPU form
+ * ops2.rs:305-308): out[i] = g[i] / (1 + exp(-g[i])) * u[i]. */
+int styx_swiglu(styx_ctx *ctx, styx_stream stream, const float *g,
+                const float *u, float *out, int n);
+
+/* moe_reduce_f32 (shaders/moe_reduce_f32.comp, moe.rs:2050-2062):
+ * x[i] += sum_{s<k} w[s] * d[s*ne + i], slot order. */
+int styx_moe_reduce(styx_ctx *ctx, styx_stream stream, const float *d,
+                    const float *w, float *x, int ne, int k);
+
+/* gather_slabs_f32 (shaders/gather_slabs_f32.comp:40-85, recorder
+ * moe.rs:1706-1744): for s < k with ids[s] != SKIP copy the three source
+ * slabs of expert ids[s] into arena slot layer*k+s.  Sources may be
+ * STYX_MEM_HOST (the GTT tier); ids are device memory.  All byte counts
+ * must be multiples of 16.  Ids >= n_expert are skipped and reported
+ * through styx_check_device_error. */
+int styx_gather_slabs(styx_ctx *ctx, styx_stream stream, const void *src_g,
+                      const void *src_u, const void *src_d,
+                      uint64_t src_bytes_g, uint64_t src_bytes_u,
+                      uint64_t src_bytes_d, void *arena_g, void *arena_u,
+                      void *arena_d, uint64_t dst_bytes_g,
+                      uint64_t dst_bytes_u, uint64_t dst_bytes_d,
+                      const int32_t *ids, int n_expert, int layer, int k);
+
+/* The prefetch form of the same copy, driven by host-known ids (the
+ * prepare_prefetch path, moe.rs:2169-2383): one cudaMemcpyAsync per slab on
+ * `stream` (a copy-engine transfer from pinned host memory). */
+int styx_gather_slabs_async(styx_ctx *ctx, styx_stream stream,
+                            const void *src_g, const void *src_u,
+                            const void *src_d, uint64_t src_bytes_g,
+                            uint64_t src_bytes_u, uint64_t src_bytes_d,
+                            void *arena_g, void *arena_u, void *arena_d,
+                            uint64_t dst_bytes_g, uint64_t dst_bytes_u,
+                            uint64_t dst_bytes_d, const int32_t *host_ids,
+                            int n_expert, int layer, int k);
+
+/* ----------------------------------------------------- fused MoE block */
+
+/* One expert tensor (ExpMat, moe.rs:97-106) with its placement.  For slot
+ * s the kernels read, in this order of precedence:
+ *   hot   + ids[16+s] * slab_bytes        if ids[16+s] != SKIP
+ *   arena + ids[32+s] * arena_slab_bytes  if ids[32+s] != SKIP
+ *   full  + ids[48+s] * slab_bytes        otherwise
+ * which is the three-way split of rec_matvec_id (moe.rs:1649-1700) in one
+ * kernel.  `full` must be device memory for the fused kernels (cold slabs in
+ * STYX_MEM_HOST go through styx_gather_slabs into the arena first).
+ * Bases 16-byte aligned; slab_bytes and arena_slab_bytes multiples of 16.
+ * n_hot / n_arena bound the hot indices and arena slots (full ids are
+ * bounded by n_expert): an id out of range is skipped and reported through
+ * styx_check_device_error. */
+typedef struct styx_expert_tensor {
+    const void *full;
+    const void *hot;
+    const void *arena;
+    uint64_t slab_bytes;
+    uint64_t arena_slab_bytes;
+    int32_t qtype;
+    uint32_t n_hot;
+    uint32_t n_arena;
+} styx_expert_tensor;
+
+/* Per-layer MoE weights (Layer, moe.rs:108-144). */
+typedef struct styx_moe_layer {
+    const float *ffn_norm;     /* f32[n_embd] */
+    const float *router;       /* f32[n_expert][n_embd] (ffn_gate_inp) */
+    const uint32_t *remap;     /* u32[n_expert] expert -> hot index, or NULL */
+    const uint32_t *pmap;      /* u32[n_expert] expert -> arena slot, or NULL */
+    styx_expert_tensor gate, up, down;
+} styx_moe_layer;
+
+/* Hyper-parameters (HParams, moe.rs:550-587). */
+typedef struct styx_moe_dims {
+    int32_t n_embd;            /* H */
+    int32_t n_ff;              /* F, expert_feed_forward_length */
+    int32_t n_expert;          /* E */
+    int32_t n_expert_used;     /* k */
+    int32_t norm_topk;         /* renormalise top-k weights (ArchCfg.norm_topk) */
+    float rms_eps;
+} styx_moe_dims;
+
+/* Workspace bytes styx_moe_block needs for these dims. */
+int styx_moe_workspace_bytes(const styx_moe_dims *dims, uint64_t *out);
+/* Zeroes a workspace (required once before its first use). */
+int styx_moe_workspace_init(styx_ctx *ctx, styx_stream stream, void *ws,
+                            uint64_t bytes);
+
+/* The MoE block of one layer (moe.rs:1974-2062):
+ *   xnorm = rms(x, ffn_norm); logits = router . xnorm; topk_softmax;
+ *   h = silu(gate_e . xnorm) * (up_e . xnorm); d = down_e . h;
+ *   x += sum_s w[s] d[s]  (slot order).
+ * x: f32[n_embd], updated in place.  ids: the ids buffer; this layer's
+ * 64-int block at ids + layer*64 is written.  weights_out: f32[k] or NULL.
+ * Three kernels on `stream`: route, gate/up+SiLU, down+combine. */
+int styx_moe_block(styx_ctx *ctx, styx_stream stream,
+                   const styx_moe_dims *dims, const styx_moe_layer *layer_w,
+                   int layer, float *x, int32_t *ids, float *weights_out,
+                   void *workspace, uint64_t workspace_bytes);
+
+/* Debug / test views of the last styx_moe_block's intermediates kept in the
+ * workspace: which = 0 xnorm f32[H], 1 logits f32[E], 2 h f32[k*F],
+ * 3 weights f32[k].  Returns a device pointer into the workspace. */
+int styx_moe_workspace_view(const styx_moe_dims *dims, void *workspace,
+                            int which, void **out);
+
+/* ------------------------------------------------- synthetic weights
+ * Device-side generator for benchmark-sized synthetic expert tensors:
+ * values N(0, sigma) from a counter-based hash of (seed, index), quantised
+ * per block with the same min/max scheme as the test oracle's quantiser.
+ * Writes nrows rows of ncols elements of `qtype` to dst. */
+int styx_synth_quant(styx_ctx *ctx, styx_stream stream, int qtype, void *dst,
+                     uint64_t nrows, int ncols, uint64_t seed, float sigma);
+/* Same values as float32 (for checks): dst f32[nrows*ncols]. */
+int styx_synth_f32(styx_ctx *ctx, styx_stream stream, float *dst, uint64_t n,
+                   uint64_t seed, uint64_t offset, float sigma);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

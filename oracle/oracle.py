@@ -40,6 +40,7 @@ def lib():
         sigs = {
             "or_dequant_row": (i, [i, vp, i, vp]),
             "or_quantize_row": (i, [i, vp, i, vp]),
+            "or_quantize_rows": (i, [i, vp, C.c_longlong, i, vp]),
             "or_matvec_q": (None, [i, vp, i, i, vp, vp]),
             "or_mul_mat_vec_id": (None, [i, vp, C.c_size_t, i, i, vp, i, vp, i, vp]),
             "or_rms_norm": (None, [vp, vp, i, f, vp]),
@@ -80,10 +81,8 @@ def quantize(qtype: int, x: np.ndarray) -> np.ndarray:
     x2 = x.reshape(-1, x.shape[-1])
     rb = row_bytes(qtype, x2.shape[1])
     out = np.zeros((x2.shape[0], rb), dtype=np.uint8)
-    L = lib()
-    for r in range(x2.shape[0]):
-        rc = L.or_quantize_row(qtype, _p(x2[r]), x2.shape[1], _p(out[r]))
-        assert rc == 0
+    rc = lib().or_quantize_rows(qtype, _p(x2), x2.shape[0], x2.shape[1], _p(out))
+    assert rc == 0
     return out.reshape(x.shape[:-1] + (rb,))
 
 

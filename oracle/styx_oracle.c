@@ -379,6 +379,16 @@ int or_quantize_row(int qtype, const float *x, int ncols, uint8_t *out) {
     return 0;
 }
 
+int or_quantize_rows(int qtype, const float *x, long long nrows, int ncols, uint8_t *out) {
+    size_t rb = or_row_bytes(qtype, ncols);
+    if (rb == 0) return -1;
+    int bad = 0;
+#pragma omp parallel for schedule(static) reduction(| : bad)
+    for (long long r = 0; r < nrows; r++)
+        bad |= or_quantize_row(qtype, x + (size_t)r * ncols, ncols, out + (size_t)r * rb) != 0;
+    return bad ? -1 : 0;
+}
+
 /* ----------------------------------------------------------------- GEMVs */
 
 /* one row: dequantise, then a column-order f32 dot, products rounded before

@@ -47,6 +47,8 @@ int or_dequant_row(int qtype, const uint8_t *row, int ncols, float *out);
 /* Test-data quantizers (NOT a restatement of ggml's quantizers: a simple,
  * deterministic min/max scheme producing valid blocks of each format). */
 int or_quantize_row(int qtype, const float *x, int ncols, uint8_t *out);
+/* nrows rows at once (OpenMP over rows) */
+int or_quantize_rows(int qtype, const float *x, long long nrows, int ncols, uint8_t *out);
 
 /* y[r] = sum_c deq(W)[r][c] * x[c], column order, f32 (kernels.rs:380-392) */
 void or_matvec_q(int qtype, const uint8_t *w, int nrows, int ncols,

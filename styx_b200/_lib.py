@@ -1,0 +1,126 @@
+"""ctypes binding of libstyx_moe.so (include/styx_moe.h).
+
+There is no fallback: if the library is missing, importing the ops raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libstyx_moe.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "styx_moe.h")
+
+STYX_OK, STYX_EINVAL, STYX_ECUDA, STYX_ENOMEM, STYX_ETIMEOUT, STYX_EUNSUPPORTED = 0, -1, -2, -3, -4, -5
+F32, Q8_0, Q4_K, Q5_K, Q6_K = 0, 8, 12, 13, 14
+QTYPES = {"q8_0": Q8_0, "q4_K": Q4_K, "q5_K": Q5_K, "q6_K": Q6_K}
+BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
+SKIP = 0xFFFFFFFF
+IDS_PER_LAYER = 64
+MEM_DEVICE, MEM_HOST = 0, 1
+
+
+class StyxError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"styx error {code}: {msg}")
+        self.code = code
+
+
+class ExpertTensor(C.Structure):
+    _fields_ = [("full", C.c_void_p), ("hot", C.c_void_p), ("arena", C.c_void_p),
+                ("slab_bytes", C.c_uint64), ("arena_slab_bytes", C.c_uint64),
+                ("qtype", C.c_int32), ("n_hot", C.c_uint32), ("n_arena", C.c_uint32)]
+
+
+class MoeLayer(C.Structure):
+    _fields_ = [("ffn_norm", C.c_void_p), ("router", C.c_void_p), ("remap", C.c_void_p),
+                ("pmap", C.c_void_p), ("gate", ExpertTensor), ("up", ExpertTensor),
+                ("down", ExpertTensor)]
+
+
+class MoeDims(C.Structure):
+    _fields_ = [("n_embd", C.c_int32), ("n_ff", C.c_int32), ("n_expert", C.c_int32),
+                ("n_expert_used", C.c_int32), ("norm_topk", C.c_int32), ("rms_eps", C.c_float)]
+
+
+_vp, _i, _f, _u64 = C.c_void_p, C.c_int, C.c_float, C.c_uint64
+_SIGS = {
+    "styx_last_error": (C.c_char_p, []),
+    "styx_init": (_i, [_i, C.POINTER(_vp)]),
+    "styx_destroy": (None, [_vp]),
+    "styx_vram_bytes": (_i, [_vp, C.POINTER(_u64)]),
+    "styx_device_info": (_i, [_vp, C.POINTER(_i), C.c_char_p, _i]),
+    "styx_check_device_error": (_i, [_vp, _vp]),
+    "styx_alloc": (_i, [_vp, _u64, _i, C.POINTER(_vp)]),
+    "styx_free": (_i, [_vp, _vp]),
+    "styx_upload": (_i, [_vp, _vp, _u64, _vp, _u64, _vp]),
+    "styx_download": (_i, [_vp, _vp, _vp, _u64, _u64, _vp]),
+    "styx_copy": (_i, [_vp, _vp, _u64, _vp, _u64, _u64, _vp]),
+    "styx_memset": (_i, [_vp, _vp, _i, _u64, _vp]),
+    "styx_stream_create": (_i, [_vp, C.POINTER(_vp)]),
+    "styx_stream_destroy": (_i, [_vp, _vp]),
+    "styx_stream_sync": (_i, [_vp, _vp]),
+    "styx_event_create": (_i, [_vp, C.POINTER(_vp)]),
+    "styx_event_destroy": (_i, [_vp, _vp]),
+    "styx_event_record": (_i, [_vp, _vp, _vp]),
+    "styx_stream_wait_event": (_i, [_vp, _vp, _vp]),
+    "styx_graph_begin": (_i, [_vp, _vp]),
+    "styx_graph_end": (_i, [_vp, _vp, C.POINTER(_vp)]),
+    "styx_graph_launch": (_i, [_vp, _vp, _vp]),
+    "styx_graph_destroy": (_i, [_vp, _vp]),
+    "styx_rms_norm": (_i, [_vp, _vp, _vp, _vp, _f, _i, _i, _vp]),
+    "styx_matvec_f32": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    "styx_topk_softmax": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "styx_mul_mat_vec_id": (_i, [_vp, _vp, _i, _vp, _u64, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp, _i]),
+    "styx_swiglu": (_i, [_vp, _vp, _vp, _vp, _vp, _i]),
+    "styx_moe_reduce": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i]),
+    "styx_gather_slabs": (_i, [_vp, _vp, _vp, _vp, _vp, _u64, _u64, _u64, _vp, _vp, _vp,
+                               _u64, _u64, _u64, _vp, _i, _i, _i]),
+    "styx_gather_slabs_async": (_i, [_vp, _vp, _vp, _vp, _vp, _u64, _u64, _u64, _vp, _vp, _vp,
+                                     _u64, _u64, _u64, _vp, _i, _i, _i]),
+    "styx_moe_workspace_bytes": (_i, [C.POINTER(MoeDims), C.POINTER(_u64)]),
+    "styx_moe_workspace_init": (_i, [_vp, _vp, _vp, _u64]),
+    "styx_moe_workspace_view": (_i, [C.POINTER(MoeDims), _vp, _i, C.POINTER(_vp)]),
+    "styx_moe_block": (_i, [_vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp,
+                            _vp, _vp, _u64]),
+    "styx_synth_quant": (_i, [_vp, _vp, _i, _vp, _u64, _i, _u64, _f]),
+    "styx_synth_f32": (_i, [_vp, _vp, _vp, _u64, _u64, _u64, _f]),
+}
+
+_lib = None
+
+
+def header_functions() -> list[str]:
+    """Names of the functions include/styx_moe.h declares."""
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(styx_[a-z0-9_]+)\s*\(", txt)))
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m styx_b200.build` "
+                "(there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != STYX_OK:
+        msg = lib().styx_last_error()
+        raise StyxError(rc, msg.decode() if msg else "")
+
+
+def row_bytes(qtype: int, ncols: int) -> int:
+    be, bb = BLOCK[qtype]
+    assert ncols % be == 0
+    return ncols // be * bb

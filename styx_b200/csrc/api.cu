@@ -1,0 +1,792 @@
+// api.cu -- the extern "C" surface of libstyx_moe.so (include/styx_moe.h).
+//
+// Host-side validation, workspace layout and launch planning for the MoE
+// block; the kernels live in moe_kernels.cu and synth.cu.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/styx_moe.h"
+#include "kernels.h"
+
+struct styx_ctx {
+    int device = 0;
+    int sm_count = 0;
+    char name[256] = {0};
+    int *d_err = nullptr;   // device error word of bounded waits
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess) return fail(STYX_ECUDA, "%s: %s", #call, cudaGetErrorString(e_));   \
+    } while (0)
+
+#define NEED(cond, ...)                                                                            \
+    do {                                                                                           \
+        if (!(cond)) return fail(STYX_EINVAL, __VA_ARGS__);                                        \
+    } while (0)
+
+inline cudaStream_t S(styx_stream s) { return static_cast<cudaStream_t>(s); }
+
+int enter(styx_ctx *ctx) {
+    if (!ctx) return fail(STYX_EINVAL, "null ctx");
+    CK(cudaSetDevice(ctx->device));
+    return STYX_OK;
+}
+#define ENTER(ctx)                                                                                 \
+    do {                                                                                           \
+        int rc_ = enter(ctx);                                                                      \
+        if (rc_) return rc_;                                                                       \
+    } while (0)
+
+bool qtype_ok(int qt) { return qt == STYX_Q8_0 || qt == STYX_Q4_K || qt == STYX_Q5_K || qt == STYX_Q6_K; }
+int blk_elems(int qt) { return qt == STYX_Q8_0 ? 32 : 256; }
+int blk_bytes(int qt) {
+    return qt == STYX_Q8_0 ? 34 : qt == STYX_Q4_K ? 144 : qt == STYX_Q5_K ? 176 : qt == STYX_Q6_K ? 210 : 0;
+}
+// bytes of one row of ncols elements, 0 if not representable
+long long row_bytes(int qt, int ncols) {
+    if (!qtype_ok(qt) || ncols <= 0 || ncols % blk_elems(qt)) return 0;
+    return static_cast<long long>(ncols / blk_elems(qt)) * blk_bytes(qt);
+}
+// 64-element units (qdot.cuh) need ncols % 64 == 0 (q8_0) / % 256 (k-quants)
+bool units_ok(int qt, int ncols) { return ncols > 0 && ncols % (qt == STYX_Q8_0 ? 64 : 256) == 0; }
+int pow2ceil(int v) {
+    int p = 1;
+    while (p < v) p <<= 1;
+    return p;
+}
+bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// [p, p+bytes) inside the device allocation that holds p.  Pointers the
+// driver does not know as device allocations (mapped host memory) pass:
+// their extent cannot be queried here.
+// (The driver function is looked up through the runtime, so the library has
+// no link-time dependency on libcuda.)
+using MemRangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
+MemRangeFn mem_range_fn() {
+    static MemRangeFn fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            f = nullptr;
+        }
+        return reinterpret_cast<MemRangeFn>(f);
+    }();
+    return fn;
+}
+
+bool extent_ok(const void *p, uint64_t bytes) {
+    if (!p || bytes == 0) return true;
+    MemRangeFn fn = mem_range_fn();
+    if (!fn) return true;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) return true;
+    return reinterpret_cast<uintptr_t>(p) + bytes <= static_cast<uintptr_t>(base) + size;
+}
+size_t a16(size_t v) { return (v + 15) & ~size_t(15); }
+size_t a128(size_t v) { return (v + 127) & ~size_t(127); }
+
+struct WsLayout {
+    size_t counter, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, total;
+};
+
+WsLayout ws_layout(const styx_moe_dims &d) {
+    WsLayout L{};
+    size_t o = 0;
+    auto take = [&](size_t n) {
+        size_t r = o;
+        o = (o + n + 255) & ~size_t(255);
+        return r;
+    };
+    const size_t H = d.n_embd, E = d.n_expert, kF = static_cast<size_t>(d.n_expert_used) * d.n_ff;
+    L.counter = take(256);
+    L.xnorm = take(H * 4);
+    L.xd1 = take(H);
+    L.xd2 = take(H);
+    L.xd3 = take(H);
+    L.xscale = take(H / 32 * 4);
+    L.logits = take(E * 4);
+    L.weights = take(16 * 4);
+    L.h = take(kF * 4);
+    L.g = take(kF * 4);   // unfused gate/up fallback
+    L.u = take(kF * 4);
+    L.total = o;
+    return L;
+}
+
+int check_dims(const styx_moe_dims *d) {
+    NEED(d, "null dims");
+    NEED(d->n_embd > 0 && d->n_embd % 256 == 0 && d->n_embd <= 16384, "n_embd %d: need a multiple of 256, <= 16384",
+         d->n_embd);
+    NEED(d->n_ff > 0 && d->n_ff % 256 == 0 && d->n_ff <= 2048, "n_ff %d: need a multiple of 256, <= 2048",
+         d->n_ff);
+    NEED(d->n_expert > 0 && d->n_expert <= STYX_MAX_EXPERTS, "n_expert %d out of range", d->n_expert);
+    NEED(d->n_expert_used > 0 && d->n_expert_used <= STYX_MAX_TOPK && d->n_expert_used <= d->n_expert,
+         "n_expert_used %d out of range", d->n_expert_used);
+    return STYX_OK;
+}
+
+int check_tensor(const styx_expert_tensor &t, const char *what, int nrows, int ncols, int n_expert) {
+    NEED(qtype_ok(t.qtype), "%s: unsupported qtype %d", what, t.qtype);
+    NEED(!t.hot || t.n_hot > 0, "%s: hot buffer with n_hot = 0", what);
+    NEED(!t.arena || t.n_arena > 0, "%s: arena with n_arena = 0", what);
+    NEED(extent_ok(t.full, t.slab_bytes * static_cast<uint64_t>(n_expert)), "%s: full tensor smaller than %d slabs",
+         what, n_expert);
+    NEED(extent_ok(t.hot, t.slab_bytes * t.n_hot), "%s: hot buffer smaller than n_hot slabs", what);
+    NEED(extent_ok(t.arena, t.arena_slab_bytes * t.n_arena), "%s: arena smaller than n_arena slots", what);
+    NEED(units_ok(t.qtype, ncols), "%s: %d columns not supported for qtype %d", what, ncols, t.qtype);
+    const long long need = row_bytes(t.qtype, ncols) * nrows;
+    NEED(static_cast<long long>(t.slab_bytes) >= need, "%s: slab_bytes %llu < %lld", what,
+         (unsigned long long)t.slab_bytes, need);
+    NEED(t.full || t.hot || t.arena, "%s: no source buffer", what);
+    NEED(t.slab_bytes % 16 == 0, "%s: slab_bytes must be a multiple of 16", what);
+    NEED(t.arena_slab_bytes % 16 == 0, "%s: arena_slab_bytes must be a multiple of 16", what);
+    NEED(al16(t.full) && al16(t.hot) && al16(t.arena), "%s: buffers must be 16-byte aligned", what);
+    if (t.full) {
+        cudaPointerAttributes pa{};
+        if (cudaPointerGetAttributes(&pa, t.full) == cudaSuccess)
+            NEED(pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged,
+                 "%s: full tensor must be device memory for the fused kernels "
+                 "(gather host slabs into the arena first)", what);
+    }
+    return STYX_OK;
+}
+
+styx::ExpSrc to_src(const styx_expert_tensor &t, int n_expert) {
+    return styx::ExpSrc{static_cast<const uint8_t *>(t.full),
+                        static_cast<const uint8_t *>(t.hot),
+                        static_cast<const uint8_t *>(t.arena),
+                        t.slab_bytes,
+                        t.arena_slab_bytes,
+                        static_cast<uint32_t>(n_expert),
+                        t.n_hot,
+                        t.n_arena};
+}
+
+// reference-shaped 3-way expert GEMV (rec_matvec_id, moe.rs:1649-1700): hot,
+// arena and full-tensor rows, each a SKIP-gated dispatch over all k slots
+int matvec_id_3way(const styx_expert_tensor &t, int n_expert, const int32_t *ids64, int nrows, int ncols, int k,
+                   const float *x, int ne11, float *y, int *err, cudaStream_t st) {
+    const int units = ncols / 64;
+    styx::MatVecIdArgs a{};
+    a.err = err;
+    a.nrows = nrows;
+    a.ncols = ncols;
+    a.rb = static_cast<int>(row_bytes(t.qtype, ncols));
+    a.n_ids = k;
+    a.x = x;
+    a.stride_b = ncols;
+    a.ne11 = ne11;
+    a.y = y;
+    a.stride_d = nrows;
+    a.units = units;
+    a.gs = std::min(32, pow2ceil(units));
+    struct Row { const void *buf; uint64_t stride; int off; int count; } rows[3] = {
+        {t.hot, t.slab_bytes, 16, static_cast<int>(t.n_hot)},
+        {t.arena, t.arena_slab_bytes, 32, static_cast<int>(t.n_arena)},
+        {t.full, t.slab_bytes, 48, n_expert}};
+    for (auto &r : rows) {
+        if (!r.buf) continue;
+        a.a = static_cast<const uint8_t *>(r.buf);
+        a.expert_bytes = r.stride;
+        a.n_expert = r.count;
+        a.ids = ids64 + r.off;
+        CK(styx::launch_matvec_id(a, t.qtype, st));
+    }
+    return STYX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *styx_last_error(void) { return g_err.c_str(); }
+
+int styx_init(int device, styx_ctx **out) {
+    NEED(out, "null out");
+    int n = 0;
+    CK(cudaGetDeviceCount(&n));
+    NEED(device >= 0 && device < n, "device %d not present (%d devices)", device, n);
+    CK(cudaSetDevice(device));
+    cudaDeviceProp prop{};
+    CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10)
+        return fail(STYX_EUNSUPPORTED, "device %d (%s) is sm_%d%d; this library is built for sm_100a", device,
+                    prop.name, prop.major, prop.minor);
+    auto *c = new styx_ctx();
+    c->device = device;
+    c->sm_count = prop.multiProcessorCount;
+    snprintf(c->name, sizeof(c->name), "%s", prop.name);
+    cudaError_t e = cudaMalloc(&c->d_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        delete c;
+        return fail(STYX_ECUDA, "error word: %s", cudaGetErrorString(e));
+    }
+    *out = c;
+    return STYX_OK;
+}
+
+void styx_destroy(styx_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    cudaFree(ctx->d_err);
+    delete ctx;
+}
+
+int styx_vram_bytes(styx_ctx *ctx, uint64_t *out) {
+    ENTER(ctx);
+    NEED(out, "null out");
+    size_t fr = 0, tot = 0;
+    CK(cudaMemGetInfo(&fr, &tot));
+    *out = tot;
+    return STYX_OK;
+}
+
+int styx_device_info(styx_ctx *ctx, int *sm_count, char *name, int name_len) {
+    NEED(ctx, "null ctx");
+    if (sm_count) *sm_count = ctx->sm_count;
+    if (name && name_len > 0) snprintf(name, static_cast<size_t>(name_len), "%s", ctx->name);
+    return STYX_OK;
+}
+
+int styx_check_device_error(styx_ctx *ctx, styx_stream stream) {
+    ENTER(ctx);
+    int h = 0;
+    CK(cudaMemcpyAsync(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, S(stream)));
+    CK(cudaStreamSynchronize(S(stream)));
+    if (h) {
+        CK(cudaMemsetAsync(ctx->d_err, 0, sizeof(int), S(stream)));
+        CK(cudaStreamSynchronize(S(stream)));
+        return fail(STYX_ETIMEOUT, "device-side bounded wait gave up (code %d)", h);
+    }
+    return STYX_OK;
+}
+
+int styx_alloc(styx_ctx *ctx, uint64_t bytes, int kind, void **out) {
+    ENTER(ctx);
+    NEED(out, "null out");
+    NEED(bytes > 0, "zero-byte allocation");
+    void *p = nullptr;
+    cudaError_t e;
+    if (kind == STYX_MEM_DEVICE) e = cudaMalloc(&p, bytes);
+    else if (kind == STYX_MEM_HOST) e = cudaHostAlloc(&p, bytes, cudaHostAllocMapped | cudaHostAllocPortable);
+    else return fail(STYX_EINVAL, "unknown memory kind %d", kind);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(STYX_ENOMEM, "allocating %llu bytes (kind %d): %s", (unsigned long long)bytes, kind,
+                    cudaGetErrorString(e));
+    }
+    if (kind == STYX_MEM_HOST) {
+        // kernels read the GTT tier through the host address (UVA)
+        void *dp = nullptr;
+        if (cudaHostGetDevicePointer(&dp, p, 0) != cudaSuccess || dp != p) {
+            cudaGetLastError();
+            cudaFreeHost(p);
+            return fail(STYX_EUNSUPPORTED, "pinned host memory is not mapped at its host address");
+        }
+    }
+    *out = p;
+    return STYX_OK;
+}
+
+int styx_free(styx_ctx *ctx, void *ptr) {
+    ENTER(ctx);
+    if (!ptr) return STYX_OK;
+    cudaPointerAttributes pa{};
+    CK(cudaPointerGetAttributes(&pa, ptr));
+    if (pa.type == cudaMemoryTypeHost) CK(cudaFreeHost(ptr));
+    else CK(cudaFree(ptr));
+    return STYX_OK;
+}
+
+int styx_upload(styx_ctx *ctx, void *dst, uint64_t dst_off, const void *src, uint64_t n, styx_stream stream) {
+    ENTER(ctx);
+    NEED(dst && src, "null pointer");
+    CK(cudaMemcpyAsync(static_cast<uint8_t *>(dst) + dst_off, src, n, cudaMemcpyDefault, S(stream)));
+    return STYX_OK;
+}
+
+int styx_download(styx_ctx *ctx, void *dst, const void *src, uint64_t src_off, uint64_t n, styx_stream stream) {
+    ENTER(ctx);
+    NEED(dst && src, "null pointer");
+    CK(cudaMemcpyAsync(dst, static_cast<const uint8_t *>(src) + src_off, n, cudaMemcpyDefault, S(stream)));
+    CK(cudaStreamSynchronize(S(stream)));
+    return STYX_OK;
+}
+
+int styx_copy(styx_ctx *ctx, const void *src, uint64_t src_off, void *dst, uint64_t dst_off, uint64_t n,
+              styx_stream stream) {
+    ENTER(ctx);
+    NEED(dst && src, "null pointer");
+    CK(cudaMemcpyAsync(static_cast<uint8_t *>(dst) + dst_off, static_cast<const uint8_t *>(src) + src_off, n,
+                       cudaMemcpyDefault, S(stream)));
+    return STYX_OK;
+}
+
+int styx_memset(styx_ctx *ctx, void *dst, int value, uint64_t n, styx_stream stream) {
+    ENTER(ctx);
+    NEED(dst, "null pointer");
+    CK(cudaMemsetAsync(dst, value, n, S(stream)));
+    return STYX_OK;
+}
+
+int styx_stream_create(styx_ctx *ctx, styx_stream *out) {
+    ENTER(ctx);
+    NEED(out, "null out");
+    cudaStream_t s;
+    CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    *out = s;
+    return STYX_OK;
+}
+int styx_stream_destroy(styx_ctx *ctx, styx_stream stream) {
+    ENTER(ctx);
+    if (stream) CK(cudaStreamDestroy(S(stream)));
+    return STYX_OK;
+}
+int styx_stream_sync(styx_ctx *ctx, styx_stream stream) {
+    ENTER(ctx);
+    CK(cudaStreamSynchronize(S(stream)));
+    return STYX_OK;
+}
+int styx_event_create(styx_ctx *ctx, styx_event *out) {
+    ENTER(ctx);
+    NEED(out, "null out");
+    cudaEvent_t e;
+    CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    *out = e;
+    return STYX_OK;
+}
+int styx_event_destroy(styx_ctx *ctx, styx_event ev) {
+    ENTER(ctx);
+    if (ev) CK(cudaEventDestroy(static_cast<cudaEvent_t>(ev)));
+    return STYX_OK;
+}
+int styx_event_record(styx_ctx *ctx, styx_event ev, styx_stream stream) {
+    ENTER(ctx);
+    CK(cudaEventRecord(static_cast<cudaEvent_t>(ev), S(stream)));
+    return STYX_OK;
+}
+int styx_stream_wait_event(styx_ctx *ctx, styx_stream stream, styx_event ev) {
+    ENTER(ctx);
+    CK(cudaStreamWaitEvent(S(stream), static_cast<cudaEvent_t>(ev), 0));
+    return STYX_OK;
+}
+
+int styx_graph_begin(styx_ctx *ctx, styx_stream stream) {
+    ENTER(ctx);
+    NEED(stream, "graph recording needs a non-default stream");
+    CK(cudaStreamBeginCapture(S(stream), cudaStreamCaptureModeThreadLocal));
+    return STYX_OK;
+}
+
+int styx_graph_end(styx_ctx *ctx, styx_stream stream, styx_graph *out) {
+    ENTER(ctx);
+    NEED(stream && out, "null stream / out");
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamEndCapture(S(stream), &g));
+    cudaGraphExec_t ex = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(STYX_ECUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(e));
+    *out = ex;
+    return STYX_OK;
+}
+
+int styx_graph_launch(styx_ctx *ctx, styx_graph graph, styx_stream stream) {
+    ENTER(ctx);
+    NEED(graph, "null graph");
+    CK(cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph), S(stream)));
+    return STYX_OK;
+}
+
+int styx_graph_destroy(styx_ctx *ctx, styx_graph graph) {
+    ENTER(ctx);
+    if (graph) CK(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph)));
+    return STYX_OK;
+}
+
+// ------------------------------------------------------------ single ops
+int styx_rms_norm(styx_ctx *ctx, styx_stream stream, const float *x, const float *w, float eps, int ncols,
+                  int nrows, float *out) {
+    ENTER(ctx);
+    NEED(x && out && ncols > 0 && nrows > 0, "bad rms_norm arguments");
+    CK(styx::launch_rms_norm(x, w, eps, ncols, nrows, out, S(stream)));
+    return STYX_OK;
+}
+
+int styx_matvec_f32(styx_ctx *ctx, styx_stream stream, const float *a, int nrows, int ncols, int stride_a,
+                    const float *x, float *d) {
+    ENTER(ctx);
+    NEED(a && x && d && nrows > 0 && ncols > 0 && stride_a >= ncols, "bad matvec_f32 arguments");
+    CK(styx::launch_matvec_f32(a, nrows, ncols, stride_a, x, d, S(stream)));
+    return STYX_OK;
+}
+
+int styx_topk_softmax(styx_ctx *ctx, styx_stream stream, const float *logits, int n, int k, int renorm,
+                      const uint32_t *remap, const uint32_t *pmap, float *weights, int32_t *ids64) {
+    ENTER(ctx);
+    NEED(logits && weights && ids64, "null pointer");
+    NEED(n > 0 && n <= STYX_MAX_EXPERTS, "n %d out of range", n);
+    NEED(k > 0 && k <= STYX_MAX_TOPK && k <= n, "k %d out of range", k);
+    CK(styx::launch_topk(logits, n, k, renorm, remap, pmap, weights, ids64, S(stream)));
+    return STYX_OK;
+}
+
+int styx_mul_mat_vec_id(styx_ctx *ctx, styx_stream stream, int qtype, const void *a, uint64_t expert_bytes,
+                        int n_expert, int nrows, int ncols, const int32_t *ids, int n_ids, const float *x,
+                        int stride_b, int ne11, float *y, int stride_d) {
+    ENTER(ctx);
+    NEED(a && ids && x && y, "null pointer");
+    NEED(qtype_ok(qtype), "unsupported qtype %d", qtype);
+    NEED(units_ok(qtype, ncols), "ncols %d not supported for qtype %d", ncols, qtype);
+    NEED(nrows > 0 && n_ids > 0 && ne11 > 0 && stride_b >= ncols && stride_d >= nrows && n_expert > 0, "bad shape");
+    NEED(ncols <= 65536, "ncols too large");
+    const long long rb = row_bytes(qtype, ncols);
+    NEED(expert_bytes >= static_cast<uint64_t>(rb) * nrows, "expert_bytes smaller than nrows rows");
+    if (qtype == STYX_Q4_K || qtype == STYX_Q5_K)
+        NEED(al16(a) && expert_bytes % 16 == 0 && rb % 16 == 0, "q4_K/q5_K matrices must be 16-byte aligned");
+    else
+        NEED((reinterpret_cast<uintptr_t>(a) & 1) == 0 && expert_bytes % 2 == 0, "matrix must be 2-byte aligned");
+    NEED(extent_ok(a, expert_bytes * static_cast<uint64_t>(n_expert)), "matrix buffer smaller than n_expert experts");
+    NEED(extent_ok(y, (static_cast<uint64_t>(n_ids - 1) * stride_d + nrows) * 4), "y buffer too small");
+    NEED(extent_ok(x, (static_cast<uint64_t>(std::min(ne11, n_ids) - 1) * stride_b + ncols) * 4), "x buffer too small");
+    styx::MatVecIdArgs m{};
+    m.a = static_cast<const uint8_t *>(a);
+    m.expert_bytes = expert_bytes;
+    m.n_expert = n_expert;
+    m.err = ctx->d_err;
+    m.nrows = nrows;
+    m.ncols = ncols;
+    m.rb = static_cast<int>(rb);
+    m.ids = ids;
+    m.n_ids = n_ids;
+    m.x = x;
+    m.stride_b = stride_b;
+    m.ne11 = ne11;
+    m.y = y;
+    m.stride_d = stride_d;
+    m.units = ncols / 64;
+    m.gs = std::min(32, pow2ceil(m.units));
+    CK(styx::launch_matvec_id(m, qtype, S(stream)));
+    return STYX_OK;
+}
+
+int styx_swiglu(styx_ctx *ctx, styx_stream stream, const float *g, const float *u, float *out, int n) {
+    ENTER(ctx);
+    NEED(g && u && out && n > 0, "bad swiglu arguments");
+    CK(styx::launch_swiglu(g, u, out, n, S(stream)));
+    return STYX_OK;
+}
+
+int styx_moe_reduce(styx_ctx *ctx, styx_stream stream, const float *d, const float *w, float *x, int ne, int k) {
+    ENTER(ctx);
+    NEED(d && w && x && ne > 0 && k > 0, "bad moe_reduce arguments");
+    CK(styx::launch_moe_reduce(d, w, x, ne, k, S(stream)));
+    return STYX_OK;
+}
+
+// true if a kernel may dereference p: device/managed memory, or pinned host
+// memory mapped at the same address (UVA)
+static bool device_readable(const void *p) {
+    cudaPointerAttributes pa{};
+    if (cudaPointerGetAttributes(&pa, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged) return true;
+    return pa.type == cudaMemoryTypeHost && pa.devicePointer == p;
+}
+
+static bool is_device_mem(const void *p) {
+    cudaPointerAttributes pa{};
+    if (cudaPointerGetAttributes(&pa, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged;
+}
+
+static int gather_check(const void *sg, const void *su, const void *sd, uint64_t bg, uint64_t bu, uint64_t bd,
+                        void *ag, void *au, void *ad, uint64_t dg, uint64_t du, uint64_t dd, int n_expert, int layer,
+                        int k) {
+    NEED(sg && su && sd && ag && au && ad, "null pointer");
+    NEED(n_expert > 0 && layer >= 0, "bad n_expert / layer");
+    const uint64_t ne = static_cast<uint64_t>(n_expert), slots = (static_cast<uint64_t>(layer) + 1) * k;
+    NEED(extent_ok(sg, bg * ne) && extent_ok(su, bu * ne) && extent_ok(sd, bd * ne),
+         "a source tensor is smaller than n_expert slabs");
+    NEED(extent_ok(ag, dg * slots) && extent_ok(au, du * slots) && extent_ok(ad, dd * slots),
+         "an arena is smaller than (layer+1)*k slots");
+    NEED(device_readable(sg) && device_readable(su) && device_readable(sd),
+         "gather sources must be device memory or mapped pinned host memory (STYX_MEM_HOST)");
+    NEED(is_device_mem(ag) && is_device_mem(au) && is_device_mem(ad), "arenas must be device memory");
+    NEED(bg % 16 == 0 && bu % 16 == 0 && bd % 16 == 0 && dg % 16 == 0 && du % 16 == 0 && dd % 16 == 0,
+         "slab sizes must be multiples of 16 bytes");
+    NEED(bg <= dg && bu <= du && bd <= dd, "arena slot smaller than the source slab");
+    NEED(al16(sg) && al16(su) && al16(sd) && al16(ag) && al16(au) && al16(ad), "buffers must be 16-byte aligned");
+    NEED(k > 0 && k <= STYX_MAX_TOPK, "k %d out of range", k);
+    return STYX_OK;
+}
+
+int styx_gather_slabs(styx_ctx *ctx, styx_stream stream, const void *src_g, const void *src_u, const void *src_d,
+                      uint64_t src_bytes_g, uint64_t src_bytes_u, uint64_t src_bytes_d, void *arena_g,
+                      void *arena_u, void *arena_d, uint64_t dst_bytes_g, uint64_t dst_bytes_u,
+                      uint64_t dst_bytes_d, const int32_t *ids, int n_expert, int layer, int k) {
+    ENTER(ctx);
+    int rc = gather_check(src_g, src_u, src_d, src_bytes_g, src_bytes_u, src_bytes_d, arena_g, arena_u, arena_d,
+                          dst_bytes_g, dst_bytes_u, dst_bytes_d, n_expert, layer, k);
+    if (rc) return rc;
+    NEED(ids, "null ids");
+    styx::GatherArgs a{};
+    a.n_expert = n_expert;
+    a.err = ctx->d_err;
+    a.src[0] = static_cast<const uint8_t *>(src_g);
+    a.src[1] = static_cast<const uint8_t *>(src_u);
+    a.src[2] = static_cast<const uint8_t *>(src_d);
+    a.src_bytes[0] = src_bytes_g;
+    a.src_bytes[1] = src_bytes_u;
+    a.src_bytes[2] = src_bytes_d;
+    a.dst[0] = static_cast<uint8_t *>(arena_g);
+    a.dst[1] = static_cast<uint8_t *>(arena_u);
+    a.dst[2] = static_cast<uint8_t *>(arena_d);
+    a.dst_bytes[0] = dst_bytes_g;
+    a.dst_bytes[1] = dst_bytes_u;
+    a.dst_bytes[2] = dst_bytes_d;
+    a.ids = ids;
+    a.layer = layer;
+    a.k = k;
+    CK(styx::launch_gather(a, S(stream)));
+    return STYX_OK;
+}
+
+int styx_gather_slabs_async(styx_ctx *ctx, styx_stream stream, const void *src_g, const void *src_u,
+                            const void *src_d, uint64_t src_bytes_g, uint64_t src_bytes_u, uint64_t src_bytes_d,
+                            void *arena_g, void *arena_u, void *arena_d, uint64_t dst_bytes_g,
+                            uint64_t dst_bytes_u, uint64_t dst_bytes_d, const int32_t *host_ids, int n_expert,
+                            int layer, int k) {
+    ENTER(ctx);
+    int rc = gather_check(src_g, src_u, src_d, src_bytes_g, src_bytes_u, src_bytes_d, arena_g, arena_u, arena_d,
+                          dst_bytes_g, dst_bytes_u, dst_bytes_d, n_expert, layer, k);
+    if (rc) return rc;
+    NEED(host_ids, "null ids");
+    for (int s = 0; s < k; s++)
+        NEED(static_cast<uint32_t>(host_ids[s]) == STYX_SKIP || (host_ids[s] >= 0 && host_ids[s] < n_expert),
+             "id %d of slot %d out of range", host_ids[s], s);
+    const void *src[3] = {src_g, src_u, src_d};
+    void *dst[3] = {arena_g, arena_u, arena_d};
+    const uint64_t sb[3] = {src_bytes_g, src_bytes_u, src_bytes_d}, db[3] = {dst_bytes_g, dst_bytes_u, dst_bytes_d};
+    for (int s = 0; s < k; s++) {
+        const uint32_t e = static_cast<uint32_t>(host_ids[s]);
+        if (e == STYX_SKIP) continue;
+        const uint64_t slot = static_cast<uint64_t>(layer) * k + s;
+        for (int t = 0; t < 3; t++)
+            CK(cudaMemcpyAsync(static_cast<uint8_t *>(dst[t]) + slot * db[t],
+                               static_cast<const uint8_t *>(src[t]) + e * sb[t], sb[t], cudaMemcpyDefault,
+                               S(stream)));
+    }
+    return STYX_OK;
+}
+
+// ---------------------------------------------------------- MoE block
+int styx_moe_workspace_bytes(const styx_moe_dims *dims, uint64_t *out) {
+    int rc = check_dims(dims);
+    if (rc) return rc;
+    NEED(out, "null out");
+    *out = ws_layout(*dims).total;
+    return STYX_OK;
+}
+
+int styx_moe_workspace_init(styx_ctx *ctx, styx_stream stream, void *ws, uint64_t bytes) {
+    ENTER(ctx);
+    NEED(ws, "null workspace");
+    CK(cudaMemsetAsync(ws, 0, bytes, S(stream)));
+    return STYX_OK;
+}
+
+int styx_moe_workspace_view(const styx_moe_dims *dims, void *workspace, int which, void **out) {
+    int rc = check_dims(dims);
+    if (rc) return rc;
+    NEED(workspace && out, "null pointer");
+    const WsLayout L = ws_layout(*dims);
+    size_t off;
+    switch (which) {
+    case 0: off = L.xnorm; break;
+    case 1: off = L.logits; break;
+    case 2: off = L.h; break;
+    case 3: off = L.weights; break;
+    default: return fail(STYX_EINVAL, "unknown view %d", which);
+    }
+    *out = static_cast<uint8_t *>(workspace) + off;
+    return STYX_OK;
+}
+
+int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims, const styx_moe_layer *lw, int layer,
+                   float *x, int32_t *ids, float *weights_out, void *workspace, uint64_t workspace_bytes) {
+    ENTER(ctx);
+    int rc = check_dims(dims);
+    if (rc) return rc;
+    NEED(lw && x && ids && workspace, "null pointer");
+    NEED(layer >= 0, "negative layer");
+    NEED(lw->router && lw->ffn_norm, "router and ffn_norm are required");
+    const int H = dims->n_embd, F = dims->n_ff, E = dims->n_expert, k = dims->n_expert_used;
+    if ((rc = check_tensor(lw->gate, "gate", F, H, E))) return rc;
+    if ((rc = check_tensor(lw->up, "up", F, H, E))) return rc;
+    if ((rc = check_tensor(lw->down, "down", H, F, E))) return rc;
+    const WsLayout L = ws_layout(*dims);
+    NEED(workspace_bytes >= L.total, "workspace %llu bytes < %llu", (unsigned long long)workspace_bytes,
+         (unsigned long long)L.total);
+    NEED(al16(workspace) && al16(x) && al16(lw->router), "workspace, x and router must be 16-byte aligned");
+    NEED(extent_ok(workspace, L.total), "workspace allocation smaller than workspace_bytes");
+    NEED(extent_ok(lw->router, static_cast<uint64_t>(E) * H * 4), "router smaller than n_expert x n_embd");
+    NEED(extent_ok(lw->ffn_norm, static_cast<uint64_t>(H) * 4) && extent_ok(x, static_cast<uint64_t>(H) * 4),
+         "ffn_norm / x smaller than n_embd");
+    NEED(extent_ok(ids, (static_cast<uint64_t>(layer) + 1) * STYX_IDS_PER_LAYER * 4), "ids buffer too small");
+    NEED(!lw->remap || extent_ok(lw->remap, static_cast<uint64_t>(E) * 4), "remap smaller than n_expert");
+    NEED(!lw->pmap || extent_ok(lw->pmap, static_cast<uint64_t>(E) * 4), "pmap smaller than n_expert");
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    int32_t *ids64 = ids + static_cast<size_t>(layer) * STYX_IDS_PER_LAYER;
+    float *wts = weights_out ? weights_out : reinterpret_cast<float *>(ws + L.weights);
+    const cudaStream_t st = S(stream);
+
+    // 1. route
+    styx::RouteArgs ra{};
+    ra.x = x;
+    ra.norm_w = lw->ffn_norm;
+    ra.eps = dims->rms_eps;
+    ra.router = lw->router;
+    ra.E = E;
+    ra.H = H;
+    ra.k = k;
+    ra.renorm = dims->norm_topk;
+    ra.remap = lw->remap;
+    ra.pmap = lw->pmap;
+    ra.xnorm = reinterpret_cast<float *>(ws + L.xnorm);
+    ra.xd1 = reinterpret_cast<int8_t *>(ws + L.xd1);
+    ra.xd2 = ws + L.xd2;
+    ra.xd3 = ws + L.xd3;
+    ra.xscale = reinterpret_cast<float *>(ws + L.xscale);
+    ra.logits = reinterpret_cast<float *>(ws + L.logits);
+    ra.weights = wts;
+    ra.ids64 = ids64;
+    ra.counter = reinterpret_cast<unsigned *>(ws + L.counter);
+    ra.err = ctx->d_err;
+    CK(styx::launch_route(ra, st));
+
+    float *h = reinterpret_cast<float *>(ws + L.h);
+    const int units_g = H / 64;
+    // 2. gate/up + SiLU
+    if (lw->gate.qtype == lw->up.qtype && units_g <= 32) {
+        styx::GateUpArgs ga{};
+        ga.gate = to_src(lw->gate, E);
+        ga.up = to_src(lw->up, E);
+        ga.ids64 = ids64;
+        ga.xd1 = ra.xd1;
+        ga.xd2 = ra.xd2;
+        ga.xd3 = ra.xd3;
+        ga.xscale = ra.xscale;
+        ga.h = h;
+        ga.H = H;
+        ga.F = F;
+        ga.k = k;
+        ga.rb_g = static_cast<int>(row_bytes(lw->gate.qtype, H));
+        ga.rb_u = static_cast<int>(row_bytes(lw->up.qtype, H));
+        ga.units = units_g;
+        ga.gs = pow2ceil(units_g);
+        ga.ch = 8;
+        ga.up_off = static_cast<uint32_t>(a16(static_cast<size_t>(ga.ch) * ga.rb_g + 32));
+        ga.stage_bytes = ga.up_off + static_cast<uint32_t>(a16(static_cast<size_t>(ga.ch) * ga.rb_u + 32));
+        const int T = k * F;
+        const int grid = std::max(1, std::min(ctx->sm_count, (T + ga.ch - 1) / ga.ch));
+        const int rows_per_cta = (T + grid - 1) / grid;
+        const int max_st = static_cast<int>((227 * 1024 - 256) / ga.stage_bytes);
+        NEED(max_st >= 2, "gate/up rows too large for shared memory");
+        ga.nst = std::max(2, std::min({16, max_st, (rows_per_cta + ga.ch - 1) / ga.ch + 1}));
+        ga.err = ctx->d_err;
+        CK(styx::launch_gate_up(ga, lw->gate.qtype, grid, st));
+    } else {
+        float *g = reinterpret_cast<float *>(ws + L.g), *u = reinterpret_cast<float *>(ws + L.u);
+        if ((rc = matvec_id_3way(lw->gate, E, ids64, F, H, k, ra.xnorm, 1, g, ctx->d_err, st))) return rc;
+        if ((rc = matvec_id_3way(lw->up, E, ids64, F, H, k, ra.xnorm, 1, u, ctx->d_err, st))) return rc;
+        CK(styx::launch_swiglu(g, u, h, k * F, st));
+    }
+
+    // 3. down + weighted combine into x
+    styx::DownArgs da{};
+    da.down = to_src(lw->down, E);
+    da.ids64 = ids64;
+    da.h = h;
+    da.w = wts;
+    da.x = x;
+    da.d_out = nullptr;
+    da.H = H;
+    da.F = F;
+    da.k = k;
+    da.rb = static_cast<int>(row_bytes(lw->down.qtype, F));
+    da.units = F / 64;
+    da.gs = pow2ceil(da.units);
+    da.rc = 4;
+    da.slot_stride = static_cast<uint32_t>(a16(static_cast<size_t>(da.rc) * da.rb + 32));
+    da.stage_bytes = da.slot_stride * static_cast<uint32_t>(k);
+    const int grid_d = std::max(1, std::min(ctx->sm_count, H / da.rc));
+    const int rows_d = (H + grid_d - 1) / grid_d;
+    da.dig_off = 512;
+    const size_t kF = static_cast<size_t>(k) * F;
+    const size_t dig_bytes = kF * 3 + kF / 32 * 4;
+    const int chunks = (rows_d + da.rc - 1) / da.rc;
+    const size_t fixed = a128(a128(da.dig_off + dig_bytes) + static_cast<size_t>(std::max(2, chunks)) * k * da.rc * 4);
+    NEED(fixed < 227 * 1024, "down kernel: k*n_ff too large for shared memory");
+    int nst = std::min({16, chunks, static_cast<int>((227 * 1024 - fixed) / da.stage_bytes)});
+    NEED(nst >= 1, "down rows too large for shared memory");
+    da.nst = nst;
+    da.part_off = static_cast<uint32_t>(a128(da.dig_off + dig_bytes));
+    da.stage_off = static_cast<uint32_t>(a128(da.part_off + static_cast<size_t>(std::max(2, nst)) * k * da.rc * 4));
+    const uint32_t smem_d = da.stage_off + static_cast<uint32_t>(nst) * da.stage_bytes;
+    NEED(smem_d <= 227 * 1024, "down kernel needs %u bytes of shared memory", smem_d);
+    da.err = ctx->d_err;
+    CK(styx::launch_down(da, lw->down.qtype, grid_d, smem_d, st));
+    return STYX_OK;
+}
+
+// ------------------------------------------------------------- synth
+int styx_synth_quant(styx_ctx *ctx, styx_stream stream, int qtype, void *dst, uint64_t nrows, int ncols,
+                     uint64_t seed, float sigma) {
+    ENTER(ctx);
+    NEED(dst, "null dst");
+    NEED(qtype_ok(qtype) && row_bytes(qtype, ncols) > 0, "bad qtype/ncols");
+    CK(styx::launch_synth_quant(qtype, static_cast<uint8_t *>(dst), nrows, ncols, seed, sigma, S(stream)));
+    return STYX_OK;
+}
+
+int styx_synth_f32(styx_ctx *ctx, styx_stream stream, float *dst, uint64_t n, uint64_t seed, uint64_t offset,
+                   float sigma) {
+    ENTER(ctx);
+    NEED(dst, "null dst");
+    CK(styx::launch_synth_f32(dst, n, seed, offset, sigma, S(stream)));
+    return STYX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,181 @@
+// common.cuh -- shared device helpers for the styx B200 MoE kernels.
+//
+// * PTX wrappers for mbarriers and 1-D bulk copies (cp.async.bulk, the TMA
+//   engine's non-tensor form) used to stage expert slabs into shared memory.
+// * Bounded waits: every spin on an mbarrier gives up after ~1 s of device
+//   clock, sets the context's device error word and lets the kernel finish.
+// * dp4a wrappers and the "digit" decomposition of activations used by the
+//   quantised dot products (see qdot.cuh).
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/styx_moe.h"
+
+namespace styx {
+
+constexpr uint32_t kSkip = 0xFFFFFFFFu;
+constexpr int kIdsPerLayer = STYX_IDS_PER_LAYER;
+
+// device error codes written to the error word
+enum : int {
+    kErrNone = 0,
+    kErrWaitFull = 1,    // consumer gave up waiting for a bulk copy
+    kErrWaitEmpty = 2,   // producer gave up waiting for a free stage
+    kErrWaitRoute = 3,   // route: last-block handoff failed
+    kErrBadId = 4,       // an expert id / hot index / arena slot out of range
+};
+
+// ~1 s at the B200's 1.9 GHz SM clock
+constexpr long long kSpinCycles = 2000000000LL;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase.  Returns false (and records `code` in
+// the error word) if the phase did not complete within kSpinCycles.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    long long t0 = clock64();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (clock64() - t0 > kSpinCycles) {
+            if (err) atomicExch(err, code);
+            return false;
+        }
+    }
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Programmatic dependent launch (sm_90+): wait for the previous grid's
+// memory, and allow the next grid to be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// ---------------------------------------------------------------- dp4a
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+    return __dp4a(static_cast<int>(a), static_cast<int>(b), c);
+}
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+    return static_cast<int>(__dp4a(a, b, static_cast<unsigned>(c)));
+}
+// signed a (s8 lanes) x unsigned b (u8 lanes)
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
+    int r;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+// ------------------------------------------------ unaligned smem loads
+// 16 bytes from any 1-byte aligned address (shared or global): the aligned
+// words that cover the range and a funnel shift.  Touches no byte outside
+// the 4-byte words that hold [p, p+16).
+__device__ __forceinline__ uint4 lds16_unaligned(const uint8_t *p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const uint32_t sh = static_cast<uint32_t>(a & 3) * 8u;
+    const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3];
+    const uint32_t w4 = sh ? w[4] : 0u;
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh),
+                      __funnelshift_r(w2, w3, sh), __funnelshift_r(w3, w4, sh));
+}
+__device__ __forceinline__ uint2 lds8_unaligned(const uint8_t *p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const uint32_t sh = static_cast<uint32_t>(a & 3) * 8u;
+    const uint32_t w0 = w[0], w1 = w[1];
+    const uint32_t w2 = sh ? w[2] : 0u;
+    return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
+}
+
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFFu)));
+}
+
+// ------------------------------------------------------ digit vectors
+// An activation vector v (length n, n % 32 == 0) is carried to the quantised
+// dot products as three byte planes and a power-of-two scale per 32-element
+// group g:
+//   v[i] ~= s_g * (D1[i] + D2[i]/256 + D3[i]/65536)
+// D1 = floor(v/s) in [-64, 63] (s8), D2 = floor(256*frac) in [0,255] (u8),
+// D3 = round(256*frac') in [0,255] (u8).  s_g = 2^(e-5) for 2^e <= max|v_g|.
+// The representation error is below s_g * 2^-16 <= max|v_g| * 2^-21, so a
+// dot product against integer weight codes is exact to ~f32 precision while
+// the inner loop runs on dp4a.
+struct DigitsView {
+    int8_t *d1;
+    uint8_t *d2;
+    uint8_t *d3;
+    float *scale;   // n/32 group scales
+};
+
+// one 32-element group, one element per lane of a full warp
+__device__ __forceinline__ void digits_group_warp(float v, int lane, const DigitsView &dv, int g) {
+    float a = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    float s = 1.0f;
+    if (a > 0.f && a < INFINITY) {
+        int e = ((__float_as_uint(a) >> 23) & 0xFF);   // biased exponent of max
+        int se = e - 5;                                 // s = 2^(E-5)
+        if (se < 1) se = 1;
+        s = __uint_as_float(static_cast<uint32_t>(se) << 23);
+    }
+    const float q = v / s;                 // exact: s is a power of two
+    const float f1 = floorf(q);
+    const float r1 = (q - f1) * 256.f;     // exact
+    const float f2 = floorf(r1);
+    const float r2 = (r1 - f2) * 256.f;
+    float f3 = rintf(r2);
+    if (f3 > 255.f) f3 = 255.f;
+    const int i = g * 32 + lane;
+    dv.d1[i] = static_cast<int8_t>(static_cast<int>(f1));
+    dv.d2[i] = static_cast<uint8_t>(static_cast<int>(f2));
+    dv.d3[i] = static_cast<uint8_t>(static_cast<int>(f3));
+    if (lane == 0) dv.scale[g] = s;
+}
+
+}  // namespace styx

@@ -1,0 +1,119 @@
+// kernels.h -- host-side launch interface of the styx B200 kernels
+// (internal to libstyx_moe.so; the public surface is include/styx_moe.h).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace styx {
+
+// One expert tensor with its placement (see styx_expert_tensor).
+struct ExpSrc {
+    const uint8_t *full;
+    const uint8_t *hot;
+    const uint8_t *arena;
+    uint64_t slab;
+    uint64_t aslab;
+    uint32_t nfull, nhot, narena;   // id bounds of each source
+};
+
+struct RouteArgs {
+    const float *x;          // residual f32[H]
+    const float *norm_w;     // ffn_norm f32[H] or null
+    float eps;
+    const float *router;     // f32[E][H]
+    int E, H, k, renorm;
+    const uint32_t *remap, *pmap;
+    float *xnorm;            // out f32[H]
+    int8_t *xd1;             // out digit planes of xnorm
+    uint8_t *xd2, *xd3;
+    float *xscale;           // out f32[H/32]
+    float *logits;           // out f32[E]
+    float *weights;          // out f32[k]
+    int32_t *ids64;          // out: the layer's 64-int id block
+    unsigned *counter;       // zero on entry, zero on exit
+    int *err;
+};
+
+struct GateUpArgs {
+    ExpSrc gate, up;
+    const int32_t *ids64;
+    const int8_t *xd1;
+    const uint8_t *xd2, *xd3;
+    const float *xscale;
+    float *h;                // out f32[k][F]
+    int H, F, k;
+    int rb_g, rb_u;          // row bytes
+    int units, gs;           // 64-element units per row, lane group size
+    int ch, nst;             // rows per chunk, pipeline stages
+    uint32_t stage_bytes, up_off;
+    int *err;
+};
+
+struct DownArgs {
+    ExpSrc down;
+    const int32_t *ids64;
+    const float *h;          // f32[k][F]
+    const float *w;          // f32[k]
+    float *x;                // residual f32[H], += combine
+    float *d_out;            // optional f32[k][H]
+    int H, F, k, rb;
+    int units, gs;
+    int rc, nst;             // rows per chunk, stages
+    uint32_t stage_bytes, slot_stride;
+    uint32_t dig_off, part_off, stage_off;
+    int *err;
+};
+
+struct MatVecIdArgs {
+    const uint8_t *a;
+    uint64_t expert_bytes;
+    int n_expert;
+    int *err;
+    int nrows, ncols, rb;
+    const int32_t *ids;
+    int n_ids;
+    const float *x;
+    int stride_b, ne11;
+    float *y;
+    int stride_d;
+    int units, gs;
+};
+
+struct GatherArgs {
+    const uint8_t *src[3];
+    uint64_t src_bytes[3];
+    uint8_t *dst[3];
+    uint64_t dst_bytes[3];
+    const int32_t *ids;
+    int n_expert;
+    int *err;
+    int layer, k;
+};
+
+// launchers (return the launch error)
+cudaError_t launch_route(const RouteArgs &a, cudaStream_t st);
+cudaError_t launch_gate_up(const GateUpArgs &a, int qtype, int grid, cudaStream_t st);
+cudaError_t launch_down(const DownArgs &a, int qtype, int grid, uint32_t smem, cudaStream_t st);
+cudaError_t launch_matvec_id(const MatVecIdArgs &a, int qtype, cudaStream_t st);
+cudaError_t launch_rms_norm(const float *x, const float *w, float eps, int ncols, int nrows,
+                            float *out, cudaStream_t st);
+cudaError_t launch_matvec_f32(const float *a, int nrows, int ncols, int stride_a, const float *x,
+                              float *d, cudaStream_t st);
+cudaError_t launch_topk(const float *logits, int n, int k, int renorm, const uint32_t *remap,
+                        const uint32_t *pmap, float *weights, int32_t *ids64, cudaStream_t st);
+cudaError_t launch_swiglu(const float *g, const float *u, float *out, int n, cudaStream_t st);
+cudaError_t launch_moe_reduce(const float *d, const float *w, float *x, int ne, int k,
+                              cudaStream_t st);
+cudaError_t launch_gather(const GatherArgs &a, cudaStream_t st);
+cudaError_t launch_synth_quant(int qtype, uint8_t *dst, uint64_t nrows, int ncols, uint64_t seed,
+                               float sigma, cudaStream_t st);
+cudaError_t launch_synth_f32(float *dst, uint64_t n, uint64_t seed, uint64_t offset, float sigma,
+                             cudaStream_t st);
+
+// shared-memory plan of the fused kernels (computed on the host)
+int gate_up_smem(const GateUpArgs &a);
+constexpr int kConsumerWarps = 8;
+constexpr int kFusedThreads = 32 * (kConsumerWarps + 1);
+
+}  // namespace styx

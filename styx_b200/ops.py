@@ -1,0 +1,271 @@
+"""Torch-facing wrappers of the styx MoE-block operators.
+
+Each function mirrors one dispatch that MoeModel::forward_token records for
+the MoE block (crates/model/src/moe.rs:1974-2062) and calls the sm_100a
+kernels of libstyx_moe.so through its C ABI.  Device tensors are passed by
+pointer; work is queued on torch's current CUDA stream.  There is no CPU
+path: without the library or a GPU these functions raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import (BLOCK, IDS_PER_LAYER, Q4_K, Q5_K, Q6_K, Q8_0, SKIP, ExpertTensor,  # noqa: F401
+                   MoeDims, MoeLayer, StyxError, check, lib, row_bytes)
+
+_ctxs: dict[int, "Context"] = {}
+
+
+class Context:
+    """styx_ctx for one CUDA device (Gpu::new, crates/vk-backend/src/lib.rs:356)."""
+
+    def __init__(self, device: int = 0):
+        self.device = device
+        h = C.c_void_p()
+        check(lib().styx_init(device, C.byref(h)))
+        self.handle = h
+        n = C.c_int()
+        name = C.create_string_buffer(256)
+        check(lib().styx_device_info(h, C.byref(n), name, 256))
+        self.sm_count = n.value
+        self.name = name.value.decode()
+
+    def vram_bytes(self) -> int:
+        v = C.c_uint64()
+        check(lib().styx_vram_bytes(self.handle, C.byref(v)))
+        return v.value
+
+    def check_device_error(self, stream=None) -> None:
+        check(lib().styx_check_device_error(self.handle, _stream(stream)))
+
+
+def ctx(device: Optional[int] = None) -> Context:
+    if device is None:
+        device = torch.cuda.current_device()
+    if device not in _ctxs:
+        _ctxs[device] = Context(device)
+    return _ctxs[device]
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    if t is None:
+        return None
+    return C.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream)
+
+
+def _dev(t: torch.Tensor) -> int:
+    assert t.is_cuda, "styx ops take CUDA tensors"
+    return t.device.index
+
+
+class HostBuffer:
+    """Pinned, device-mapped host memory (STYX_MEM_HOST, the GTT tier of
+    create_buffer_host_shared, lib.rs:802).  `.tensor` is a CPU uint8 view
+    whose data_ptr the kernels can read."""
+
+    def __init__(self, nbytes: int, device: Optional[int] = None):
+        self.ctx = ctx(device)
+        p = C.c_void_p()
+        check(lib().styx_alloc(self.ctx.handle, nbytes, _lib.MEM_HOST, C.byref(p)))
+        self.ptr = p.value
+        self.nbytes = nbytes
+        arr = (C.c_uint8 * nbytes).from_address(self.ptr)
+        self.tensor = torch.frombuffer(arr, dtype=torch.uint8)
+
+    def free(self) -> None:
+        if self.ptr:
+            self.tensor = None
+            check(lib().styx_free(self.ctx.handle, C.c_void_p(self.ptr)))
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------ ops
+def rms_norm(x: torch.Tensor, w: Optional[torch.Tensor], eps: float) -> torch.Tensor:
+    nrows = 1 if x.dim() == 1 else x.shape[0]
+    out = torch.empty_like(x)
+    check(lib().styx_rms_norm(ctx(_dev(x)).handle, _stream(), _ptr(x), _ptr(w), eps, x.shape[-1], nrows,
+                              _ptr(out)))
+    return out
+
+
+def matvec_f32(a: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    d = torch.empty(a.shape[0], dtype=torch.float32, device=a.device)
+    check(lib().styx_matvec_f32(ctx(_dev(a)).handle, _stream(), _ptr(a), a.shape[0], a.shape[1], a.stride(0),
+                                _ptr(x), _ptr(d)))
+    return d
+
+
+def topk_softmax(logits: torch.Tensor, k: int, renorm: bool = True, remap: Optional[torch.Tensor] = None,
+                 pmap: Optional[torch.Tensor] = None):
+    """-> (weights f32[k], ids64 i32[64]) (shaders/topk_softmax_f32.comp)."""
+    w = torch.empty(k, dtype=torch.float32, device=logits.device)
+    ids = torch.full((IDS_PER_LAYER,), -1, dtype=torch.int32, device=logits.device)
+    check(lib().styx_topk_softmax(ctx(_dev(logits)).handle, _stream(), _ptr(logits), logits.numel(), k,
+                                  int(renorm), _ptr(remap), _ptr(pmap), _ptr(w), _ptr(ids)))
+    return w, ids
+
+
+def mul_mat_vec_id(qtype: int, a: torch.Tensor, expert_bytes: int, nrows: int, ncols: int, ids: torch.Tensor,
+                   x: torch.Tensor, ne11: int, y: Optional[torch.Tensor] = None,
+                   n_expert: Optional[int] = None) -> torch.Tensor:
+    """y[s*nrows + r] = deq(A[ids[s]])[r] . x[s % ne11] (MatVecIdPush semantics)."""
+    n_ids = ids.numel()
+    if n_expert is None:
+        n_expert = a.numel() // expert_bytes
+    if y is None:
+        y = torch.zeros(n_ids * nrows, dtype=torch.float32, device=a.device)
+    check(lib().styx_mul_mat_vec_id(ctx(_dev(a)).handle, _stream(), qtype, _ptr(a), expert_bytes, n_expert, nrows,
+                                    ncols, _ptr(ids), n_ids, _ptr(x), ncols, ne11, _ptr(y), nrows))
+    return y
+
+
+def swiglu(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    out = torch.empty_like(g)
+    check(lib().styx_swiglu(ctx(_dev(g)).handle, _stream(), _ptr(g), _ptr(u), _ptr(out), g.numel()))
+    return out
+
+
+def moe_reduce(d: torch.Tensor, w: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """x += sum_s w[s] * d[s] in place (shaders/moe_reduce_f32.comp)."""
+    check(lib().styx_moe_reduce(ctx(_dev(x)).handle, _stream(), _ptr(d), _ptr(w), _ptr(x), x.numel(), w.numel()))
+    return x
+
+
+def gather_slabs(srcs, src_bytes, arenas, dst_bytes, ids: torch.Tensor, layer: int, k: int,
+                 n_expert: Optional[int] = None) -> None:
+    """shaders/gather_slabs_f32.comp: srcs may be HostBuffer tensors (GTT)."""
+    if n_expert is None:
+        n_expert = srcs[0].numel() // src_bytes[0]
+    check(lib().styx_gather_slabs(ctx(_dev(ids)).handle, _stream(), *[_ptr(s) for s in srcs], *src_bytes,
+                                  *[_ptr(a) for a in arenas], *dst_bytes, _ptr(ids), n_expert, layer, k))
+
+
+def gather_slabs_async(srcs, src_bytes, arenas, dst_bytes, host_ids, layer: int, k: int, stream=None,
+                       n_expert: Optional[int] = None) -> None:
+    if n_expert is None:
+        n_expert = srcs[0].numel() // src_bytes[0]
+    ids = (C.c_int32 * len(host_ids))(*[int(v) for v in host_ids])
+    check(lib().styx_gather_slabs_async(ctx(_dev(arenas[0])).handle, _stream(stream), *[_ptr(s) for s in srcs],
+                                        *src_bytes, *[_ptr(a) for a in arenas], *dst_bytes, ids, n_expert, layer,
+                                        k))
+
+
+def synth_quant(qtype: int, nrows: int, ncols: int, seed: int, sigma: float, out: Optional[torch.Tensor] = None,
+                device: Optional[int] = None) -> torch.Tensor:
+    """Synthetic N(0, sigma) rows quantised on the device."""
+    rb = row_bytes(qtype, ncols)
+    if out is None:
+        out = torch.empty(nrows * rb, dtype=torch.uint8, device=f"cuda:{device if device is not None else torch.cuda.current_device()}")
+    check(lib().styx_synth_quant(ctx(_dev(out)).handle, _stream(), qtype, _ptr(out), nrows, ncols, seed, sigma))
+    return out
+
+
+def synth_f32(n: int, seed: int, offset: int, sigma: float, device: Optional[int] = None) -> torch.Tensor:
+    out = torch.empty(n, dtype=torch.float32, device=f"cuda:{device if device is not None else torch.cuda.current_device()}")
+    check(lib().styx_synth_f32(ctx(_dev(out)).handle, _stream(), _ptr(out), n, seed, offset, sigma))
+    return out
+
+
+# ------------------------------------------------------------ MoE block
+@dataclass
+class Experts:
+    """One expert tensor and its placement (ExpMat, moe.rs:97-106).
+
+    full: uint8 [E*slab] (device); hot: dense hot slabs or None; arena: the
+    arena base or None (global slot = layer*k + s)."""
+    qtype: int
+    full: Optional[torch.Tensor]
+    slab_bytes: int
+    hot: Optional[torch.Tensor] = None
+    arena: Optional[torch.Tensor] = None
+    arena_slab_bytes: int = 0
+
+    def struct(self) -> ExpertTensor:
+        n_hot = self.hot.numel() // self.slab_bytes if self.hot is not None else 0
+        n_arena = self.arena.numel() // self.arena_slab_bytes if self.arena is not None else 0
+        return ExpertTensor(self.full.data_ptr() if self.full is not None else None,
+                            self.hot.data_ptr() if self.hot is not None else None,
+                            self.arena.data_ptr() if self.arena is not None else None,
+                            self.slab_bytes, self.arena_slab_bytes, self.qtype, n_hot, n_arena)
+
+
+@dataclass
+class LayerWeights:
+    """Per-layer MoE weights (Layer, moe.rs:108-144)."""
+    ffn_norm: torch.Tensor          # f32[H]
+    router: torch.Tensor            # f32[E][H]
+    gate: Experts
+    up: Experts
+    down: Experts
+    remap: Optional[torch.Tensor] = None   # i32/u32[E], -1 = SKIP
+    pmap: Optional[torch.Tensor] = None
+
+    def struct(self) -> MoeLayer:
+        return MoeLayer(self.ffn_norm.data_ptr(), self.router.data_ptr(),
+                        self.remap.data_ptr() if self.remap is not None else None,
+                        self.pmap.data_ptr() if self.pmap is not None else None,
+                        self.gate.struct(), self.up.struct(), self.down.struct())
+
+
+@dataclass
+class Dims:
+    n_embd: int
+    n_ff: int
+    n_expert: int
+    n_expert_used: int
+    norm_topk: bool = True
+    rms_eps: float = 1e-6
+
+    def struct(self) -> MoeDims:
+        return MoeDims(self.n_embd, self.n_ff, self.n_expert, self.n_expert_used, int(self.norm_topk),
+                       self.rms_eps)
+
+
+class MoeBlock:
+    """The MoE block of MoeModel::forward_token on one device.
+
+    Holds the workspace; `forward` runs route, gate/up+SiLU and
+    down+combine (3 kernels) and updates x in place."""
+
+    def __init__(self, dims: Dims, device: int = 0):
+        self.dims = dims
+        self.device = device
+        self._dims = dims.struct()
+        n = C.c_uint64()
+        check(lib().styx_moe_workspace_bytes(C.byref(self._dims), C.byref(n)))
+        self.ws_bytes = n.value
+        self.workspace = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=f"cuda:{device}")
+        self.ctx = ctx(device)
+        self._structs: dict[int, MoeLayer] = {}
+
+    def forward(self, x: torch.Tensor, layer_w: LayerWeights, layer: int, ids: torch.Tensor,
+                weights_out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        st = layer_w.struct()
+        check(lib().styx_moe_block(self.ctx.handle, _stream(stream), C.byref(self._dims), C.byref(st), layer,
+                                   _ptr(x), _ptr(ids), _ptr(weights_out), _ptr(self.workspace),
+                                   self.ws_bytes))
+        return x
+
+    def view(self, which: int, n: int) -> torch.Tensor:
+        """xnorm (0), logits (1), h (2), weights (3) of the last forward."""
+        p = C.c_void_p()
+        check(lib().styx_moe_workspace_view(C.byref(self._dims), _ptr(self.workspace), which, C.byref(p)))
+        off = p.value - self.workspace.data_ptr()
+        return self.workspace[off: off + 4 * n].view(torch.float32)
