@@ -309,6 +309,8 @@ def main() -> int:
         replay(i)
     stream.synchronize()
     blk.ctx.check_device_error(stream)
+    kernel_path = {1: "single cooperative kernel per MoE block", 2: "three kernels per MoE block"}.get(
+        blk.ctx.last_moe_path(), "unknown")
 
     def barrier():
         if pg:
@@ -392,10 +394,10 @@ def main() -> int:
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8-dp4a/f32 (q4_K,q6_K weights)", "data": "synthetic",
-            "config": workload_config(world),
+            "config": dict(workload_config(world), kernels=kernel_path),
             "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": H * 4,
                     "d2h_bytes_per_step": H * 4 + L * 256, "wall_s": t_wall},
-            "gpu_launches": args.steps * L * 3,
+            "gpu_launches": args.steps * L * (1 if blk.ctx.last_moe_path() == 1 else 3),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "unit_of_work": "one MoE block (route + gate/up + down kernels)",

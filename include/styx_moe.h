@@ -78,10 +78,24 @@ void styx_destroy(styx_ctx *ctx);
 int styx_vram_bytes(styx_ctx *ctx, uint64_t *out);
 /* SM count and name of the bound device (Gpu::device_name). */
 int styx_device_info(styx_ctx *ctx, int *sm_count, char *name, int name_len);
-/* Reads and clears the device-side error word that bounded waits set
- * (returns STYX_ETIMEOUT if one fired since the last call).  Synchronises
- * the stream. */
+/* Reads and clears the device-side error word that bounded waits and
+ * device-side id bounds checks set (STYX_ETIMEOUT / STYX_EINVAL if one fired
+ * since the last call).  Synchronises the stream.  After a timeout, re-run
+ * styx_moe_workspace_init on the workspaces in use. */
 int styx_check_device_error(styx_ctx *ctx, styx_stream stream);
+
+/* Options.  STYX_OPT_MOE_KERNELS selects how styx_moe_block runs: 0 = auto
+ * (the single cooperative kernel when the shape and formats fit, else three
+ * kernels), 1 = single kernel only (STYX_EUNSUPPORTED if it does not fit),
+ * 2 = three kernels.  STYX_OPT_MOE_LAST_PATH (read only) = 1 or 2, the form
+ * the last styx_moe_block call used.  STYX_OPT_TRACE = 1 makes the single
+ * kernel record 16 clock64 stamps per CTA at its phase boundaries into the
+ * workspace (styx_moe_workspace_view 4: int64[CTAs][16]). */
+#define STYX_OPT_MOE_KERNELS 1
+#define STYX_OPT_MOE_LAST_PATH 2
+#define STYX_OPT_TRACE 3
+int styx_set_option(styx_ctx *ctx, int option, int64_t value);
+int styx_get_option(styx_ctx *ctx, int option, int64_t *value);
 
 /* ------------------------------------------------------------ memory */
 /* create_buffer / create_buffer_host / create_buffer_host_shared
@@ -257,7 +271,8 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream,
 
 /* Debug / test views of the last styx_moe_block's intermediates kept in the
  * workspace: which = 0 xnorm f32[H], 1 logits f32[E], 2 h f32[k*F],
- * 3 weights f32[k].  Returns a device pointer into the workspace. */
+ * 3 weights f32[k], 4 phase trace int64[CTAs][16] (STYX_OPT_TRACE).  Returns a
+ * device pointer into the workspace. */
 int styx_moe_workspace_view(const styx_moe_dims *dims, void *workspace,
                             int which, void **out);
 

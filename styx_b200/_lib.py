@@ -19,6 +19,8 @@ BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
 SKIP = 0xFFFFFFFF
 IDS_PER_LAYER = 64
 MEM_DEVICE, MEM_HOST = 0, 1
+OPT_MOE_KERNELS, OPT_MOE_LAST_PATH, OPT_TRACE = 1, 2, 3
+MOE_AUTO, MOE_FUSED, MOE_SPLIT = 0, 1, 2
 
 
 class StyxError(RuntimeError):
@@ -52,6 +54,8 @@ _SIGS = {
     "styx_vram_bytes": (_i, [_vp, C.POINTER(_u64)]),
     "styx_device_info": (_i, [_vp, C.POINTER(_i), C.c_char_p, _i]),
     "styx_check_device_error": (_i, [_vp, _vp]),
+    "styx_set_option": (_i, [_vp, _i, C.c_int64]),
+    "styx_get_option": (_i, [_vp, _i, C.POINTER(C.c_int64)]),
     "styx_alloc": (_i, [_vp, _u64, _i, C.POINTER(_vp)]),
     "styx_free": (_i, [_vp, _vp]),
     "styx_upload": (_i, [_vp, _vp, _u64, _vp, _u64, _vp]),

@@ -19,6 +19,9 @@ struct styx_ctx {
     int sm_count = 0;
     char name[256] = {0};
     int *d_err = nullptr;   // device error word of bounded waits
+    int moe_kernels = 0;    // STYX_OPT_MOE_KERNELS
+    int last_path = 0;      // STYX_OPT_MOE_LAST_PATH
+    int trace = 0;          // STYX_OPT_TRACE
 };
 
 namespace {
@@ -110,8 +113,10 @@ bool extent_ok(const void *p, uint64_t bytes) {
 size_t a16(size_t v) { return (v + 15) & ~size_t(15); }
 size_t a128(size_t v) { return (v + 127) & ~size_t(127); }
 
+constexpr size_t kTraceCtas = 1024;   // phase stamps: 16 per CTA
+
 struct WsLayout {
-    size_t counter, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, total;
+    size_t counter, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, trace, total;
 };
 
 WsLayout ws_layout(const styx_moe_dims &d) {
@@ -134,6 +139,7 @@ WsLayout ws_layout(const styx_moe_dims &d) {
     L.h = take(kF * 4);
     L.g = take(kF * 4);   // unfused gate/up fallback
     L.u = take(kF * 4);
+    L.trace = take(kTraceCtas * 16 * 8);
     L.total = o;
     return L;
 }
@@ -282,9 +288,34 @@ int styx_check_device_error(styx_ctx *ctx, styx_stream stream) {
     if (h) {
         CK(cudaMemsetAsync(ctx->d_err, 0, sizeof(int), S(stream)));
         CK(cudaStreamSynchronize(S(stream)));
+        if (h == 4) return fail(STYX_EINVAL, "a kernel skipped an out-of-range expert id / hot index / arena slot");
         return fail(STYX_ETIMEOUT, "device-side bounded wait gave up (code %d)", h);
     }
     return STYX_OK;
+}
+
+int styx_set_option(styx_ctx *ctx, int option, int64_t value) {
+    NEED(ctx, "null ctx");
+    switch (option) {
+    case STYX_OPT_MOE_KERNELS:
+        NEED(value >= 0 && value <= 2, "STYX_OPT_MOE_KERNELS: 0, 1 or 2");
+        ctx->moe_kernels = static_cast<int>(value);
+        return STYX_OK;
+    case STYX_OPT_TRACE:
+        ctx->trace = value ? 1 : 0;
+        return STYX_OK;
+    default: return fail(STYX_EINVAL, "unknown or read-only option %d", option);
+    }
+}
+
+int styx_get_option(styx_ctx *ctx, int option, int64_t *value) {
+    NEED(ctx && value, "null pointer");
+    switch (option) {
+    case STYX_OPT_MOE_KERNELS: *value = ctx->moe_kernels; return STYX_OK;
+    case STYX_OPT_MOE_LAST_PATH: *value = ctx->last_path; return STYX_OK;
+    case STYX_OPT_TRACE: *value = ctx->trace; return STYX_OK;
+    default: return fail(STYX_EINVAL, "unknown option %d", option);
+    }
 }
 
 int styx_alloc(styx_ctx *ctx, uint64_t bytes, int kind, void **out) {
@@ -638,10 +669,61 @@ int styx_moe_workspace_view(const styx_moe_dims *dims, void *workspace, int whic
     case 1: off = L.logits; break;
     case 2: off = L.h; break;
     case 3: off = L.weights; break;
+    case 4: off = L.trace; break;
     default: return fail(STYX_EINVAL, "unknown view %d", which);
     }
     *out = static_cast<uint8_t *>(workspace) + off;
     return STYX_OK;
+}
+
+// Shared-memory plan of the single-kernel MoE block for these dims; false if
+// it does not fit one CTA per SM (the caller then uses three kernels).
+static bool plan_fused(const styx_moe_dims &d, const styx_moe_layer &lw, int sms, styx::FusedArgs &a,
+                       uint32_t &smem) {
+    const int H = d.n_embd, F = d.n_ff, E = d.n_expert, k = d.n_expert_used;
+    const int qg = lw.gate.qtype, qd = lw.down.qtype;
+    if (lw.up.qtype != qg || !styx::fused_supported(qg, qd)) return false;
+    const int units_g = H / 64, units_d = F / 64;
+    if (units_g > 32 || units_d > 32 || k > 16) return false;
+    const size_t kLimit = 227 * 1024;
+    const int G = sms;
+    const int rows_per_cta = (E + G - 1) / G;
+    a.units_g = units_g;
+    a.gs_g = pow2ceil(units_g);
+    a.units_d = units_d;
+    a.gs_d = pow2ceil(units_d);
+    a.rb_g = static_cast<int>(row_bytes(qg, H));
+    a.rb_u = static_cast<int>(row_bytes(lw.up.qtype, H));
+    a.rb_d = static_cast<int>(row_bytes(qd, F));
+    // region A: router rows (>= E floats, they hold the logits later), norm,
+    // x_norm, x_norm digits; reused for h digits in the down phase
+    a.rrows_floats = (std::max(rows_per_cta * H, E) + 3) & ~3;   // keeps what follows 16-byte aligned
+    const size_t a_route = a16(static_cast<size_t>(a.rrows_floats) * 4) + 2 * static_cast<size_t>(H) * 4 +
+                           3 * static_cast<size_t>(H) + H / 32 * 4;
+    const size_t kF = static_cast<size_t>(k) * F;
+    const size_t a_down = 3 * kF + kF / 32 * 4;
+    const size_t size_a = a128(std::max(a_route, a_down));
+    // gate/up: one row pair per warp per chunk; every chunk of the CTA resident
+    a.ch = 16 * (32 / a.gs_g);
+    const long long T = static_cast<long long>(k) * F;
+    const int rows_g = static_cast<int>((T + G - 1) / G);
+    const int chunks_g = (rows_g + a.ch - 1) / a.ch + 1;   // +1: a slot boundary
+    if (chunks_g > 16) return false;
+    const size_t gu_bytes = static_cast<size_t>(rows_g) * (a.rb_g + a.rb_u) + static_cast<size_t>(chunks_g) * 2 * 48;
+    // down: all of the CTA's output rows, every slot, one chunk
+    const int rows_d = (H + G - 1) / G;
+    a.rc = rows_d;
+    a.dslot_stride = static_cast<uint32_t>(a16(static_cast<size_t>(a.rc) * a.rb_d + 32));
+    a.dstage_bytes = a.dslot_stride * static_cast<uint32_t>(k);
+    const size_t part = a128(2 * static_cast<size_t>(k) * a.rc * 4);
+    a.off_a = styx::kFusedHeader;
+    a.off_part = static_cast<uint32_t>(a.off_a + size_a);
+    a.off_ring = static_cast<uint32_t>(a.off_part + part);
+    a.off_down = static_cast<uint32_t>(a128(a.off_ring + gu_bytes));
+    const size_t total = a.off_down + a.dstage_bytes;
+    if (total > kLimit) return false;
+    smem = static_cast<uint32_t>(total);
+    return true;
 }
 
 int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims, const styx_moe_layer *lw, int layer,
@@ -671,6 +753,44 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
     int32_t *ids64 = ids + static_cast<size_t>(layer) * STYX_IDS_PER_LAYER;
     float *wts = weights_out ? weights_out : reinterpret_cast<float *>(ws + L.weights);
     const cudaStream_t st = S(stream);
+
+    // the single cooperative kernel when the shape fits, else three kernels
+    if (ctx->moe_kernels != 2) {
+        styx::FusedArgs fa{};
+        uint32_t smem = 0;
+        const bool fits = al16(lw->ffn_norm) && plan_fused(*dims, *lw, ctx->sm_count, fa, smem);
+        if (!fits && ctx->moe_kernels == 1)
+            return fail(STYX_EUNSUPPORTED, "single-kernel MoE block does not fit these dims / formats");
+        if (fits) {
+            fa.x = x;
+            fa.norm_w = lw->ffn_norm;
+            fa.eps = dims->rms_eps;
+            fa.router = lw->router;
+            fa.E = E;
+            fa.H = H;
+            fa.F = F;
+            fa.k = k;
+            fa.renorm = dims->norm_topk;
+            fa.remap = lw->remap;
+            fa.pmap = lw->pmap;
+            fa.gate = to_src(lw->gate, E);
+            fa.up = to_src(lw->up, E);
+            fa.down = to_src(lw->down, E);
+            fa.ids64 = ids64;
+            fa.weights = wts;
+            fa.logits = reinterpret_cast<float *>(ws + L.logits);
+            fa.xnorm = reinterpret_cast<float *>(ws + L.xnorm);
+            fa.h = reinterpret_cast<float *>(ws + L.h);
+            fa.counters = reinterpret_cast<unsigned *>(ws + L.counter);
+            fa.err = ctx->d_err;
+            fa.trace = ctx->trace ? reinterpret_cast<long long *>(ws + L.trace) : nullptr;
+            NEED(!ctx->trace || ctx->sm_count <= static_cast<int>(kTraceCtas), "too many CTAs to trace");
+            CK(styx::launch_fused(fa, lw->gate.qtype, lw->down.qtype, ctx->sm_count, smem, st));
+            ctx->last_path = 1;
+            return STYX_OK;
+        }
+    }
+    ctx->last_path = 2;
 
     // 1. route
     styx::RouteArgs ra{};

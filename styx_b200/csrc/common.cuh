@@ -108,6 +108,18 @@ __device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
     asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
     return r;
 }
+// unsigned a (u8 lanes) x signed b (s8 lanes)
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int r;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+// byte i (0..3, i a run-time value) of w as an exact float, without I2F:
+// the byte becomes the low mantissa byte of 2^23, then 2^23 is subtracted
+__device__ __forceinline__ float byte_to_f(uint32_t w, uint32_t i) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u | i)) - 8388608.f;
+}
 
 // ------------------------------------------------ unaligned smem loads
 // 16 bytes from any 1-byte aligned address (shared or global): the aligned
@@ -152,30 +164,108 @@ struct DigitsView {
     float *scale;   // n/32 group scales
 };
 
-// one 32-element group, one element per lane of a full warp
-__device__ __forceinline__ void digits_group_warp(float v, int lane, const DigitsView &dv, int g) {
-    float a = fabsf(v);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    float s = 1.0f;
+// power-of-two group scale s for group max |v| = a, and 1/s (both exact)
+__device__ __forceinline__ float digits_scale(float a, float &inv) {
+    int se = 127;   // s = 1
     if (a > 0.f && a < INFINITY) {
-        int e = ((__float_as_uint(a) >> 23) & 0xFF);   // biased exponent of max
-        int se = e - 5;                                 // s = 2^(E-5)
+        se = ((__float_as_uint(a) >> 23) & 0xFF) - 5;   // s = 2^(E-5)
         if (se < 1) se = 1;
-        s = __uint_as_float(static_cast<uint32_t>(se) << 23);
     }
-    const float q = v / s;                 // exact: s is a power of two
+    inv = __uint_as_float(static_cast<uint32_t>(254 - se) << 23);
+    return __uint_as_float(static_cast<uint32_t>(se) << 23);
+}
+
+// the three digits of one element (q = v * (1/s), exact for a power-of-two s)
+__device__ __forceinline__ void digits_of(float v, float inv, int &d1, int &d2, int &d3) {
+    const float q = v * inv;
     const float f1 = floorf(q);
     const float r1 = (q - f1) * 256.f;     // exact
     const float f2 = floorf(r1);
     const float r2 = (r1 - f2) * 256.f;
     float f3 = rintf(r2);
     if (f3 > 255.f) f3 = 255.f;
+    d1 = static_cast<int>(f1);
+    d2 = static_cast<int>(f2);
+    d3 = static_cast<int>(f3);
+}
+
+// one 32-element group, one element per lane of a full warp
+__device__ __forceinline__ void digits_group_warp(float v, int lane, const DigitsView &dv, int g) {
+    float a = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    float inv;
+    const float s = digits_scale(a, inv);
+    int d1, d2, d3;
+    digits_of(v, inv, d1, d2, d3);
     const int i = g * 32 + lane;
-    dv.d1[i] = static_cast<int8_t>(static_cast<int>(f1));
-    dv.d2[i] = static_cast<uint8_t>(static_cast<int>(f2));
-    dv.d3[i] = static_cast<uint8_t>(static_cast<int>(f3));
+    dv.d1[i] = static_cast<int8_t>(d1);
+    dv.d2[i] = static_cast<uint8_t>(d2);
+    dv.d3[i] = static_cast<uint8_t>(d3);
     if (lane == 0) dv.scale[g] = s;
+}
+
+// Digits of a whole vector v[n] (n % 32 == 0) by a group of `nthreads`
+// threads (a multiple of 32, all of them calling): EPT elements per thread
+// (8 or 16), 32/EPT threads per 32-element group sharing the group max by
+// shuffles; same digits as digits_group_warp.  GLOBAL: v is read through L2
+// (__ldcg), else v is shared memory.
+template <int EPT, bool GLOBAL>
+__device__ __forceinline__ void digits_vector(const float *v, int n, int8_t *pd1, uint8_t *pd2, uint8_t *pd3,
+                                              float *scale, int t, int nthreads) {
+    static_assert(EPT == 8 || EPT == 16, "8 or 16 elements per thread");
+    constexpr int TPG = 32 / EPT;                                // threads per group
+    const int nparts = n / EPT;
+    const int lim = ((nparts + 31) >> 5) << 5;                   // every lane of a warp iterates alike
+    for (int pidx = t; pidx < lim; pidx += nthreads) {
+        const bool on = pidx < nparts;
+        float x[EPT];
+#pragma unroll
+        for (int i = 0; i < EPT / 4; i++) {
+            const float4 *src = reinterpret_cast<const float4 *>(v + static_cast<size_t>(pidx) * EPT) + i;
+            const float4 q = on ? (GLOBAL ? __ldcg(src) : *src) : make_float4(0.f, 0.f, 0.f, 0.f);
+            x[4 * i] = q.x;
+            x[4 * i + 1] = q.y;
+            x[4 * i + 2] = q.z;
+            x[4 * i + 3] = q.w;
+        }
+        float a = 0.f;
+#pragma unroll
+        for (int i = 0; i < EPT; i++) a = fmaxf(a, fabsf(x[i]));
+#pragma unroll
+        for (int o = 1; o < TPG; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        float inv;
+        const float s = digits_scale(a, inv);
+        uint32_t w1[EPT / 4], w2[EPT / 4], w3[EPT / 4];
+#pragma unroll
+        for (int i = 0; i < EPT / 4; i++) {
+            uint32_t a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                int d1, d2, d3;
+                digits_of(x[4 * i + j], inv, d1, d2, d3);
+                a1 |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * j);
+                a2 |= static_cast<uint32_t>(d2) << (8 * j);
+                a3 |= static_cast<uint32_t>(d3) << (8 * j);
+            }
+            w1[i] = a1;
+            w2[i] = a2;
+            w3[i] = a3;
+        }
+        if (on) {
+            const size_t o = static_cast<size_t>(pidx) * EPT;
+            if constexpr (EPT == 16) {
+                *reinterpret_cast<uint4 *>(pd1 + o) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+                *reinterpret_cast<uint4 *>(pd2 + o) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+                *reinterpret_cast<uint4 *>(pd3 + o) = make_uint4(w3[0], w3[1], w3[2], w3[3]);
+            } else {
+                *reinterpret_cast<uint2 *>(pd1 + o) = make_uint2(w1[0], w1[1]);
+                *reinterpret_cast<uint2 *>(pd2 + o) = make_uint2(w2[0], w2[1]);
+                *reinterpret_cast<uint2 *>(pd3 + o) = make_uint2(w3[0], w3[1]);
+            }
+            if (pidx % TPG == 0) scale[pidx / TPG] = s;
+        }
+    }
 }
 
 }  // namespace styx

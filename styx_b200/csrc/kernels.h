@@ -65,6 +65,33 @@ struct DownArgs {
     int *err;
 };
 
+// the single-kernel MoE block (moe_fused.cu)
+struct FusedArgs {
+    float *x;
+    const float *norm_w;
+    float eps;
+    const float *router;
+    int E, H, F, k, renorm;
+    const uint32_t *remap, *pmap;
+    ExpSrc gate, up, down;
+    int32_t *ids64;
+    float *weights;
+    float *logits;           // workspace f32[E]
+    float *xnorm;            // workspace f32[H] (written by CTA 0)
+    float *h;                // workspace f32[k][F]
+    unsigned *counters;      // workspace, 3 words, zero between launches
+    int *err;
+    long long *trace;        // optional: 16 clock64 stamps per CTA (phase boundaries)
+    // shared-memory plan (every chunk of a CTA is resident at once)
+    int rrows_floats;        // router-row buffer (>= E floats: holds the logits later)
+    uint32_t off_a, off_part, off_ring, off_down;
+    int ch;                  // gate/up rows per chunk (<= 16 chunks per CTA)
+    int rb_g, rb_u, rb_d;
+    int rc;                  // down output rows per chunk (<= 16 chunks per CTA)
+    uint32_t dstage_bytes, dslot_stride;
+    int units_g, gs_g, units_d, gs_d;
+};
+
 struct MatVecIdArgs {
     const uint8_t *a;
     uint64_t expert_bytes;
@@ -110,6 +137,11 @@ cudaError_t launch_synth_quant(int qtype, uint8_t *dst, uint64_t nrows, int ncol
                                float sigma, cudaStream_t st);
 cudaError_t launch_synth_f32(float *dst, uint64_t n, uint64_t seed, uint64_t offset, float sigma,
                              cudaStream_t st);
+
+cudaError_t launch_fused(const FusedArgs &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st);
+bool fused_supported(int qg, int qd);
+int fused_block_threads();
+constexpr uint32_t kFusedHeader = 1280;
 
 // shared-memory plan of the fused kernels (computed on the host)
 int gate_up_smem(const GateUpArgs &a);

@@ -388,11 +388,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
 
     // consumers: h -> digits (shared), weights
     const int cw = warp - 1;
-    {
-        const DigitsView dv{hd1, hd2, hd3, hsc};
-        for (int g = cw; g < (kF >> 5); g += kConsumerWarps) digits_group_warp(p.h[g * 32 + lane], lane, dv, g);
-        if (cw == 0 && lane < p.k) wts[lane] = p.w[lane];
-    }
+    digits_vector<8, true>(p.h, kF, hd1, hd2, hd3, hsc, threadIdx.x - 32, kConsumerWarps * 32);
+    if (cw == 0 && lane < p.k) wts[lane] = p.w[lane];
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 
     const int rpw = 32 / p.gs;

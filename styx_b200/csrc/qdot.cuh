@@ -73,28 +73,36 @@ __device__ __forceinline__ void load_xunit(XUnit &x, const int8_t *d1, const uin
     }
 }
 
+// I1 + I2/256 + I3/65536 with two conversions: I2*256 + I3 stays below 2^31
+// for every code range used here (|I2| <= 32*255*255)
 __device__ __forceinline__ float digits_to_f(int i1, int i2, int i3) {
-    return static_cast<float>(i1) +
-           (static_cast<float>(i2) + static_cast<float>(i3) * (1.f / 256.f)) * (1.f / 256.f);
+    return static_cast<float>(i1) + static_cast<float>(i2 * 256 + i3) * (1.f / 65536.f);
 }
 
-__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return __byte_perm(w, 0u, 0x4440u | (i & 3)); }
+// signed byte i of w as an exact float (bias the byte by 128, as byte_to_f)
+__device__ __forceinline__ float sbyte_to_f(uint32_t w_xor80, uint32_t i) {
+    return __uint_as_float(__byte_perm(w_xor80, 0x4B000000u, 0x7650u | i)) - 8388736.f;
+}
 
-// 6-bit scale/min of sub-block j (0..7) from the 12 scale bytes held in
-// s0 (bytes 0-3), s1 (4-7), s2 (8-11): get_scale_min, moe.rs:512-521.
-__device__ __forceinline__ void kq_scale_min(uint32_t s0, uint32_t s1, uint32_t s2, int j, float &sc,
-                                             float &m) {
-    const int jl = j & 3;
-    const uint32_t b0 = byte_of(s0, jl), b1 = byte_of(s1, jl), b2 = byte_of(s2, jl);
-    const uint32_t lo_sc = b0 & 63u, lo_m = b1 & 63u;
-    const uint32_t hi_sc = (b2 & 0x0Fu) | ((b0 >> 6) << 4);
-    const uint32_t hi_m = (b2 >> 4) | ((b1 >> 6) << 4);
-    sc = static_cast<float>(j < 4 ? lo_sc : hi_sc);
-    m = static_cast<float>(j < 4 ? lo_m : hi_m);
+// The 6-bit scales (sc) and mins (m) of four sub-blocks at once, one per
+// byte: sub-blocks 0-3 (hi4 = false) or 4-7 (hi4 = true), from the 12 scale
+// bytes in s0 (bytes 0-3), s1 (4-7), s2 (8-11).  Packed form of
+// get_scale_min (crates/model/src/moe.rs:512-521):
+//   j < 4:  sc = s[j] & 63,                        m = s[j+4] & 63
+//   j >= 4: sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4, m = (s[j+4] >> 4) | (s[j] >> 6) << 4
+__device__ __forceinline__ void kq_scales4(uint32_t s0, uint32_t s1, uint32_t s2, bool hi4, uint32_t &sc,
+                                           uint32_t &m) {
+    const uint32_t sc_lo = s0 & 0x3F3F3F3Fu, m_lo = s1 & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
+    const uint32_t m_hi = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
+    sc = hi4 ? sc_hi : sc_lo;
+    m = hi4 ? m_hi : m_lo;
 }
 
 // ------------------------------------------------------------- q4_K
 // block: f16 d, f16 dmin, 12 scale bytes, 128 qs bytes; 16-byte aligned.
+// High nibbles are masked in place (16x their value) and the 1/16 folded
+// into the scale, so each code word costs one LOP per half.
 __device__ __forceinline__ float dot_q4K(const uint8_t *row, int u, const XUnit &x) {
     const int b = u >> 2, jj = u & 3;
     const uint8_t *blk = row + b * 144;
@@ -105,20 +113,22 @@ __device__ __forceinline__ float dot_q4K(const uint8_t *row, int u, const XUnit 
     int l1 = 0, l2 = 0, l3 = 0, h1 = 0, h2 = 0, h3 = 0;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        const uint32_t lo = q[i] & 0x0F0F0F0Fu, hi = (q[i] >> 4) & 0x0F0F0F0Fu;
+        const uint32_t lo = q[i] & 0x0F0F0F0Fu, hi = q[i] & 0xF0F0F0F0u;
         l1 = dp4a_ss(lo, x.d1[i], l1);
         l2 = dp4a_uu(lo, x.d2[i], l2);
         l3 = dp4a_uu(lo, x.d3[i], l3);
-        h1 = dp4a_ss(hi, x.d1[8 + i], h1);
+        h1 = dp4a_us(hi, x.d1[8 + i], h1);
         h2 = dp4a_uu(hi, x.d2[8 + i], h2);
         h3 = dp4a_uu(hi, x.d3[8 + i], h3);
     }
     const float d = h2f(hd.x), dm = h2f(hd.x >> 16);
-    float sc1, m1, sc2, m2;
-    kq_scale_min(hd.y, hd.z, hd.w, 2 * jj, sc1, m1);
-    kq_scale_min(hd.y, hd.z, hd.w, 2 * jj + 1, sc2, m2);
+    uint32_t scw, mw;
+    kq_scales4(hd.y, hd.z, hd.w, jj >= 2, scw, mw);
+    const uint32_t bi = static_cast<uint32_t>((2 * jj) & 3);   // byte of sub-block 2jj; 2jj+1 is next
+    const float sc1 = byte_to_f(scw, bi), sc2 = byte_to_f(scw, bi + 1);
+    const float m1 = byte_to_f(mw, bi), m2 = byte_to_f(mw, bi + 1);
     const float flo = digits_to_f(l1, l2, l3) * x.s[0];
-    const float fhi = digits_to_f(h1, h2, h3) * x.s[2];
+    const float fhi = digits_to_f(h1, h2, h3) * (x.s[2] * 0.0625f);
     return (d * sc1) * flo - (dm * m1) * (x.xs[0] + x.xs[1]) + (d * sc2) * fhi -
            (dm * m2) * (x.xs[2] + x.xs[3]);
 }
@@ -149,9 +159,11 @@ __device__ __forceinline__ float dot_q5K(const uint8_t *row, int u, const XUnit 
         h3 = dp4a_uu(hi, x.d3[8 + i], h3);
     }
     const float d = h2f(hd.x), dm = h2f(hd.x >> 16);
-    float sc1, m1, sc2, m2;
-    kq_scale_min(hd.y, hd.z, hd.w, 2 * jj, sc1, m1);
-    kq_scale_min(hd.y, hd.z, hd.w, 2 * jj + 1, sc2, m2);
+    uint32_t scw, mw;
+    kq_scales4(hd.y, hd.z, hd.w, jj >= 2, scw, mw);
+    const uint32_t bi = static_cast<uint32_t>((2 * jj) & 3);
+    const float sc1 = byte_to_f(scw, bi), sc2 = byte_to_f(scw, bi + 1);
+    const float m1 = byte_to_f(mw, bi), m2 = byte_to_f(mw, bi + 1);
     const float flo = digits_to_f(l1, l2, l3) * x.s[0];
     const float fhi = digits_to_f(h1, h2, h3) * x.s[2];
     return (d * sc1) * flo - (dm * m1) * (x.xs[0] + x.xs[1]) + (d * sc2) * fhi -
@@ -186,10 +198,10 @@ __device__ __forceinline__ float dot_q6K(const uint8_t *row, int u, const XUnit 
         }
     }
     // scales[8n + t + 2q]: bytes t, t+2 of S.x (q = 0, 1) and of S.y (q = 2, 3)
-    const float sc0 = static_cast<float>(static_cast<int8_t>(byte_of(S.x, t)));
-    const float sc1 = static_cast<float>(static_cast<int8_t>(byte_of(S.x, t + 2)));
-    const float sc2 = static_cast<float>(static_cast<int8_t>(byte_of(S.y, t)));
-    const float sc3 = static_cast<float>(static_cast<int8_t>(byte_of(S.y, t + 2)));
+    const uint32_t sx = S.x ^ 0x80808080u, sy = S.y ^ 0x80808080u;
+    const uint32_t tb = static_cast<uint32_t>(t);
+    const float sc0 = sbyte_to_f(sx, tb), sc1 = sbyte_to_f(sx, tb + 2);
+    const float sc2 = sbyte_to_f(sy, tb), sc3 = sbyte_to_f(sy, tb + 2);
     const float acc = sc0 * (digits_to_f(i1[0], i2[0], i3[0]) * x.s[0] - 32.f * x.xs[0]) +
                       sc1 * (digits_to_f(i1[1], i2[1], i3[1]) * x.s[1] - 32.f * x.xs[1]) +
                       sc2 * (digits_to_f(i1[2], i2[2], i3[2]) * x.s[2] - 32.f * x.xs[2]) +

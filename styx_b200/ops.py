@@ -43,6 +43,22 @@ class Context:
     def check_device_error(self, stream=None) -> None:
         check(lib().styx_check_device_error(self.handle, _stream(stream)))
 
+    def set_option(self, option: int, value: int) -> None:
+        check(lib().styx_set_option(self.handle, option, value))
+
+    def get_option(self, option: int) -> int:
+        v = C.c_int64()
+        check(lib().styx_get_option(self.handle, option, C.byref(v)))
+        return v.value
+
+    def set_moe_kernels(self, mode: int) -> None:
+        """0 auto, 1 the single cooperative kernel, 2 three kernels."""
+        self.set_option(_lib.OPT_MOE_KERNELS, mode)
+
+    def last_moe_path(self) -> int:
+        """1 = single kernel, 2 = three kernels (the last styx_moe_block)."""
+        return self.get_option(_lib.OPT_MOE_LAST_PATH)
+
 
 def ctx(device: Optional[int] = None) -> Context:
     if device is None:
