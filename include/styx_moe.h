@@ -269,6 +269,25 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream,
                    int layer, float *x, int32_t *ids, float *weights_out,
                    void *workspace, uint64_t workspace_bytes);
 
+/* styx_moe_block without a caller workspace; it has no counterpart in the
+ * reference.  For callers that cannot allocate device memory (a host that
+ * binds only the compute entry points, or one whose whole device budget is
+ * committed to expert tensors and arenas): the scratch is a static device
+ * array of STYX_NOALLOC_SCRATCH_BYTES per device, and nothing is allocated.
+ *   - Dims whose styx_moe_workspace_bytes exceeds that size are rejected
+ *     (STYX_EINVAL).
+ *   - The first call on a device looks up the array and zeroes it; make it
+ *     before any stream capture (it fails while the stream is capturing).
+ *   - Every call zeroes the scratch's counter words on `stream` first.
+ *   - All calls on one device share the one scratch: calls that overlap (on
+ *     different streams or host threads) race.  Serialise them.
+ *   - styx_moe_workspace_view does not apply to it. */
+#define STYX_NOALLOC_SCRATCH_BYTES (512u * 1024u)
+int styx_moe_block_noalloc(styx_ctx *ctx, styx_stream stream,
+                           const styx_moe_dims *dims,
+                           const styx_moe_layer *layer_w, int layer, float *x,
+                           int32_t *ids, float *weights_out);
+
 /* Debug / test views of the last styx_moe_block's intermediates kept in the
  * workspace: which = 0 xnorm f32[H], 1 logits f32[E], 2 h f32[k*F],
  * 3 weights f32[k], 4 phase trace int64[CTAs][16] (STYX_OPT_TRACE).  Returns a

@@ -88,6 +88,7 @@ _SIGS = {
     "styx_moe_workspace_view": (_i, [C.POINTER(MoeDims), _vp, _i, C.POINTER(_vp)]),
     "styx_moe_block": (_i, [_vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp,
                             _vp, _vp, _u64]),
+    "styx_moe_block_noalloc": (_i, [_vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp, _vp]),
     "styx_synth_quant": (_i, [_vp, _vp, _i, _vp, _u64, _i, _u64, _f]),
     "styx_synth_f32": (_i, [_vp, _vp, _vp, _u64, _u64, _u64, _f]),
 }

@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include <cuda.h>
@@ -889,6 +890,56 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
     da.err = ctx->d_err;
     CK(styx::launch_down(da, lw->down.qtype, grid_d, smem_d, st));
     return STYX_OK;
+}
+
+// ------------------------------------------------ MoE block, no allocation
+// Scratch of styx_moe_block_noalloc: one statically sized array per device
+// (module global memory, zero at module load), shared by every call on that
+// device.  Its address is looked up once per device with the device current.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[STYX_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kMaxDevices] = {};
+
+// first call on a device: resolve the symbol and zero the whole scratch
+int noalloc_scratch(styx_ctx *ctx, cudaStream_t st, void **out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NEED(ctx->device >= 0 && ctx->device < kMaxDevices, "device %d out of range", ctx->device);
+    void *&p = g_noalloc_ptr[ctx->device];
+    if (!p) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        CK(cudaStreamIsCapturing(st, &cs));
+        NEED(cs == cudaStreamCaptureStatusNone,
+             "styx_moe_block_noalloc: the first call on a device sets up its scratch and must not be "
+             "made while the stream is being captured");
+        void *q = nullptr;
+        CK(cudaGetSymbolAddress(&q, g_noalloc_scratch));
+        CK(cudaMemset(q, 0, STYX_NOALLOC_SCRATCH_BYTES));
+        p = q;
+    }
+    *out = p;
+    return STYX_OK;
+}
+}  // namespace
+
+int styx_moe_block_noalloc(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims, const styx_moe_layer *lw,
+                           int layer, float *x, int32_t *ids, float *weights_out) {
+    ENTER(ctx);
+    int rc = check_dims(dims);
+    if (rc) return rc;
+    const WsLayout L = ws_layout(*dims);
+    NEED(L.total <= STYX_NOALLOC_SCRATCH_BYTES,
+         "styx_moe_block_noalloc: these dims need %llu bytes of scratch, above its static %llu bytes; "
+         "use styx_moe_block with a caller workspace",
+         (unsigned long long)L.total, (unsigned long long)STYX_NOALLOC_SCRATCH_BYTES);
+    void *scratch = nullptr;
+    if ((rc = noalloc_scratch(ctx, S(stream), &scratch))) return rc;
+    // the counter words must be zero when the block starts (a timed-out
+    // wait of an earlier call can leave them set)
+    CK(cudaMemsetAsync(static_cast<uint8_t *>(scratch) + L.counter, 0, 256, S(stream)));
+    return styx_moe_block(ctx, stream, dims, lw, layer, x, ids, weights_out, scratch, STYX_NOALLOC_SCRATCH_BYTES);
 }
 
 // ------------------------------------------------------------- synth
