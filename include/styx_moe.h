@@ -89,8 +89,8 @@ int styx_check_device_error(styx_ctx *ctx, styx_stream stream);
  * kernels), 1 = single kernel only (STYX_EUNSUPPORTED if it does not fit),
  * 2 = three kernels.  STYX_OPT_MOE_LAST_PATH (read only) = 1 or 2, the form
  * the last styx_moe_block call used.  STYX_OPT_TRACE = 1 makes the single
- * kernel record 16 clock64 stamps per CTA at its phase boundaries into the
- * workspace (styx_moe_workspace_view 4: int64[CTAs][16]). */
+ * kernel record 32 clock64 stamps per CTA at its phase boundaries into the
+ * workspace (styx_moe_workspace_view 4: int64[CTAs][32]). */
 #define STYX_OPT_MOE_KERNELS 1
 #define STYX_OPT_MOE_LAST_PATH 2
 #define STYX_OPT_TRACE 3
@@ -290,7 +290,7 @@ int styx_moe_block_noalloc(styx_ctx *ctx, styx_stream stream,
 
 /* Debug / test views of the last styx_moe_block's intermediates kept in the
  * workspace: which = 0 xnorm f32[H], 1 logits f32[E], 2 h f32[k*F],
- * 3 weights f32[k], 4 phase trace int64[CTAs][16] (STYX_OPT_TRACE).  Returns a
+ * 3 weights f32[k], 4 phase trace int64[CTAs][32] (STYX_OPT_TRACE).  Returns a
  * device pointer into the workspace. */
 int styx_moe_workspace_view(const styx_moe_dims *dims, void *workspace,
                             int which, void **out);

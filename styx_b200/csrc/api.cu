@@ -114,10 +114,15 @@ bool extent_ok(const void *p, uint64_t bytes) {
 size_t a16(size_t v) { return (v + 15) & ~size_t(15); }
 size_t a128(size_t v) { return (v + 127) & ~size_t(127); }
 
-constexpr size_t kTraceCtas = 1024;   // phase stamps: 16 per CTA
+constexpr size_t kTraceCtas = 256;   // phase stamps: styx::kTraceStamps per CTA
 
+// The counter block: word 0 is the three-kernel route's hand-off counter
+// (zero between launches); the single kernel's 64-bit launch and h-arrival
+// counters sit at kGenOffset and are never reset except by
+// styx_moe_workspace_init (which also clears the tagged slots they guard).
+constexpr size_t kGenOffset = 128;
 struct WsLayout {
-    size_t counter, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, trace, total;
+    size_t counter, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, lgslot, trace, total;
 };
 
 WsLayout ws_layout(const styx_moe_dims &d) {
@@ -140,7 +145,8 @@ WsLayout ws_layout(const styx_moe_dims &d) {
     L.h = take(kF * 4);
     L.g = take(kF * 4);   // unfused gate/up fallback
     L.u = take(kF * 4);
-    L.trace = take(kTraceCtas * 16 * 8);
+    L.lgslot = take(E * 8);
+    L.trace = take(kTraceCtas * styx::kTraceStamps * 8);
     L.total = o;
     return L;
 }
@@ -688,7 +694,6 @@ static bool plan_fused(const styx_moe_dims &d, const styx_moe_layer &lw, int sms
     if (units_g > 32 || units_d > 32 || k > 16) return false;
     const size_t kLimit = 227 * 1024;
     const int G = sms;
-    const int rows_per_cta = (E + G - 1) / G;
     a.units_g = units_g;
     a.gs_g = pow2ceil(units_g);
     a.units_d = units_d;
@@ -696,21 +701,26 @@ static bool plan_fused(const styx_moe_dims &d, const styx_moe_layer &lw, int sms
     a.rb_g = static_cast<int>(row_bytes(qg, H));
     a.rb_u = static_cast<int>(row_bytes(lw.up.qtype, H));
     a.rb_d = static_cast<int>(row_bytes(qd, F));
-    // region A: router rows (>= E floats, they hold the logits later), norm,
-    // x_norm, x_norm digits; reused for h digits in the down phase
-    a.rrows_floats = (std::max(rows_per_cta * H, E) + 3) & ~3;   // keeps what follows 16-byte aligned
-    const size_t a_route = a16(static_cast<size_t>(a.rrows_floats) * 4) + 2 * static_cast<size_t>(H) * 4 +
-                           3 * static_cast<size_t>(H) + H / 32 * 4;
+    // region A: x_norm, its digits, the logits; reused for h digits in the
+    // down phase
+    const size_t a_route = static_cast<size_t>(H) * 4 + 3 * static_cast<size_t>(H) + H / 32 * 4 +
+                           static_cast<size_t>(E) * 4;
     const size_t kF = static_cast<size_t>(k) * F;
     const size_t a_down = 3 * kF + kF / 32 * 4;
     const size_t size_a = a128(std::max(a_route, a_down));
-    // gate/up: one row pair per warp per chunk; every chunk of the CTA resident
-    a.ch = 16 * (32 / a.gs_g);
+    // gate/up: about six chunks per CTA (each at most two slot segments of
+    // gate rows and of up rows); every chunk of the CTA resident
+    const int rpw_g = 32 / a.gs_g;
     const long long T = static_cast<long long>(k) * F;
     const int rows_g = static_cast<int>((T + G - 1) / G);
-    const int chunks_g = (rows_g + a.ch - 1) / a.ch + 1;   // +1: a slot boundary
-    if (chunks_g > 16) return false;
-    const size_t gu_bytes = static_cast<size_t>(rows_g) * (a.rb_g + a.rb_u) + static_cast<size_t>(chunks_g) * 2 * 48;
+    a.ch = std::max(rpw_g, ((rows_g + 5) / 6 + rpw_g - 1) / rpw_g * rpw_g);
+    const int chunks_g = (rows_g + a.ch - 1) / a.ch;
+    if (chunks_g > 16 || a.ch > F) return false;
+    a.gu_up_off = static_cast<uint32_t>(a16(static_cast<size_t>(a.ch) * a.rb_g + 96));
+    a.gu_stride = a.gu_up_off + static_cast<uint32_t>(a16(static_cast<size_t>(a.ch) * a.rb_u + 96));
+    // (the top-k's per-warp rank counts use the same area before any copy)
+    const size_t gu_bytes = std::max(static_cast<size_t>(chunks_g) * a.gu_stride,
+                                     static_cast<size_t>(styx::fused_block_threads() / 32) * E * 4);
     // down: all of the CTA's output rows, every slot, one chunk
     const int rows_d = (H + G - 1) / G;
     a.rc = rows_d;
@@ -782,7 +792,9 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
             fa.logits = reinterpret_cast<float *>(ws + L.logits);
             fa.xnorm = reinterpret_cast<float *>(ws + L.xnorm);
             fa.h = reinterpret_cast<float *>(ws + L.h);
-            fa.counters = reinterpret_cast<unsigned *>(ws + L.counter);
+            fa.lgslot = reinterpret_cast<uint64_t *>(ws + L.lgslot);
+            fa.gen = reinterpret_cast<unsigned long long *>(ws + L.counter + kGenOffset);
+            fa.hdone = fa.gen + 1;
             fa.err = ctx->d_err;
             fa.trace = ctx->trace ? reinterpret_cast<long long *>(ws + L.trace) : nullptr;
             NEED(!ctx->trace || ctx->sm_count <= static_cast<int>(kTraceCtas), "too many CTAs to trace");
@@ -936,9 +948,10 @@ int styx_moe_block_noalloc(styx_ctx *ctx, styx_stream stream, const styx_moe_dim
          (unsigned long long)L.total, (unsigned long long)STYX_NOALLOC_SCRATCH_BYTES);
     void *scratch = nullptr;
     if ((rc = noalloc_scratch(ctx, S(stream), &scratch))) return rc;
-    // the counter words must be zero when the block starts (a timed-out
-    // wait of an earlier call can leave them set)
-    CK(cudaMemsetAsync(static_cast<uint8_t *>(scratch) + L.counter, 0, 256, S(stream)));
+    // the hand-off counter must be zero when the block starts (a timed-out
+    // wait of an earlier call can leave it set); the launch counter after it
+    // must keep counting
+    CK(cudaMemsetAsync(static_cast<uint8_t *>(scratch) + L.counter, 0, kGenOffset, S(stream)));
     return styx_moe_block(ctx, stream, dims, lw, layer, x, ids, weights_out, scratch, STYX_NOALLOC_SCRATCH_BYTES);
 }
 

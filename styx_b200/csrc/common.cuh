@@ -65,6 +65,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// The same test, but a thread whose phase is not complete may be suspended
+// (leaving its issue slots to the other warps) until the phase completes or
+// about kSuspendNs have passed (0: plain polling, no suspension).
+#ifndef STYX_MBAR_SUSPEND_NS
+#define STYX_MBAR_SUSPEND_NS 20000
+#endif
+constexpr uint32_t kSuspendNs = STYX_MBAR_SUSPEND_NS;
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+    return ok != 0;
+}
 
 // Bounded wait on an mbarrier phase.  Returns false (and records `code` in
 // the error word) if the phase did not complete within kSpinCycles.
@@ -72,7 +90,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     if (mbar_try_wait(bar, parity)) return true;
     long long t0 = clock64();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (kSuspendNs ? mbar_try_wait_suspend(bar, parity) : mbar_try_wait(bar, parity)) return true;
         if (clock64() - t0 > kSpinCycles) {
             if (err) atomicExch(err, code);
             return false;
@@ -93,6 +111,11 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 // Programmatic dependent launch (sm_90+): wait for the previous grid's
 // memory, and allow the next grid to be scheduled.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Warm L2 with [src, src + bytes) (no data comes back to the SM, so it is safe
+// before the grid dependency resolves).  src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 // ---------------------------------------------------------------- dp4a
@@ -210,11 +233,55 @@ __device__ __forceinline__ void digits_group_warp(float v, int lane, const Digit
 // (8 or 16), 32/EPT threads per 32-element group sharing the group max by
 // shuffles; same digits as digits_group_warp.  GLOBAL: v is read through L2
 // (__ldcg), else v is shared memory.
+// Digits of part pidx (elements pidx*EPT ..) of a vector whose values this
+// thread holds in x; the 32/EPT threads of a group are adjacent lanes and
+// all call together (on = false for padding parts).
+template <int EPT>
+__device__ __forceinline__ void digits_part(const float (&x)[EPT], bool on, int pidx, int8_t *pd1, uint8_t *pd2,
+                                            uint8_t *pd3, float *scale) {
+    static_assert(EPT == 8 || EPT == 16, "8 or 16 elements per thread");
+    constexpr int TPG = 32 / EPT;                                // threads per group
+    float a = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPT; i++) a = fmaxf(a, fabsf(x[i]));
+#pragma unroll
+    for (int o = 1; o < TPG; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    float inv;
+    const float s = digits_scale(a, inv);
+    uint32_t w1[EPT / 4], w2[EPT / 4], w3[EPT / 4];
+#pragma unroll
+    for (int i = 0; i < EPT / 4; i++) {
+        uint32_t a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int d1, d2, d3;
+            digits_of(x[4 * i + j], inv, d1, d2, d3);
+            a1 |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * j);
+            a2 |= static_cast<uint32_t>(d2) << (8 * j);
+            a3 |= static_cast<uint32_t>(d3) << (8 * j);
+        }
+        w1[i] = a1;
+        w2[i] = a2;
+        w3[i] = a3;
+    }
+    if (on) {
+        const size_t o = static_cast<size_t>(pidx) * EPT;
+        if constexpr (EPT == 16) {
+            *reinterpret_cast<uint4 *>(pd1 + o) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+            *reinterpret_cast<uint4 *>(pd2 + o) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+            *reinterpret_cast<uint4 *>(pd3 + o) = make_uint4(w3[0], w3[1], w3[2], w3[3]);
+        } else {
+            *reinterpret_cast<uint2 *>(pd1 + o) = make_uint2(w1[0], w1[1]);
+            *reinterpret_cast<uint2 *>(pd2 + o) = make_uint2(w2[0], w2[1]);
+            *reinterpret_cast<uint2 *>(pd3 + o) = make_uint2(w3[0], w3[1]);
+        }
+        if (pidx % TPG == 0) scale[pidx / TPG] = s;
+    }
+}
+
 template <int EPT, bool GLOBAL>
 __device__ __forceinline__ void digits_vector(const float *v, int n, int8_t *pd1, uint8_t *pd2, uint8_t *pd3,
                                               float *scale, int t, int nthreads) {
-    static_assert(EPT == 8 || EPT == 16, "8 or 16 elements per thread");
-    constexpr int TPG = 32 / EPT;                                // threads per group
     const int nparts = n / EPT;
     const int lim = ((nparts + 31) >> 5) << 5;                   // every lane of a warp iterates alike
     for (int pidx = t; pidx < lim; pidx += nthreads) {
@@ -229,42 +296,7 @@ __device__ __forceinline__ void digits_vector(const float *v, int n, int8_t *pd1
             x[4 * i + 2] = q.z;
             x[4 * i + 3] = q.w;
         }
-        float a = 0.f;
-#pragma unroll
-        for (int i = 0; i < EPT; i++) a = fmaxf(a, fabsf(x[i]));
-#pragma unroll
-        for (int o = 1; o < TPG; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-        float inv;
-        const float s = digits_scale(a, inv);
-        uint32_t w1[EPT / 4], w2[EPT / 4], w3[EPT / 4];
-#pragma unroll
-        for (int i = 0; i < EPT / 4; i++) {
-            uint32_t a1 = 0, a2 = 0, a3 = 0;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                int d1, d2, d3;
-                digits_of(x[4 * i + j], inv, d1, d2, d3);
-                a1 |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * j);
-                a2 |= static_cast<uint32_t>(d2) << (8 * j);
-                a3 |= static_cast<uint32_t>(d3) << (8 * j);
-            }
-            w1[i] = a1;
-            w2[i] = a2;
-            w3[i] = a3;
-        }
-        if (on) {
-            const size_t o = static_cast<size_t>(pidx) * EPT;
-            if constexpr (EPT == 16) {
-                *reinterpret_cast<uint4 *>(pd1 + o) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
-                *reinterpret_cast<uint4 *>(pd2 + o) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
-                *reinterpret_cast<uint4 *>(pd3 + o) = make_uint4(w3[0], w3[1], w3[2], w3[3]);
-            } else {
-                *reinterpret_cast<uint2 *>(pd1 + o) = make_uint2(w1[0], w1[1]);
-                *reinterpret_cast<uint2 *>(pd2 + o) = make_uint2(w2[0], w2[1]);
-                *reinterpret_cast<uint2 *>(pd3 + o) = make_uint2(w3[0], w3[1]);
-            }
-            if (pidx % TPG == 0) scale[pidx / TPG] = s;
-        }
+        digits_part<EPT>(x, on, pidx, pd1, pd2, pd3, scale);
     }
 }
 

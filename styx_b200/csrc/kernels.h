@@ -76,16 +76,21 @@ struct FusedArgs {
     ExpSrc gate, up, down;
     int32_t *ids64;
     float *weights;
-    float *logits;           // workspace f32[E]
-    float *xnorm;            // workspace f32[H] (written by CTA 0)
-    float *h;                // workspace f32[k][F]
-    unsigned *counters;      // workspace, 3 words, zero between launches
+    float *logits;           // workspace f32[E] (debug view)
+    float *xnorm;            // workspace f32[H] (debug view, written by CTA 0)
+    float *h;                // workspace f32[k][F] (debug view)
+    // grid-wide exchange of the logits: {value bits, tag} words; a launch's
+    // tag is (launch number) + 1, the launch number read from *gen (old / grid)
+    uint64_t *lgslot;        // workspace u64[E]
+    unsigned long long *gen; // workspace, incremented once per CTA per launch, never reset
+    unsigned long long *hdone; // workspace, likewise, once a CTA's h rows are stored
     int *err;
-    long long *trace;        // optional: 16 clock64 stamps per CTA (phase boundaries)
+    long long *trace;        // optional: kTraceStamps clock64 stamps per CTA (phase boundaries)
     // shared-memory plan (every chunk of a CTA is resident at once)
-    int rrows_floats;        // router-row buffer (>= E floats: holds the logits later)
     uint32_t off_a, off_part, off_ring, off_down;
-    int ch;                  // gate/up rows per chunk (<= 16 chunks per CTA)
+    int ch;                  // gate/up rows per chunk (<= 16 chunks per CTA, a multiple of 32 / gs_g)
+    uint32_t gu_up_off;      // offset of the up rows inside a chunk
+    uint32_t gu_stride;      // bytes per gate/up chunk
     int rb_g, rb_u, rb_d;
     int rc;                  // down output rows per chunk (<= 16 chunks per CTA)
     uint32_t dstage_bytes, dslot_stride;
@@ -141,7 +146,8 @@ cudaError_t launch_synth_f32(float *dst, uint64_t n, uint64_t seed, uint64_t off
 cudaError_t launch_fused(const FusedArgs &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st);
 bool fused_supported(int qg, int qd);
 int fused_block_threads();
-constexpr uint32_t kFusedHeader = 1280;
+constexpr uint32_t kFusedHeader = 1792;
+constexpr int kTraceStamps = 32;   // phase stamps per CTA (STYX_OPT_TRACE)
 
 // shared-memory plan of the fused kernels (computed on the host)
 int gate_up_smem(const GateUpArgs &a);

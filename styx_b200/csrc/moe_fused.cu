@@ -5,22 +5,30 @@
 // rows for all k slots) fits in shared memory at the shapes this kernel is
 // planned for (the host checks), so every bulk copy is issued up front and
 // the whole layer streams from HBM at once.  Phases of CTA b of G:
-//   0  thread 0 bulk-copies this CTA's router rows (e = b, b+G, ...) and
-//      ffn_norm into shared memory (inputs that do not depend on x);
+//   0  barrier init; L2 prefetch of this CTA's router rows (e = b, b+G, ...)
+//      and ffn_norm; the next kernel in the stream may launch (PDL); wait
+//      for the previous grid;
 //   1  RMSNorm of x (every CTA, same fixed order -> identical x_norm), the
-//      router dot products of its rows -> logits[e]; x_norm -> dp4a digits
-//      in shared memory; arrive on counter 0;
-//   2  wait for counter 0 == G (bounded), read all logits, softmax + top-k
-//      (rank form of topk_softmax_f32.comp): every CTA computes the same ids;
-//      CTA 0 publishes the id rows and the weights;
-//   3  thread 0 issues the CTA's gate/up chunks and then its down chunks;
-//      warps: gate/up dot products on dp4a, SiLU(g)*u -> h (global);
-//      arrive on counter 1;
-//   4  wait for counter 1 == G (all of h written); h -> digits in shared
-//      memory; down dot products from the prefetched rows; slot-ordered
-//      combine x[r] += sum_s w[s] d[s][r] (moe_reduce_f32.comp).
-// The counters live in the workspace; the last CTA through a wait resets the
-// counter before it, so the workspace is reusable by the next launch.
+//      router dot products of its rows -> tagged logit slots;
+//   2  read all E logit slots (polling each until it carries this launch's
+//      tag, bounded); top-k in rank form (topk_softmax_f32.comp), warps 1-15
+//      counting, warp 0 the softmax statistics: every CTA computes the same
+//      ids;
+//   3  warp 0 resolves the k slots (weights, id rows, slab sources; CTA 0
+//      publishes them) and issues the CTA's gate/up chunks (one lane per
+//      chunk) and down rows (one lane per slot) while warps 1-15 turn x_norm
+//      into dp4a digits; all warps then run the gate/up dot products as
+//      chunks land (the chunk's mbarrier also publishes the slot sources),
+//      SiLU(g)*u -> h (global);
+//   4  grid-wide wait for h (one fence and one count per CTA); h -> digits
+//      in shared memory; down dot products from the prefetched rows;
+//      slot-ordered combine x[r] += sum_s w[s] d[s][r] (moe_reduce_f32.comp).
+// Logits go through tagged exchange words: one 64-bit {value bits, tag}
+// word written and read with single 64-bit relaxed accesses, so a reader
+// that sees this launch's tag also sees its value, with no fence or counter.
+// The tag is the launch number + 1 (the workspace's launch counter, bumped
+// once by every CTA, divided by the grid size); the h arrival count is never
+// reset either: nothing in the workspace needs clearing between launches.
 // Every wait is bounded (~1 s) and reports through the device error word.
 #include <cfloat>
 
@@ -30,34 +38,62 @@
 
 namespace styx {
 
+// 1: the down rows are requested once the CTA's first gate/up chunk has
+// landed (gate/up bytes first, the down stream overlaps the gate/up work);
+// 0: every copy is requested at once
+#ifndef STYX_FUSED_DOWN_LATE
+#define STYX_FUSED_DOWN_LATE 0
+#endif
+
 constexpr int kFusedWarps = 16;
 constexpr int kFusedBlock = 32 * kFusedWarps;
-// shared-memory header: 33 mbarriers, reduction scratch, weights, ids,
+// shared-memory header: 32 mbarriers, reduction scratch, weights, ids,
 // flags, per-slot source pointers; region A starts at kFusedHeader
 constexpr int kHdrRed = 512;
 constexpr int kHdrSrc = 896;
-constexpr int kFusedHeaderBytes = 1280;
-static_assert(kHdrSrc + 3 * 16 * 8 <= kFusedHeaderBytes, "fused header overflow");
+constexpr int kHdrArgs = 1280;   // a copy of the launch's FusedArgs
+constexpr int kFusedHeaderBytes = 1792;
+static_assert(kHdrSrc + 3 * 16 * 8 <= kHdrArgs, "fused header overflow");
+static_assert(sizeof(FusedArgs) <= kFusedHeaderBytes - kHdrArgs && sizeof(FusedArgs) % 8 == 0,
+              "FusedArgs does not fit its header slot");
 static_assert(kFusedHeaderBytes == static_cast<int>(kFusedHeader), "host and device header sizes differ");
-static_assert(33 * 8 <= kHdrRed, "mbarriers overlap the reduction scratch");
+static_assert(32 * 8 <= kHdrRed, "mbarriers overlap the reduction scratch");
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// ---- tagged exchange words {f32 value bits (low), u32 tag (high)}
+// written with a 64-bit atomic exchange: performed at L2 at once, not held
+// in the SM's store path behind other traffic
+__device__ __forceinline__ void st_slot(uint64_t *p, float v, uint32_t tag) {
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    atomicExch(reinterpret_cast<unsigned long long *>(p), w);
+}
+__device__ __forceinline__ uint64_t ld_slot(const uint64_t *p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ uint32_t slot_tag(uint64_t w) { return static_cast<uint32_t>(w >> 32); }
+__device__ __forceinline__ float slot_val(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
 
-// bounded wait until *p >= target; false (and error code) on timeout
-__device__ bool spin_geq(const unsigned *p, unsigned target, int *err, int code) {
+// re-read *p until it carries `tag`; bounded (~1 s), after which `ok` is
+// cleared, the error word set and the last word read returned
+__device__ __noinline__ uint64_t poll_slot(const uint64_t *p, uint32_t tag, uint64_t w, bool &ok, int *err) {
+    if (!ok) return w;
     const long long t0 = clock64();
-    while (ld_acquire(p) < target) {
+    while (slot_tag(w) != tag) {
         if (clock64() - t0 > kSpinCycles) {
-            if (err) atomicExch(err, code);
-            return false;
+            if (err) atomicExch(err, kErrWaitRoute);
+            ok = false;
+            return w;
         }
-        __nanosleep(32);
+        __nanosleep(128);
+        w = ld_slot(p);
     }
-    return true;
+    return w;
 }
 
 __device__ __forceinline__ const uint8_t *fused_slot_src(const ExpSrc &t, int hot, int arena, int full) {
@@ -72,7 +108,7 @@ __device__ __forceinline__ const uint8_t *fused_slot_src(const ExpSrc &t, int ho
     return nullptr;
 }
 
-// block-wide deterministic sum / max (fixed tree over the 16 warps)
+// block-wide deterministic sum (fixed tree over the 16 warps)
 __device__ __forceinline__ float fblock_sum(float v, float *red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -85,23 +121,6 @@ __device__ __forceinline__ float fblock_sum(float v, float *red) {
     for (int o = 8; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
     return __shfl_sync(0xffffffffu, t, 0);
 }
-__device__ __forceinline__ float fblock_max(float v, float *red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = lane < kFusedWarps ? red[lane] : -INFINITY;
-#pragma unroll
-    for (int o = 8; o; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
-    return __shfl_sync(0xffffffffu, t, 0);
-}
-
-// shared-memory bytes reserved for n rows of rb bytes (room for the cover)
-__device__ __forceinline__ size_t chunk_bytes(int n, int rb) {
-    return (static_cast<size_t>(n) * rb + 32 + 15) & ~size_t(15);
-}
 
 // 16-byte aligned cover of [p, p + n)
 __device__ __forceinline__ void cover16(const uint8_t *p, size_t n, uintptr_t &a, uint32_t &len) {
@@ -110,11 +129,39 @@ __device__ __forceinline__ void cover16(const uint8_t *p, size_t n, uintptr_t &a
     len = static_cast<uint32_t>(((s + n + 15) & ~uintptr_t(15)) - a);
 }
 
+// Gate/up chunk c of a CTA: CTA rows [c*ch, c*ch + n) of the flattened
+// (slot, row) range starting at gbeg.  A chunk holds at most two segments:
+// rows rrA.. of slot sA (nA rows), then rows 0.. of slot sA + 1.
+struct GuChunk {
+    int sA, rrA, n, nA;
+};
+__device__ __forceinline__ GuChunk gu_chunk(int c, int ch, int gbeg, int nrows, int F) {
+    GuChunk g;
+    const int r0 = gbeg + c * ch;
+    g.sA = r0 / F;
+    g.rrA = r0 - g.sA * F;
+    g.n = min(ch, nrows - c * ch);
+    g.nA = min(g.n, F - g.rrA);
+    return g;
+}
+// shared-memory offset of segment B inside a gate (or up) area
+__device__ __forceinline__ uint32_t seg_b_off(int nA, int rb) {
+    return static_cast<uint32_t>((static_cast<size_t>(nA) * rb + 32 + 15) & ~size_t(15));
+}
+
 template <int QG, int QD>
-__global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const FusedArgs p) {
+__global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_constant__ FusedArgs pa) {
     extern __shared__ __align__(128) uint8_t smem[];
+    // The launch parameters, read once in parallel into shared memory: reading
+    // them field by field from the parameter bank costs a constant-cache miss
+    // on each first touch in every phase of every launch.
+    if (threadIdx.x < sizeof(FusedArgs) / 8)
+        reinterpret_cast<uint64_t *>(smem + kHdrArgs)[threadIdx.x] =
+            reinterpret_cast<const uint64_t *>(&pa)[threadIdx.x];
+    __syncthreads();
+    const FusedArgs &p = *reinterpret_cast<const FusedArgs *>(smem + kHdrArgs);
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *full_gu = bar, *full_d = bar + 16, *bar_router = bar + 32;
+    uint64_t *full_gu = bar, *full_d = bar + 16;
     float *red = reinterpret_cast<float *>(smem + kHdrRed);  // 32 floats
     float *wts = red + 32;                                    // 16 floats
     int *sel = reinterpret_cast<int *>(wts + 16);             // 16 ints
@@ -122,15 +169,15 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const FusedArgs p)
     const uint8_t **src_g = reinterpret_cast<const uint8_t **>(smem + kHdrSrc);   // 16 pointers each
     const uint8_t **src_u = src_g + 16;
     const uint8_t **src_d = src_u + 16;
-    uint8_t *region_a = smem + p.off_a;                       // router rows, norm, xn, x digits
-    float *rrows = reinterpret_cast<float *>(region_a);
-    float *snorm = rrows + p.rrows_floats;
-    float *xn = snorm + p.H;
-    int8_t *xd1 = reinterpret_cast<int8_t *>(xn + p.H);
-    uint8_t *xd2 = reinterpret_cast<uint8_t *>(xd1) + p.H;
-    uint8_t *xd3 = xd2 + p.H;
-    float *xsc = reinterpret_cast<float *>(xd3 + p.H);
-    const int kF = p.k * p.F;                                 // phase 4: h digits in region A
+    const int H = p.H, F = p.F, k = p.k, E = p.E;
+    uint8_t *region_a = smem + p.off_a;                       // x_norm, its digits, the logits
+    float *xn = reinterpret_cast<float *>(region_a);
+    int8_t *xd1 = reinterpret_cast<int8_t *>(xn + H);
+    uint8_t *xd2 = reinterpret_cast<uint8_t *>(xd1) + H;
+    uint8_t *xd3 = xd2 + H;
+    float *xsc = reinterpret_cast<float *>(xd3 + H);
+    float *lg = xsc + (H >> 5);
+    const int kF = k * F;                                     // phase 4: h digits in region A
     int8_t *hd1 = reinterpret_cast<int8_t *>(region_a);
     uint8_t *hd2 = reinterpret_cast<uint8_t *>(hd1) + kF;
     uint8_t *hd3 = hd2 + kF;
@@ -141,18 +188,20 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const FusedArgs p)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, b = blockIdx.x;
-    const int H = p.H, F = p.F, k = p.k, E = p.E;
     const long long T = static_cast<long long>(k) * F;
     const int gbeg = static_cast<int>(T * b / G), gend = static_cast<int>(T * (b + 1) / G);
+    const int nrows = gend - gbeg;
+    const int n_chunks = (nrows + p.ch - 1) / p.ch;
     const int dbeg = static_cast<int>(static_cast<long long>(H) * b / G);
     const int dend = static_cast<int>(static_cast<long long>(H) * (b + 1) / G);
     const int n_dchunks = (dend - dbeg + p.rc - 1) / p.rc;
     const int n_rows_mine = b < E ? (E - 1 - b) / G + 1 : 0;   // router rows e = b + G*j
 
-#define STYX_STAMP(i_)                                                     \
+#define STYX_STAMP_T(t_, i_)                                               \
     do {                                                                   \
-        if (tid == 0 && p.trace) p.trace[b * 16 + (i_)] = clock64();        \
+        if (tid == (t_) && p.trace) p.trace[b * kTraceStamps + (i_)] = clock64(); \
     } while (0)
+#define STYX_STAMP(i_) STYX_STAMP_T(0, i_)
     STYX_STAMP(0);
     // ------------------------------------------------ phase 0
     if (tid == 0) {
@@ -160,258 +209,322 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const FusedArgs p)
             mbar_init(&full_gu[i], 1);
             mbar_init(&full_d[i], 1);
         }
-        mbar_init(bar_router, 1);
         fence_mbar_init();
-        const uint32_t rb = static_cast<uint32_t>(H) * 4u;
-        mbar_arrive_expect_tx(bar_router, rb * static_cast<uint32_t>(n_rows_mine + 1));
-        bulk_g2s(snorm, p.norm_w, rb, bar_router);
-        for (int j = 0; j < n_rows_mine; j++)
-            bulk_g2s(rrows + static_cast<size_t>(j) * H, p.router + static_cast<size_t>(b + G * j) * H, rb,
-                     bar_router);
     }
+    pdl_trigger();
+    for (int j = tid; j < n_rows_mine; j += kFusedBlock)
+        prefetch_l2(p.router + static_cast<size_t>(b + G * j) * H, static_cast<uint32_t>(H) * 4u);
+    if (tid == kFusedBlock - 1) prefetch_l2(p.norm_w, static_cast<uint32_t>(H) * 4u);
     pdl_wait();
+    // this launch's tag (published to the block by the barriers in phase 1)
+    uint32_t *s_tag = reinterpret_cast<uint32_t *>(s_flag + 2);
+    if (tid == 0) *s_tag = static_cast<uint32_t>(atomicAdd(p.gen, 1ull) / static_cast<unsigned long long>(G)) + 1u;
+    STYX_STAMP(1);
 
     // ------------------------------------------------ phase 1: RMSNorm + router
     const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+    const float4 *n4 = reinterpret_cast<const float4 *>(p.norm_w);
+    float4 *xn4 = reinterpret_cast<float4 *>(xn);
     const int H4 = H >> 2;
+    // at most one float4 of each vector per thread (H <= 2048): the norm
+    // weights and the first router row are loaded together with x
+    const bool one = H4 <= kFusedBlock;
+    float4 npre = make_float4(0.f, 0.f, 0.f, 0.f), rpre = npre;
+    if (one && tid < H4) {
+        npre = __ldg(n4 + tid);
+        if (n_rows_mine > 0) rpre = __ldg(reinterpret_cast<const float4 *>(p.router + static_cast<size_t>(b) * H) + tid);
+    }
     float ss = 0.f;
     for (int i = tid; i < H4; i += kFusedBlock) {
         const float4 v = __ldcg(x4 + i);
-        reinterpret_cast<float4 *>(xn)[i] = v;   // raw x for now
+        xn4[i] = v;   // raw x for now
         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
     ss = fblock_sum(ss, red);   // (its barriers also publish the mbarrier inits)
-    STYX_STAMP(1);
     const float scale = 1.0f / sqrtf(ss / static_cast<float>(H) + p.eps);
-    const bool rok = mbar_wait(bar_router, 0, p.err, kErrWaitRoute);
-    STYX_STAMP(2);
-    for (int i = tid; i < H4; i += kFusedBlock) {
-        float4 v = reinterpret_cast<float4 *>(xn)[i];
-        const float4 w = rok ? reinterpret_cast<const float4 *>(snorm)[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+    for (int i = tid; i < H4; i += kFusedBlock) {   // same i -> thread mapping: no barrier needed
+        float4 v = xn4[i];
+        const float4 w = one ? npre : __ldg(n4 + i);
         v.x = v.x * scale * w.x;
         v.y = v.y * scale * w.y;
         v.z = v.z * scale * w.z;
         v.w = v.w * scale * w.w;
-        reinterpret_cast<float4 *>(xn)[i] = v;
+        xn4[i] = v;
     }
-    __syncthreads();
+    STYX_STAMP(2);
     for (int j = 0; j < n_rows_mine; j++) {
         float acc = 0.f;
-        const float4 *r4 = reinterpret_cast<const float4 *>(rrows + static_cast<size_t>(j) * H);
+        const float4 *r4 = reinterpret_cast<const float4 *>(p.router + static_cast<size_t>(b + G * j) * H);
         for (int i = tid; i < H4; i += kFusedBlock) {
-            const float4 r = r4[i], v = reinterpret_cast<const float4 *>(xn)[i];
+            const float4 r = (one && j == 0) ? rpre : __ldg(r4 + i), v = xn4[i];
             acc += r.x * v.x + r.y * v.y + r.z * v.z + r.w * v.w;
         }
         acc = fblock_sum(acc, red);
-        if (tid == 0) __stcg(p.logits + b + G * j, acc);
+        if (tid == 0) {
+            st_slot(p.lgslot + b + G * j, acc, *s_tag);
+            p.logits[b + G * j] = acc;   // debug view
+        }
     }
-    {   // x_norm digits (every CTA keeps its own copy for the gate/up dots)
-        const DigitsView dv{xd1, xd2, xd3, xsc};
-        for (int g = warp; g < (H >> 5); g += kFusedWarps) digits_group_warp(xn[g * 32 + lane], lane, dv, g);
-    }
-    if (b == 0)   // test / debug view of x_norm
-        for (int i = tid; i < H; i += kFusedBlock) p.xnorm[i] = xn[i];
-    __threadfence();
-    __syncthreads();
+    __syncthreads();   // x_norm complete in shared memory, tag visible
+    const uint32_t tag = *s_tag;
     STYX_STAMP(3);
-    if (tid == 0) {
-        atomicAdd(p.counters + 0, 1u);
-        s_flag[0] = spin_geq(p.counters + 0, static_cast<unsigned>(G), p.err, kErrWaitRoute) ? 1 : 0;
-    }
     STYX_STAMP(4);
-    __syncthreads();
 
     // ------------------------------------------------ phase 2: top-k
-    float *lg = rrows;   // router rows are consumed; the logits go here
-    for (int i = tid; i < E; i += kFusedBlock) lg[i] = __ldcg(p.logits + i);
+    if (warp == 0) {   // one warp per CTA polls: L2 stays free for the stores it waits for
+        bool ok = true;
+        for (int i = lane; i < E; i += 32) {
+            uint64_t w = ld_slot(p.lgslot + i);
+            if (slot_tag(w) != tag) w = poll_slot(p.lgslot + i, tag, w, ok, p.err);
+            lg[i] = slot_val(w);
+        }
+    }
+    if (tid < 16) sel[tid] = -1;
     __syncthreads();
     STYX_STAMP(5);
-    {
-        float m = -INFINITY;
-        for (int i = tid; i < E; i += kFusedBlock) m = fmaxf(m, lg[i]);
-        const float mx = fblock_max(m, red);
-        float se = 0.f;
-        for (int i = tid; i < E; i += kFusedBlock) se += expf(lg[i] - mx);
-        const float sum = fblock_sum(se, red);
-        STYX_STAMP(6);
-        if (tid < 16) sel[tid] = -1;
-        __syncthreads();
-        // rank of every finite logit (strict '>' first, equal values ordered
-        // by index): the serial scan's s-th pick is the element of rank s
-        for (int i = tid; i < E; i += kFusedBlock) {
-            const float v = lg[i];
-            if (v > -INFINITY) {
-                int gt = 0, eq = 0;
-                const float4 *l4 = reinterpret_cast<const float4 *>(lg);
-                const int E4 = E >> 2;
+    float mx = -INFINITY, sum = 0.f;
+    if (warp == 0) {
+        // softmax statistics (lane-strided partials, fixed shuffle tree);
+        // only warp 0 needs them, for the weights
 #pragma unroll 4
-                for (int j4 = 0; j4 < E4; j4++) {
-                    const float4 u = l4[j4];
-                    const int j = 4 * j4;
-                    gt += (u.x > v) + (u.y > v) + (u.z > v) + (u.w > v);
-                    eq += ((u.x == v) & (j < i)) + ((u.y == v) & (j + 1 < i)) + ((u.z == v) & (j + 2 < i)) +
-                          ((u.w == v) & (j + 3 < i));
-                }
-                for (int j = E4 * 4; j < E; j++) {
-                    const float u = lg[j];
-                    gt += u > v;
-                    eq += (u == v) & (j < i);
-                }
-                if (gt + eq < k) sel[gt + eq] = i;
+        for (int i = lane; i < E; i += 32) mx = fmaxf(mx, lg[i]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+#pragma unroll 4
+        for (int i = lane; i < E; i += 32) sum += expf(lg[i] - mx);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        STYX_STAMP(16);
+    } else {
+        // rank of every finite logit (strict '>' first, equal values ordered
+        // by index): the serial scan's s-th pick is the element of rank s.
+        // Warps 1..15 each count over a stretch of j for every candidate
+        // (every shared load a broadcast); partial counts go to the gate/up
+        // area, which no copy has touched yet.
+        int *rpart = reinterpret_cast<int *>(gubuf);
+        const int w = warp - 1, nw = kFusedWarps - 1;
+        const int js = (E + nw - 1) / nw, ja = w * js, jb = min(E, ja + js);
+        for (int cb = 0; cb < E; cb += 128) {
+            const int c0 = cb + 4 * lane;
+            float mv[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) mv[q] = c0 + q < E ? lg[c0 + q] : 0.f;
+            int cnt[4] = {0, 0, 0, 0};
+#pragma unroll 4
+            for (int j = ja; j < jb; j++) {
+                const float u = lg[j];
+#pragma unroll
+                for (int q = 0; q < 4; q++) cnt[q] += (u > mv[q]) | ((u == mv[q]) & (j < c0 + q));
+            }
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                if (c0 + q < E) rpart[w * E + c0 + q] = cnt[q];
+        }
+        STYX_STAMP_T(32, 17);
+    }
+    __syncthreads();
+    STYX_STAMP(18);
+    for (int c = tid; c < E; c += kFusedBlock) {
+        const int *rpart = reinterpret_cast<const int *>(gubuf);
+        int rank = 0;
+        for (int w = 0; w < kFusedWarps - 1; w++) rank += rpart[w * E + c];
+        if (lg[c] > -INFINITY && rank < k) sel[rank] = c;
+    }
+    __syncthreads();
+    STYX_STAMP(6);
+
+    // ------------------------------------------------ phase 3: gate/up + SiLU
+    if (warp == 0) {
+        // lane s < k: slot s's weight, id rows and slab sources
+        const int s = lane;
+        float w = 0.f;
+        int e = -1;
+        if (s < k) {
+            e = sel[s];
+            const float best = e >= 0 ? lg[e] : -INFINITY;
+            w = expf(best - mx) / sum;
+        }
+        float wsum = 0.f;   // slot order, as topk_softmax_f32.comp:50
+        for (int t = 0; t < k; t++) wsum += __shfl_sync(0xffffffffu, w, t);
+        if (s < k) {
+            const float wr = p.renorm ? w / wsum : w;
+            wts[s] = wr;
+            const uint32_t hot = (e >= 0 && p.remap) ? p.remap[e] : kSkip;
+            int hi = -1, ai = -1, fi = -1;
+            if (hot != kSkip) {
+                hi = static_cast<int>(hot);
+            } else {
+                const uint32_t a = (e >= 0 && p.pmap) ? p.pmap[e] : kSkip;
+                if (a != kSkip) ai = static_cast<int>(a);
+                else fi = e;
+            }
+            src_g[s] = fused_slot_src(p.gate, hi, ai, fi);
+            src_u[s] = fused_slot_src(p.up, hi, ai, fi);
+            src_d[s] = fused_slot_src(p.down, hi, ai, fi);
+            if (b == 0) {
+                if (e >= 0 && (!src_g[s] || !src_u[s] || !src_d[s])) atomicExch(p.err, kErrBadId);
+                p.weights[s] = wr;
+                p.ids64[s] = e;
+                p.ids64[16 + s] = hi;
+                p.ids64[32 + s] = ai;
+                p.ids64[48 + s] = fi;
             }
         }
-        __syncthreads();
-        STYX_STAMP(7);
-        if (warp == 0) {
-            // lane s < k: slot s's weight, id rows and slab sources
-            const int s = lane;
-            float w = 0.f;
-            int e = -1;
-            if (s < k) {
-                e = sel[s];
-                const float best = e >= 0 ? lg[e] : -INFINITY;
-                w = expf(best - mx) / sum;
+        __syncwarp();   // sources visible to every lane before the arrives that publish them
+        STYX_STAMP(19);
+        // ---- every expert byte this CTA needs: gate/up chunk c on lane c
+        // (gate segments, then up segments, each with room for its 16-byte
+        // cover), then the down rows of slot s on lane s
+        if (lane < n_chunks) {
+            const GuChunk c = gu_chunk(lane, p.ch, gbeg, nrows, F);
+            uint8_t *cb = gubuf + static_cast<size_t>(lane) * p.gu_stride;
+            const uint8_t *segs[4] = {nullptr, nullptr, nullptr, nullptr};
+            uint32_t lens[4] = {0, 0, 0, 0};
+            uintptr_t addr[4] = {0, 0, 0, 0};
+            uint8_t *dst[4] = {cb, cb + seg_b_off(c.nA, p.rb_g), cb + p.gu_up_off,
+                               cb + p.gu_up_off + seg_b_off(c.nA, p.rb_u)};
+            const int nB = c.n - c.nA;
+            if (src_g[c.sA]) segs[0] = src_g[c.sA] + static_cast<size_t>(c.rrA) * p.rb_g;
+            if (src_u[c.sA]) segs[2] = src_u[c.sA] + static_cast<size_t>(c.rrA) * p.rb_u;
+            if (nB > 0) {
+                segs[1] = src_g[c.sA + 1];
+                segs[3] = src_u[c.sA + 1];
             }
-            float wsum = 0.f;   // slot order, as topk_softmax_f32.comp:50
-            for (int t = 0; t < k; t++) wsum += __shfl_sync(0xffffffffu, w, t);
-            if (s < k) {
-                const float wr = p.renorm ? w / wsum : w;
-                wts[s] = wr;
-                const uint32_t hot = (e >= 0 && p.remap) ? p.remap[e] : kSkip;
-                int hi = -1, ai = -1, fi = -1;
-                if (hot != kSkip) {
-                    hi = static_cast<int>(hot);
-                } else {
-                    const uint32_t a = (e >= 0 && p.pmap) ? p.pmap[e] : kSkip;
-                    if (a != kSkip) ai = static_cast<int>(a);
-                    else fi = e;
-                }
-                src_g[s] = fused_slot_src(p.gate, hi, ai, fi);
-                src_u[s] = fused_slot_src(p.up, hi, ai, fi);
-                src_d[s] = fused_slot_src(p.down, hi, ai, fi);
-                if (b == 0) {
-                    if (e >= 0 && (!src_g[s] || !src_u[s] || !src_d[s])) atomicExch(p.err, kErrBadId);
-                    p.weights[s] = wr;
-                    p.ids64[s] = e;
-                    p.ids64[16 + s] = hi;
-                    p.ids64[32 + s] = ai;
-                    p.ids64[48 + s] = fi;
-                }
+            uint32_t total = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                if (!segs[i]) continue;
+                const int rows = (i & 1) ? nB : c.nA;
+                const int rb = i < 2 ? p.rb_g : p.rb_u;
+                cover16(segs[i], static_cast<size_t>(rows) * rb, addr[i], lens[i]);
+                total += lens[i];
+            }
+            if (total == 0) {
+                mbar_arrive(&full_gu[lane]);
+            } else {
+                mbar_arrive_expect_tx(&full_gu[lane], total);
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    if (lens[i]) bulk_g2s(dst[i], reinterpret_cast<const void *>(addr[i]), lens[i], &full_gu[lane]);
+            }
+        }
+        STYX_STAMP(20);
+#if STYX_FUSED_DOWN_LATE
+        // the down rows are needed only after the grid-wide wait for h: let
+        // the gate/up bytes land first
+        if (n_chunks > 0) mbar_wait(&full_gu[0], 0, p.err, kErrWaitFull);
+#endif
+        for (int c = 0; c < n_dchunks; c++) {
+            const int r0 = dbeg + c * p.rc, n = min(p.rc, dend - r0);
+            uintptr_t a = 0;
+            uint32_t len = 0;
+            if (s < k && src_d[s])
+                cover16(src_d[s] + static_cast<size_t>(r0) * p.rb_d, static_cast<size_t>(n) * p.rb_d, a, len);
+            uint32_t total = len;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+            if (lane == 0) {
+                if (total == 0) mbar_arrive(&full_d[c]);
+                else mbar_arrive_expect_tx(&full_d[c], total);
             }
             __syncwarp();
-            // ---- issue every expert byte this CTA needs, one lane per copy:
-            // gate/up chunks (lane ci), packed back to back (gate rows, then
-            // up rows, each with room for the 16-byte cover) ...
-            int ci = 0;
-            size_t off = 0;
-            for (int r = gbeg; r < gend; ci++) {
-                const int sl = r / F, rr = r - sl * F;
-                const int n = min(p.ch, min(gend - r, F - rr));
-                const size_t up_off = chunk_bytes(n, p.rb_g);
-                if (ci == lane) {
-                    uint8_t *dst = gubuf + off;
-                    if (src_g[sl] && src_u[sl]) {
-                        uintptr_t ga, ua;
-                        uint32_t gl, ul;
-                        cover16(src_g[sl] + static_cast<size_t>(rr) * p.rb_g, static_cast<size_t>(n) * p.rb_g, ga, gl);
-                        cover16(src_u[sl] + static_cast<size_t>(rr) * p.rb_u, static_cast<size_t>(n) * p.rb_u, ua, ul);
-                        mbar_arrive_expect_tx(&full_gu[ci], gl + ul);
-                        bulk_g2s(dst, reinterpret_cast<const void *>(ga), gl, &full_gu[ci]);
-                        bulk_g2s(dst + up_off, reinterpret_cast<const void *>(ua), ul, &full_gu[ci]);
-                    } else {
-                        mbar_arrive(&full_gu[ci]);
-                    }
-                }
-                off += up_off + chunk_bytes(n, p.rb_u);
-                r += n;
-            }
-            // ... then the down rows of every slot (lane s)
-            for (int c = 0; c < n_dchunks; c++) {
-                const int r0 = dbeg + c * p.rc, n = min(p.rc, dend - r0);
-                uintptr_t a = 0;
-                uint32_t len = 0;
-                if (s < k && src_d[s])
-                    cover16(src_d[s] + static_cast<size_t>(r0) * p.rb_d, static_cast<size_t>(n) * p.rb_d, a, len);
-                uint32_t total = len;
-#pragma unroll
-                for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-                if (lane == 0) {
-                    if (total == 0) mbar_arrive(&full_d[c]);
-                    else mbar_arrive_expect_tx(&full_d[c], total);
-                }
-                __syncwarp();
-                if (len)
-                    bulk_g2s(dbuf + static_cast<size_t>(c) * p.dstage_bytes + static_cast<size_t>(s) * p.dslot_stride,
-                             reinterpret_cast<const void *>(a), len, &full_d[c]);
-            }
+            if (len)
+                bulk_g2s(dbuf + static_cast<size_t>(c) * p.dstage_bytes + static_cast<size_t>(s) * p.dslot_stride,
+                         reinterpret_cast<const void *>(a), len, &full_d[c]);
         }
-        __syncthreads();
+        STYX_STAMP(21);
+    } else {
+        // x_norm digits (every CTA keeps its own copy for the gate/up dots),
+        // computed while warp 0 issues the copies and the bytes are in flight
+        const DigitsView dv{xd1, xd2, xd3, xsc};
+        for (int g = warp - 1; g < (H >> 5); g += kFusedWarps - 1) digits_group_warp(xn[g * 32 + lane], lane, dv, g);
+        if (b == 0)   // test / debug view of x_norm
+            for (int i = tid - 32; i < H; i += kFusedBlock - 32) p.xnorm[i] = xn[i];
+        STYX_STAMP_T(32, 22);
     }
-
-    STYX_STAMP(8);
-    // ------------------------------------------------ phase 3: gate/up + SiLU
+    __syncthreads();
+    STYX_STAMP(7);
     {
-        const int units = p.units_g, gs = p.gs_g, rpw = 32 / gs;
+        const int units = p.units_g, gs = p.gs_g, rpw = 32 / gs, stride = kFusedWarps * rpw;
         const int ug = lane & (gs - 1), grp = lane / gs;
         const bool active = ug < units;
         XUnit x;
         if (active) load_xunit<QG>(x, xd1, xd2, xd3, xsc, ug);
         bool ok = true;
-        int ci = 0;
-        size_t off = 0;
-        for (int r = gbeg; r < gend; ci++) {
-            const int s = r / F, rr = r - s * F;
-            const int n = min(p.ch, min(gend - r, F - rr));
-            if (ok) ok = mbar_wait(&full_gu[ci], 0, p.err, kErrWaitFull);
-            if (ci == 0) STYX_STAMP(9);
-            const uint8_t *gsrc = src_g[s], *usrc = src_u[s];
-            const bool valid = ok && gsrc && usrc;
-            const uint8_t *base = gubuf + off;
-            const size_t up_off = chunk_bytes(n, p.rb_g);
-            off += up_off + chunk_bytes(n, p.rb_u);
-            const uint8_t *gb =
-                base + (valid ? (reinterpret_cast<uintptr_t>(gsrc + static_cast<size_t>(rr) * p.rb_g) & 15) : 0);
-            const uint8_t *ub = base + up_off +
-                                (valid ? (reinterpret_cast<uintptr_t>(usrc + static_cast<size_t>(rr) * p.rb_u) & 15) : 0);
-            for (int t = warp * rpw; t < n; t += kFusedWarps * rpw) {
-                const int row = t + grp;
-                float g = 0.f, u = 0.f;
-                if (valid && active && row < n) {
-                    g = unit_dot<QG>(gb + static_cast<size_t>(row) * p.rb_g, ug, x);
-                    u = unit_dot<QG>(ub + static_cast<size_t>(row) * p.rb_u, ug, x);
+        int waited = -1;
+        bool first = true;
+        // CTA row q = qb + grp; rows are dealt to the warps in arrival order
+        for (int qb = warp * rpw; qb < nrows; qb += stride) {
+            const int q = qb + grp;
+            float g = 0.f, u = 0.f;
+            int r = -1;
+            if (q < nrows) {
+                const int ci = q / p.ch;   // ch % rpw == 0: the whole lane group is in one chunk
+                if (ci != waited) {
+                    if (ok) ok = mbar_wait(&full_gu[ci], 0, p.err, kErrWaitFull);
+                    waited = ci;
                 }
-                for (int o = gs >> 1; o; o >>= 1) {
-                    g += __shfl_xor_sync(0xffffffffu, g, o);
-                    u += __shfl_xor_sync(0xffffffffu, u, o);
+                const GuChunk c = gu_chunk(ci, p.ch, gbeg, nrows, F);
+                const int t = q - ci * p.ch;
+                const bool inA = t < c.nA;
+                const int s = inA ? c.sA : c.sA + 1;
+                const int rr = inA ? c.rrA + t : t - c.nA;
+                const int tt = inA ? t : t - c.nA;   // row inside its segment
+                r = s * F + rr;
+                const uint8_t *gsrc = src_g[s], *usrc = src_u[s];
+                if (ok && gsrc && usrc && active) {
+                    const uint8_t *cb = gubuf + static_cast<size_t>(ci) * p.gu_stride;
+                    const uint8_t *gseg = inA ? gsrc + static_cast<size_t>(c.rrA) * p.rb_g : gsrc;
+                    const uint8_t *useg = inA ? usrc + static_cast<size_t>(c.rrA) * p.rb_u : usrc;
+                    const uint8_t *gb = cb + (inA ? 0u : seg_b_off(c.nA, p.rb_g)) +
+                                        (reinterpret_cast<uintptr_t>(gseg) & 15) + static_cast<size_t>(tt) * p.rb_g;
+                    const uint8_t *ub = cb + p.gu_up_off + (inA ? 0u : seg_b_off(c.nA, p.rb_u)) +
+                                        (reinterpret_cast<uintptr_t>(useg) & 15) + static_cast<size_t>(tt) * p.rb_u;
+                    g = unit_dot<QG>(gb, ug, x);
+                    u = unit_dot<QG>(ub, ug, x);
                 }
-                // swiglu split (ops2.rs:305-308): g / (1 + exp(-g)) * u
-                if (ug == 0 && row < n) __stcg(p.h + static_cast<size_t>(s) * F + rr + row, g / (1.0f + expf(-g)) * u);
             }
-            r += n;
+            if (first) {
+                STYX_STAMP_T(32, 8);
+                first = false;
+            }
+            for (int o = gs >> 1; o; o >>= 1) {
+                g += __shfl_xor_sync(0xffffffffu, g, o);
+                u += __shfl_xor_sync(0xffffffffu, u, o);
+            }
+            // swiglu split (ops2.rs:305-308): g / (1 + exp(-g)) * u
+            if (ug == 0 && r >= 0) __stcg(p.h + r, g / (1.0f + expf(-g)) * u);
         }
     }
-    __threadfence();
+    __syncthreads();   // the CTA's h rows are stored; region A is reused below
+    STYX_STAMP(9);
+    // Grid-wide wait for h: thread 0 fences (ordering the whole CTA's h stores,
+    // which the barrier above made its own) and counts the CTA in; the count
+    // is never reset, so launch n waits for (n + 1) * G arrivals.
+    if (tid == 0) {
+        __threadfence();
+        atomicAdd(p.hdone, 1ull);
+        const unsigned long long target = static_cast<unsigned long long>(tag) * static_cast<unsigned long long>(G);
+        const long long t0 = clock64();
+        while (ld_acquire_u64(p.hdone) < target) {
+            if (clock64() - t0 > kSpinCycles) {
+                atomicExch(p.err, kErrWaitRoute);
+                break;
+            }
+            __nanosleep(32);
+        }
+    }
     __syncthreads();
     STYX_STAMP(10);
-    if (tid == 0) {
-        const unsigned prev = atomicAdd(p.counters + 1, 1u);
-        // every CTA has passed the phase-1 wait once counter 1 is complete
-        if (prev == static_cast<unsigned>(G) - 1) atomicExch(p.counters + 0, 0u);
-        s_flag[1] = spin_geq(p.counters + 1, static_cast<unsigned>(G), p.err, kErrWaitRoute) ? 1 : 0;
-        const unsigned prev2 = atomicAdd(p.counters + 2, 1u);
-        if (prev2 == static_cast<unsigned>(G) - 1) {
-            atomicExch(p.counters + 1, 0u);
-            atomicExch(p.counters + 2, 0u);
-        }
-    }
-    __syncthreads();
-    STYX_STAMP(11);
 
     // ------------------------------------------------ phase 4: down + combine
-    // h -> digits: two threads per 32-element group, all loads in flight
-    digits_vector<8, true>(p.h, kF, hd1, hd2, hd3, hsc, tid, kFusedBlock);
+    // h -> digits, every load of a part in flight at once
+    if (kF <= 16 * kFusedBlock)
+        digits_vector<16, true>(p.h, kF, hd1, hd2, hd3, hsc, tid, kFusedBlock);
+    else
+        digits_vector<8, true>(p.h, kF, hd1, hd2, hd3, hsc, tid, kFusedBlock);
     __syncthreads();
-    STYX_STAMP(12);
+    STYX_STAMP(11);
     {
         const int units = p.units_d, gs = p.gs_d, rpw = 32 / gs;
         const int ug = lane & (gs - 1), grp = lane / gs;
@@ -424,11 +537,11 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const FusedArgs p)
         XUnit x;
         if (!multi && slot0 < k && active)
             load_xunit<QD>(x, hd1 + slot0 * F, hd2 + slot0 * F, hd3 + slot0 * F, hsc + slot0 * (F >> 5), ug);
-        bool ok = s_flag[1] != 0;
+        bool ok = true;
         for (int c = 0; c < n_dchunks; c++) {
             const int r0 = dbeg + c * p.rc, n = min(p.rc, dend - r0);
             if (ok) ok = mbar_wait(&full_d[c], 0, p.err, kErrWaitFull);
-            if (c == 0) STYX_STAMP(13);
+            if (c == 0) STYX_STAMP(12);
             float *part = dpart + static_cast<size_t>(c & 1) * k * p.rc;
             for (int s = slot0; ok && s < k; s += sstep) {
                 if (multi && active)
@@ -437,16 +550,22 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const FusedArgs p)
                 const uint8_t *base = dbuf + static_cast<size_t>(c) * p.dstage_bytes +
                                       static_cast<size_t>(s) * p.dslot_stride +
                                       (src ? (reinterpret_cast<uintptr_t>(src + static_cast<size_t>(r0) * p.rb_d) & 15) : 0);
-                for (int t = sub * rpw; t < n; t += nwps * rpw) {
-                    const int row = t + grp;
-                    float v = 0.f;
-                    if (src && active && row < n) v = unit_dot<QD>(base + static_cast<size_t>(row) * p.rb_d, ug, x);
-                    for (int o = gs >> 1; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                    if (ug == 0 && row < n) part[s * p.rc + row] = v;
+                // two rows per lane group per pass: independent dot products in flight
+                for (int t = sub * 2 * rpw; t < n; t += nwps * 2 * rpw) {
+                    const int ra = t + grp, rb = t + rpw + grp;
+                    float va = 0.f, vb = 0.f;
+                    if (src && active && ra < n) va = unit_dot<QD>(base + static_cast<size_t>(ra) * p.rb_d, ug, x);
+                    if (src && active && rb < n) vb = unit_dot<QD>(base + static_cast<size_t>(rb) * p.rb_d, ug, x);
+                    for (int o = gs >> 1; o; o >>= 1) {
+                        va += __shfl_xor_sync(0xffffffffu, va, o);
+                        vb += __shfl_xor_sync(0xffffffffu, vb, o);
+                    }
+                    if (ug == 0 && ra < n) part[s * p.rc + ra] = va;
+                    if (ug == 0 && rb < n) part[s * p.rc + rb] = vb;
                 }
             }
             __syncthreads();
-            STYX_STAMP(14);
+            STYX_STAMP(13);
             if (ok && tid < n) {
                 float acc = 0.f;
                 for (int s = 0; s < k; s++) acc = __fadd_rn(acc, __fmul_rn(wts[s], part[s * p.rc + tid]));
@@ -454,10 +573,15 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const FusedArgs p)
             }
         }
     }
-    STYX_STAMP(15);
+    STYX_STAMP(14);
 #undef STYX_STAMP
+#undef STYX_STAMP_T
 }
 
+// Cooperative launch (every CTA co-resident: the tagged-slot reads are
+// grid-wide waits) with programmatic stream serialisation: the kernel lets
+// the next one launch at entry and waits for the previous grid before it
+// touches the workspace or x.
 template <int QG, int QD>
 static cudaError_t launch_fused_t(const FusedArgs &a, int grid, uint32_t smem, cudaStream_t st) {
     auto kern = k_moe_fused<QG, QD>;
@@ -470,9 +594,19 @@ static cudaError_t launch_fused_t(const FusedArgs &a, int grid, uint32_t smem, c
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (occ < 1 || grid > occ * sms) return cudaErrorCooperativeLaunchTooLarge;
-    void *args[] = {const_cast<FusedArgs *>(&a)};
-    return cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(kern), dim3(grid), dim3(kFusedBlock), args,
-                                       smem, st);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kFusedBlock);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 cudaError_t launch_fused(const FusedArgs &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st) {
