@@ -1,4 +1,4 @@
-"""ctypes binding of libstyx_moe.so (include/styx_moe.h).
+"""ctypes binding of libstyx_moe.so (include/styx_moe.h, include/styx_residency.h).
 
 There is no fallback: if the library is missing, importing the ops raises.
 """
@@ -10,7 +10,9 @@ import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libstyx_moe.so")
-HEADER = os.path.join(os.path.dirname(HERE), "include", "styx_moe.h")
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")
+HEADER = os.path.join(INCLUDE, "styx_moe.h")
+HEADERS = [HEADER, os.path.join(INCLUDE, "styx_residency.h")]
 
 STYX_OK, STYX_EINVAL, STYX_ECUDA, STYX_ENOMEM, STYX_ETIMEOUT, STYX_EUNSUPPORTED = 0, -1, -2, -3, -4, -5
 F32, Q8_0, Q4_K, Q5_K, Q6_K = 0, 8, 12, 13, 14
@@ -39,6 +41,11 @@ class MoeLayer(C.Structure):
     _fields_ = [("ffn_norm", C.c_void_p), ("router", C.c_void_p), ("remap", C.c_void_p),
                 ("pmap", C.c_void_p), ("gate", ExpertTensor), ("up", ExpertTensor),
                 ("down", ExpertTensor)]
+
+
+class RepinSwap(C.Structure):
+    _fields_ = [("layer", C.c_int32), ("slot", C.c_int32), ("old_expert", C.c_uint32),
+                ("new_expert", C.c_uint32)]
 
 
 class MoeDims(C.Structure):
@@ -89,6 +96,18 @@ _SIGS = {
     "styx_moe_block": (_i, [_vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp,
                             _vp, _vp, _u64]),
     "styx_moe_block_noalloc": (_i, [_vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp, _vp]),
+    # include/styx_residency.h
+    "styx_expert_budget": (_u64, [_u64, _u64, _u64, _u64, _u64, _i, _u64, _i]),
+    "styx_arena_bytes": (_u64, [_i, _i, C.POINTER(_u64)]),
+    "styx_residency_create": (_i, [_i, _i, _i, _u64, C.POINTER(_vp)]),
+    "styx_residency_destroy": (None, [_vp]),
+    "styx_residency_pin": (_i, [_vp, _vp, _vp, _vp, _i, _u64, C.POINTER(_i)]),
+    "styx_residency_pin_csv": (_i, [_vp, C.c_char_p, C.c_size_t, _u64, C.POINTER(_i)]),
+    "styx_residency_layer": (_i, [_vp, _i, _vp, _vp, C.POINTER(_i)]),
+    "styx_residency_hits": (_i, [_vp, _i, _vp]),
+    "styx_residency_maybe_repin": (_i, [_vp, _vp, _u64, _u64, _i, C.POINTER(RepinSwap), _i, C.POINTER(_i)]),
+    "styx_residency_hot_cold": (_i, [_vp, _vp, _vp, _vp]),
+    "styx_residency_prefetch_plan": (_i, [_vp, _vp, _vp, _vp]),
     "styx_synth_quant": (_i, [_vp, _vp, _i, _vp, _u64, _i, _u64, _f]),
     "styx_synth_f32": (_i, [_vp, _vp, _vp, _u64, _u64, _u64, _f]),
 }
@@ -97,8 +116,8 @@ _lib = None
 
 
 def header_functions() -> list[str]:
-    """Names of the functions include/styx_moe.h declares."""
-    txt = open(HEADER).read()
+    """Names of the functions the public headers (include/*.h) declare."""
+    txt = "".join(open(h).read() for h in HEADERS)
     txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
     return sorted(set(re.findall(r"\b(styx_[a-z0-9_]+)\s*\(", txt)))
 

@@ -25,7 +25,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
           f"-I{os.path.join(ROOT, 'include')}", "--expt-relaxed-constexpr"]
 # per-source extra flags: the synthetic quantiser must round like the C oracle
 EXTRA = {"synth.cu": ["-fmad=false"]}
-SOURCES = ["moe_kernels.cu", "moe_fused.cu", "synth.cu", "api.cu"]
+SOURCES = ["moe_kernels.cu", "moe_fused.cu", "synth.cu", "api.cu", "residency.cpp"]
 HEADERS = ["common.cuh", "qdot.cuh", "kernels.h"]
 
 
@@ -45,11 +45,12 @@ def _stale(target: str, deps: list[str]) -> bool:
 
 def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(OUT_DIR, exist_ok=True)
-    hdrs = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", "styx_moe.h")]
+    hdrs = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", h)
+                                                         for h in ("styx_moe.h", "styx_residency.h")]
     objs = []
     for src in SOURCES:
         sp = os.path.join(CSRC, src)
-        op = os.path.join(OUT_DIR, src.replace(".cu", ".o"))
+        op = os.path.join(OUT_DIR, os.path.splitext(src)[0] + ".o")
         objs.append(op)
         if force or _stale(op, [sp] + hdrs):
             cmd = [nvcc()] + ARCH + COMMON + EXTRA.get(src, []) + ["-c", sp, "-o", op]

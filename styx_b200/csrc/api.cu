@@ -235,9 +235,16 @@ int matvec_id_3way(const styx_expert_tensor &t, int n_expert, const int32_t *ids
 
 }  // namespace
 
+// error reporting for the library's other translation units
+int styx::set_error(int code, const char *msg) {
+    g_err = msg;
+    return code;
+}
+
 extern "C" {
 
 const char *styx_last_error(void) { return g_err.c_str(); }
+
 
 int styx_init(int device, styx_ctx **out) {
     NEED(out, "null out");

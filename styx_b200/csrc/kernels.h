@@ -143,6 +143,9 @@ cudaError_t launch_synth_quant(int qtype, uint8_t *dst, uint64_t nrows, int ncol
 cudaError_t launch_synth_f32(float *dst, uint64_t n, uint64_t seed, uint64_t offset, float sigma,
                              cudaStream_t st);
 
+// leaves `msg` for styx_last_error() and returns `code` (api.cu)
+int set_error(int code, const char *msg);
+
 cudaError_t launch_fused(const FusedArgs &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st);
 bool fused_supported(int qg, int qd);
 int fused_block_threads();

@@ -285,3 +285,123 @@ class MoeBlock:
         check(lib().styx_moe_workspace_view(C.byref(self._dims), _ptr(self.workspace), which, C.byref(p)))
         off = p.value - self.workspace.data_ptr()
         return self.workspace[off: off + 4 * n].view(torch.float32)
+
+
+# ---------------------------------------------------------------- residency
+def expert_budget(device_vram: int, headroom: int = 1024 << 20, pinned: int = 0, kv_max: int = 0,
+                  arena: int = 0, explicit: Optional[int] = None, all_vram: bool = False) -> int:
+    """MoeModel::load's expert VRAM budget (moe.rs:741-753), in bytes."""
+    return lib().styx_expert_budget(device_vram, headroom, pinned, kv_max, arena, int(explicit is not None),
+                                    explicit or 0, int(all_vram))
+
+
+def arena_bytes(n_layers: int, k: int, max_slab: tuple) -> int:
+    """The gather arena's size (moe.rs:727-740)."""
+    arr = (C.c_uint64 * 3)(*max_slab)
+    return lib().styx_arena_bytes(n_layers, k, arr)
+
+
+class Residency:
+    """Expert placement of MoeModel (moe.rs:692-813, 984-995, 1450-1521,
+    2169-2213): popularity pinning, the per-layer remap tables the kernels
+    read, online repin decisions, HUD counts and the prefetch plan.  Host
+    logic only (libstyx_moe.so, C++); `apply_swaps` applies a repin on the
+    device with styx_copy, as the reference does with copy_region."""
+
+    def __init__(self, n_layers: int, n_expert: int, k: int, cost_per_expert: int):
+        import numpy as np
+        self._np = np
+        self.n_layers, self.n_expert, self.k = n_layers, n_expert, k
+        h = C.c_void_p()
+        check(lib().styx_residency_create(n_layers, n_expert, k, cost_per_expert, C.byref(h)))
+        self.handle = h
+        self._destroy = lib().styx_residency_destroy   # still bound at interpreter exit
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            self._destroy(self.handle)
+            self.handle = None
+
+    def _ids(self, ids):
+        a = self._np.ascontiguousarray(ids, dtype=self._np.int32).reshape(-1)
+        assert a.size >= self.n_layers * IDS_PER_LAYER, "ids: n_layers x 64 int32"
+        return a
+
+    def pin(self, layer, expert, hits, budget: int) -> int:
+        np = self._np
+        la = np.ascontiguousarray(layer, np.int32)
+        ea = np.ascontiguousarray(expert, np.int32)
+        ha = np.ascontiguousarray(hits, np.uint64)
+        n = C.c_int()
+        check(lib().styx_residency_pin(self.handle, la.ctypes.data, ea.ctypes.data, ha.ctypes.data, la.size,
+                                       budget, C.byref(n)))
+        return n.value
+
+    def pin_csv(self, text: str, budget: int) -> int:
+        raw = text.encode()
+        n = C.c_int()
+        check(lib().styx_residency_pin_csv(self.handle, raw, len(raw), budget, C.byref(n)))
+        return n.value
+
+    def layer(self, layer: int):
+        """(remap u32[E], slot_experts u32[n_slots]) of one layer."""
+        np = self._np
+        remap = np.empty(self.n_expert, np.uint32)
+        slots = np.empty(self.n_expert, np.uint32)
+        n = C.c_int()
+        check(lib().styx_residency_layer(self.handle, layer, remap.ctypes.data, slots.ctypes.data, C.byref(n)))
+        return remap, slots[: n.value].copy()
+
+    def hits(self, layer: int):
+        h = self._np.empty(self.n_expert, self._np.uint64)
+        check(lib().styx_residency_hits(self.handle, layer, h.ctypes.data))
+        return h
+
+    def maybe_repin(self, ids, n_past: int, interval: int, max_per_layer: int = 2):
+        """MoeModel::maybe_repin: list of (layer, slot, old_expert, new_expert)."""
+        a = self._ids(ids)
+        cap = self.n_layers * max(max_per_layer, 0)
+        buf = (_lib.RepinSwap * max(cap, 1))()
+        n = C.c_int()
+        check(lib().styx_residency_maybe_repin(self.handle, a.ctypes.data, n_past, interval, max_per_layer, buf,
+                                               cap, C.byref(n)))
+        return [(buf[i].layer, buf[i].slot, buf[i].old_expert, buf[i].new_expert) for i in range(n.value)]
+
+    def hot_cold(self, ids):
+        np = self._np
+        a = self._ids(ids)
+        hot = np.empty(self.n_layers, np.uint32)
+        cold = np.empty(self.n_layers, np.uint32)
+        check(lib().styx_residency_hot_cold(self.handle, a.ctypes.data, hot.ctypes.data, cold.ctypes.data))
+        return hot, cold
+
+    def prefetch_plan(self, ids):
+        """(pmap u32[n_layers, E], pf_ids int32[n_layers, 64]) for the next token."""
+        np = self._np
+        a = self._ids(ids)
+        pmap = np.empty((self.n_layers, self.n_expert), np.uint32)
+        pf = np.full((self.n_layers, IDS_PER_LAYER), -1, np.int32)
+        check(lib().styx_residency_prefetch_plan(self.handle, a.ctypes.data, pmap.ctypes.data, pf.ctypes.data))
+        return pmap, pf
+
+    def apply_swaps(self, swaps, layers: list, remaps: list, stream=None) -> None:
+        """Apply repin swaps on the device (moe.rs:1482-1504): for each swap
+        copy the new expert's slab of the full gate/up/down tensors into its
+        hot slot (styx_copy), then upload each touched layer's remap table.
+        layers[l]: LayerWeights with full and hot tensors; remaps[l]: the
+        device remap tensor (int32/uint32[E]) the kernels read."""
+        cx = ctx(layers[0].gate.full.device.index).handle
+        touched = set()
+        for (l, slot, _old, new) in swaps:
+            lw = layers[l]
+            for ex in (lw.gate, lw.up, lw.down):
+                check(lib().styx_copy(cx, _ptr(ex.full), new * ex.slab_bytes, _ptr(ex.hot), slot * ex.slab_bytes,
+                                      ex.slab_bytes, _stream(stream)))
+            touched.add(l)
+        for l in sorted(touched):
+            remap, _ = self.layer(l)
+            host = torch.from_numpy(remap.view(self._np.int32).copy())
+            check(lib().styx_upload(cx, _ptr(remaps[l]), 0, C.c_void_p(host.data_ptr()), host.numel() * 4,
+                                    _stream(stream)))
+            if stream is None:
+                torch.cuda.synchronize(remaps[l].device)
