@@ -269,6 +269,29 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream,
                    int layer, float *x, int32_t *ids, float *weights_out,
                    void *workspace, uint64_t workspace_bytes);
 
+/* Expert parallelism (no counterpart in the reference, which runs on one
+ * device): the form of styx_moe_block for a model whose experts are split
+ * over ranks.  Every rank routes (the same kernels on the same data give
+ * every rank the same ids and weights); this rank holds only its own
+ * experts, in layer_w's hot buffers (remap: expert -> local slot or SKIP)
+ * and/or arena, with `full` NULL in each tensor, and a slot whose expert it
+ * does not hold contributes zero.  partial: f32[k * n_embd], written
+ * partial[s*n_embd + r] = w[s] * d[s][r] for the slots held here and 0 for
+ * the others; x is read (RMSNorm, router), not updated.  Sum `partial` over
+ * the ranks (one all-reduce per layer, e.g. NCCL), then styx_moe_combine
+ * adds it into x.  Runs the three-kernel form. */
+int styx_moe_block_ep(styx_ctx *ctx, styx_stream stream,
+                      const styx_moe_dims *dims, const styx_moe_layer *layer_w,
+                      int layer, const float *x, int32_t *ids,
+                      float *weights_out, float *partial, void *workspace,
+                      uint64_t workspace_bytes);
+/* x[i] += sum_{s<k} partial[s*ne + i], summed in slot order
+ * (moe_reduce_f32.comp:8-13 with the weights already applied).  With one
+ * non-zero contributor per slot the cross-rank sum is exact, so the result
+ * equals the single-device styx_moe_block bit for bit. */
+int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial,
+                     float *x, int ne, int k);
+
 /* styx_moe_block without a caller workspace; it has no counterpart in the
  * reference.  For callers that cannot allocate device memory (a host that
  * binds only the compute entry points, or one whose whole device budget is

@@ -96,6 +96,9 @@ _SIGS = {
     "styx_moe_block": (_i, [_vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp,
                             _vp, _vp, _u64]),
     "styx_moe_block_noalloc": (_i, [_vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp, _vp]),
+    "styx_moe_block_ep": (_i, [_vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp, _vp, _vp,
+                               _vp, _u64]),
+    "styx_moe_combine": (_i, [_vp, _vp, _vp, _vp, _i, _i]),
     # include/styx_residency.h
     "styx_expert_budget": (_u64, [_u64, _u64, _u64, _u64, _u64, _i, _u64, _i]),
     "styx_arena_bytes": (_u64, [_i, _i, C.POINTER(_u64)]),

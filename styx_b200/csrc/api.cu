@@ -690,6 +690,123 @@ int styx_moe_workspace_view(const styx_moe_dims *dims, void *workspace, int whic
     return STYX_OK;
 }
 
+// The three-kernel MoE block (route, gate/up + SiLU, down + combine).  With
+// `partial` the down kernel writes w[s]*d[s][r] per slot there instead of
+// updating x; `quiet` makes a missing full tensor mean "another device's
+// expert" (expert parallelism) rather than an error.
+static int moe_block_split(styx_ctx *ctx, cudaStream_t st, const styx_moe_dims &dm, const styx_moe_layer &lwr,
+                           float *x, int32_t *ids64, float *wts, uint8_t *ws, const WsLayout &L, float *partial,
+                           bool quiet) {
+    const styx_moe_dims *dims = &dm;
+    const styx_moe_layer *lw = &lwr;
+    const int H = dims->n_embd, F = dims->n_ff, E = dims->n_expert, k = dims->n_expert_used;
+    int rc = STYX_OK;
+    // 1. route
+    styx::RouteArgs ra{};
+    ra.x = x;
+    ra.norm_w = lw->ffn_norm;
+    ra.eps = dims->rms_eps;
+    ra.router = lw->router;
+    ra.E = E;
+    ra.H = H;
+    ra.k = k;
+    ra.renorm = dims->norm_topk;
+    ra.remap = lw->remap;
+    ra.pmap = lw->pmap;
+    ra.xnorm = reinterpret_cast<float *>(ws + L.xnorm);
+    ra.xd1 = reinterpret_cast<int8_t *>(ws + L.xd1);
+    ra.xd2 = ws + L.xd2;
+    ra.xd3 = ws + L.xd3;
+    ra.xscale = reinterpret_cast<float *>(ws + L.xscale);
+    ra.logits = reinterpret_cast<float *>(ws + L.logits);
+    ra.weights = wts;
+    ra.ids64 = ids64;
+    ra.counter = reinterpret_cast<unsigned *>(ws + L.counter);
+    ra.err = ctx->d_err;
+    CK(styx::launch_route(ra, st));
+
+    float *h = reinterpret_cast<float *>(ws + L.h);
+    const int units_g = H / 64;
+    // 2. gate/up + SiLU
+    if (lw->gate.qtype == lw->up.qtype && units_g <= 32) {
+        styx::GateUpArgs ga{};
+        ga.gate = to_src(lw->gate, E);
+        ga.up = to_src(lw->up, E);
+        ga.ids64 = ids64;
+        ga.xd1 = ra.xd1;
+        ga.xd2 = ra.xd2;
+        ga.xd3 = ra.xd3;
+        ga.xscale = ra.xscale;
+        ga.h = h;
+        ga.H = H;
+        ga.F = F;
+        ga.k = k;
+        ga.rb_g = static_cast<int>(row_bytes(lw->gate.qtype, H));
+        ga.rb_u = static_cast<int>(row_bytes(lw->up.qtype, H));
+        ga.units = units_g;
+        ga.gs = pow2ceil(units_g);
+        ga.ch = 8;
+        ga.up_off = static_cast<uint32_t>(a16(static_cast<size_t>(ga.ch) * ga.rb_g + 32));
+        ga.stage_bytes = ga.up_off + static_cast<uint32_t>(a16(static_cast<size_t>(ga.ch) * ga.rb_u + 32));
+        const int T = k * F;
+        const int grid = std::max(1, std::min(ctx->sm_count, (T + ga.ch - 1) / ga.ch));
+        const int rows_per_cta = (T + grid - 1) / grid;
+        const int max_st = static_cast<int>((227 * 1024 - 256) / ga.stage_bytes);
+        NEED(max_st >= 2, "gate/up rows too large for shared memory");
+        ga.nst = std::max(2, std::min({16, max_st, (rows_per_cta + ga.ch - 1) / ga.ch + 1}));
+        ga.quiet = quiet ? 1 : 0;
+        ga.err = ctx->d_err;
+        CK(styx::launch_gate_up(ga, lw->gate.qtype, grid, st));
+    } else {
+        float *g = reinterpret_cast<float *>(ws + L.g), *u = reinterpret_cast<float *>(ws + L.u);
+        // slots no dispatch writes (another device's experts) must not hold stale values
+        if (quiet) {
+            CK(cudaMemsetAsync(g, 0, static_cast<size_t>(k) * F * 4, st));
+            CK(cudaMemsetAsync(u, 0, static_cast<size_t>(k) * F * 4, st));
+        }
+        if ((rc = matvec_id_3way(lw->gate, E, ids64, F, H, k, ra.xnorm, 1, g, ctx->d_err, st))) return rc;
+        if ((rc = matvec_id_3way(lw->up, E, ids64, F, H, k, ra.xnorm, 1, u, ctx->d_err, st))) return rc;
+        CK(styx::launch_swiglu(g, u, h, k * F, st));
+    }
+
+    // 3. down + weighted combine into x
+    styx::DownArgs da{};
+    da.down = to_src(lw->down, E);
+    da.ids64 = ids64;
+    da.h = h;
+    da.w = wts;
+    da.x = x;
+    da.partial = partial;
+    da.quiet = quiet ? 1 : 0;
+    da.H = H;
+    da.F = F;
+    da.k = k;
+    da.rb = static_cast<int>(row_bytes(lw->down.qtype, F));
+    da.units = F / 64;
+    da.gs = pow2ceil(da.units);
+    da.rc = 4;
+    da.slot_stride = static_cast<uint32_t>(a16(static_cast<size_t>(da.rc) * da.rb + 32));
+    da.stage_bytes = da.slot_stride * static_cast<uint32_t>(k);
+    const int grid_d = std::max(1, std::min(ctx->sm_count, H / da.rc));
+    const int rows_d = (H + grid_d - 1) / grid_d;
+    da.dig_off = 512;
+    const size_t kF = static_cast<size_t>(k) * F;
+    const size_t dig_bytes = kF * 3 + kF / 32 * 4;
+    const int chunks = (rows_d + da.rc - 1) / da.rc;
+    const size_t fixed = a128(a128(da.dig_off + dig_bytes) + static_cast<size_t>(std::max(2, chunks)) * k * da.rc * 4);
+    NEED(fixed < 227 * 1024, "down kernel: k*n_ff too large for shared memory");
+    int nst = std::min({16, chunks, static_cast<int>((227 * 1024 - fixed) / da.stage_bytes)});
+    NEED(nst >= 1, "down rows too large for shared memory");
+    da.nst = nst;
+    da.part_off = static_cast<uint32_t>(a128(da.dig_off + dig_bytes));
+    da.stage_off = static_cast<uint32_t>(a128(da.part_off + static_cast<size_t>(std::max(2, nst)) * k * da.rc * 4));
+    const uint32_t smem_d = da.stage_off + static_cast<uint32_t>(nst) * da.stage_bytes;
+    NEED(smem_d <= 227 * 1024, "down kernel needs %u bytes of shared memory", smem_d);
+    da.err = ctx->d_err;
+    CK(styx::launch_down(da, lw->down.qtype, grid_d, smem_d, st));
+    return STYX_OK;
+}
+
 // Shared-memory plan of the single-kernel MoE block for these dims; false if
 // it does not fit one CTA per SM (the caller then uses three kernels).
 static bool plan_fused(const styx_moe_dims &d, const styx_moe_layer &lw, int sms, styx::FusedArgs &a,
@@ -744,8 +861,9 @@ static bool plan_fused(const styx_moe_dims &d, const styx_moe_layer &lw, int sms
     return true;
 }
 
-int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims, const styx_moe_layer *lw, int layer,
-                   float *x, int32_t *ids, float *weights_out, void *workspace, uint64_t workspace_bytes) {
+// Argument checks shared by the MoE block entry points.
+static int check_block(styx_ctx *ctx, const styx_moe_dims *dims, const styx_moe_layer *lw, int layer, const float *x,
+                       const int32_t *ids, void *workspace, uint64_t workspace_bytes, WsLayout &Lout) {
     ENTER(ctx);
     int rc = check_dims(dims);
     if (rc) return rc;
@@ -757,6 +875,7 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
     if ((rc = check_tensor(lw->up, "up", F, H, E))) return rc;
     if ((rc = check_tensor(lw->down, "down", H, F, E))) return rc;
     const WsLayout L = ws_layout(*dims);
+    Lout = L;
     NEED(workspace_bytes >= L.total, "workspace %llu bytes < %llu", (unsigned long long)workspace_bytes,
          (unsigned long long)L.total);
     NEED(al16(workspace) && al16(x) && al16(lw->router), "workspace, x and router must be 16-byte aligned");
@@ -767,6 +886,17 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
     NEED(extent_ok(ids, (static_cast<uint64_t>(layer) + 1) * STYX_IDS_PER_LAYER * 4), "ids buffer too small");
     NEED(!lw->remap || extent_ok(lw->remap, static_cast<uint64_t>(E) * 4), "remap smaller than n_expert");
     NEED(!lw->pmap || extent_ok(lw->pmap, static_cast<uint64_t>(E) * 4), "pmap smaller than n_expert");
+    (void)F;
+    (void)k;
+    return STYX_OK;
+}
+
+int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims, const styx_moe_layer *lw, int layer,
+                   float *x, int32_t *ids, float *weights_out, void *workspace, uint64_t workspace_bytes) {
+    WsLayout L;
+    int rc = check_block(ctx, dims, lw, layer, x, ids, workspace, workspace_bytes, L);
+    if (rc) return rc;
+    const int H = dims->n_embd, F = dims->n_ff, E = dims->n_expert, k = dims->n_expert_used;
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     int32_t *ids64 = ids + static_cast<size_t>(layer) * STYX_IDS_PER_LAYER;
     float *wts = weights_out ? weights_out : reinterpret_cast<float *>(ws + L.weights);
@@ -811,103 +941,32 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
         }
     }
     ctx->last_path = 2;
+    return moe_block_split(ctx, st, *dims, *lw, x, ids64, wts, ws, L, nullptr, false);
+}
 
-    // 1. route
-    styx::RouteArgs ra{};
-    ra.x = x;
-    ra.norm_w = lw->ffn_norm;
-    ra.eps = dims->rms_eps;
-    ra.router = lw->router;
-    ra.E = E;
-    ra.H = H;
-    ra.k = k;
-    ra.renorm = dims->norm_topk;
-    ra.remap = lw->remap;
-    ra.pmap = lw->pmap;
-    ra.xnorm = reinterpret_cast<float *>(ws + L.xnorm);
-    ra.xd1 = reinterpret_cast<int8_t *>(ws + L.xd1);
-    ra.xd2 = ws + L.xd2;
-    ra.xd3 = ws + L.xd3;
-    ra.xscale = reinterpret_cast<float *>(ws + L.xscale);
-    ra.logits = reinterpret_cast<float *>(ws + L.logits);
-    ra.weights = wts;
-    ra.ids64 = ids64;
-    ra.counter = reinterpret_cast<unsigned *>(ws + L.counter);
-    ra.err = ctx->d_err;
-    CK(styx::launch_route(ra, st));
+// ------------------------------------------------ MoE block, expert parallel
+int styx_moe_block_ep(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims, const styx_moe_layer *lw,
+                      int layer, const float *x, int32_t *ids, float *weights_out, float *partial, void *workspace,
+                      uint64_t workspace_bytes) {
+    WsLayout L;
+    int rc = check_block(ctx, dims, lw, layer, x, ids, workspace, workspace_bytes, L);
+    if (rc) return rc;
+    const uint64_t pbytes = static_cast<uint64_t>(dims->n_expert_used) * dims->n_embd * 4;
+    NEED(partial && al16(partial) && extent_ok(partial, pbytes), "partial: 16-byte aligned f32[k * n_embd] required");
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    int32_t *ids64 = ids + static_cast<size_t>(layer) * STYX_IDS_PER_LAYER;
+    float *wts = weights_out ? weights_out : reinterpret_cast<float *>(ws + L.weights);
+    ctx->last_path = 2;
+    return moe_block_split(ctx, S(stream), *dims, *lw, const_cast<float *>(x), ids64, wts, ws, L, partial, true);
+}
 
-    float *h = reinterpret_cast<float *>(ws + L.h);
-    const int units_g = H / 64;
-    // 2. gate/up + SiLU
-    if (lw->gate.qtype == lw->up.qtype && units_g <= 32) {
-        styx::GateUpArgs ga{};
-        ga.gate = to_src(lw->gate, E);
-        ga.up = to_src(lw->up, E);
-        ga.ids64 = ids64;
-        ga.xd1 = ra.xd1;
-        ga.xd2 = ra.xd2;
-        ga.xd3 = ra.xd3;
-        ga.xscale = ra.xscale;
-        ga.h = h;
-        ga.H = H;
-        ga.F = F;
-        ga.k = k;
-        ga.rb_g = static_cast<int>(row_bytes(lw->gate.qtype, H));
-        ga.rb_u = static_cast<int>(row_bytes(lw->up.qtype, H));
-        ga.units = units_g;
-        ga.gs = pow2ceil(units_g);
-        ga.ch = 8;
-        ga.up_off = static_cast<uint32_t>(a16(static_cast<size_t>(ga.ch) * ga.rb_g + 32));
-        ga.stage_bytes = ga.up_off + static_cast<uint32_t>(a16(static_cast<size_t>(ga.ch) * ga.rb_u + 32));
-        const int T = k * F;
-        const int grid = std::max(1, std::min(ctx->sm_count, (T + ga.ch - 1) / ga.ch));
-        const int rows_per_cta = (T + grid - 1) / grid;
-        const int max_st = static_cast<int>((227 * 1024 - 256) / ga.stage_bytes);
-        NEED(max_st >= 2, "gate/up rows too large for shared memory");
-        ga.nst = std::max(2, std::min({16, max_st, (rows_per_cta + ga.ch - 1) / ga.ch + 1}));
-        ga.err = ctx->d_err;
-        CK(styx::launch_gate_up(ga, lw->gate.qtype, grid, st));
-    } else {
-        float *g = reinterpret_cast<float *>(ws + L.g), *u = reinterpret_cast<float *>(ws + L.u);
-        if ((rc = matvec_id_3way(lw->gate, E, ids64, F, H, k, ra.xnorm, 1, g, ctx->d_err, st))) return rc;
-        if ((rc = matvec_id_3way(lw->up, E, ids64, F, H, k, ra.xnorm, 1, u, ctx->d_err, st))) return rc;
-        CK(styx::launch_swiglu(g, u, h, k * F, st));
-    }
-
-    // 3. down + weighted combine into x
-    styx::DownArgs da{};
-    da.down = to_src(lw->down, E);
-    da.ids64 = ids64;
-    da.h = h;
-    da.w = wts;
-    da.x = x;
-    da.d_out = nullptr;
-    da.H = H;
-    da.F = F;
-    da.k = k;
-    da.rb = static_cast<int>(row_bytes(lw->down.qtype, F));
-    da.units = F / 64;
-    da.gs = pow2ceil(da.units);
-    da.rc = 4;
-    da.slot_stride = static_cast<uint32_t>(a16(static_cast<size_t>(da.rc) * da.rb + 32));
-    da.stage_bytes = da.slot_stride * static_cast<uint32_t>(k);
-    const int grid_d = std::max(1, std::min(ctx->sm_count, H / da.rc));
-    const int rows_d = (H + grid_d - 1) / grid_d;
-    da.dig_off = 512;
-    const size_t kF = static_cast<size_t>(k) * F;
-    const size_t dig_bytes = kF * 3 + kF / 32 * 4;
-    const int chunks = (rows_d + da.rc - 1) / da.rc;
-    const size_t fixed = a128(a128(da.dig_off + dig_bytes) + static_cast<size_t>(std::max(2, chunks)) * k * da.rc * 4);
-    NEED(fixed < 227 * 1024, "down kernel: k*n_ff too large for shared memory");
-    int nst = std::min({16, chunks, static_cast<int>((227 * 1024 - fixed) / da.stage_bytes)});
-    NEED(nst >= 1, "down rows too large for shared memory");
-    da.nst = nst;
-    da.part_off = static_cast<uint32_t>(a128(da.dig_off + dig_bytes));
-    da.stage_off = static_cast<uint32_t>(a128(da.part_off + static_cast<size_t>(std::max(2, nst)) * k * da.rc * 4));
-    const uint32_t smem_d = da.stage_off + static_cast<uint32_t>(nst) * da.stage_bytes;
-    NEED(smem_d <= 227 * 1024, "down kernel needs %u bytes of shared memory", smem_d);
-    da.err = ctx->d_err;
-    CK(styx::launch_down(da, lw->down.qtype, grid_d, smem_d, st));
+int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial, float *x, int ne, int k) {
+    ENTER(ctx);
+    NEED(partial && x, "null pointer");
+    NEED(ne > 0 && k > 0 && k <= STYX_MAX_TOPK, "bad ne %d / k %d", ne, k);
+    NEED(extent_ok(partial, static_cast<uint64_t>(ne) * k * 4) && extent_ok(x, static_cast<uint64_t>(ne) * 4),
+         "partial / x smaller than k * ne / ne");
+    CK(styx::launch_combine_partial(partial, x, ne, k, S(stream)));
     return STYX_OK;
 }
 

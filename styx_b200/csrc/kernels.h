@@ -47,6 +47,7 @@ struct GateUpArgs {
     int units, gs;           // 64-element units per row, lane group size
     int ch, nst;             // rows per chunk, pipeline stages
     uint32_t stage_bytes, up_off;
+    int quiet;               // a slot whose fallback full tensor is null is not this device's: no error
     int *err;
 };
 
@@ -56,7 +57,8 @@ struct DownArgs {
     const float *h;          // f32[k][F]
     const float *w;          // f32[k]
     float *x;                // residual f32[H], += combine
-    float *d_out;            // optional f32[k][H]
+    float *partial;          // optional f32[k][H]: w[s]*d[s][r] per slot, written instead of the combine into x
+    int quiet;               // as GateUpArgs::quiet
     int H, F, k, rb;
     int units, gs;
     int rc, nst;             // rows per chunk, stages
@@ -137,6 +139,7 @@ cudaError_t launch_topk(const float *logits, int n, int k, int renorm, const uin
 cudaError_t launch_swiglu(const float *g, const float *u, float *out, int n, cudaStream_t st);
 cudaError_t launch_moe_reduce(const float *d, const float *w, float *x, int ne, int k,
                               cudaStream_t st);
+cudaError_t launch_combine_partial(const float *partial, float *x, int ne, int k, cudaStream_t st);
 cudaError_t launch_gather(const GatherArgs &a, cudaStream_t st);
 cudaError_t launch_synth_quant(int qtype, uint8_t *dst, uint64_t nrows, int ncols, uint64_t seed,
                                float sigma, cudaStream_t st);

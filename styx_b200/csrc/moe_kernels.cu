@@ -24,8 +24,10 @@ namespace styx {
 // Source slab of slot s: hot row, then arena row, then full-tensor row (the
 // three-way split of rec_matvec_id, moe.rs:1649-1700).  An index outside its
 // source is skipped (nullptr) and reported; `report` is false on re-reads.
+// With `quiet`, a full-tensor fallback with no full tensor (an expert another
+// device holds, expert parallelism) is skipped without a report.
 __device__ __forceinline__ const uint8_t *slot_src(const ExpSrc &t, const int32_t *ids64, int s, int *err,
-                                                   bool report) {
+                                                   bool report, bool quiet = false) {
     const uint32_t h = static_cast<uint32_t>(ids64[16 + s]);
     const uint32_t a = static_cast<uint32_t>(ids64[32 + s]);
     const uint32_t g = static_cast<uint32_t>(ids64[48 + s]);
@@ -39,7 +41,7 @@ __device__ __forceinline__ const uint8_t *slot_src(const ExpSrc &t, const int32_
         else bad = true;
     } else if (g != kSkip) {
         if (t.full && g < t.nfull) p = t.full + static_cast<uint64_t>(g) * t.slab;
-        else bad = true;
+        else bad = t.full || !quiet;
     }
     if (bad && report && err) atomicExch(err, kErrBadId);
     return p;
@@ -229,8 +231,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_gate_up(const GateUpArgs p
                 const int st = ci % p.nst;
                 if (ci >= p.nst && !mbar_wait(&empty[st], ((ci / p.nst) - 1) & 1, p.err, kErrWaitEmpty))
                     break;
-                const uint8_t *gsrc = slot_src(p.gate, p.ids64, s, p.err, true);
-                const uint8_t *usrc = slot_src(p.up, p.ids64, s, p.err, true);
+                const uint8_t *gsrc = slot_src(p.gate, p.ids64, s, p.err, true, p.quiet);
+                const uint8_t *usrc = slot_src(p.up, p.ids64, s, p.err, true, p.quiet);
                 uint8_t *dst = stages + static_cast<size_t>(st) * p.stage_bytes;
                 if (gsrc && usrc) {
                     const uintptr_t g0 = reinterpret_cast<uintptr_t>(gsrc + static_cast<size_t>(rr) * p.rb_g);
@@ -266,8 +268,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_gate_up(const GateUpArgs p
         const int n = min(p.ch, min(rend - r, p.F - rr));
         const int st = ci % p.nst;
         if (!mbar_wait(&full[st], (ci / p.nst) & 1, p.err, kErrWaitFull)) break;
-        const uint8_t *gsrc = slot_src(p.gate, p.ids64, s, p.err, false);
-        const uint8_t *usrc = slot_src(p.up, p.ids64, s, p.err, false);
+        const uint8_t *gsrc = slot_src(p.gate, p.ids64, s, p.err, false, p.quiet);
+        const uint8_t *usrc = slot_src(p.up, p.ids64, s, p.err, false, p.quiet);
         const bool valid = gsrc && usrc;
         const uint8_t *base = stages + static_cast<size_t>(st) * p.stage_bytes;
         const uint8_t *gbase =
@@ -360,7 +362,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
                 uint8_t *dst = stages + static_cast<size_t>(st) * p.stage_bytes;
                 uint32_t total = 0;
                 for (int s = 0; s < p.k; s++) {
-                    const uint8_t *src = slot_src(p.down, p.ids64, s, p.err, true);
+                    const uint8_t *src = slot_src(p.down, p.ids64, s, p.err, true, p.quiet);
                     if (!src) continue;
                     const uintptr_t a0 = reinterpret_cast<uintptr_t>(src + static_cast<size_t>(r0) * p.rb);
                     const uintptr_t aa = a0 & ~uintptr_t(15);
@@ -373,7 +375,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
                 }
                 mbar_arrive_expect_tx(&full[st], total);
                 for (int s = 0; s < p.k; s++) {
-                    const uint8_t *src = slot_src(p.down, p.ids64, s, p.err, false);
+                    const uint8_t *src = slot_src(p.down, p.ids64, s, p.err, false, p.quiet);
                     if (!src) continue;
                     const uintptr_t a0 = reinterpret_cast<uintptr_t>(src + static_cast<size_t>(r0) * p.rb);
                     const uintptr_t aa = a0 & ~uintptr_t(15);
@@ -417,7 +419,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
         for (int s = slot0; ok && s < p.k; s += sstep) {
             if (multi && active)
                 load_xunit<QT>(x, hd1 + s * p.F, hd2 + s * p.F, hd3 + s * p.F, hsc + s * (p.F >> 5), ug);
-            const uint8_t *src = slot_src(p.down, p.ids64, s, p.err, false);
+            const uint8_t *src = slot_src(p.down, p.ids64, s, p.err, false, p.quiet);
             const uint8_t *base = stages + static_cast<size_t>(st) * p.stage_bytes +
                                   static_cast<size_t>(s) * p.slot_stride +
                                   (src ? (reinterpret_cast<uintptr_t>(src + static_cast<size_t>(r0) * p.rb) & 15) : 0);
@@ -432,11 +434,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
         const int ct = threadIdx.x - 32;
         if (ok && ct < n) {
-            float acc = 0.f;
-            for (int s = 0; s < p.k; s++) acc = __fadd_rn(acc, __fmul_rn(wts[s], part[s * p.rc + ct]));
-            p.x[r0 + ct] = __fadd_rn(p.x[r0 + ct], acc);
-            if (p.d_out)
-                for (int s = 0; s < p.k; s++) p.d_out[static_cast<size_t>(s) * p.H + r0 + ct] = part[s * p.rc + ct];
+            if (p.partial) {   // per-slot contributions for a cross-device sum (expert parallelism)
+                for (int s = 0; s < p.k; s++)
+                    p.partial[static_cast<size_t>(s) * p.H + r0 + ct] = __fmul_rn(wts[s], part[s * p.rc + ct]);
+            } else {
+                float acc = 0.f;
+                for (int s = 0; s < p.k; s++) acc = __fadd_rn(acc, __fmul_rn(wts[s], part[s * p.rc + ct]));
+                p.x[r0 + ct] = __fadd_rn(p.x[r0 + ct], acc);
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
@@ -608,6 +613,23 @@ __global__ void k_moe_reduce(const float *d, const float *w, float *x, int ne, i
     float acc = 0.f;
     for (int s = 0; s < k; s++) acc = __fadd_rn(acc, __fmul_rn(w[s], d[static_cast<size_t>(s) * ne + i]));
     x[i] = __fadd_rn(x[i], acc);
+}
+
+// x[i] += sum_s partial[s*ne + i] in slot order: moe_reduce_f32.comp with the
+// weights already applied by the devices that own the slots (each slot has
+// one non-zero contributor, so the cross-device sum before this is exact and
+// the result equals the single-device combine bit for bit)
+__global__ void k_combine_partial(const float *partial, float *x, int ne, int k) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= ne) return;
+    float acc = 0.f;
+    for (int s = 0; s < k; s++) acc = __fadd_rn(acc, partial[static_cast<size_t>(s) * ne + i]);
+    x[i] = __fadd_rn(x[i], acc);
+}
+
+cudaError_t launch_combine_partial(const float *partial, float *x, int ne, int k, cudaStream_t st) {
+    k_combine_partial<<<(ne + 255) / 256, 256, 0, st>>>(partial, x, ne, k);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_moe_reduce(const float *d, const float *w, float *x, int ne, int k, cudaStream_t st) {

@@ -279,6 +279,23 @@ class MoeBlock:
                                    self.ws_bytes))
         return x
 
+    def forward_ep(self, x: torch.Tensor, layer_w: LayerWeights, layer: int, ids: torch.Tensor,
+                   partial: torch.Tensor, weights_out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        """Expert-parallel half of the block: partial[s, r] = w[s] * d[s][r]
+        for the slots whose experts this rank holds (0 elsewhere); x is not
+        updated.  Sum `partial` over the ranks, then `combine`."""
+        st = layer_w.struct()
+        check(lib().styx_moe_block_ep(self.ctx.handle, _stream(stream), C.byref(self._dims), C.byref(st), layer,
+                                      _ptr(x), _ptr(ids), _ptr(weights_out), _ptr(partial), _ptr(self.workspace),
+                                      self.ws_bytes))
+        return partial
+
+    def combine(self, partial: torch.Tensor, x: torch.Tensor, stream=None) -> torch.Tensor:
+        """x += the slot-ordered sum of the (rank-summed) partials."""
+        check(lib().styx_moe_combine(self.ctx.handle, _stream(stream), _ptr(partial), _ptr(x), self.dims.n_embd,
+                                     self.dims.n_expert_used))
+        return x
+
     def view(self, which: int, n: int) -> torch.Tensor:
         """xnorm (0), logits (1), h (2), weights (3) of the last forward."""
         p = C.c_void_p()
