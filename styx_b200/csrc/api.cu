@@ -116,10 +116,11 @@ size_t a128(size_t v) { return (v + 127) & ~size_t(127); }
 
 constexpr size_t kTraceCtas = 256;   // phase stamps: styx::kTraceStamps per CTA
 
-// The counter block: word 0 is the three-kernel route's hand-off counter
-// (zero between launches); the single kernel's 64-bit launch and h-arrival
-// counters sit at kGenOffset and are never reset except by
-// styx_moe_workspace_init (which also clears the tagged slots they guard).
+// The counter block (512 B): word 0 is the three-kernel route's hand-off
+// counter (zero between launches); the single kernel's 64-bit launch counter
+// and its 16 per-slot h-arrival counters follow at kGenOffset and are never
+// reset except by styx_moe_workspace_init (which also clears the tagged slots
+// they guard).
 constexpr size_t kGenOffset = 128;
 struct WsLayout {
     size_t counter, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, lgslot, trace, total;
@@ -134,7 +135,7 @@ WsLayout ws_layout(const styx_moe_dims &d) {
         return r;
     };
     const size_t H = d.n_embd, E = d.n_expert, kF = static_cast<size_t>(d.n_expert_used) * d.n_ff;
-    L.counter = take(256);
+    L.counter = take(512);
     L.xnorm = take(H * 4);
     L.xd1 = take(H);
     L.xd2 = take(H);
@@ -931,7 +932,7 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
             fa.h = reinterpret_cast<float *>(ws + L.h);
             fa.lgslot = reinterpret_cast<uint64_t *>(ws + L.lgslot);
             fa.gen = reinterpret_cast<unsigned long long *>(ws + L.counter + kGenOffset);
-            fa.hdone = fa.gen + 1;
+            fa.hcount = fa.gen + 1;
             fa.err = ctx->d_err;
             fa.trace = ctx->trace ? reinterpret_cast<long long *>(ws + L.trace) : nullptr;
             NEED(!ctx->trace || ctx->sm_count <= static_cast<int>(kTraceCtas), "too many CTAs to trace");

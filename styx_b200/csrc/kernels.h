@@ -85,7 +85,7 @@ struct FusedArgs {
     // tag is (launch number) + 1, the launch number read from *gen (old / grid)
     uint64_t *lgslot;        // workspace u64[E]
     unsigned long long *gen; // workspace, incremented once per CTA per launch, never reset
-    unsigned long long *hdone; // workspace, likewise, once a CTA's h rows are stored
+    unsigned long long *hcount; // workspace u64[16]: rows of h stored per slot, never reset
     int *err;
     long long *trace;        // optional: kTraceStamps clock64 stamps per CTA (phase boundaries)
     // shared-memory plan (every chunk of a CTA is resident at once)

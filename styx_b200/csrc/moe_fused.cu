@@ -20,14 +20,16 @@
 //      into dp4a digits; all warps then run the gate/up dot products as
 //      chunks land (the chunk's mbarrier also publishes the slot sources),
 //      SiLU(g)*u -> h (global);
-//   4  grid-wide wait for h (one fence and one count per CTA); h -> digits
-//      in shared memory; down dot products from the prefetched rows;
-//      slot-ordered combine x[r] += sum_s w[s] d[s][r] (moe_reduce_f32.comp).
+//   4  each CTA counts its h rows into per-slot arrival counters (one fence);
+//      the warps of slot s wait for slot s alone, turn h[s] into digits in
+//      shared memory and run the CTA's down rows for slot s from the
+//      prefetched rows; slot-ordered combine x[r] += sum_s w[s] d[s][r]
+//      (moe_reduce_f32.comp).
 // Logits go through tagged exchange words: one 64-bit {value bits, tag}
 // word written and read with single 64-bit relaxed accesses, so a reader
 // that sees this launch's tag also sees its value, with no fence or counter.
 // The tag is the launch number + 1 (the workspace's launch counter, bumped
-// once by every CTA, divided by the grid size); the h arrival count is never
+// once by every CTA, divided by the grid size); the h arrival counts are never
 // reset either: nothing in the workspace needs clearing between launches.
 // Every wait is bounded (~1 s) and reports through the device error word.
 #include <cfloat>
@@ -106,6 +108,36 @@ __device__ __forceinline__ const uint8_t *fused_slot_src(const ExpSrc &t, int ho
         return (t.full && static_cast<uint32_t>(full) < t.nfull) ? t.full + static_cast<uint64_t>(full) * t.slab
                                                                   : nullptr;
     return nullptr;
+}
+
+// barrier among the nthreads threads (whole warps) that work on slot s:
+// named barrier 1 + s (0 is __syncthreads), or the warp itself
+__device__ __forceinline__ void slot_group_sync(int s, int nthreads) {
+    if (nthreads == 32) __syncwarp();
+    else asm volatile("bar.sync %0, %1;" ::"r"(1 + s), "r"(nthreads) : "memory");
+}
+
+// two block-wide deterministic sums at once (fixed tree over the 16 warps)
+__device__ __forceinline__ float2 fblock_sum2(float2 v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        v.x += __shfl_xor_sync(0xffffffffu, v.x, o);
+        v.y += __shfl_xor_sync(0xffffffffu, v.y, o);
+    }
+    __syncthreads();
+    if (lane == 0) {
+        red[warp] = v.x;
+        red[kFusedWarps + warp] = v.y;
+    }
+    __syncthreads();
+    float a = lane < kFusedWarps ? red[lane] : 0.f, c = lane < kFusedWarps ? red[kFusedWarps + lane] : 0.f;
+#pragma unroll
+    for (int o = 8; o; o >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, o);
+        c += __shfl_xor_sync(0xffffffffu, c, o);
+    }
+    return make_float2(__shfl_sync(0xffffffffu, a, 0), __shfl_sync(0xffffffffu, c, 0));
 }
 
 // block-wide deterministic sum (fixed tree over the 16 warps)
@@ -194,7 +226,6 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
     const int n_chunks = (nrows + p.ch - 1) / p.ch;
     const int dbeg = static_cast<int>(static_cast<long long>(H) * b / G);
     const int dend = static_cast<int>(static_cast<long long>(H) * (b + 1) / G);
-    const int n_dchunks = (dend - dbeg + p.rc - 1) / p.rc;
     const int n_rows_mine = b < E ? (E - 1 - b) / G + 1 : 0;   // router rows e = b + G*j
 
 #define STYX_STAMP_T(t_, i_)                                               \
@@ -215,10 +246,13 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
     for (int j = tid; j < n_rows_mine; j += kFusedBlock)
         prefetch_l2(p.router + static_cast<size_t>(b + G * j) * H, static_cast<uint32_t>(H) * 4u);
     if (tid == kFusedBlock - 1) prefetch_l2(p.norm_w, static_cast<uint32_t>(H) * 4u);
-    pdl_wait();
-    // this launch's tag (published to the block by the barriers in phase 1)
+    // this launch's tag (published to the block by the barriers in phase 1).
+    // Safe before the grid dependency resolves: every CTA of the previous
+    // launch on this workspace took its number before any of them could exit
+    // (each waits in phase 2 for all of that launch's logits).
     uint32_t *s_tag = reinterpret_cast<uint32_t *>(s_flag + 2);
     if (tid == 0) *s_tag = static_cast<uint32_t>(atomicAdd(p.gen, 1ull) / static_cast<unsigned long long>(G)) + 1u;
+    pdl_wait();
     STYX_STAMP(1);
 
     // ------------------------------------------------ phase 1: RMSNorm + router
@@ -234,14 +268,24 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
         npre = __ldg(n4 + tid);
         if (n_rows_mine > 0) rpre = __ldg(reinterpret_cast<const float4 *>(p.router + static_cast<size_t>(b) * H) + tid);
     }
-    float ss = 0.f;
+    // one block reduction for both sum(x^2) and the first router row's
+    // sum(r * w * x): logit = scale * sum(r * w * x) with scale the RMSNorm
+    // factor (the same value as sum(r * x_norm) up to rounding order)
+    float ss = 0.f, rd = 0.f;
     for (int i = tid; i < H4; i += kFusedBlock) {
         const float4 v = __ldcg(x4 + i);
         xn4[i] = v;   // raw x for now
         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        if (one) rd += rpre.x * npre.x * v.x + rpre.y * npre.y * v.y + rpre.z * npre.z * v.z + rpre.w * npre.w * v.w;
     }
-    ss = fblock_sum(ss, red);   // (its barriers also publish the mbarrier inits)
+    const float2 red2 = fblock_sum2(make_float2(ss, rd), red);   // (its barriers also publish the mbarrier inits)
+    ss = red2.x;
     const float scale = 1.0f / sqrtf(ss / static_cast<float>(H) + p.eps);
+    if (one && n_rows_mine > 0 && tid == 0) {
+        const float acc = scale * red2.y;
+        st_slot(p.lgslot + b, acc, *s_tag);
+        p.logits[b] = acc;   // debug view
+    }
     for (int i = tid; i < H4; i += kFusedBlock) {   // same i -> thread mapping: no barrier needed
         float4 v = xn4[i];
         const float4 w = one ? npre : __ldg(n4 + i);
@@ -252,11 +296,11 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
         xn4[i] = v;
     }
     STYX_STAMP(2);
-    for (int j = 0; j < n_rows_mine; j++) {
+    for (int j = one ? 1 : 0; j < n_rows_mine; j++) {   // further router rows (E > grid, or H > 2048)
         float acc = 0.f;
         const float4 *r4 = reinterpret_cast<const float4 *>(p.router + static_cast<size_t>(b + G * j) * H);
         for (int i = tid; i < H4; i += kFusedBlock) {
-            const float4 r = (one && j == 0) ? rpre : __ldg(r4 + i), v = xn4[i];
+            const float4 r = __ldg(r4 + i), v = xn4[i];
             acc += r.x * v.x + r.y * v.y + r.z * v.z + r.w * v.w;
         }
         acc = fblock_sum(acc, red);
@@ -414,23 +458,23 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
         // the gate/up bytes land first
         if (n_chunks > 0) mbar_wait(&full_gu[0], 0, p.err, kErrWaitFull);
 #endif
-        for (int c = 0; c < n_dchunks; c++) {
-            const int r0 = dbeg + c * p.rc, n = min(p.rc, dend - r0);
+        {   // the CTA's down rows of every slot, one chunk (rc >= dend - dbeg)
+            const int n = dend - dbeg;
             uintptr_t a = 0;
             uint32_t len = 0;
-            if (s < k && src_d[s])
-                cover16(src_d[s] + static_cast<size_t>(r0) * p.rb_d, static_cast<size_t>(n) * p.rb_d, a, len);
+            if (s < k && src_d[s] && n > 0)
+                cover16(src_d[s] + static_cast<size_t>(dbeg) * p.rb_d, static_cast<size_t>(n) * p.rb_d, a, len);
             uint32_t total = len;
 #pragma unroll
             for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
             if (lane == 0) {
-                if (total == 0) mbar_arrive(&full_d[c]);
-                else mbar_arrive_expect_tx(&full_d[c], total);
+                if (total == 0) mbar_arrive(&full_d[0]);
+                else mbar_arrive_expect_tx(&full_d[0], total);
             }
             __syncwarp();
             if (len)
-                bulk_g2s(dbuf + static_cast<size_t>(c) * p.dstage_bytes + static_cast<size_t>(s) * p.dslot_stride,
-                         reinterpret_cast<const void *>(a), len, &full_d[c]);
+                bulk_g2s(dbuf + static_cast<size_t>(s) * p.dslot_stride, reinterpret_cast<const void *>(a), len,
+                         &full_d[0]);
         }
         STYX_STAMP(21);
     } else {
@@ -498,33 +542,24 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
     }
     __syncthreads();   // the CTA's h rows are stored; region A is reused below
     STYX_STAMP(9);
-    // Grid-wide wait for h: thread 0 fences (ordering the whole CTA's h stores,
-    // which the barrier above made its own) and counts the CTA in; the count
-    // is never reset, so launch n waits for (n + 1) * G arrivals.
+    // Per-slot arrival counts of h (never reset): each CTA adds the number of
+    // rows it stored for each slot it covers, so slot s of launch n is
+    // complete at (n + 1) * F.  Thread 0 fences first, ordering the CTA's h
+    // stores, which the barrier above made its own.
     if (tid == 0) {
         __threadfence();
-        atomicAdd(p.hdone, 1ull);
-        const unsigned long long target = static_cast<unsigned long long>(tag) * static_cast<unsigned long long>(G);
-        const long long t0 = clock64();
-        while (ld_acquire_u64(p.hdone) < target) {
-            if (clock64() - t0 > kSpinCycles) {
-                atomicExch(p.err, kErrWaitRoute);
-                break;
-            }
-            __nanosleep(32);
+        for (int r = gbeg; r < gend;) {
+            const int s = r / F, e = min(gend, (s + 1) * F);
+            atomicAdd(p.hcount + s, static_cast<unsigned long long>(e - r));
+            r = e;
         }
     }
-    __syncthreads();
     STYX_STAMP(10);
 
     // ------------------------------------------------ phase 4: down + combine
-    // h -> digits, every load of a part in flight at once
-    if (kF <= 16 * kFusedBlock)
-        digits_vector<16, true>(p.h, kF, hd1, hd2, hd3, hsc, tid, kFusedBlock);
-    else
-        digits_vector<8, true>(p.h, kF, hd1, hd2, hd3, hsc, tid, kFusedBlock);
-    __syncthreads();
-    STYX_STAMP(11);
+    // The warps of slot s wait for slot s's h only, turn it into digits in
+    // shared memory themselves and run the CTA's down rows for slot s; the
+    // slots proceed independently until the combine.
     {
         const int units = p.units_d, gs = p.gs_d, rpw = 32 / gs;
         const int ug = lane & (gs - 1), grp = lane / gs;
@@ -534,43 +569,75 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
         const int slot0 = multi ? warp : warp / nwps;
         const int sub = multi ? 0 : warp % nwps;
         const int sstep = multi ? kFusedWarps : 1 << 30;
-        XUnit x;
-        if (!multi && slot0 < k && active)
-            load_xunit<QD>(x, hd1 + slot0 * F, hd2 + slot0 * F, hd3 + slot0 * F, hsc + slot0 * (F >> 5), ug);
+        const int gthreads = nwps * 32, gt = sub * 32 + lane;   // thread index inside the slot's warps
+        const int n = dend - dbeg;                              // the CTA's down rows (one chunk)
+        const unsigned long long htarget = static_cast<unsigned long long>(tag) * static_cast<unsigned long long>(F);
         bool ok = true;
-        for (int c = 0; c < n_dchunks; c++) {
-            const int r0 = dbeg + c * p.rc, n = min(p.rc, dend - r0);
-            if (ok) ok = mbar_wait(&full_d[c], 0, p.err, kErrWaitFull);
-            if (c == 0) STYX_STAMP(12);
-            float *part = dpart + static_cast<size_t>(c & 1) * k * p.rc;
-            for (int s = slot0; ok && s < k; s += sstep) {
-                if (multi && active)
-                    load_xunit<QD>(x, hd1 + s * F, hd2 + s * F, hd3 + s * F, hsc + s * (F >> 5), ug);
-                const uint8_t *src = src_d[s];
-                const uint8_t *base = dbuf + static_cast<size_t>(c) * p.dstage_bytes +
-                                      static_cast<size_t>(s) * p.dslot_stride +
-                                      (src ? (reinterpret_cast<uintptr_t>(src + static_cast<size_t>(r0) * p.rb_d) & 15) : 0);
-                // two rows per lane group per pass: independent dot products in flight
-                for (int t = sub * 2 * rpw; t < n; t += nwps * 2 * rpw) {
-                    const int ra = t + grp, rb = t + rpw + grp;
-                    float va = 0.f, vb = 0.f;
-                    if (src && active && ra < n) va = unit_dot<QD>(base + static_cast<size_t>(ra) * p.rb_d, ug, x);
-                    if (src && active && rb < n) vb = unit_dot<QD>(base + static_cast<size_t>(rb) * p.rb_d, ug, x);
-                    for (int o = gs >> 1; o; o >>= 1) {
-                        va += __shfl_xor_sync(0xffffffffu, va, o);
-                        vb += __shfl_xor_sync(0xffffffffu, vb, o);
+        bool have_rows = false;
+        for (int s = slot0; s < k; s += sstep) {
+            if (gt == 0) {
+                const long long t0 = clock64();
+                while (ld_acquire_u64(p.hcount + s) < htarget) {
+                    if (clock64() - t0 > kSpinCycles) {
+                        atomicExch(p.err, kErrWaitRoute);
+                        break;
                     }
-                    if (ug == 0 && ra < n) part[s * p.rc + ra] = va;
-                    if (ug == 0 && rb < n) part[s * p.rc + rb] = vb;
+                    __nanosleep(32);
                 }
             }
-            __syncthreads();
-            STYX_STAMP(13);
-            if (ok && tid < n) {
-                float acc = 0.f;
-                for (int s = 0; s < k; s++) acc = __fadd_rn(acc, __fmul_rn(wts[s], part[s * p.rc + tid]));
-                p.x[r0 + tid] = __fadd_rn(p.x[r0 + tid], acc);
+            slot_group_sync(s, gthreads);
+            if (s == slot0) STYX_STAMP(11);
+            {   // h[s] -> digits: 16 elements per thread, two threads per 32-element group
+                int8_t *d1 = hd1 + s * F;
+                uint8_t *d2 = hd2 + s * F, *d3 = hd3 + s * F;
+                float *sc = hsc + s * (F >> 5);
+                const float4 *hv = reinterpret_cast<const float4 *>(p.h + static_cast<size_t>(s) * F);
+                const int nparts = F >> 4, lim = ((nparts + 31) >> 5) << 5;
+                for (int pidx = gt; pidx < lim; pidx += gthreads) {
+                    const bool on = pidx < nparts;
+                    float xv[16];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float4 q = on ? __ldcg(hv + pidx * 4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        xv[4 * i] = q.x;
+                        xv[4 * i + 1] = q.y;
+                        xv[4 * i + 2] = q.z;
+                        xv[4 * i + 3] = q.w;
+                    }
+                    digits_part<16>(xv, on, pidx, d1, d2, d3, sc);
+                }
             }
+            slot_group_sync(s, gthreads);
+            XUnit x;
+            if (active) load_xunit<QD>(x, hd1 + s * F, hd2 + s * F, hd3 + s * F, hsc + s * (F >> 5), ug);
+            if (!have_rows) {
+                if (ok) ok = mbar_wait(&full_d[0], 0, p.err, kErrWaitFull);
+                have_rows = true;
+                if (s == slot0) STYX_STAMP(12);
+            }
+            const uint8_t *src = src_d[s];
+            const uint8_t *base = dbuf + static_cast<size_t>(s) * p.dslot_stride +
+                                  (src ? (reinterpret_cast<uintptr_t>(src + static_cast<size_t>(dbeg) * p.rb_d) & 15) : 0);
+            // two rows per lane group per pass: independent dot products in flight
+            for (int t = sub * 2 * rpw; t < n; t += nwps * 2 * rpw) {
+                const int ra = t + grp, rb = t + rpw + grp;
+                float va = 0.f, vb = 0.f;
+                if (ok && src && active && ra < n) va = unit_dot<QD>(base + static_cast<size_t>(ra) * p.rb_d, ug, x);
+                if (ok && src && active && rb < n) vb = unit_dot<QD>(base + static_cast<size_t>(rb) * p.rb_d, ug, x);
+                for (int o = gs >> 1; o; o >>= 1) {
+                    va += __shfl_xor_sync(0xffffffffu, va, o);
+                    vb += __shfl_xor_sync(0xffffffffu, vb, o);
+                }
+                if (ug == 0 && ra < n) dpart[s * p.rc + ra] = va;
+                if (ug == 0 && rb < n) dpart[s * p.rc + rb] = vb;
+            }
+        }
+        __syncthreads();
+        STYX_STAMP(13);
+        if (ok && tid < n) {
+            float acc = 0.f;
+            for (int s = 0; s < k; s++) acc = __fadd_rn(acc, __fmul_rn(wts[s], dpart[s * p.rc + tid]));
+            p.x[dbeg + tid] = __fadd_rn(p.x[dbeg + tid], acc);
         }
     }
     STYX_STAMP(14);
