@@ -40,13 +40,6 @@
 
 namespace styx {
 
-// 1: the down rows are requested once the CTA's first gate/up chunk has
-// landed (gate/up bytes first, the down stream overlaps the gate/up work);
-// 0: every copy is requested at once
-#ifndef STYX_FUSED_DOWN_LATE
-#define STYX_FUSED_DOWN_LATE 0
-#endif
-
 constexpr int kFusedWarps = 16;
 constexpr int kFusedBlock = 32 * kFusedWarps;
 // shared-memory header: 32 mbarriers, reduction scratch, weights, ids,
@@ -453,11 +446,6 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
             }
         }
         STYX_STAMP(20);
-#if STYX_FUSED_DOWN_LATE
-        // the down rows are needed only after the grid-wide wait for h: let
-        // the gate/up bytes land first
-        if (n_chunks > 0) mbar_wait(&full_gu[0], 0, p.err, kErrWaitFull);
-#endif
         {   // the CTA's down rows of every slot, one chunk (rc >= dend - dbeg)
             const int n = dend - dbeg;
             uintptr_t a = 0;
