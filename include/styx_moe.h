@@ -87,8 +87,9 @@ int styx_check_device_error(styx_ctx *ctx, styx_stream stream);
 /* Options.  STYX_OPT_MOE_KERNELS selects how styx_moe_block runs: 0 = auto
  * (the single cooperative kernel when the shape and formats fit, else three
  * kernels), 1 = single kernel only (STYX_EUNSUPPORTED if it does not fit),
- * 2 = three kernels.  STYX_OPT_MOE_LAST_PATH (read only) = 1 or 2, the form
- * the last styx_moe_block call used.  STYX_OPT_TRACE = 1 makes the single
+ * 2 = three kernels.  STYX_OPT_MOE_LAST_PATH (read only) = 1 (single
+ * kernel), 2 (three kernels) or 3 (host-read form: some full tensor is in
+ * STYX_MEM_HOST memory), the form the last styx_moe_block call used.  STYX_OPT_TRACE = 1 makes the single
  * kernel record 32 clock64 stamps per CTA at its phase boundaries into the
  * workspace (styx_moe_workspace_view 4: int64[CTAs][32]). */
 #define STYX_OPT_MOE_KERNELS 1
@@ -215,8 +216,11 @@ int styx_gather_slabs_async(styx_ctx *ctx, styx_stream stream,
  *   arena + ids[32+s] * arena_slab_bytes  if ids[32+s] != SKIP
  *   full  + ids[48+s] * slab_bytes        otherwise
  * which is the three-way split of rec_matvec_id (moe.rs:1649-1700) in one
- * kernel.  `full` must be device memory for the fused kernels (cold slabs in
- * STYX_MEM_HOST go through styx_gather_slabs into the arena first).
+ * kernel.  `hot` and `arena` are device memory.  `full` is device memory, or
+ * STYX_MEM_HOST memory for the cold tier: styx_moe_block then reads those
+ * slabs in place over the host link (mul_mat_vec_id dispatches per source, as
+ * the reference reads its GTT tensors), and styx_gather_slabs[_async] can
+ * bring predicted cold slabs into the arena ahead of time.
  * Bases 16-byte aligned; slab_bytes and arena_slab_bytes multiples of 16.
  * n_hot / n_arena bound the hot indices and arena slots (full ids are
  * bounded by n_expert): an id out of range is skipped and reported through

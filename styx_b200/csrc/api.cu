@@ -123,7 +123,7 @@ constexpr size_t kTraceCtas = 256;   // phase stamps: styx::kTraceStamps per CTA
 // they guard).
 constexpr size_t kGenOffset = 128;
 struct WsLayout {
-    size_t counter, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, lgslot, trace, total;
+    size_t counter, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, d, lgslot, trace, total;
 };
 
 WsLayout ws_layout(const styx_moe_dims &d) {
@@ -144,8 +144,9 @@ WsLayout ws_layout(const styx_moe_dims &d) {
     L.logits = take(E * 4);
     L.weights = take(16 * 4);
     L.h = take(kF * 4);
-    L.g = take(kF * 4);   // unfused gate/up fallback
+    L.g = take(kF * 4);   // gate / up outputs of the mul_mat_vec_id forms
     L.u = take(kF * 4);
+    L.d = take(static_cast<size_t>(d.n_expert_used) * H * 4);   // down outputs of the host-read form
     L.lgslot = take(E * 8);
     L.trace = take(kTraceCtas * styx::kTraceStamps * 8);
     L.total = o;
@@ -182,12 +183,36 @@ int check_tensor(const styx_expert_tensor &t, const char *what, int nrows, int n
     NEED(al16(t.full) && al16(t.hot) && al16(t.arena), "%s: buffers must be 16-byte aligned", what);
     if (t.full) {
         cudaPointerAttributes pa{};
-        if (cudaPointerGetAttributes(&pa, t.full) == cudaSuccess)
+        if (cudaPointerGetAttributes(&pa, t.full) == cudaSuccess) {
+            // device memory, or pinned host memory mapped at the same address
+            // (the cold tier: read in place over the host link)
+            NEED(pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged ||
+                     (pa.type == cudaMemoryTypeHost && pa.devicePointer == t.full),
+                 "%s: full tensor must be device memory or STYX_MEM_HOST memory", what);
+        } else {
+            cudaGetLastError();
+        }
+    }
+    for (const void *b : {t.hot, t.arena}) {
+        cudaPointerAttributes pa{};
+        if (b && cudaPointerGetAttributes(&pa, b) == cudaSuccess)
             NEED(pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged,
-                 "%s: full tensor must be device memory for the fused kernels "
-                 "(gather host slabs into the arena first)", what);
+                 "%s: hot buffer and arena must be device memory", what);
+        else if (b)
+            cudaGetLastError();
     }
     return STYX_OK;
+}
+
+// full tensor held in pinned host memory (the cold tier)
+bool full_in_host(const styx_expert_tensor &t) {
+    if (!t.full) return false;
+    cudaPointerAttributes pa{};
+    if (cudaPointerGetAttributes(&pa, t.full) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return pa.type == cudaMemoryTypeHost;
 }
 
 styx::ExpSrc to_src(const styx_expert_tensor &t, int n_expert) {
@@ -691,6 +716,52 @@ int styx_moe_workspace_view(const styx_moe_dims *dims, void *workspace, int whic
     return STYX_OK;
 }
 
+// The MoE block when some expert tensor's full slabs are in pinned host
+// memory (the cold tier of MoeModel::load, moe.rs:856-870): every expert
+// matvec is a mul_mat_vec_id dispatch per source row (hot, arena, full), as
+// rec_matvec_id records them (moe.rs:1649-1700), reading the host slabs in
+// place over the host link with plain loads; then SiLU, the down matvec of
+// every slot and moe_reduce.  Slots without an expert keep zeros (weight 0).
+static int moe_block_host_read(styx_ctx *ctx, cudaStream_t st, const styx_moe_dims &d, const styx_moe_layer &lw,
+                               float *x, int32_t *ids64, float *wts, uint8_t *ws, const WsLayout &L) {
+    const int H = d.n_embd, F = d.n_ff, E = d.n_expert, k = d.n_expert_used;
+    styx::RouteArgs ra{};
+    ra.x = x;
+    ra.norm_w = lw.ffn_norm;
+    ra.eps = d.rms_eps;
+    ra.router = lw.router;
+    ra.E = E;
+    ra.H = H;
+    ra.k = k;
+    ra.renorm = d.norm_topk;
+    ra.remap = lw.remap;
+    ra.pmap = lw.pmap;
+    ra.xnorm = reinterpret_cast<float *>(ws + L.xnorm);
+    ra.xd1 = reinterpret_cast<int8_t *>(ws + L.xd1);
+    ra.xd2 = ws + L.xd2;
+    ra.xd3 = ws + L.xd3;
+    ra.xscale = reinterpret_cast<float *>(ws + L.xscale);
+    ra.logits = reinterpret_cast<float *>(ws + L.logits);
+    ra.weights = wts;
+    ra.ids64 = ids64;
+    ra.counter = reinterpret_cast<unsigned *>(ws + L.counter);
+    ra.err = ctx->d_err;
+    CK(styx::launch_route(ra, st));
+    float *g = reinterpret_cast<float *>(ws + L.g), *u = reinterpret_cast<float *>(ws + L.u);
+    float *h = reinterpret_cast<float *>(ws + L.h), *dd = reinterpret_cast<float *>(ws + L.d);
+    const size_t kF = static_cast<size_t>(k) * F;
+    CK(cudaMemsetAsync(g, 0, kF * 4, st));
+    CK(cudaMemsetAsync(u, 0, kF * 4, st));
+    CK(cudaMemsetAsync(dd, 0, static_cast<size_t>(k) * H * 4, st));
+    int rc;
+    if ((rc = matvec_id_3way(lw.gate, E, ids64, F, H, k, ra.xnorm, 1, g, ctx->d_err, st))) return rc;
+    if ((rc = matvec_id_3way(lw.up, E, ids64, F, H, k, ra.xnorm, 1, u, ctx->d_err, st))) return rc;
+    CK(styx::launch_swiglu(g, u, h, static_cast<int>(kF), st));
+    if ((rc = matvec_id_3way(lw.down, E, ids64, H, F, k, h, k, dd, ctx->d_err, st))) return rc;
+    CK(styx::launch_moe_reduce(dd, wts, x, H, k, st));
+    return STYX_OK;
+}
+
 // The three-kernel MoE block (route, gate/up + SiLU, down + combine).  With
 // `partial` the down kernel writes w[s]*d[s][r] per slot there instead of
 // updating x; `quiet` makes a missing full tensor mean "another device's
@@ -902,6 +973,12 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
     int32_t *ids64 = ids + static_cast<size_t>(layer) * STYX_IDS_PER_LAYER;
     float *wts = weights_out ? weights_out : reinterpret_cast<float *>(ws + L.weights);
     const cudaStream_t st = S(stream);
+
+    // experts read in place from pinned host memory: mul_mat_vec_id dispatches
+    if (full_in_host(lw->gate) || full_in_host(lw->up) || full_in_host(lw->down)) {
+        ctx->last_path = 3;
+        return moe_block_host_read(ctx, st, *dims, *lw, x, ids64, wts, ws, L);
+    }
 
     // the single cooperative kernel when the shape fits, else three kernels
     if (ctx->moe_kernels != 2) {
