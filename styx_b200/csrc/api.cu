@@ -883,7 +883,7 @@ static int moe_block_split(styx_ctx *ctx, cudaStream_t st, const styx_moe_dims &
 // it does not fit one CTA per SM (the caller then uses three kernels).
 static bool plan_fused(const styx_moe_dims &d, const styx_moe_layer &lw, int sms, styx::FusedArgs &a,
                        uint32_t &smem) {
-    const int H = d.n_embd, F = d.n_ff, E = d.n_expert, k = d.n_expert_used;
+    const int H = d.n_embd, F = d.n_ff, k = d.n_expert_used;
     const int qg = lw.gate.qtype, qd = lw.down.qtype;
     if (lw.up.qtype != qg || !styx::fused_supported(qg, qd)) return false;
     const int units_g = H / 64, units_d = F / 64;
@@ -897,13 +897,12 @@ static bool plan_fused(const styx_moe_dims &d, const styx_moe_layer &lw, int sms
     a.rb_g = static_cast<int>(row_bytes(qg, H));
     a.rb_u = static_cast<int>(row_bytes(lw.up.qtype, H));
     a.rb_d = static_cast<int>(row_bytes(qd, F));
-    // region A: x_norm, its digits, the logits; reused for h digits in the
-    // down phase
-    const size_t a_route = static_cast<size_t>(H) * 4 + 3 * static_cast<size_t>(H) + H / 32 * 4 +
-                           static_cast<size_t>(E) * 4;
+    // region A: x_norm and its digits, reused for h digits in the down phase;
+    // then the E logits (kept until the softmax after the gate/up phase)
+    const size_t a_route = static_cast<size_t>(H) * 4 + 3 * static_cast<size_t>(H) + H / 32 * 4;
     const size_t kF = static_cast<size_t>(k) * F;
     const size_t a_down = 3 * kF + kF / 32 * 4;
-    const size_t size_a = a128(std::max(a_route, a_down));
+    const size_t size_a = a128(std::max(a_route, a_down)) + a128(static_cast<size_t>(d.n_expert) * 4);
     // gate/up: about six chunks per CTA (each at most two slot segments of
     // gate rows and of up rows); every chunk of the CTA resident
     const int rpw_g = 32 / a.gs_g;
@@ -914,9 +913,7 @@ static bool plan_fused(const styx_moe_dims &d, const styx_moe_layer &lw, int sms
     if (chunks_g > 16 || a.ch > F) return false;
     a.gu_up_off = static_cast<uint32_t>(a16(static_cast<size_t>(a.ch) * a.rb_g + 96));
     a.gu_stride = a.gu_up_off + static_cast<uint32_t>(a16(static_cast<size_t>(a.ch) * a.rb_u + 96));
-    // (the top-k's per-warp rank counts use the same area before any copy)
-    const size_t gu_bytes = std::max(static_cast<size_t>(chunks_g) * a.gu_stride,
-                                     static_cast<size_t>(styx::fused_block_threads() / 32) * E * 4);
+    const size_t gu_bytes = static_cast<size_t>(chunks_g) * a.gu_stride;
     // down: all of the CTA's output rows, every slot, one chunk
     const int rows_d = (H + G - 1) / G;
     a.rc = rows_d;

@@ -74,23 +74,6 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 __device__ __forceinline__ uint32_t slot_tag(uint64_t w) { return static_cast<uint32_t>(w >> 32); }
 __device__ __forceinline__ float slot_val(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
 
-// re-read *p until it carries `tag`; bounded (~1 s), after which `ok` is
-// cleared, the error word set and the last word read returned
-__device__ __noinline__ uint64_t poll_slot(const uint64_t *p, uint32_t tag, uint64_t w, bool &ok, int *err) {
-    if (!ok) return w;
-    const long long t0 = clock64();
-    while (slot_tag(w) != tag) {
-        if (clock64() - t0 > kSpinCycles) {
-            if (err) atomicExch(err, kErrWaitRoute);
-            ok = false;
-            return w;
-        }
-        __nanosleep(128);
-        w = ld_slot(p);
-    }
-    return w;
-}
-
 __device__ __forceinline__ const uint8_t *fused_slot_src(const ExpSrc &t, int hot, int arena, int full) {
     if (hot >= 0)
         return (t.hot && static_cast<uint32_t>(hot) < t.nhot) ? t.hot + static_cast<uint64_t>(hot) * t.slab : nullptr;
@@ -102,6 +85,102 @@ __device__ __forceinline__ const uint8_t *fused_slot_src(const ExpSrc &t, int ho
                                                                   : nullptr;
     return nullptr;
 }
+
+// logits a lane of warp 0 holds: up to STYX_MAX_EXPERTS / 32
+constexpr int kLogitRegs = STYX_MAX_EXPERTS / 32;
+
+// Order-preserving key of a float that is > -inf (NaN excluded by the
+// caller): larger float -> larger key, never 0; -0 is folded into +0, which
+// the comparison treats as equal.
+__device__ __forceinline__ uint32_t order_key(float f) {
+    const uint32_t u = __float_as_uint(f + 0.0f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k ^ 0x80000000u) : ~k);
+}
+
+// Selection as topk_softmax_f32.comp:39-46: k times the largest untaken
+// logit by strict '>', the lowest index among equals, never -inf or NaN.
+// Lane l holds the keys of elements l + 32 j, j < NP (0 = not eligible); each
+// pick is a warp max over keys, then a warp min over the indices holding
+// that key.  A lane's candidates have increasing indices, so its first
+// maximal register is its lowest such index.  Lane s < k receives pick s
+// (e = -1, ke = 0 when fewer than k logits are eligible).
+template <int NP>
+__device__ __forceinline__ void warp_pick(uint32_t *key, int k, int lane, int &e, uint32_t &ke) {
+    for (int s = 0; s < k; s++) {
+        uint32_t bk = key[0];
+        int bj = 0;
+#pragma unroll
+        for (int j = 1; j < NP; j++)
+            if (key[j] > bk) {
+                bk = key[j];
+                bj = j;
+            }
+        const uint32_t K = __reduce_max_sync(0xffffffffu, bk);
+        if (K == 0) break;   // the remaining slots stay empty
+        const uint32_t mine = (bk == K) ? static_cast<uint32_t>(lane + 32 * bj) : 0xffffffffu;
+        const uint32_t I = __reduce_min_sync(0xffffffffu, mine);
+        if (mine == I) {
+#pragma unroll
+            for (int j = 0; j < NP; j++)
+                if (j == bj) key[j] = 0u;
+        }
+        if (lane == s) {
+            e = static_cast<int>(I);
+            ke = K;
+        }
+    }
+}
+
+// The same selection for at most 4 keys per lane (E <= 128): each lane first
+// orders its own (key, index) pairs, key descending and index ascending among
+// equal keys, so its candidate for every pick is its head and a pick costs
+// two reductions and a shift on the winning lane.
+__device__ __forceinline__ void cx_desc(uint32_t &ka, int &ia, uint32_t &kb, int &ib) {
+    if (kb > ka || (kb == ka && ib < ia)) {
+        const uint32_t tk = ka;
+        ka = kb;
+        kb = tk;
+        const int ti = ia;
+        ia = ib;
+        ib = ti;
+    }
+}
+__device__ __forceinline__ void warp_pick_sorted4(const uint32_t *key, int k, int lane, int &e, uint32_t &ke) {
+    uint32_t k0 = key[0], k1 = key[1], k2 = key[2], k3 = key[3];
+    int i0 = lane, i1 = lane + 32, i2 = lane + 64, i3 = lane + 96;
+    cx_desc(k0, i0, k1, i1);
+    cx_desc(k2, i2, k3, i3);
+    cx_desc(k0, i0, k2, i2);
+    cx_desc(k1, i1, k3, i3);
+    cx_desc(k1, i1, k2, i2);
+    for (int s = 0; s < k; s++) {
+        const uint32_t K = __reduce_max_sync(0xffffffffu, k0);
+        if (K == 0) break;   // the remaining slots stay empty
+        const uint32_t mine = k0 == K ? static_cast<uint32_t>(i0) : 0xffffffffu;
+        const uint32_t I = __reduce_min_sync(0xffffffffu, mine);
+        if (mine == I) {
+            k0 = k1;
+            i0 = i1;
+            k1 = k2;
+            i1 = i2;
+            k2 = k3;
+            i2 = i3;
+            k3 = 0u;
+        }
+        if (lane == s) {
+            e = static_cast<int>(I);
+            ke = K;
+        }
+    }
+}
+
+// Named barriers: 0 is __syncthreads, 1 + s the warps of slot s in the down
+// phase (s < 8 when a slot has more than one warp), kBarWarp0 warp 0 alone.
+constexpr int kBarWarp0 = 15;
+__device__ __forceinline__ void warp_converge(int id) { asm volatile("bar.sync %0, 32;" ::"r"(id) : "memory"); }
 
 // barrier among the nthreads threads (whole warps) that work on slot s:
 // named barrier 1 + s (0 is __syncthreads), or the warp itself
@@ -133,7 +212,16 @@ __device__ __forceinline__ float2 fblock_sum2(float2 v, float *red) {
     return make_float2(__shfl_sync(0xffffffffu, a, 0), __shfl_sync(0xffffffffu, c, 0));
 }
 
-// block-wide deterministic sum (fixed tree over the 16 warps)
+// sum(r * w * x) over one float4, with one fixed sequence of roundings
+__device__ __forceinline__ float rwx4(float4 r, float4 w, float4 x) {
+    float a = __fmul_rn(__fmul_rn(r.x, w.x), x.x);
+    a = __fmaf_rn(__fmul_rn(r.y, w.y), x.y, a);
+    a = __fmaf_rn(__fmul_rn(r.z, w.z), x.z, a);
+    return __fmaf_rn(__fmul_rn(r.w, w.w), x.w, a);
+}
+
+// block-wide deterministic sum (fixed tree over the 16 warps; the same tree
+// as fblock_sum2's second component)
 __device__ __forceinline__ float fblock_sum(float v, float *red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -189,25 +277,24 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
     uint64_t *full_gu = bar, *full_d = bar + 16;
     float *red = reinterpret_cast<float *>(smem + kHdrRed);  // 32 floats
     float *wts = red + 32;                                    // 16 floats
-    int *sel = reinterpret_cast<int *>(wts + 16);             // 16 ints
-    int *s_flag = sel + 16;                                   // 16 ints
+    int *s_flag = reinterpret_cast<int *>(wts + 32);          // 16 ints (after 16 spare)
     const uint8_t **src_g = reinterpret_cast<const uint8_t **>(smem + kHdrSrc);   // 16 pointers each
     const uint8_t **src_u = src_g + 16;
     const uint8_t **src_d = src_u + 16;
     const int H = p.H, F = p.F, k = p.k, E = p.E;
-    uint8_t *region_a = smem + p.off_a;                       // x_norm, its digits, the logits
+    uint8_t *region_a = smem + p.off_a;                       // x_norm and its digits
     float *xn = reinterpret_cast<float *>(region_a);
     int8_t *xd1 = reinterpret_cast<int8_t *>(xn + H);
     uint8_t *xd2 = reinterpret_cast<uint8_t *>(xd1) + H;
     uint8_t *xd3 = xd2 + H;
     float *xsc = reinterpret_cast<float *>(xd3 + H);
-    float *lg = xsc + (H >> 5);
     const int kF = k * F;                                     // phase 4: h digits in region A
     int8_t *hd1 = reinterpret_cast<int8_t *>(region_a);
     uint8_t *hd2 = reinterpret_cast<uint8_t *>(hd1) + kF;
     uint8_t *hd3 = hd2 + kF;
     float *hsc = reinterpret_cast<float *>(hd3 + kF);
     float *dpart = reinterpret_cast<float *>(smem + p.off_part);
+    float *lgs = dpart - ((E + 31) & ~31);                    // the logits, at the end of region A
     uint8_t *gubuf = smem + p.off_ring;
     uint8_t *dbuf = smem + p.off_down;
 
@@ -263,13 +350,19 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
     }
     // one block reduction for both sum(x^2) and the first router row's
     // sum(r * w * x): logit = scale * sum(r * w * x) with scale the RMSNorm
-    // factor (the same value as sum(r * x_norm) up to rounding order)
+    // factor (the same value as sum(r * x_norm) up to rounding order).  Every
+    // router row goes through the same roundings, so equal rows give equal
+    // logits and the top-k's index order decides between them.
     float ss = 0.f, rd = 0.f;
+    float4 xr = npre;   // this thread's float4 of raw x (one-float4 case)
     for (int i = tid; i < H4; i += kFusedBlock) {
         const float4 v = __ldcg(x4 + i);
         xn4[i] = v;   // raw x for now
         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        if (one) rd += rpre.x * npre.x * v.x + rpre.y * npre.y * v.y + rpre.z * npre.z * v.z + rpre.w * npre.w * v.w;
+        if (one) {
+            xr = v;
+            rd = rwx4(rpre, npre, v);
+        }
     }
     const float2 red2 = fblock_sum2(make_float2(ss, rd), red);   // (its barriers also publish the mbarrier inits)
     ss = red2.x;
@@ -292,11 +385,16 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
     for (int j = one ? 1 : 0; j < n_rows_mine; j++) {   // further router rows (E > grid, or H > 2048)
         float acc = 0.f;
         const float4 *r4 = reinterpret_cast<const float4 *>(p.router + static_cast<size_t>(b + G * j) * H);
-        for (int i = tid; i < H4; i += kFusedBlock) {
-            const float4 r = __ldg(r4 + i), v = xn4[i];
-            acc += r.x * v.x + r.y * v.y + r.z * v.z + r.w * v.w;
+        if (one) {   // the first row's form and reduction tree
+            if (tid < H4) acc = rwx4(__ldg(r4 + tid), npre, xr);
+            acc = scale * fblock_sum(acc, red);
+        } else {
+            for (int i = tid; i < H4; i += kFusedBlock) {
+                const float4 r = __ldg(r4 + i), v = xn4[i];
+                acc += r.x * v.x + r.y * v.y + r.z * v.z + r.w * v.w;
+            }
+            acc = fblock_sum(acc, red);
         }
-        acc = fblock_sum(acc, red);
         if (tid == 0) {
             st_slot(p.lgslot + b + G * j, acc, *s_tag);
             p.logits[b + G * j] = acc;   // debug view
@@ -307,106 +405,99 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
     STYX_STAMP(3);
     STYX_STAMP(4);
 
-    // ------------------------------------------------ phase 2: top-k
-    if (warp == 0) {   // one warp per CTA polls: L2 stays free for the stores it waits for
-        bool ok = true;
-        for (int i = lane; i < E; i += 32) {
-            uint64_t w = ld_slot(p.lgslot + i);
-            if (slot_tag(w) != tag) w = poll_slot(p.lgslot + i, tag, w, ok, p.err);
-            lg[i] = slot_val(w);
-        }
-    }
-    if (tid < 16) sel[tid] = -1;
-    __syncthreads();
-    STYX_STAMP(5);
-    float mx = -INFINITY, sum = 0.f;
-    if (warp == 0) {
-        // softmax statistics (lane-strided partials, fixed shuffle tree);
-        // only warp 0 needs them, for the weights
-#pragma unroll 4
-        for (int i = lane; i < E; i += 32) mx = fmaxf(mx, lg[i]);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-#pragma unroll 4
-        for (int i = lane; i < E; i += 32) sum += expf(lg[i] - mx);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        STYX_STAMP(16);
-    } else {
-        // rank of every finite logit (strict '>' first, equal values ordered
-        // by index): the serial scan's s-th pick is the element of rank s.
-        // Warps 1..15 each count over a stretch of j for every candidate
-        // (every shared load a broadcast); partial counts go to the gate/up
-        // area, which no copy has touched yet.
-        int *rpart = reinterpret_cast<int *>(gubuf);
-        const int w = warp - 1, nw = kFusedWarps - 1;
-        const int js = (E + nw - 1) / nw, ja = w * js, jb = min(E, ja + js);
-        for (int cb = 0; cb < E; cb += 128) {
-            const int c0 = cb + 4 * lane;
-            float mv[4];
-#pragma unroll
-            for (int q = 0; q < 4; q++) mv[q] = c0 + q < E ? lg[c0 + q] : 0.f;
-            int cnt[4] = {0, 0, 0, 0};
-#pragma unroll 4
-            for (int j = ja; j < jb; j++) {
-                const float u = lg[j];
-#pragma unroll
-                for (int q = 0; q < 4; q++) cnt[q] += (u > mv[q]) | ((u == mv[q]) & (j < c0 + q));
-            }
-#pragma unroll
-            for (int q = 0; q < 4; q++)
-                if (c0 + q < E) rpart[w * E + c0 + q] = cnt[q];
-        }
-        STYX_STAMP_T(32, 17);
+    // ------------------------------------------------ phase 2: x_norm digits
+    // Every CTA keeps its own digits of x_norm for the gate/up dots; all
+    // warps build them while the logits travel between CTAs.  (Warp 0 runs
+    // the top-k alone afterwards: with other warps still busy on the SM its
+    // shuffles and reductions were several times slower.)
+    {
+        const DigitsView dv{xd1, xd2, xd3, xsc};
+        for (int g = warp; g < (H >> 5); g += kFusedWarps) digits_group_warp(xn[g * 32 + lane], lane, dv, g);
+        if (b == 0)   // test / debug view of x_norm
+            for (int i = tid; i < H; i += kFusedBlock) p.xnorm[i] = xn[i];
     }
     __syncthreads();
-    STYX_STAMP(18);
-    for (int c = tid; c < E; c += kFusedBlock) {
-        const int *rpart = reinterpret_cast<const int *>(gubuf);
-        int rank = 0;
-        for (int w = 0; w < kFusedWarps - 1; w++) rank += rpart[w * E + c];
-        if (lg[c] > -INFINITY && rank < k) sel[rank] = c;
-    }
-    __syncthreads();
-    STYX_STAMP(6);
+    STYX_STAMP(22);
 
-    // ------------------------------------------------ phase 3: gate/up + SiLU
+    // ------------------------------------------------ phase 3: top-k (warp 0)
+    // Warp 0 gathers the E logits into registers (element i on lane i % 32,
+    // register i / 32), picks the k winners with warp reductions, resolves
+    // their slabs and issues the copies; the softmax weights are computed
+    // once the copies are in flight.
     if (warp == 0) {
-        // lane s < k: slot s's weight, id rows and slab sources
-        const int s = lane;
-        float w = 0.f;
-        int e = -1;
-        if (s < k) {
-            e = sel[s];
-            const float best = e >= 0 ? lg[e] : -INFINITY;
-            w = expf(best - mx) / sum;
+        const int nper = (E + 31) >> 5;
+        float lv[kLogitRegs];
+        // The whole warp polls in step (no lane ever waits alone, so the
+        // warp stays converged for the reductions that follow): each pass
+        // re-reads the words still missing their tag; bounded (~1 s).
+        uint32_t need = 0;   // bit j: word lane + 32 j not yet read with this launch's tag
+#pragma unroll
+        for (int j = 0; j < kLogitRegs; j++) {
+            lv[j] = -INFINITY;
+            if (j < nper && lane + 32 * j < E) need |= 1u << j;
         }
-        float wsum = 0.f;   // slot order, as topk_softmax_f32.comp:50
-        for (int t = 0; t < k; t++) wsum += __shfl_sync(0xffffffffu, w, t);
-        if (s < k) {
-            const float wr = p.renorm ? w / wsum : w;
-            wts[s] = wr;
+        const long long t0 = clock64();
+        for (;;) {
+            // every word of the lane is re-read each pass, all reads in
+            // flight at once, with no lane-dependent branch
+            uint64_t w[kLogitRegs];
+#pragma unroll
+            for (int j = 0; j < kLogitRegs; j++)
+                if (j < nper) w[j] = ld_slot(p.lgslot + min(lane + 32 * j, E - 1));
+#pragma unroll
+            for (int j = 0; j < kLogitRegs; j++)
+                if (j < nper) {
+                    const bool got = (need >> j & 1u) && slot_tag(w[j]) == tag;
+                    lv[j] = got ? slot_val(w[j]) : lv[j];
+                    need = got ? need & ~(1u << j) : need;
+                }
+            if (!__any_sync(0xffffffffu, need != 0)) break;
+            // lane 0's clock decides for the warp: lanes need not read the
+            // clock together, and a lane leaving alone would leave the others
+            // in a warp-wide vote it never joins
+            if (__shfl_sync(0xffffffffu, static_cast<int>(clock64() - t0 > kSpinCycles), 0)) {
+                if (lane == 0) atomicExch(p.err, kErrWaitRoute);
+                break;
+            }
+            __nanosleep(64);
+        }
+        // bring the warp back together before the reductions: after the
+        // poll the lanes can run as separate groups, and every full-warp
+        // shuffle or reduction then pays for regrouping them (measured at
+        // several times its cost); a 32-thread named barrier reconverges it
+        warp_converge(kBarWarp0);
+        STYX_STAMP(5);
+        uint32_t key[kLogitRegs];
+#pragma unroll
+        for (int j = 0; j < kLogitRegs; j++) key[j] = lv[j] > -INFINITY ? order_key(lv[j]) : 0u;
+        int e = -1;            // lane s < k: the expert of slot s
+        uint32_t ke = 0;       // and its key
+        if (nper <= 4) warp_pick_sorted4(key, k, lane, e, ke);
+        else warp_pick<kLogitRegs>(key, k, lane, e, ke);
+        STYX_STAMP(17);
+        // lane s < k: slot s's slab sources and id rows
+        int hi = -1, ai = -1, fi = -1;
+        if (lane < k) {
             const uint32_t hot = (e >= 0 && p.remap) ? p.remap[e] : kSkip;
-            int hi = -1, ai = -1, fi = -1;
             if (hot != kSkip) {
                 hi = static_cast<int>(hot);
             } else {
-                const uint32_t a = (e >= 0 && p.pmap) ? p.pmap[e] : kSkip;
-                if (a != kSkip) ai = static_cast<int>(a);
+                const uint32_t am = (e >= 0 && p.pmap) ? p.pmap[e] : kSkip;
+                if (am != kSkip) ai = static_cast<int>(am);
                 else fi = e;
             }
-            src_g[s] = fused_slot_src(p.gate, hi, ai, fi);
-            src_u[s] = fused_slot_src(p.up, hi, ai, fi);
-            src_d[s] = fused_slot_src(p.down, hi, ai, fi);
+            src_g[lane] = fused_slot_src(p.gate, hi, ai, fi);
+            src_u[lane] = fused_slot_src(p.up, hi, ai, fi);
+            src_d[lane] = fused_slot_src(p.down, hi, ai, fi);
             if (b == 0) {
-                if (e >= 0 && (!src_g[s] || !src_u[s] || !src_d[s])) atomicExch(p.err, kErrBadId);
-                p.weights[s] = wr;
-                p.ids64[s] = e;
-                p.ids64[16 + s] = hi;
-                p.ids64[32 + s] = ai;
-                p.ids64[48 + s] = fi;
+                if (e >= 0 && (!src_g[lane] || !src_u[lane] || !src_d[lane])) atomicExch(p.err, kErrBadId);
+                p.ids64[lane] = e;
+                p.ids64[16 + lane] = hi;
+                p.ids64[32 + lane] = ai;
+                p.ids64[48 + lane] = fi;
             }
         }
+        const int s = lane;
         __syncwarp();   // sources visible to every lane before the arrives that publish them
         STYX_STAMP(19);
         // ---- every expert byte this CTA needs: gate/up chunk c on lane c
@@ -453,6 +544,7 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
             if (s < k && src_d[s] && n > 0)
                 cover16(src_d[s] + static_cast<size_t>(dbeg) * p.rb_d, static_cast<size_t>(n) * p.rb_d, a, len);
             uint32_t total = len;
+            warp_converge(kBarWarp0);   // after the per-chunk issue branches
 #pragma unroll
             for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
             if (lane == 0) {
@@ -465,14 +557,12 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
                          &full_d[0]);
         }
         STYX_STAMP(21);
-    } else {
-        // x_norm digits (every CTA keeps its own copy for the gate/up dots),
-        // computed while warp 0 issues the copies and the bytes are in flight
-        const DigitsView dv{xd1, xd2, xd3, xsc};
-        for (int g = warp - 1; g < (H >> 5); g += kFusedWarps - 1) digits_group_warp(xn[g * 32 + lane], lane, dv, g);
-        if (b == 0)   // test / debug view of x_norm
-            for (int i = tid - 32; i < H; i += kFusedBlock - 32) p.xnorm[i] = xn[i];
-        STYX_STAMP_T(32, 22);
+        // the logits and the picked ones stay in shared memory for the
+        // softmax weights, computed after the gate/up phase (off this path)
+#pragma unroll
+        for (int j = 0; j < kLogitRegs; j++)
+            if (j < nper && lane + 32 * j < E) lgs[lane + 32 * j] = lv[j];
+        if (lane < k) wts[lane] = ke ? key_value(ke) : -INFINITY;
     }
     __syncthreads();
     STYX_STAMP(7);
@@ -520,6 +610,7 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
                 STYX_STAMP_T(32, 8);
                 first = false;
             }
+            __syncwarp();   // regroup the lanes after the waits and branches above
             for (int o = gs >> 1; o; o >>= 1) {
                 g += __shfl_xor_sync(0xffffffffu, g, o);
                 u += __shfl_xor_sync(0xffffffffu, u, o);
@@ -540,6 +631,26 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
             const int s = r / F, e = min(gend, (s + 1) * F);
             atomicAdd(p.hcount + s, static_cast<unsigned long long>(e - r));
             r = e;
+        }
+    }
+    if (warp == 1) {
+        // softmax statistics over all E logits (lane-strided partials, fixed
+        // shuffle tree) and the weights in slot order
+        // (topk_softmax_f32.comp:47-52); wts[s] holds slot s's logit until here
+        float mx = -INFINITY, sum = 0.f;
+        for (int i = lane; i < E; i += 32) mx = fmaxf(mx, lgs[i]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (int i = lane; i < E; i += 32) sum += expf(lgs[i] - mx);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const float w = lane < k ? expf(wts[lane] - mx) / sum : 0.f;
+        float wsum = 0.f;
+        for (int t = 0; t < k; t++) wsum += __shfl_sync(0xffffffffu, w, t);
+        if (lane < k) {
+            const float wr = p.renorm ? w / wsum : w;
+            wts[lane] = wr;
+            if (b == 0) p.weights[lane] = wr;
         }
     }
     STYX_STAMP(10);
@@ -612,6 +723,7 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
                 float va = 0.f, vb = 0.f;
                 if (ok && src && active && ra < n) va = unit_dot<QD>(base + static_cast<size_t>(ra) * p.rb_d, ug, x);
                 if (ok && src && active && rb < n) vb = unit_dot<QD>(base + static_cast<size_t>(rb) * p.rb_d, ug, x);
+                __syncwarp();   // regroup the lanes after the branches above
                 for (int o = gs >> 1; o; o >>= 1) {
                     va += __shfl_xor_sync(0xffffffffu, va, o);
                     vb += __shfl_xor_sync(0xffffffffu, vb, o);

@@ -339,6 +339,32 @@ def test_moe_block_placement_is_invariant(mode):
     assert np.array_equal(x_pl.view(np.uint32), x_full.view(np.uint32))
 
 
+@pytest.mark.parametrize("mode", [_lib.MOE_AUTO, _lib.MOE_SPLIT], ids=["auto", "split"])
+@pytest.mark.parametrize("H,F,E,top,second", [
+    (1024, 512, 32, [29, 3, 17, 4], [30, 11]),
+    (256, 256, 512, [300, 7, 511, 149], [450, 148]),   # E > SM count: several router rows per CTA
+], ids=["E32", "E512"])
+def test_moe_block_routing_ties(mode, H, F, E, top, second):
+    """Exactly equal logits (duplicated router rows) are taken lowest index
+    first, as the reference's serial scan with strict '>' does
+    (topk_softmax_f32.comp:39-46); the single-kernel block picks on one warp
+    with reductions, the three-kernel block with the standalone top-k."""
+    c = make_case(31, H, F, E, 8, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K))
+    xn = O.rms_norm(c.x, c.norm, c.eps)
+    base = (0.05 * np.sign(xn)).astype(np.float32)
+    c.router[top] = base
+    c.router[second] = 0.5 * base
+    ref = oracle_block(c)
+    assert list(ref["ids64"][:6]) == sorted(top) + sorted(second)
+    blk, x, ids, w = _run_block(c, _upload_layer(c), mode=mode)
+    assert blk.path == (1 if mode == _lib.MOE_AUTO else 2)
+    logits = blk.view(1, E).cpu().numpy()
+    assert np.all(logits[top] == logits[top[0]]) and np.all(logits[second] == logits[second[0]])
+    assert np.array_equal(id_rows(ids, c.k), id_rows(ref["ids64"], c.k))
+    np.testing.assert_allclose(w, ref["weights"], rtol=1e-5, atol=1e-7)
+    assert rel_to_max(x, ref["x"]) < 1e-3
+
+
 def test_moe_block_full_size_cfg2_spot_check():
     """All 128 experts of a 30B-A3B-shaped layer generated on the device;
     the selected slabs are brought back and the oracle recomputes the block."""
