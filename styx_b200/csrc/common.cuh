@@ -198,18 +198,24 @@ __device__ __forceinline__ float digits_scale(float a, float &inv) {
     return __uint_as_float(static_cast<uint32_t>(se) << 23);
 }
 
-// the three digits of one element (q = v * (1/s), exact for a power-of-two s)
+// the three digits of one element (q = v * (1/s), exact for a power-of-two s).
+// floor and round-to-nearest-even of values below 2^22 in magnitude come from
+// one add of 1.5 * 2^23 with the matching rounding mode: the sum's unit is 1,
+// so its low mantissa bits are the integer (no float-to-int conversion).
 __device__ __forceinline__ void digits_of(float v, float inv, int &d1, int &d2, int &d3) {
-    const float q = v * inv;
-    const float f1 = floorf(q);
-    const float r1 = (q - f1) * 256.f;     // exact
-    const float f2 = floorf(r1);
-    const float r2 = (r1 - f2) * 256.f;
-    float f3 = rintf(r2);
-    if (f3 > 255.f) f3 = 255.f;
-    d1 = static_cast<int>(f1);
-    d2 = static_cast<int>(f2);
-    d3 = static_cast<int>(f3);
+    constexpr float kM = 12582912.0f;      // 1.5 * 2^23
+    constexpr int kMi = 0x4B400000;        // its bit pattern
+    const float q = v * inv;               // |q| < 64
+    const float t1 = __fadd_rd(q, kM);     // kM + floor(q)
+    const float f1 = t1 - kM;
+    const float r1 = (q - f1) * 256.f;     // exact, in [0, 256)
+    const float t2 = __fadd_rd(r1, kM);
+    const float f2 = t2 - kM;
+    const float r2 = (r1 - f2) * 256.f;    // in [0, 256)
+    const float t3 = __fadd_rn(r2, kM);    // kM + rint(r2), ties to even
+    d1 = __float_as_int(t1) - kMi;
+    d2 = __float_as_int(t2) - kMi;
+    d3 = min(__float_as_int(t3) - kMi, 255);
 }
 
 // one 32-element group, one element per lane of a full warp
