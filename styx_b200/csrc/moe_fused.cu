@@ -315,11 +315,9 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
 #define STYX_STAMP(i_) STYX_STAMP_T(0, i_)
     STYX_STAMP(0);
     // ------------------------------------------------ phase 0
-    if (tid == 0) {
-        for (int i = 0; i < 16; i++) {
-            mbar_init(&full_gu[i], 1);
-            mbar_init(&full_d[i], 1);
-        }
+    if (tid < 16) {   // one thread per barrier: the gate/up chunks', and the down rows'
+        mbar_init(&full_gu[tid], 1);
+        if (tid == 0) mbar_init(&full_d[0], 1);
         fence_mbar_init();
     }
     pdl_trigger();
@@ -459,7 +457,6 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
                 if (lane == 0) atomicExch(p.err, kErrWaitRoute);
                 break;
             }
-            __nanosleep(64);
         }
         // bring the warp back together before the reductions: after the
         // poll the lanes can run as separate groups, and every full-warp
@@ -681,7 +678,6 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
                         atomicExch(p.err, kErrWaitRoute);
                         break;
                     }
-                    __nanosleep(32);
                 }
             }
             slot_group_sync(s, gthreads);
