@@ -177,6 +177,11 @@ __device__ __forceinline__ void warp_pick_sorted4(const uint32_t *key, int k, in
     }
 }
 
+// Cross-CTA polls spin without pausing for this long (a normal wait ends
+// well within it), then pause between reads so that a wait that runs out
+// does not load L2 for its whole second.
+constexpr long long kPollFreeCycles = 100000;
+
 // Named barriers: 0 is __syncthreads, 1 + s the warps of slot s in the down
 // phase (s < 8 when a slot has more than one warp), kBarWarp0 warp 0 alone.
 constexpr int kBarWarp0 = 15;
@@ -453,10 +458,12 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
             // lane 0's clock decides for the warp: lanes need not read the
             // clock together, and a lane leaving alone would leave the others
             // in a warp-wide vote it never joins
-            if (__shfl_sync(0xffffffffu, static_cast<int>(clock64() - t0 > kSpinCycles), 0)) {
+            const long long dt = __shfl_sync(0xffffffffu, clock64() - t0, 0);
+            if (dt > kSpinCycles) {
                 if (lane == 0) atomicExch(p.err, kErrWaitRoute);
                 break;
             }
+            if (dt > kPollFreeCycles) __nanosleep(256);
         }
         // bring the warp back together before the reductions: after the
         // poll the lanes can run as separate groups, and every full-warp
@@ -674,10 +681,12 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
             if (gt == 0) {
                 const long long t0 = clock64();
                 while (ld_acquire_u64(p.hcount + s) < htarget) {
-                    if (clock64() - t0 > kSpinCycles) {
+                    const long long dt = clock64() - t0;
+                    if (dt > kSpinCycles) {
                         atomicExch(p.err, kErrWaitRoute);
                         break;
                     }
+                    if (dt > kPollFreeCycles) __nanosleep(256);
                 }
             }
             slot_group_sync(s, gthreads);
@@ -737,6 +746,14 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
         }
     }
     STYX_STAMP(14);
+    // No CTA leaves with copies in flight into its shared memory, even after
+    // a wait above gave up: thread 0 waits (bounded) for every barrier its
+    // copies complete on (already complete on the normal path).
+    if (tid == 0) {
+        bool fine = true;
+        for (int c = 0; c < n_chunks && fine; c++) fine = mbar_wait(&full_gu[c], 0, p.err, kErrWaitFull);
+        if (fine) mbar_wait(&full_d[0], 0, p.err, kErrWaitFull);
+    }
 #undef STYX_STAMP
 #undef STYX_STAMP_T
 }
