@@ -10,21 +10,20 @@
 //      for the previous grid;
 //   1  RMSNorm of x (every CTA, same fixed order -> identical x_norm), the
 //      router dot products of its rows -> tagged logit slots;
-//   2  read all E logit slots (polling each until it carries this launch's
-//      tag, bounded); top-k in rank form (topk_softmax_f32.comp), warps 1-15
-//      counting, warp 0 the softmax statistics: every CTA computes the same
-//      ids;
-//   3  warp 0 resolves the k slots (weights, id rows, slab sources; CTA 0
-//      publishes them) and issues the CTA's gate/up chunks (one lane per
-//      chunk) and down rows (one lane per slot) while warps 1-15 turn x_norm
-//      into dp4a digits; all warps then run the gate/up dot products as
-//      chunks land (the chunk's mbarrier also publishes the slot sources),
-//      SiLU(g)*u -> h (global);
+//   2  all warps turn x_norm into dp4a digits; warp 0 reads all E logit
+//      slots (polling until each carries this launch's tag, bounded) and
+//      picks the top-k in registers with warp reductions (the selection of
+//      topk_softmax_f32.comp): every CTA computes the same ids;
+//   3  warp 0 resolves the k slots (id rows, slab sources; CTA 0 publishes
+//      the ids) and issues the CTA's gate/up chunks (one lane per chunk) and
+//      down rows (one lane per slot); all warps then run the gate/up dot
+//      products as chunks land (the chunk's mbarrier also publishes the slot
+//      sources), SiLU(g)*u -> h (global);
 //   4  each CTA counts its h rows into per-slot arrival counters (one fence);
-//      the warps of slot s wait for slot s alone, turn h[s] into digits in
-//      shared memory and run the CTA's down rows for slot s from the
-//      prefetched rows; slot-ordered combine x[r] += sum_s w[s] d[s][r]
-//      (moe_reduce_f32.comp).
+//      warp 1 computes the softmax weights; the warps of slot s wait for
+//      slot s alone, turn h[s] into digits in shared memory and run the
+//      CTA's down rows for slot s from the prefetched rows; slot-ordered
+//      combine x[r] += sum_s w[s] d[s][r] (moe_reduce_f32.comp).
 // Logits go through tagged exchange words: one 64-bit {value bits, tag}
 // word written and read with single 64-bit relaxed accesses, so a reader
 // that sees this launch's tag also sees its value, with no fence or counter.
