@@ -1,4 +1,5 @@
-"""ctypes binding of libstyx_moe.so (include/styx_moe.h, include/styx_residency.h).
+"""ctypes binding of libstyx_moe.so (include/styx_moe.h, include/styx_residency.h,
+include/styx_gguf.h).
 
 There is no fallback: if the library is missing, importing the ops raises.
 """
@@ -12,9 +13,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libstyx_moe.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 HEADER = os.path.join(INCLUDE, "styx_moe.h")
-HEADERS = [HEADER, os.path.join(INCLUDE, "styx_residency.h")]
+HEADERS = [HEADER, os.path.join(INCLUDE, "styx_residency.h"), os.path.join(INCLUDE, "styx_gguf.h")]
 
 STYX_OK, STYX_EINVAL, STYX_ECUDA, STYX_ENOMEM, STYX_ETIMEOUT, STYX_EUNSUPPORTED = 0, -1, -2, -3, -4, -5
+STYX_EIO, STYX_EEOF, STYX_EDATA = -6, -7, -8
 F32, Q8_0, Q4_K, Q5_K, Q6_K = 0, 8, 12, 13, 14
 QTYPES = {"q8_0": Q8_0, "q4_K": Q4_K, "q5_K": Q5_K, "q6_K": Q6_K}
 BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
@@ -29,6 +31,11 @@ class StyxError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"styx error {code}: {msg}")
         self.code = code
+
+
+class GgufTensorInfo(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("n_dims", C.c_uint32), ("dims", C.POINTER(C.c_uint64)),
+                ("ggml_type", C.c_uint32), ("offset", C.c_uint64), ("size_bytes", C.c_uint64)]
 
 
 class ExpertTensor(C.Structure):
@@ -111,6 +118,30 @@ _SIGS = {
     "styx_residency_maybe_repin": (_i, [_vp, _vp, _u64, _u64, _i, C.POINTER(RepinSwap), _i, C.POINTER(_i)]),
     "styx_residency_hot_cold": (_i, [_vp, _vp, _vp, _vp]),
     "styx_residency_prefetch_plan": (_i, [_vp, _vp, _vp, _vp]),
+    # include/styx_gguf.h
+    "styx_gguf_open": (_i, [C.c_char_p, C.POINTER(_vp)]),
+    "styx_gguf_open_memory": (_i, [_vp, _u64, C.POINTER(_vp)]),
+    "styx_gguf_close": (None, [_vp]),
+    "styx_gguf_version": (C.c_uint32, [_vp]),
+    "styx_gguf_data_start": (_u64, [_vp]),
+    "styx_gguf_file_bytes": (_u64, [_vp]),
+    "styx_gguf_kv_count": (_u64, [_vp]),
+    "styx_gguf_kv_key": (_i, [_vp, _u64, C.POINTER(C.c_char_p)]),
+    "styx_gguf_kv_value": (_i, [_vp, _u64, C.POINTER(_u64)]),
+    "styx_gguf_find_kv": (C.c_int64, [_vp, C.c_char_p]),
+    "styx_gguf_node_type": (_i, [_vp, _u64, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(_u64)]),
+    "styx_gguf_node_scalar": (_i, [_vp, _u64, _u64, _vp]),
+    "styx_gguf_node_string": (_i, [_vp, _u64, _u64, C.POINTER(_vp), C.POINTER(_u64)]),
+    "styx_gguf_node_elem": (_i, [_vp, _u64, _u64, C.POINTER(_u64)]),
+    "styx_gguf_get_u32": (_i, [_vp, C.c_char_p, C.POINTER(C.c_uint32)]),
+    "styx_gguf_get_f32": (_i, [_vp, C.c_char_p, C.POINTER(C.c_float)]),
+    "styx_gguf_get_str": (_i, [_vp, C.c_char_p, C.POINTER(_vp), C.POINTER(_u64)]),
+    "styx_gguf_tensor_count": (_u64, [_vp]),
+    "styx_gguf_tensor": (_i, [_vp, _u64, C.POINTER(GgufTensorInfo)]),
+    "styx_gguf_find_tensor": (C.c_int64, [_vp, C.c_char_p]),
+    "styx_gguf_tensor_data": (_i, [_vp, _u64, C.POINTER(_vp)]),
+    "styx_gguf_type_size": (_i, [C.c_uint32, C.POINTER(_u64), C.POINTER(_u64)]),
+    "styx_gguf_tensor_bytes": (_i, [C.c_uint32, C.POINTER(_u64), C.c_uint32, C.POINTER(_u64)]),
     "styx_synth_quant": (_i, [_vp, _vp, _i, _vp, _u64, _i, _u64, _f]),
     "styx_synth_f32": (_i, [_vp, _vp, _vp, _u64, _u64, _u64, _f]),
 }
