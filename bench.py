@@ -358,6 +358,9 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="styx", choices=["styx", "reference"])
     ap.add_argument("--layers", type=int, default=N_LAYERS)
+    ap.add_argument("--launch", choices=["layers", "block"], default="block",
+                    help="block: one styx_moe_block call per layer; layers: every MoE layer of a "
+                         "token in one launch (styx_moe_blocks with STYX_OPT_MOE_LAYERS)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--no-cpu", action="store_true")
@@ -399,23 +402,31 @@ def main() -> int:
     ids = torch.zeros(L * 64, dtype=torch.int32, device=dev)
     stream = torch.cuda.Stream(device=dev)
 
+    if args.launch == "layers":
+        blk.ctx.set_option(_lib.OPT_MOE_LAYERS, 1)
+
+    def moe_layers():
+        if args.launch == "layers":
+            blk.forward_layers(x, layers, 0, ids)
+        else:
+            for layer in range(L):
+                blk.forward(x, layers[layer], layer, ids)
+
     def token(i):
         x.copy_(bank[i % bank.shape[0]])
-        for layer in range(L):
-            blk.forward(x, layers[layer], layer, ids)
+        moe_layers()
 
     with torch.cuda.stream(stream):
         token(0)
     stream.synchronize()
     blk.ctx.check_device_error(stream)
 
-    # record one token (48 x 3 kernels) through the C ABI's graph API
+    # record one token through the C ABI's graph API
     graph = C.c_void_p()
     sp = C.c_void_p(stream.cuda_stream)
     _lib.check(lib.styx_graph_begin(cx, sp))
     with torch.cuda.stream(stream):
-        for layer in range(L):
-            blk.forward(x, layers[layer], layer, ids)
+        moe_layers()
     _lib.check(lib.styx_graph_end(cx, sp, C.byref(graph)))
 
     def replay(i):
@@ -427,8 +438,10 @@ def main() -> int:
         replay(i)
     stream.synchronize()
     blk.ctx.check_device_error(stream)
-    kernel_path = {1: "single cooperative kernel per MoE block", 2: "three kernels per MoE block"}.get(
-        blk.ctx.last_moe_path(), "unknown")
+    path = blk.ctx.last_moe_path()
+    kernel_path = {1: "single cooperative kernel per MoE block", 2: "three kernels per MoE block",
+                   4: "single cooperative kernel running every MoE layer of a token per launch"}.get(path, "unknown")
+    launches_per_token = {1: L, 2: 3 * L, 4: -(-L // 80)}.get(path, 0)
 
     def barrier():
         if pg:
@@ -515,10 +528,11 @@ def main() -> int:
             "config": dict(workload_config(world), kernels=kernel_path),
             "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": H * 4,
                     "d2h_bytes_per_step": H * 4 + L * 256, "wall_s": t_wall},
-            "gpu_launches": args.steps * L * (1 if blk.ctx.last_moe_path() == 1 else 3),
+            "gpu_launches": args.steps * launches_per_token,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "unit_of_work": "one MoE block (route + gate/up + down kernels)",
+                         "unit_of_work": "one MoE layer (route + gate/up + down); time per layer = "
+                                         "step time / layers",
                          "alg_bytes": ALG_BYTES_LAYER, "peak_kind": peak_kind,
                          "us_per_layer": t_layer * 1e6},
             "cpu_baseline": cpu,

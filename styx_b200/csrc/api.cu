@@ -23,6 +23,7 @@ struct styx_ctx {
     int moe_kernels = 0;    // STYX_OPT_MOE_KERNELS
     int last_path = 0;      // STYX_OPT_MOE_LAST_PATH
     int trace = 0;          // STYX_OPT_TRACE
+    int moe_layers = 0;     // STYX_OPT_MOE_LAYERS
 };
 
 namespace {
@@ -123,7 +124,7 @@ constexpr size_t kTraceCtas = 256;   // phase stamps: styx::kTraceStamps per CTA
 // they guard).
 constexpr size_t kGenOffset = 128;
 struct WsLayout {
-    size_t counter, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, d, lgslot, trace, total;
+    size_t counter, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, d, lgslot, xslot, trace, total;
 };
 
 WsLayout ws_layout(const styx_moe_dims &d) {
@@ -148,6 +149,7 @@ WsLayout ws_layout(const styx_moe_dims &d) {
     L.u = take(kF * 4);
     L.d = take(static_cast<size_t>(d.n_expert_used) * H * 4);   // down outputs of the host-read form
     L.lgslot = take(E * 8);
+    L.xslot = take(H * 8);   // x rows passed between the layers of one launch
     L.trace = take(kTraceCtas * styx::kTraceStamps * 8);
     L.total = o;
     return L;
@@ -344,6 +346,9 @@ int styx_set_option(styx_ctx *ctx, int option, int64_t value) {
     case STYX_OPT_TRACE:
         ctx->trace = value ? 1 : 0;
         return STYX_OK;
+    case STYX_OPT_MOE_LAYERS:
+        ctx->moe_layers = value ? 1 : 0;
+        return STYX_OK;
     default: return fail(STYX_EINVAL, "unknown or read-only option %d", option);
     }
 }
@@ -354,6 +359,7 @@ int styx_get_option(styx_ctx *ctx, int option, int64_t *value) {
     case STYX_OPT_MOE_KERNELS: *value = ctx->moe_kernels; return STYX_OK;
     case STYX_OPT_MOE_LAST_PATH: *value = ctx->last_path; return STYX_OK;
     case STYX_OPT_TRACE: *value = ctx->trace; return STYX_OK;
+    case STYX_OPT_MOE_LAYERS: *value = ctx->moe_layers; return STYX_OK;
     default: return fail(STYX_EINVAL, "unknown option %d", option);
     }
 }
@@ -930,6 +936,37 @@ static bool plan_fused(const styx_moe_dims &d, const styx_moe_layer &lw, int sms
     return true;
 }
 
+// The per-layer part of the single kernel's arguments (the plan part comes
+// from plan_fused).
+static void fill_fused(styx::FusedArgs &fa, const styx_ctx *ctx, const styx_moe_dims &d, const styx_moe_layer &lw,
+                       float *x, int32_t *ids64, float *wts, uint8_t *ws, const WsLayout &L) {
+    const int E = d.n_expert;
+    fa.x = x;
+    fa.norm_w = lw.ffn_norm;
+    fa.eps = d.rms_eps;
+    fa.router = lw.router;
+    fa.E = E;
+    fa.H = d.n_embd;
+    fa.F = d.n_ff;
+    fa.k = d.n_expert_used;
+    fa.renorm = d.norm_topk;
+    fa.remap = lw.remap;
+    fa.pmap = lw.pmap;
+    fa.gate = to_src(lw.gate, E);
+    fa.up = to_src(lw.up, E);
+    fa.down = to_src(lw.down, E);
+    fa.ids64 = ids64;
+    fa.weights = wts;
+    fa.logits = reinterpret_cast<float *>(ws + L.logits);
+    fa.xnorm = reinterpret_cast<float *>(ws + L.xnorm);
+    fa.h = reinterpret_cast<float *>(ws + L.h);
+    fa.lgslot = reinterpret_cast<uint64_t *>(ws + L.lgslot);
+    fa.gen = reinterpret_cast<unsigned long long *>(ws + L.counter + kGenOffset);
+    fa.hcount = fa.gen + 1;
+    fa.err = ctx->d_err;
+    fa.trace = ctx->trace ? reinterpret_cast<long long *>(ws + L.trace) : nullptr;
+}
+
 // Argument checks shared by the MoE block entry points.
 static int check_block(styx_ctx *ctx, const styx_moe_dims *dims, const styx_moe_layer *lw, int layer, const float *x,
                        const int32_t *ids, void *workspace, uint64_t workspace_bytes, WsLayout &Lout) {
@@ -965,7 +1002,6 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
     WsLayout L;
     int rc = check_block(ctx, dims, lw, layer, x, ids, workspace, workspace_bytes, L);
     if (rc) return rc;
-    const int H = dims->n_embd, F = dims->n_ff, E = dims->n_expert, k = dims->n_expert_used;
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     int32_t *ids64 = ids + static_cast<size_t>(layer) * STYX_IDS_PER_LAYER;
     float *wts = weights_out ? weights_out : reinterpret_cast<float *>(ws + L.weights);
@@ -985,31 +1021,8 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
         if (!fits && ctx->moe_kernels == 1)
             return fail(STYX_EUNSUPPORTED, "single-kernel MoE block does not fit these dims / formats");
         if (fits) {
-            fa.x = x;
-            fa.norm_w = lw->ffn_norm;
-            fa.eps = dims->rms_eps;
-            fa.router = lw->router;
-            fa.E = E;
-            fa.H = H;
-            fa.F = F;
-            fa.k = k;
-            fa.renorm = dims->norm_topk;
-            fa.remap = lw->remap;
-            fa.pmap = lw->pmap;
-            fa.gate = to_src(lw->gate, E);
-            fa.up = to_src(lw->up, E);
-            fa.down = to_src(lw->down, E);
-            fa.ids64 = ids64;
-            fa.weights = wts;
-            fa.logits = reinterpret_cast<float *>(ws + L.logits);
-            fa.xnorm = reinterpret_cast<float *>(ws + L.xnorm);
-            fa.h = reinterpret_cast<float *>(ws + L.h);
-            fa.lgslot = reinterpret_cast<uint64_t *>(ws + L.lgslot);
-            fa.gen = reinterpret_cast<unsigned long long *>(ws + L.counter + kGenOffset);
-            fa.hcount = fa.gen + 1;
-            fa.err = ctx->d_err;
-            fa.trace = ctx->trace ? reinterpret_cast<long long *>(ws + L.trace) : nullptr;
             NEED(!ctx->trace || ctx->sm_count <= static_cast<int>(kTraceCtas), "too many CTAs to trace");
+            fill_fused(fa, ctx, *dims, *lw, x, ids64, wts, ws, L);
             CK(styx::launch_fused(fa, lw->gate.qtype, lw->down.qtype, ctx->sm_count, smem, st));
             ctx->last_path = 1;
             return STYX_OK;
@@ -1017,6 +1030,61 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
     }
     ctx->last_path = 2;
     return moe_block_split(ctx, st, *dims, *lw, x, ids64, wts, ws, L, nullptr, false);
+}
+
+// ------------------------------------------------ MoE blocks of consecutive layers
+int styx_moe_blocks(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims, const styx_moe_layer *layers,
+                    int n_layers, int first_layer, float *x, int32_t *ids, float *weights_out, void *workspace,
+                    uint64_t workspace_bytes) {
+    ENTER(ctx);
+    NEED(layers && n_layers >= 1, "need at least one layer");
+    NEED(first_layer >= 0, "negative first layer");
+    WsLayout L{};
+    for (int i = 0; i < n_layers; i++) {
+        const int rc = check_block(ctx, dims, &layers[i], first_layer + i, x, ids, workspace, workspace_bytes, L);
+        if (rc) return rc;
+    }
+    const int k = dims->n_expert_used;
+    // one launch when every layer takes the single kernel with the same formats
+    styx::FusedArgs plan{};
+    uint32_t smem = 0;
+    const styx_moe_layer &l0 = layers[0];
+    bool multi = ctx->moe_layers && n_layers > 1 && ctx->moe_kernels != 2 &&
+                 plan_fused(*dims, l0, ctx->sm_count, plan, smem);
+    for (int i = 0; multi && i < n_layers; i++) {
+        const styx_moe_layer &li = layers[i];
+        multi = al16(li.ffn_norm) && !full_in_host(li.gate) && !full_in_host(li.up) && !full_in_host(li.down) &&
+                li.gate.qtype == l0.gate.qtype && li.up.qtype == l0.up.qtype && li.down.qtype == l0.down.qtype;
+    }
+    if (multi && ctx->trace && ctx->sm_count > static_cast<int>(kTraceCtas)) multi = false;
+    if (!multi) {
+        for (int i = 0; i < n_layers; i++) {
+            const int rc = styx_moe_block(ctx, stream, dims, &layers[i], first_layer + i, x, ids,
+                                          weights_out ? weights_out + static_cast<size_t>(i) * k : nullptr,
+                                          workspace, workspace_bytes);
+            if (rc) return rc;
+        }
+        return STYX_OK;
+    }
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    const cudaStream_t st = S(stream);
+    static thread_local styx::FusedLaunch la;   // 31 KB of kernel parameter, built here
+    for (int base = 0; base < n_layers; base += styx::kMaxFusedLayers) {
+        const int n = std::min(styx::kMaxFusedLayers, n_layers - base);
+        la.n = n;
+        la.xslot = reinterpret_cast<uint64_t *>(ws + L.xslot);
+        for (int j = 0; j < n; j++) {
+            const int i = base + j;
+            la.layer[j] = plan;
+            fill_fused(la.layer[j], ctx, *dims, layers[i], x,
+                       ids + static_cast<size_t>(first_layer + i) * STYX_IDS_PER_LAYER,
+                       weights_out ? weights_out + static_cast<size_t>(i) * k : reinterpret_cast<float *>(ws + L.weights),
+                       ws, L);
+        }
+        CK(styx::launch_fused_layers(la, l0.gate.qtype, l0.down.qtype, ctx->sm_count, smem, st));
+    }
+    ctx->last_path = 4;
+    return STYX_OK;
 }
 
 // ------------------------------------------------ MoE block, expert parallel

@@ -40,6 +40,11 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
                  : "memory");
 }
 
+// before a barrier's memory is initialised again (no phase or copy pending)
+__device__ __forceinline__ void mbar_inval(uint64_t *bar) {
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

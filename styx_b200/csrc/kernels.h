@@ -99,6 +99,16 @@ struct FusedArgs {
     int units_g, gs_g, units_d, gs_d;
 };
 
+// Several consecutive layers in one launch (k_moe_fused_layers): their
+// arguments travel by value as one kernel parameter, under the 32 KiB limit.
+constexpr int kMaxFusedLayers = 80;
+struct FusedLaunch {
+    int n;                   // layers in this launch, 1..kMaxFusedLayers
+    uint64_t *xslot;         // workspace u64[H]: x rows passed between layers as tagged words
+    FusedArgs layer[kMaxFusedLayers];
+};
+static_assert(sizeof(FusedLaunch) <= 32764, "FusedLaunch exceeds the kernel parameter limit");
+
 struct MatVecIdArgs {
     const uint8_t *a;
     uint64_t expert_bytes;
@@ -150,6 +160,7 @@ cudaError_t launch_synth_f32(float *dst, uint64_t n, uint64_t seed, uint64_t off
 int set_error(int code, const char *msg);
 
 cudaError_t launch_fused(const FusedArgs &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st);
+cudaError_t launch_fused_layers(const FusedLaunch &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st);
 bool fused_supported(int qg, int qd);
 int fused_block_threads();
 constexpr uint32_t kFusedHeader = 1792;

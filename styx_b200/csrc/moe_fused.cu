@@ -70,6 +70,10 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
+// two adjacent tagged words (16-byte aligned), each read whole
+__device__ __forceinline__ void ld_slot2(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
 __device__ __forceinline__ uint32_t slot_tag(uint64_t w) { return static_cast<uint32_t>(w >> 32); }
 __device__ __forceinline__ float slot_val(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
 
@@ -266,17 +270,36 @@ __device__ __forceinline__ uint32_t seg_b_off(int nA, int rb) {
     return static_cast<uint32_t>((static_cast<size_t>(nA) * rb + 32 + 15) & ~size_t(15));
 }
 
-template <int QG, int QD>
-__global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_constant__ FusedArgs pa) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    // The launch parameters, read once in parallel into shared memory: reading
-    // them field by field from the parameter bank costs a constant-cache miss
-    // on each first touch in every phase of every launch.
+// How a layer of a launch connects to its neighbours.  The first layer of a
+// launch reads x from global memory after the grid dependency resolves; a
+// later one reads the x its predecessor published as tagged words (one per
+// row, tag = that layer's tag).  A layer with a successor publishes its output
+// rows the same way and warms L2 with the successor's router rows.
+struct LayerLink {
+    int index;                   // position of the layer in the launch
+    bool x_from_slot, x_to_slot;
+    uint64_t *xslot;             // workspace u64[H]
+    const float *next_router, *next_norm;
+};
+
+// the link sits in shared memory after the arguments, read where it is used
+// (kept in registers across the layer it would push the kernel into spills)
+constexpr int kHdrLink = kHdrArgs + ((static_cast<int>(sizeof(FusedArgs)) + 15) & ~15);
+static_assert(kHdrLink + static_cast<int>(sizeof(LayerLink)) <= kFusedHeaderBytes, "layer link overflows the header");
+
+// The launch parameters, read once in parallel into shared memory: reading
+// them field by field from the parameter bank costs a constant-cache miss on
+// each first touch in every phase.  Thread 0 also stores the layer link.
+__device__ __forceinline__ void load_args(uint8_t *smem, const FusedArgs &a, const LayerLink &lk) {
     if (threadIdx.x < sizeof(FusedArgs) / 8)
-        reinterpret_cast<uint64_t *>(smem + kHdrArgs)[threadIdx.x] =
-            reinterpret_cast<const uint64_t *>(&pa)[threadIdx.x];
-    __syncthreads();
+        reinterpret_cast<uint64_t *>(smem + kHdrArgs)[threadIdx.x] = reinterpret_cast<const uint64_t *>(&a)[threadIdx.x];
+    if (threadIdx.x == 0) *reinterpret_cast<LayerLink *>(smem + kHdrLink) = lk;
+}
+
+template <int QG, int QD>
+__device__ __forceinline__ void fused_layer(uint8_t *smem) {
     const FusedArgs &p = *reinterpret_cast<const FusedArgs *>(smem + kHdrArgs);
+    const LayerLink &lk = *reinterpret_cast<const LayerLink *>(smem + kHdrLink);
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
     uint64_t *full_gu = bar, *full_d = bar + 16;
     float *red = reinterpret_cast<float *>(smem + kHdrRed);  // 32 floats
@@ -320,21 +343,31 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
     STYX_STAMP(0);
     // ------------------------------------------------ phase 0
     if (tid < 16) {   // one thread per barrier: the gate/up chunks', and the down rows'
+        if (lk.index) {   // the previous layer's barriers: every phase complete, every copy landed
+            mbar_inval(&full_gu[tid]);
+            if (tid == 0) mbar_inval(&full_d[0]);
+        }
         mbar_init(&full_gu[tid], 1);
         if (tid == 0) mbar_init(&full_d[0], 1);
         fence_mbar_init();
     }
-    pdl_trigger();
-    for (int j = tid; j < n_rows_mine; j += kFusedBlock)
-        prefetch_l2(p.router + static_cast<size_t>(b + G * j) * H, static_cast<uint32_t>(H) * 4u);
-    if (tid == kFusedBlock - 1) prefetch_l2(p.norm_w, static_cast<uint32_t>(H) * 4u);
+    if (lk.index == 0) {
+        pdl_trigger();
+        for (int j = tid; j < n_rows_mine; j += kFusedBlock)
+            prefetch_l2(p.router + static_cast<size_t>(b + G * j) * H, static_cast<uint32_t>(H) * 4u);
+        if (tid == kFusedBlock - 1) prefetch_l2(p.norm_w, static_cast<uint32_t>(H) * 4u);
+    }
     // this launch's tag (published to the block by the barriers in phase 1).
     // Safe before the grid dependency resolves: every CTA of the previous
     // launch on this workspace took its number before any of them could exit
     // (each waits in phase 2 for all of that launch's logits).
     uint32_t *s_tag = reinterpret_cast<uint32_t *>(s_flag + 2);
+    // (A later layer of the same launch: every CTA took its number for the
+    // previous layer before any CTA could finish that layer, so the layers
+    // of a launch are numbered consecutively, as separate launches would be.)
     if (tid == 0) *s_tag = static_cast<uint32_t>(atomicAdd(p.gen, 1ull) / static_cast<unsigned long long>(G)) + 1u;
-    pdl_wait();
+    if (lk.index == 0) pdl_wait();
+    if (lk.x_from_slot) __syncthreads();   // the tag, for the poll on x below
     STYX_STAMP(1);
 
     // ------------------------------------------------ phase 1: RMSNorm + router
@@ -357,8 +390,33 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
     // logits and the top-k's index order decides between them.
     float ss = 0.f, rd = 0.f;
     float4 xr = npre;   // this thread's float4 of raw x (one-float4 case)
+    float4 xin = npre;  // a later layer: the same float4 from the tagged words
+    if (lk.x_from_slot) {
+        // the previous layer's output rows, published with its tag (= this
+        // layer's tag - 1); every warp polls in step, bounded, then regroups
+        const uint32_t want = *s_tag - 1u;
+        const bool on = one && tid < H4;
+        const uint64_t *src = lk.xslot + 4 * static_cast<size_t>(on ? tid : 0);
+        const long long t0 = clock64();
+        for (;;) {
+            uint64_t w0, w1, w2, w3;
+            ld_slot2(src, w0, w1);
+            ld_slot2(src + 2, w2, w3);
+            const bool got = slot_tag(w0) == want && slot_tag(w1) == want && slot_tag(w2) == want &&
+                             slot_tag(w3) == want;
+            xin = make_float4(slot_val(w0), slot_val(w1), slot_val(w2), slot_val(w3));
+            if (__all_sync(0xffffffffu, got || !on)) break;
+            const long long dt = __shfl_sync(0xffffffffu, clock64() - t0, 0);
+            if (dt > kSpinCycles) {
+                if (lane == 0) atomicExch(p.err, kErrWaitRoute);
+                break;
+            }
+            if (dt > kPollFreeCycles) __nanosleep(256);
+        }
+        __syncwarp();
+    }
     for (int i = tid; i < H4; i += kFusedBlock) {
-        const float4 v = __ldcg(x4 + i);
+        const float4 v = lk.x_from_slot ? xin : __ldcg(x4 + i);
         xn4[i] = v;   // raw x for now
         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         if (one) {
@@ -658,6 +716,12 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
     }
     STYX_STAMP(10);
 
+    if (lk.next_router) {   // warm L2 with the next layer's router rows and norm while h travels
+        for (int j = tid; j < n_rows_mine; j += kFusedBlock)
+            prefetch_l2(lk.next_router + static_cast<size_t>(b + G * j) * H, static_cast<uint32_t>(H) * 4u);
+        if (tid == kFusedBlock - 1) prefetch_l2(lk.next_norm, static_cast<uint32_t>(H) * 4u);
+    }
+
     // ------------------------------------------------ phase 4: down + combine
     // The warps of slot s wait for slot s's h only, turn it into digits in
     // shared memory themselves and run the CTA's down rows for slot s; the
@@ -738,10 +802,17 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
         }
         __syncthreads();
         STYX_STAMP(13);
-        if (ok && tid < n) {
-            float acc = 0.f;
-            for (int s = 0; s < k; s++) acc = __fadd_rn(acc, __fmul_rn(wts[s], dpart[s * p.rc + tid]));
-            p.x[dbeg + tid] = __fadd_rn(p.x[dbeg + tid], acc);
+        if (tid < n) {
+            float xv = p.x[dbeg + tid];
+            if (ok) {
+                float acc = 0.f;
+                for (int s = 0; s < k; s++) acc = __fadd_rn(acc, __fmul_rn(wts[s], dpart[s * p.rc + tid]));
+                xv = __fadd_rn(xv, acc);
+                p.x[dbeg + tid] = xv;
+            }
+            // the next layer of the launch reads the row from here (also after
+            // a wait gave up, so that it does not wait for the row as well)
+            if (lk.x_to_slot) st_slot(lk.xslot + dbeg + tid, xv, tag);
         }
     }
     STYX_STAMP(14);
@@ -757,13 +828,37 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_const
 #undef STYX_STAMP_T
 }
 
+template <int QG, int QD>
+__global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_constant__ FusedArgs pa) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    load_args(smem, pa, LayerLink{0, false, false, nullptr, nullptr, nullptr});
+    __syncthreads();
+    fused_layer<QG, QD>(smem);
+}
+
+// Several consecutive layers in one launch: the grid stays resident, and the
+// boundary between layers is the exchange of x through tagged words instead
+// of the end of one grid and the start of the next.
+template <int QG, int QD>
+__global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused_layers(const __grid_constant__ FusedLaunch la) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    for (int li = 0; li < la.n; li++) {
+        if (li) __syncthreads();   // every thread is done with the previous layer's shared memory
+        const bool more = li + 1 < la.n;
+        load_args(smem, la.layer[li],
+                  LayerLink{li, li > 0, more, la.xslot, more ? la.layer[li + 1].router : nullptr,
+                            more ? la.layer[li + 1].norm_w : nullptr});
+        __syncthreads();
+        fused_layer<QG, QD>(smem);
+    }
+}
+
 // Cooperative launch (every CTA co-resident: the tagged-slot reads are
 // grid-wide waits) with programmatic stream serialisation: the kernel lets
 // the next one launch at entry and waits for the previous grid before it
 // touches the workspace or x.
-template <int QG, int QD>
-static cudaError_t launch_fused_t(const FusedArgs &a, int grid, uint32_t smem, cudaStream_t st) {
-    auto kern = k_moe_fused<QG, QD>;
+template <class Kern, class Args>
+static cudaError_t launch_coop_pdl(Kern kern, const Args &a, int grid, uint32_t smem, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     int occ = 0;
@@ -790,7 +885,20 @@ static cudaError_t launch_fused_t(const FusedArgs &a, int grid, uint32_t smem, c
 
 cudaError_t launch_fused(const FusedArgs &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st) {
 #define STYX_FUSED_CASE(G_, D_) \
-    if (qg == G_ && qd == D_) return launch_fused_t<G_, D_>(a, grid, smem, st);
+    if (qg == G_ && qd == D_) return launch_coop_pdl(k_moe_fused<G_, D_>, a, grid, smem, st);
+    STYX_FUSED_CASE(STYX_Q4_K, STYX_Q6_K)
+    STYX_FUSED_CASE(STYX_Q4_K, STYX_Q4_K)
+    STYX_FUSED_CASE(STYX_Q5_K, STYX_Q6_K)
+    STYX_FUSED_CASE(STYX_Q5_K, STYX_Q5_K)
+    STYX_FUSED_CASE(STYX_Q8_0, STYX_Q8_0)
+    STYX_FUSED_CASE(STYX_Q6_K, STYX_Q6_K)
+#undef STYX_FUSED_CASE
+    return cudaErrorNotSupported;
+}
+
+cudaError_t launch_fused_layers(const FusedLaunch &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st) {
+#define STYX_FUSED_CASE(G_, D_) \
+    if (qg == G_ && qd == D_) return launch_coop_pdl(k_moe_fused_layers<G_, D_>, a, grid, smem, st);
     STYX_FUSED_CASE(STYX_Q4_K, STYX_Q6_K)
     STYX_FUSED_CASE(STYX_Q4_K, STYX_Q4_K)
     STYX_FUSED_CASE(STYX_Q5_K, STYX_Q6_K)

@@ -279,6 +279,17 @@ class MoeBlock:
                                    self.ws_bytes))
         return x
 
+    def forward_layers(self, x: torch.Tensor, layer_ws: list, first_layer: int, ids: torch.Tensor,
+                       weights_out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        """Consecutive layers first_layer.. of one token (styx_moe_blocks):
+        the same as forward() per layer in order; when every layer takes the
+        single kernel, up to 80 of them run in one launch."""
+        arr = (MoeLayer * len(layer_ws))(*[lw.struct() for lw in layer_ws])
+        check(lib().styx_moe_blocks(self.ctx.handle, _stream(stream), C.byref(self._dims), arr, len(layer_ws),
+                                    first_layer, _ptr(x), _ptr(ids), _ptr(weights_out), _ptr(self.workspace),
+                                    self.ws_bytes))
+        return x
+
     def forward_ep(self, x: torch.Tensor, layer_w: LayerWeights, layer: int, ids: torch.Tensor,
                    partial: torch.Tensor, weights_out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
         """Expert-parallel half of the block: partial[s, r] = w[s] * d[s][r]

@@ -1,0 +1,121 @@
+"""styx_moe_blocks: consecutive layers of one token in one launch (the grid
+stays resident, x passes between layers as tagged words; STYX_OPT_MOE_LAYERS)
+must give exactly what one styx_moe_block call per layer gives, layer after
+layer.
+"""
+import dataclasses
+
+import numpy as np
+import pytest
+import torch
+
+from styx_b200 import _lib, ops
+from tests.moe_case import make_case, oracle_block
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+GEN_OFFSET = 128
+
+
+def T(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def upload(c):
+    sg, su, sd = c.slabs
+    return ops.LayerWeights(T(c.norm), T(c.router), ops.Experts(c.qts[0], T(c.gate), sg),
+                            ops.Experts(c.qts[1], T(c.up), su), ops.Experts(c.qts[2], T(c.down), sd))
+
+
+def rel_to_max(got, exp):
+    got, exp = np.asarray(got, np.float64), np.asarray(exp, np.float64)
+    return float(np.max(np.abs(got - exp)) / max(np.max(np.abs(exp)), 1e-30))
+
+
+def run_both(cases, first_layer=0, reps=2):
+    lws = [upload(c) for c in cases]
+    c0 = cases[0]
+    n, k = len(cases), c0.k
+    dims = ops.Dims(c0.H, c0.F, c0.E, k)
+    one, many = ops.MoeBlock(dims, 0), ops.MoeBlock(dims, 0)
+    many.ctx.set_option(_lib.OPT_MOE_LAYERS, 1)
+    total = first_layer + n
+    try:
+        return _run_both(cases, first_layer, reps, lws, c0, n, k, one, many, total)
+    finally:
+        many.ctx.set_option(_lib.OPT_MOE_LAYERS, 0)
+
+
+def _run_both(cases, first_layer, reps, lws, c0, n, k, one, many, total):
+    for rep in range(reps):   # twice: the launch counter keeps counting on the same workspaces
+        xa, xb = T(c0.x), T(c0.x)
+        ia = torch.full((total * 64,), -7, dtype=torch.int32, device=DEV)
+        ib = ia.clone()
+        wa = torch.zeros(n * k, dtype=torch.float32, device=DEV)
+        wb = torch.zeros_like(wa)
+        for i, lw in enumerate(lws):
+            one.forward(xa, lw, first_layer + i, ia, weights_out=wa[i * k:(i + 1) * k])
+        many.forward_layers(xb, lws, first_layer, ib, weights_out=wb)
+        torch.cuda.synchronize()
+        one.ctx.check_device_error()
+        assert np.array_equal(xa.cpu().numpy().view(np.uint32), xb.cpu().numpy().view(np.uint32)), rep
+        assert np.array_equal(ia.cpu().numpy(), ib.cpu().numpy()), rep
+        assert np.array_equal(wa.cpu().numpy().view(np.uint32), wb.cpu().numpy().view(np.uint32)), rep
+    return many, xb, lws
+
+
+def test_one_launch_equals_one_call_per_layer_and_the_oracle():
+    cases = [make_case(90 + l, 1024, 512, 32, 8, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K)) for l in range(5)]
+    many, x, _ = run_both(cases, first_layer=3)
+    assert many.ctx.last_moe_path() == 4
+    xr = cases[0].x.copy()
+    for c in cases:
+        xr = oracle_block(dataclasses.replace(c, x=xr))["x"]
+    assert rel_to_max(x.cpu().numpy(), xr) < 1e-4
+
+
+def test_more_layers_than_one_launch_holds():
+    # 83 small layers: two launches (80 + 3)
+    cases = [make_case(200 + l, 512, 256, 8, 2, (_lib.Q8_0, _lib.Q8_0, _lib.Q8_0), sigma=0.01)
+             for l in range(83)]
+    many, _, _ = run_both(cases, reps=1)
+    assert many.ctx.last_moe_path() == 4
+
+
+def test_mixed_formats_fall_back_to_one_call_per_layer():
+    cases = [make_case(300, 1024, 512, 16, 4, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K)),
+             make_case(301, 1024, 512, 16, 4, (_lib.Q4_K, _lib.Q4_K, _lib.Q4_K))]
+    many, _, _ = run_both(cases, reps=1)
+    assert many.ctx.last_moe_path() == 1     # the last layer ran on its own
+
+
+def test_split_launch_numbers_time_out_inside_a_multi_layer_launch_and_recover():
+    """As tests/test_gpu_timeout.py, for a two-layer launch: half a grid on the
+    launch counter splits every layer's CTAs over two tags; every wait (logits,
+    h, x between the layers) gives up after about a second, the error word
+    says STYX_ETIMEOUT, and after styx_moe_workspace_init the call is exact."""
+    cases = [make_case(400 + l, 1024, 512, 16, 4, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K)) for l in range(2)]
+    lws = [upload(c) for c in cases]
+    blk = ops.MoeBlock(ops.Dims(1024, 512, 16, 4), 0)
+    blk.ctx.check_device_error()
+    blk.ctx.set_option(_lib.OPT_MOE_LAYERS, 1)
+    blk.workspace[GEN_OFFSET:GEN_OFFSET + 8].view(torch.int64).fill_(blk.ctx.sm_count // 2)
+    x = T(cases[0].x)
+    ids = torch.zeros(2 * 64, dtype=torch.int32, device=DEV)
+    blk.forward_layers(x, lws, 0, ids)
+    torch.cuda.synchronize()
+    assert blk.ctx.last_moe_path() == 4
+    with pytest.raises(_lib.StyxError) as ei:
+        blk.ctx.check_device_error()
+    assert ei.value.code == _lib.STYX_ETIMEOUT
+    _lib.check(_lib.lib().styx_moe_workspace_init(blk.ctx.handle, None, blk.workspace.data_ptr(), blk.ws_bytes))
+    x = T(cases[0].x)
+    blk.forward_layers(x, lws, 0, ids)
+    torch.cuda.synchronize()
+    blk.ctx.check_device_error()
+    xr = cases[0].x.copy()
+    for c in cases:
+        xr = oracle_block(dataclasses.replace(c, x=xr))["x"]
+    assert rel_to_max(x.cpu().numpy(), xr) < 1e-4
+    blk.ctx.set_option(_lib.OPT_MOE_LAYERS, 0)
