@@ -364,8 +364,17 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
     uint32_t *s_tag = reinterpret_cast<uint32_t *>(s_flag + 2);
     // (A later layer of the same launch: every CTA took its number for the
     // previous layer before any CTA could finish that layer, so the layers
-    // of a launch are numbered consecutively, as separate launches would be.)
-    if (tid == 0) *s_tag = static_cast<uint32_t>(atomicAdd(p.gen, 1ull) / static_cast<unsigned long long>(G)) + 1u;
+    // of a launch are numbered consecutively, as separate launches would be.
+    // Its tag is then the previous one + 1, known without waiting for the
+    // counter's reply.)
+    if (tid == 0) {
+        if (lk.index == 0) {
+            *s_tag = static_cast<uint32_t>(atomicAdd(p.gen, 1ull) / static_cast<unsigned long long>(G)) + 1u;
+        } else {
+            atomicAdd(p.gen, 1ull);
+            *s_tag += 1u;
+        }
+    }
     if (lk.index == 0) pdl_wait();
     if (lk.x_from_slot) __syncthreads();   // the tag, for the poll on x below
     STYX_STAMP(1);
