@@ -358,9 +358,10 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="styx", choices=["styx", "reference"])
     ap.add_argument("--layers", type=int, default=N_LAYERS)
-    ap.add_argument("--launch", choices=["layers", "block"], default="block",
-                    help="block: one styx_moe_block call per layer; layers: every MoE layer of a "
-                         "token in one launch (styx_moe_blocks with STYX_OPT_MOE_LAYERS)")
+    ap.add_argument("--launch", choices=["block", "layers", "chain"], default="block",
+                    help="block: one styx_moe_block call per layer (the fastest on B200); layers: every MoE "
+                         "layer of a token in one persistent launch (STYX_OPT_MOE_LAYERS 1); chain: one launch "
+                         "per layer without the grid-dependency wait, x passed as tagged words (2)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--no-cpu", action="store_true")
@@ -402,11 +403,10 @@ def main() -> int:
     ids = torch.zeros(L * 64, dtype=torch.int32, device=dev)
     stream = torch.cuda.Stream(device=dev)
 
-    if args.launch == "layers":
-        blk.ctx.set_option(_lib.OPT_MOE_LAYERS, 1)
+    blk.ctx.set_option(_lib.OPT_MOE_LAYERS, {"block": 0, "layers": 1, "chain": 2}[args.launch])
 
     def moe_layers():
-        if args.launch == "layers":
+        if args.launch != "block":
             blk.forward_layers(x, layers, 0, ids)
         else:
             for layer in range(L):
@@ -440,8 +440,10 @@ def main() -> int:
     blk.ctx.check_device_error(stream)
     path = blk.ctx.last_moe_path()
     kernel_path = {1: "single cooperative kernel per MoE block", 2: "three kernels per MoE block",
-                   4: "single cooperative kernel running every MoE layer of a token per launch"}.get(path, "unknown")
-    launches_per_token = {1: L, 2: 3 * L, 4: -(-L // 80)}.get(path, 0)
+                   4: "single cooperative kernel running every MoE layer of a token per launch",
+                   5: "single cooperative kernel per MoE block, launches chained (x passed as tagged words)"
+                   }.get(path, "unknown")
+    launches_per_token = {1: L, 2: 3 * L, 4: -(-L // 80), 5: L}.get(path, 0)
 
     def barrier():
         if pg:

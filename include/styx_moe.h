@@ -89,13 +89,17 @@ int styx_check_device_error(styx_ctx *ctx, styx_stream stream);
  * kernels), 1 = single kernel only (STYX_EUNSUPPORTED if it does not fit),
  * 2 = three kernels.  STYX_OPT_MOE_LAST_PATH (read only) = 1 (single
  * kernel), 2 (three kernels), 3 (host-read form: some full tensor is in
- * STYX_MEM_HOST memory) or 4 (single kernel, several layers per launch,
+ * STYX_MEM_HOST memory), 4 (single kernel, several layers per launch,
+ * styx_moe_blocks) or 5 (single kernel, one chained launch per layer,
  * styx_moe_blocks), the form the last styx_moe_block[s] call used.  STYX_OPT_TRACE = 1 makes the single
  * kernel record 32 clock64 stamps per CTA at its phase boundaries into the
  * workspace (styx_moe_workspace_view 4: int64[CTAs][32]).
- * STYX_OPT_MOE_LAYERS = 1 lets styx_moe_blocks run up to 80 single-kernel
- * layers in one launch (default 0: one launch per layer, which measures
- * faster on B200 today: the persistent form's layer loop spills registers). */
+ * STYX_OPT_MOE_LAYERS picks how styx_moe_blocks runs single-kernel layers:
+ * 0 (default) one independent styx_moe_block call per layer, 1 up to 80
+ * layers in one persistent launch (its layer loop spills registers), 2 one
+ * launch per layer, chained (a layer starts without waiting for the
+ * previous grid and takes x from it as tagged words).  On B200 the default
+ * measures fastest. */
 #define STYX_OPT_MOE_KERNELS 1
 #define STYX_OPT_MOE_LAST_PATH 2
 #define STYX_OPT_TRACE 3
@@ -281,12 +285,13 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream,
 /* The MoE blocks of n_layers consecutive layers of one token, first_layer
  * + i using layers[i], each layer's x the previous one's output: the same
  * results as n_layers styx_moe_block calls in order (weights_out, when not
- * NULL, is f32[n_layers][k]).  With STYX_OPT_MOE_LAYERS set, and when every
- * layer takes the single-kernel form with the same formats, up to 80 layers
- * run in one launch: the grid stays resident and x passes from layer to
- * layer inside it (the MoE sections of forward_token, moe.rs:1974-2062, when
- * nothing runs between them, as in a stack of MoE blocks); otherwise the
- * layers run as separate calls. */
+ * NULL, is f32[n_layers][k]).  When every layer takes the single-kernel
+ * form (the MoE sections of forward_token, moe.rs:1974-2062, when nothing
+ * runs between them, as in a stack of MoE blocks), STYX_OPT_MOE_LAYERS = 1
+ * or 2 pass x from layer to layer as tagged words in the workspace instead
+ * of through the caller's x: 1 runs up to 80 layers (with the same formats)
+ * in one launch, 2 chains one launch per layer.  Otherwise, and by default,
+ * the layers run as separate calls. */
 int styx_moe_blocks(styx_ctx *ctx, styx_stream stream,
                     const styx_moe_dims *dims, const styx_moe_layer *layers,
                     int n_layers, int first_layer, float *x, int32_t *ids,

@@ -148,8 +148,8 @@ WsLayout ws_layout(const styx_moe_dims &d) {
     L.g = take(kF * 4);   // gate / up outputs of the mul_mat_vec_id forms
     L.u = take(kF * 4);
     L.d = take(static_cast<size_t>(d.n_expert_used) * H * 4);   // down outputs of the host-read form
-    L.lgslot = take(E * 8);
-    L.xslot = take(H * 8);   // x rows passed between the layers of one launch
+    L.lgslot = take(2 * E * 8);   // two banks of logit words, by launch-tag parity
+    L.xslot = take(H * 8);        // x rows passed from one layer to the next
     L.trace = take(kTraceCtas * styx::kTraceStamps * 8);
     L.total = o;
     return L;
@@ -347,7 +347,8 @@ int styx_set_option(styx_ctx *ctx, int option, int64_t value) {
         ctx->trace = value ? 1 : 0;
         return STYX_OK;
     case STYX_OPT_MOE_LAYERS:
-        ctx->moe_layers = value ? 1 : 0;
+        NEED(value >= 0 && value <= 2, "STYX_OPT_MOE_LAYERS: 0, 1 or 2");
+        ctx->moe_layers = static_cast<int>(value);
         return STYX_OK;
     default: return fail(STYX_EINVAL, "unknown or read-only option %d", option);
     }
@@ -1023,7 +1024,8 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
         if (fits) {
             NEED(!ctx->trace || ctx->sm_count <= static_cast<int>(kTraceCtas), "too many CTAs to trace");
             fill_fused(fa, ctx, *dims, *lw, x, ids64, wts, ws, L);
-            CK(styx::launch_fused(fa, lw->gate.qtype, lw->down.qtype, ctx->sm_count, smem, st));
+            const styx::LayerLink alone{0, false, false, true, nullptr, nullptr, nullptr};
+            CK(styx::launch_fused(fa, alone, lw->gate.qtype, lw->down.qtype, ctx->sm_count, smem, st));
             ctx->last_path = 1;
             return STYX_OK;
         }
@@ -1045,18 +1047,43 @@ int styx_moe_blocks(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims
         if (rc) return rc;
     }
     const int k = dims->n_expert_used;
-    // one launch when every layer takes the single kernel with the same formats
+    // x passes between the layers as tagged words when every layer takes the
+    // single kernel (and a CTA's residual rows fit its 16 spare words)
     styx::FusedArgs plan{};
     uint32_t smem = 0;
     const styx_moe_layer &l0 = layers[0];
-    bool multi = ctx->moe_layers && n_layers > 1 && ctx->moe_kernels != 2 &&
-                 plan_fused(*dims, l0, ctx->sm_count, plan, smem);
-    for (int i = 0; multi && i < n_layers; i++) {
+    bool linked = ctx->moe_layers != 0 && n_layers > 1 && ctx->moe_kernels != 2 &&
+                  !(ctx->trace && ctx->sm_count > static_cast<int>(kTraceCtas));
+    for (int i = 0; linked && i < n_layers; i++) {
         const styx_moe_layer &li = layers[i];
-        multi = al16(li.ffn_norm) && !full_in_host(li.gate) && !full_in_host(li.up) && !full_in_host(li.down) &&
-                li.gate.qtype == l0.gate.qtype && li.up.qtype == l0.up.qtype && li.down.qtype == l0.down.qtype;
+        linked = al16(li.ffn_norm) && !full_in_host(li.gate) && !full_in_host(li.up) && !full_in_host(li.down) &&
+                 plan_fused(*dims, li, ctx->sm_count, plan, smem) && plan.rc <= 16;
     }
-    if (multi && ctx->trace && ctx->sm_count > static_cast<int>(kTraceCtas)) multi = false;
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    const cudaStream_t st = S(stream);
+    auto wts_of = [&](int i) {
+        return weights_out ? weights_out + static_cast<size_t>(i) * k : reinterpret_cast<float *>(ws + L.weights);
+    };
+    if (linked && ctx->moe_layers == 2) {   // one chained launch per layer
+        uint64_t *xslot = reinterpret_cast<uint64_t *>(ws + L.xslot);
+        for (int i = 0; i < n_layers; i++) {
+            const styx_moe_layer &li = layers[i];
+            plan_fused(*dims, li, ctx->sm_count, plan, smem);
+            fill_fused(plan, ctx, *dims, li, x, ids + static_cast<size_t>(first_layer + i) * STYX_IDS_PER_LAYER,
+                       wts_of(i), ws, L);
+            const bool more = i + 1 < n_layers;
+            const styx::LayerLink lk{0, i > 0, more, i == 0, xslot, more ? layers[i + 1].router : nullptr,
+                                     more ? layers[i + 1].ffn_norm : nullptr};
+            CK(styx::launch_fused(plan, lk, li.gate.qtype, li.down.qtype, ctx->sm_count, smem, st));
+        }
+        ctx->last_path = 5;
+        return STYX_OK;
+    }
+    // one persistent launch (per 80 layers) when, also, every layer has the same formats
+    bool multi = linked && ctx->moe_layers == 1 && plan_fused(*dims, l0, ctx->sm_count, plan, smem);
+    for (int i = 0; multi && i < n_layers; i++)
+        multi = layers[i].gate.qtype == l0.gate.qtype && layers[i].up.qtype == l0.up.qtype &&
+                layers[i].down.qtype == l0.down.qtype;
     if (!multi) {
         for (int i = 0; i < n_layers; i++) {
             const int rc = styx_moe_block(ctx, stream, dims, &layers[i], first_layer + i, x, ids,
@@ -1066,8 +1093,6 @@ int styx_moe_blocks(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims
         }
         return STYX_OK;
     }
-    uint8_t *ws = static_cast<uint8_t *>(workspace);
-    const cudaStream_t st = S(stream);
     static thread_local styx::FusedLaunch la;   // 31 KB of kernel parameter, built here
     for (int base = 0; base < n_layers; base += styx::kMaxFusedLayers) {
         const int n = std::min(styx::kMaxFusedLayers, n_layers - base);
@@ -1077,9 +1102,7 @@ int styx_moe_blocks(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims
             const int i = base + j;
             la.layer[j] = plan;
             fill_fused(la.layer[j], ctx, *dims, layers[i], x,
-                       ids + static_cast<size_t>(first_layer + i) * STYX_IDS_PER_LAYER,
-                       weights_out ? weights_out + static_cast<size_t>(i) * k : reinterpret_cast<float *>(ws + L.weights),
-                       ws, L);
+                       ids + static_cast<size_t>(first_layer + i) * STYX_IDS_PER_LAYER, wts_of(i), ws, L);
         }
         CK(styx::launch_fused_layers(la, l0.gate.qtype, l0.down.qtype, ctx->sm_count, smem, st));
     }

@@ -99,6 +99,16 @@ struct FusedArgs {
     int units_g, gs_g, units_d, gs_d;
 };
 
+// How a single-kernel layer connects to the layers before and after it (see
+// moe_fused.cu): chain flags and the x exchange words.
+struct LayerLink {
+    int index;                   // position of the layer in the launch
+    bool x_from_slot, x_to_slot;
+    bool wait_grid;              // griddepcontrol.wait before touching x / the workspace
+    uint64_t *xslot;             // workspace u64[H]
+    const float *next_router, *next_norm;
+};
+
 // Several consecutive layers in one launch (k_moe_fused_layers): their
 // arguments travel by value as one kernel parameter, under the 32 KiB limit.
 constexpr int kMaxFusedLayers = 80;
@@ -159,7 +169,8 @@ cudaError_t launch_synth_f32(float *dst, uint64_t n, uint64_t seed, uint64_t off
 // leaves `msg` for styx_last_error() and returns `code` (api.cu)
 int set_error(int code, const char *msg);
 
-cudaError_t launch_fused(const FusedArgs &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st);
+cudaError_t launch_fused(const FusedArgs &a, const LayerLink &lk, int qg, int qd, int grid, uint32_t smem,
+                         cudaStream_t st);
 cudaError_t launch_fused_layers(const FusedLaunch &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st);
 bool fused_supported(int qg, int qd);
 int fused_block_threads();

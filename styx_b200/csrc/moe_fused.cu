@@ -270,17 +270,24 @@ __device__ __forceinline__ uint32_t seg_b_off(int nA, int rb) {
     return static_cast<uint32_t>((static_cast<size_t>(nA) * rb + 32 + 15) & ~size_t(15));
 }
 
-// How a layer of a launch connects to its neighbours.  The first layer of a
-// launch reads x from global memory after the grid dependency resolves; a
+// How a layer connects to its neighbours.  A layer that starts a chain reads
+// x from global memory after the grid dependency resolves (wait_grid); a
 // later one reads the x its predecessor published as tagged words (one per
-// row, tag = that layer's tag).  A layer with a successor publishes its output
-// rows the same way and warms L2 with the successor's router rows.
-struct LayerLink {
-    int index;                   // position of the layer in the launch
-    bool x_from_slot, x_to_slot;
-    uint64_t *xslot;             // workspace u64[H]
-    const float *next_router, *next_norm;
-};
+// row, tag = the predecessor's tag = this layer's tag - 1), whether the
+// predecessor ran earlier in the same launch or in the previous launch on
+// the workspace.  A layer with a successor publishes its output rows the
+// same way and warms L2 with the successor's router rows.
+//
+// Chained launches skip the grid dependency: the next layer's CTAs start as
+// soon as their SM is free and overlap their prologue with the previous
+// layer's tail.  That is safe because before any CTA of a layer exits, every
+// CTA of that layer has started (each waits for all the layer's logits), so
+// at most two consecutive layers are resident, neither waits for the later
+// one, and the words they could both touch are kept apart: the logit words
+// alternate between two banks by tag parity, the h rows and counts of the
+// later layer are written only after every CTA of the earlier one has exited,
+// and the residual add uses the x rows read from the tagged words.
+// (LayerLink itself is declared in kernels.h, for the host.)
 
 // the link sits in shared memory after the arguments, read where it is used
 // (kept in registers across the layer it would push the kernel into spills)
@@ -360,7 +367,9 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
     // this launch's tag (published to the block by the barriers in phase 1).
     // Safe before the grid dependency resolves: every CTA of the previous
     // launch on this workspace took its number before any of them could exit
-    // (each waits in phase 2 for all of that launch's logits).
+    // (each waits in phase 2 for all of that launch's logits), and a CTA of
+    // this launch cannot be resident before one of the previous launch exits
+    // (one CTA fills an SM's registers, and the grid covers every SM).
     uint32_t *s_tag = reinterpret_cast<uint32_t *>(s_flag + 2);
     // (A later layer of the same launch: every CTA took its number for the
     // previous layer before any CTA could finish that layer, so the layers
@@ -375,7 +384,7 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
             *s_tag += 1u;
         }
     }
-    if (lk.index == 0) pdl_wait();
+    if (lk.wait_grid) pdl_wait();
     if (lk.x_from_slot) __syncthreads();   // the tag, for the poll on x below
     STYX_STAMP(1);
 
@@ -424,8 +433,15 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
         }
         __syncwarp();
     }
+    float *xown = wts + 16;   // this CTA's own rows of the raw x (<= 16), for the residual add
     for (int i = tid; i < H4; i += kFusedBlock) {
         const float4 v = lk.x_from_slot ? xin : __ldcg(x4 + i);
+        if (lk.x_from_slot) {
+            const float c[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                if (4 * i + q >= dbeg && 4 * i + q < dend && 4 * i + q - dbeg < 16) xown[4 * i + q - dbeg] = c[q];
+        }
         xn4[i] = v;   // raw x for now
         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         if (one) {
@@ -438,7 +454,7 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
     const float scale = 1.0f / sqrtf(ss / static_cast<float>(H) + p.eps);
     if (one && n_rows_mine > 0 && tid == 0) {
         const float acc = scale * red2.y;
-        st_slot(p.lgslot + b, acc, *s_tag);
+        st_slot(p.lgslot + (*s_tag & 1u) * E + b, acc, *s_tag);
         p.logits[b] = acc;   // debug view
     }
     for (int i = tid; i < H4; i += kFusedBlock) {   // same i -> thread mapping: no barrier needed
@@ -465,7 +481,7 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
             acc = fblock_sum(acc, red);
         }
         if (tid == 0) {
-            st_slot(p.lgslot + b + G * j, acc, *s_tag);
+            st_slot(p.lgslot + (*s_tag & 1u) * E + b + G * j, acc, *s_tag);
             p.logits[b + G * j] = acc;   // debug view
         }
     }
@@ -512,7 +528,7 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
             uint64_t w[kLogitRegs];
 #pragma unroll
             for (int j = 0; j < kLogitRegs; j++)
-                if (j < nper) w[j] = ld_slot(p.lgslot + min(lane + 32 * j, E - 1));
+                if (j < nper) w[j] = ld_slot(p.lgslot + (tag & 1u) * E + min(lane + 32 * j, E - 1));
 #pragma unroll
             for (int j = 0; j < kLogitRegs; j++)
                 if (j < nper) {
@@ -812,12 +828,16 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
         __syncthreads();
         STYX_STAMP(13);
         if (tid < n) {
-            float xv = p.x[dbeg + tid];
+            // the residual: the row as read from the tagged words when x came
+            // that way (written by another CTA, perhaps still draining)
+            float xv = lk.x_from_slot ? wts[16 + tid] : p.x[dbeg + tid];
             if (ok) {
                 float acc = 0.f;
                 for (int s = 0; s < k; s++) acc = __fadd_rn(acc, __fmul_rn(wts[s], dpart[s * p.rc + tid]));
                 xv = __fadd_rn(xv, acc);
-                p.x[dbeg + tid] = xv;
+                // a layer with a successor hands x on only through the tagged
+                // words; the last layer of the chain writes the caller's x
+                if (!lk.x_to_slot) p.x[dbeg + tid] = xv;
             }
             // the next layer of the launch reads the row from here (also after
             // a wait gave up, so that it does not wait for the row as well)
@@ -833,14 +853,20 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
         for (int c = 0; c < n_chunks && fine; c++) fine = mbar_wait(&full_gu[c], 0, p.err, kErrWaitFull);
         if (fine) mbar_wait(&full_d[0], 0, p.err, kErrWaitFull);
     }
+    // A chained launch that never waited on the grid dependency waits for it
+    // before it ends (long resolved by now: every CTA of the previous launch
+    // had written its x rows), so that the end of this grid still implies the
+    // end of every earlier one on the stream.
+    if (lk.index == 0 && !lk.wait_grid) pdl_wait();
 #undef STYX_STAMP
 #undef STYX_STAMP_T
 }
 
 template <int QG, int QD>
-__global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_constant__ FusedArgs pa) {
+__global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused(const __grid_constant__ FusedArgs pa,
+                                                                const __grid_constant__ LayerLink lk) {
     extern __shared__ __align__(128) uint8_t smem[];
-    load_args(smem, pa, LayerLink{0, false, false, nullptr, nullptr, nullptr});
+    load_args(smem, pa, lk);
     __syncthreads();
     fused_layer<QG, QD>(smem);
 }
@@ -855,7 +881,7 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused_layers(const __gri
         if (li) __syncthreads();   // every thread is done with the previous layer's shared memory
         const bool more = li + 1 < la.n;
         load_args(smem, la.layer[li],
-                  LayerLink{li, li > 0, more, la.xslot, more ? la.layer[li + 1].router : nullptr,
+                  LayerLink{li, li > 0, more, li == 0, la.xslot, more ? la.layer[li + 1].router : nullptr,
                             more ? la.layer[li + 1].norm_w : nullptr});
         __syncthreads();
         fused_layer<QG, QD>(smem);
@@ -866,8 +892,8 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused_layers(const __gri
 // grid-wide waits) with programmatic stream serialisation: the kernel lets
 // the next one launch at entry and waits for the previous grid before it
 // touches the workspace or x.
-template <class Kern, class Args>
-static cudaError_t launch_coop_pdl(Kern kern, const Args &a, int grid, uint32_t smem, cudaStream_t st) {
+template <class Kern, class... Args>
+static cudaError_t launch_coop_pdl(Kern kern, int grid, uint32_t smem, cudaStream_t st, const Args &...a) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     int occ = 0;
@@ -889,12 +915,13 @@ static cudaError_t launch_coop_pdl(Kern kern, const Args &a, int grid, uint32_t 
     at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kern, a);
+    return cudaLaunchKernelEx(&cfg, kern, a...);
 }
 
-cudaError_t launch_fused(const FusedArgs &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st) {
+cudaError_t launch_fused(const FusedArgs &a, const LayerLink &lk, int qg, int qd, int grid, uint32_t smem,
+                         cudaStream_t st) {
 #define STYX_FUSED_CASE(G_, D_) \
-    if (qg == G_ && qd == D_) return launch_coop_pdl(k_moe_fused<G_, D_>, a, grid, smem, st);
+    if (qg == G_ && qd == D_) return launch_coop_pdl(k_moe_fused<G_, D_>, grid, smem, st, a, lk);
     STYX_FUSED_CASE(STYX_Q4_K, STYX_Q6_K)
     STYX_FUSED_CASE(STYX_Q4_K, STYX_Q4_K)
     STYX_FUSED_CASE(STYX_Q5_K, STYX_Q6_K)
@@ -907,7 +934,7 @@ cudaError_t launch_fused(const FusedArgs &a, int qg, int qd, int grid, uint32_t 
 
 cudaError_t launch_fused_layers(const FusedLaunch &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st) {
 #define STYX_FUSED_CASE(G_, D_) \
-    if (qg == G_ && qd == D_) return launch_coop_pdl(k_moe_fused_layers<G_, D_>, a, grid, smem, st);
+    if (qg == G_ && qd == D_) return launch_coop_pdl(k_moe_fused_layers<G_, D_>, grid, smem, st, a);
     STYX_FUSED_CASE(STYX_Q4_K, STYX_Q6_K)
     STYX_FUSED_CASE(STYX_Q4_K, STYX_Q4_K)
     STYX_FUSED_CASE(STYX_Q5_K, STYX_Q6_K)
