@@ -362,6 +362,9 @@ def main() -> int:
                     help="block: one styx_moe_block call per layer (the fastest on B200); layers: every MoE "
                          "layer of a token in one persistent launch (STYX_OPT_MOE_LAYERS 1); chain: one launch "
                          "per layer without the grid-dependency wait, x passed as tagged words (2)")
+    ap.add_argument("--shared-device", action="store_true",
+                    help="cooperative launches (the library default); without it the bench, which owns its "
+                         "GPU, sets STYX_OPT_EXCLUSIVE and the single kernel is a plain launch")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--no-cpu", action="store_true")
@@ -404,6 +407,7 @@ def main() -> int:
     stream = torch.cuda.Stream(device=dev)
 
     blk.ctx.set_option(_lib.OPT_MOE_LAYERS, {"block": 0, "layers": 1, "chain": 2}[args.launch])
+    blk.ctx.set_option(_lib.OPT_EXCLUSIVE, 0 if args.shared_device else 1)
 
     def moe_layers():
         if args.launch != "block":
@@ -527,7 +531,9 @@ def main() -> int:
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8-dp4a/f32 (q4_K,q6_K weights)", "data": "synthetic",
-            "config": dict(workload_config(world), kernels=kernel_path),
+            "config": dict(workload_config(world), kernels=kernel_path,
+                           launch="cooperative" if args.shared_device else
+                           "plain (STYX_OPT_EXCLUSIVE: the bench owns its GPU)"),
             "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": H * 4,
                     "d2h_bytes_per_step": H * 4 + L * 256, "wall_s": t_wall},
             "gpu_launches": args.steps * launches_per_token,

@@ -23,7 +23,7 @@ BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
 SKIP = 0xFFFFFFFF
 IDS_PER_LAYER = 64
 MEM_DEVICE, MEM_HOST = 0, 1
-OPT_MOE_KERNELS, OPT_MOE_LAST_PATH, OPT_TRACE, OPT_MOE_LAYERS = 1, 2, 3, 4
+OPT_MOE_KERNELS, OPT_MOE_LAST_PATH, OPT_TRACE, OPT_MOE_LAYERS, OPT_EXCLUSIVE = 1, 2, 3, 4, 5
 MOE_AUTO, MOE_FUSED, MOE_SPLIT = 0, 1, 2
 
 

@@ -24,6 +24,7 @@ struct styx_ctx {
     int last_path = 0;      // STYX_OPT_MOE_LAST_PATH
     int trace = 0;          // STYX_OPT_TRACE
     int moe_layers = 0;     // STYX_OPT_MOE_LAYERS
+    int exclusive = 0;      // STYX_OPT_EXCLUSIVE
 };
 
 namespace {
@@ -350,6 +351,9 @@ int styx_set_option(styx_ctx *ctx, int option, int64_t value) {
         NEED(value >= 0 && value <= 2, "STYX_OPT_MOE_LAYERS: 0, 1 or 2");
         ctx->moe_layers = static_cast<int>(value);
         return STYX_OK;
+    case STYX_OPT_EXCLUSIVE:
+        ctx->exclusive = value ? 1 : 0;
+        return STYX_OK;
     default: return fail(STYX_EINVAL, "unknown or read-only option %d", option);
     }
 }
@@ -361,6 +365,7 @@ int styx_get_option(styx_ctx *ctx, int option, int64_t *value) {
     case STYX_OPT_MOE_LAST_PATH: *value = ctx->last_path; return STYX_OK;
     case STYX_OPT_TRACE: *value = ctx->trace; return STYX_OK;
     case STYX_OPT_MOE_LAYERS: *value = ctx->moe_layers; return STYX_OK;
+    case STYX_OPT_EXCLUSIVE: *value = ctx->exclusive; return STYX_OK;
     default: return fail(STYX_EINVAL, "unknown option %d", option);
     }
 }
@@ -1025,7 +1030,8 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
             NEED(!ctx->trace || ctx->sm_count <= static_cast<int>(kTraceCtas), "too many CTAs to trace");
             fill_fused(fa, ctx, *dims, *lw, x, ids64, wts, ws, L);
             const styx::LayerLink alone{0, false, false, true, nullptr, nullptr, nullptr};
-            CK(styx::launch_fused(fa, alone, lw->gate.qtype, lw->down.qtype, ctx->sm_count, smem, st));
+            CK(styx::launch_fused(fa, alone, lw->gate.qtype, lw->down.qtype, ctx->sm_count, smem, !ctx->exclusive,
+                                  st));
             ctx->last_path = 1;
             return STYX_OK;
         }
@@ -1074,7 +1080,8 @@ int styx_moe_blocks(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims
             const bool more = i + 1 < n_layers;
             const styx::LayerLink lk{0, i > 0, more, i == 0, xslot, more ? layers[i + 1].router : nullptr,
                                      more ? layers[i + 1].ffn_norm : nullptr};
-            CK(styx::launch_fused(plan, lk, li.gate.qtype, li.down.qtype, ctx->sm_count, smem, st));
+            CK(styx::launch_fused(plan, lk, li.gate.qtype, li.down.qtype, ctx->sm_count, smem, !ctx->exclusive,
+                                  st));
         }
         ctx->last_path = 5;
         return STYX_OK;
@@ -1104,7 +1111,7 @@ int styx_moe_blocks(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims
             fill_fused(la.layer[j], ctx, *dims, layers[i], x,
                        ids + static_cast<size_t>(first_layer + i) * STYX_IDS_PER_LAYER, wts_of(i), ws, L);
         }
-        CK(styx::launch_fused_layers(la, l0.gate.qtype, l0.down.qtype, ctx->sm_count, smem, st));
+        CK(styx::launch_fused_layers(la, l0.gate.qtype, l0.down.qtype, ctx->sm_count, smem, !ctx->exclusive, st));
     }
     ctx->last_path = 4;
     return STYX_OK;

@@ -169,9 +169,12 @@ cudaError_t launch_synth_f32(float *dst, uint64_t n, uint64_t seed, uint64_t off
 // leaves `msg` for styx_last_error() and returns `code` (api.cu)
 int set_error(int code, const char *msg);
 
+// coop: a cooperative launch; false when the caller promised the device to
+// itself (STYX_OPT_EXCLUSIVE)
 cudaError_t launch_fused(const FusedArgs &a, const LayerLink &lk, int qg, int qd, int grid, uint32_t smem,
-                         cudaStream_t st);
-cudaError_t launch_fused_layers(const FusedLaunch &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st);
+                         bool coop, cudaStream_t st);
+cudaError_t launch_fused_layers(const FusedLaunch &a, int qg, int qd, int grid, uint32_t smem, bool coop,
+                                cudaStream_t st);
 bool fused_supported(int qg, int qd);
 int fused_block_threads();
 constexpr uint32_t kFusedHeader = 1792;

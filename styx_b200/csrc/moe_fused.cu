@@ -888,12 +888,18 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused_layers(const __gri
     }
 }
 
-// Cooperative launch (every CTA co-resident: the tagged-slot reads are
-// grid-wide waits) with programmatic stream serialisation: the kernel lets
-// the next one launch at entry and waits for the previous grid before it
-// touches the workspace or x.
+// Launch with programmatic stream serialisation: the kernel lets the next
+// one launch at entry and waits for the previous grid before it touches the
+// workspace or x.  Every CTA must be resident at once (the tagged-slot reads
+// are grid-wide waits): `coop` asks the driver for that (a cooperative
+// launch); without it, co-residency follows from the grid being one CTA per
+// SM on a device nothing else is using (the caller's promise,
+// STYX_OPT_EXCLUSIVE), which lets each CTA start as soon as its SM is free
+// instead of when the whole grid fits -- about 0.7 us per launch on B200.
+// Either way a wait that cannot finish gives up after about a second.
 template <class Kern, class... Args>
-static cudaError_t launch_coop_pdl(Kern kern, int grid, uint32_t smem, cudaStream_t st, const Args &...a) {
+static cudaError_t launch_coop_pdl(Kern kern, bool coop, int grid, uint32_t smem, cudaStream_t st,
+                                   const Args &...a) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     int occ = 0;
@@ -909,19 +915,19 @@ static cudaError_t launch_coop_pdl(Kern kern, int grid, uint32_t smem, cudaStrea
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeCooperative;
-    at[0].val.cooperative = 1;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    at[1].id = cudaLaunchAttributeCooperative;
+    at[1].val.cooperative = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 2;
+    cfg.numAttrs = coop ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, a...);
 }
 
 cudaError_t launch_fused(const FusedArgs &a, const LayerLink &lk, int qg, int qd, int grid, uint32_t smem,
-                         cudaStream_t st) {
+                         bool coop, cudaStream_t st) {
 #define STYX_FUSED_CASE(G_, D_) \
-    if (qg == G_ && qd == D_) return launch_coop_pdl(k_moe_fused<G_, D_>, grid, smem, st, a, lk);
+    if (qg == G_ && qd == D_) return launch_coop_pdl(k_moe_fused<G_, D_>, coop, grid, smem, st, a, lk);
     STYX_FUSED_CASE(STYX_Q4_K, STYX_Q6_K)
     STYX_FUSED_CASE(STYX_Q4_K, STYX_Q4_K)
     STYX_FUSED_CASE(STYX_Q5_K, STYX_Q6_K)
@@ -932,9 +938,10 @@ cudaError_t launch_fused(const FusedArgs &a, const LayerLink &lk, int qg, int qd
     return cudaErrorNotSupported;
 }
 
-cudaError_t launch_fused_layers(const FusedLaunch &a, int qg, int qd, int grid, uint32_t smem, cudaStream_t st) {
+cudaError_t launch_fused_layers(const FusedLaunch &a, int qg, int qd, int grid, uint32_t smem, bool coop,
+                                cudaStream_t st) {
 #define STYX_FUSED_CASE(G_, D_) \
-    if (qg == G_ && qd == D_) return launch_coop_pdl(k_moe_fused_layers<G_, D_>, grid, smem, st, a);
+    if (qg == G_ && qd == D_) return launch_coop_pdl(k_moe_fused_layers<G_, D_>, coop, grid, smem, st, a);
     STYX_FUSED_CASE(STYX_Q4_K, STYX_Q6_K)
     STYX_FUSED_CASE(STYX_Q4_K, STYX_Q4_K)
     STYX_FUSED_CASE(STYX_Q5_K, STYX_Q6_K)

@@ -37,7 +37,7 @@ def rel_to_max(got, exp):
     return float(np.max(np.abs(got - exp)) / max(np.max(np.abs(exp)), 1e-30))
 
 
-def run_both(cases, first_layer=0, reps=2, mode=PERSISTENT):
+def run_both(cases, first_layer=0, reps=2, mode=PERSISTENT, exclusive=0):
     lws = [upload(c) for c in cases]
     c0 = cases[0]
     n, k = len(cases), c0.k
@@ -46,20 +46,23 @@ def run_both(cases, first_layer=0, reps=2, mode=PERSISTENT):
     many.ctx.set_option(_lib.OPT_MOE_LAYERS, mode)   # (the blocks of a device share one context)
     total = first_layer + n
     try:
-        return _run_both(cases, first_layer, reps, lws, c0, n, k, one, many, total)
+        return _run_both(cases, first_layer, reps, lws, c0, n, k, one, many, total, exclusive)
     finally:
         many.ctx.set_option(_lib.OPT_MOE_LAYERS, 0)
+        many.ctx.set_option(_lib.OPT_EXCLUSIVE, 0)
 
 
-def _run_both(cases, first_layer, reps, lws, c0, n, k, one, many, total):
+def _run_both(cases, first_layer, reps, lws, c0, n, k, one, many, total, exclusive):
     for rep in range(reps):   # twice: the launch counter keeps counting on the same workspaces
         xa, xb = T(c0.x), T(c0.x)
         ia = torch.full((total * 64,), -7, dtype=torch.int32, device=DEV)
         ib = ia.clone()
         wa = torch.zeros(n * k, dtype=torch.float32, device=DEV)
         wb = torch.zeros_like(wa)
+        many.ctx.set_option(_lib.OPT_EXCLUSIVE, 0)   # the reference: cooperative launches
         for i, lw in enumerate(lws):
             one.forward(xa, lw, first_layer + i, ia, weights_out=wa[i * k:(i + 1) * k])
+        many.ctx.set_option(_lib.OPT_EXCLUSIVE, exclusive)
         many.forward_layers(xb, lws, first_layer, ib, weights_out=wb)
         torch.cuda.synchronize()
         one.ctx.check_device_error()
@@ -78,6 +81,15 @@ def test_linked_layers_equal_one_call_per_layer_and_the_oracle(mode):
     for c in cases:
         xr = oracle_block(dataclasses.replace(c, x=xr))["x"]
     assert rel_to_max(x.cpu().numpy(), xr) < 1e-4
+
+
+@pytest.mark.parametrize("mode", [SEPARATE, PERSISTENT, CHAIN], ids=["separate", "persistent", "chain"])
+def test_plain_launches_equal_cooperative_ones(mode):
+    """STYX_OPT_EXCLUSIVE: the same kernels launched without the cooperative
+    attribute give the same bits."""
+    cases = [make_case(150 + l, 2048, 768, 128, 8, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K)) for l in range(3)]
+    many, _, _ = run_both(cases, mode=mode, exclusive=1)
+    assert many.ctx.last_moe_path() == PATH[mode]
 
 
 @MODES

@@ -7,7 +7,8 @@ waits for logit words and h arrivals the other half never provides.  Every
 such wait gives up after about a second, records its code in the device
 error word and lets the kernel finish (no fault, every access in bounds);
 the host then sees STYX_ETIMEOUT, and after styx_moe_workspace_init the next
-call is correct again.
+call is correct again.  The same with STYX_OPT_EXCLUSIVE (a plain launch
+instead of a cooperative one).
 """
 import ctypes as C
 
@@ -28,7 +29,8 @@ def _t(a):
     return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
 
 
-def test_split_launch_numbers_time_out_and_recover():
+@pytest.mark.parametrize("exclusive", [0, 1], ids=["cooperative", "exclusive"])
+def test_split_launch_numbers_time_out_and_recover(exclusive):
     c = make_case(81, 1024, 512, 16, 4, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K))
     sg, su, sd = c.slabs
     lw = ops.LayerWeights(ffn_norm=_t(c.norm), router=_t(c.router),
@@ -36,6 +38,7 @@ def test_split_launch_numbers_time_out_and_recover():
                           down=ops.Experts(c.qts[2], _t(c.down), sd))
     blk = ops.MoeBlock(ops.Dims(c.H, c.F, c.E, c.k), 0)
     blk.ctx.set_moe_kernels(_lib.MOE_FUSED)
+    blk.ctx.set_option(_lib.OPT_EXCLUSIVE, exclusive)
     try:
         blk.ctx.check_device_error()          # start clean
         grid = blk.ctx.sm_count
@@ -66,3 +69,4 @@ def test_split_launch_numbers_time_out_and_recover():
         assert np.max(np.abs(got - ref["x"])) <= 1e-3 * np.max(np.abs(ref["x"]))
     finally:
         blk.ctx.set_moe_kernels(_lib.MOE_AUTO)
+        blk.ctx.set_option(_lib.OPT_EXCLUSIVE, 0)
