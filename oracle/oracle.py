@@ -54,6 +54,10 @@ def lib():
                                     vp, vp, vp, vp, vp, vp, vp, vp, vp]),
             "or_moe_block_mt": (None, [vp, f, vp, i, i, i, i, i, i, i, i, vp, vp,
                                        vp, vp, i]),
+            "or_rope_neox": (None, [vp, i, i, i, f, vp]),
+            "or_attn_decode": (None, [vp, vp, vp, vp, i, i, i, i, i, f]),
+            "or_attn_block": (None, [vp, vp, f, i, i, i, i, i, vp, vp, f, i, vp, i, vp, i, vp, i, vp, i, vp,
+                                     vp]),
             "or_f16_to_f32": (f, [C.c_uint16]),
             "or_f32_to_f16": (C.c_uint16, [f]),
         }
@@ -228,3 +232,35 @@ def clamp_f16_exponents(raw: np.ndarray, qtype: int) -> None:
     his = {Q8_0: [1], Q4_K: [1, 3], Q5_K: [1, 3], Q6_K: [209]}[qtype]
     for h in his:
         v[:, h] = (v[:, h] & 0x83) | 0x30
+
+
+# ------------------------------------------------------------ attention half of a decode layer
+def rope_neox(x, head_dim, n_heads, n_tokens, freq_base, pos):
+    """rope_neox_f32 in the reference test's CPU form (ops2.rs:425-440); returns a copy."""
+    x = np.array(x, dtype=np.float32, copy=True)
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    lib().or_rope_neox(_p(x), head_dim, n_heads, n_tokens, freq_base, _p(pos))
+    return x
+
+
+def attn_decode(q, kcache, vcache, n_heads, n_t, hd, kv_dim, gqa, scale):
+    """shaders/attn_decode_f32.comp restated (every q head)."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    kcache = np.ascontiguousarray(kcache, dtype=np.float32)
+    vcache = np.ascontiguousarray(vcache, dtype=np.float32)
+    out = np.zeros(n_heads * hd, dtype=np.float32)
+    lib().or_attn_decode(_p(q), _p(kcache), _p(vcache), _p(out), n_heads, n_t, hd, kv_dim, gqa, scale)
+    return out
+
+
+def attn_block(x, attn_norm, eps, n_heads, n_kv, hd, q_norm, k_norm, rope_base, weights, pos, kcache, vcache):
+    """One layer's attention half (moe.rs:1857-1972); weights = [(qtype, raw)] for q, k, v, o.
+    Returns the new x; kcache / vcache (numpy, [n_ctx][kv_dim]) get row pos."""
+    x = np.array(x, dtype=np.float32, copy=True)
+    an = np.ascontiguousarray(attn_norm, dtype=np.float32)
+    qn = None if q_norm is None else np.ascontiguousarray(q_norm, dtype=np.float32)
+    kn = None if k_norm is None else np.ascontiguousarray(k_norm, dtype=np.float32)
+    (qq, wq), (qk, wk), (qv, wv), (qo, wo) = [(t, np.ascontiguousarray(w)) for t, w in weights]
+    lib().or_attn_block(_p(x), _p(an), eps, x.size, n_heads, n_kv, hd, int(q_norm is not None), _p(qn), _p(kn),
+                        rope_base, qq, _p(wq), qk, _p(wk), qv, _p(wv), qo, _p(wo), pos, _p(kcache), _p(vcache))
+    return x

@@ -34,6 +34,16 @@ GLSL_BUILTINS
 #include "gather_slabs_f32.inc"
 }  // namespace ref_gather
 
+namespace ref_attn {
+GLSL_BUILTINS
+#include "attn_decode_f32.inc"
+}  // namespace ref_attn
+
+namespace ref_add {
+GLSL_BUILTINS
+#include "add_flat_f32.inc"
+}  // namespace ref_add
+
 extern "C" {
 
 // matvec_strided_f32 dispatched as moe.rs:1984-1996: push {ncols, stride_a},
@@ -120,6 +130,47 @@ void ref_gather_slabs_f32(const void *gate, const void *up, const void *down, vo
         for (uint l = 0; l < 256; l++) {
             glsl_lid = l;
             ref_gather::main();
+        }
+    }
+}
+
+// attn_decode_f32 dispatched as moe.rs:1946-1964: push {n_t, hd, kv_dim,
+// gqa, scale}, groups (n_heads, 1, 1), 128 invocations with barriers.
+void ref_attn_decode_f32(const float *q, const float *k, const float *v, float *o, uint n_heads, uint n_t, uint hd,
+                         uint kv_dim, uint gqa, float scale) {
+    ref_attn::data_q = const_cast<float *>(q);
+    ref_attn::data_k = const_cast<float *>(k);
+    ref_attn::data_v = const_cast<float *>(v);
+    ref_attn::data_o = o;
+    ref_attn::p.n_t = n_t;
+    ref_attn::p.hd = hd;
+    ref_attn::p.kv_dim = kv_dim;
+    ref_attn::p.gqa = gqa;
+    ref_attn::p.scale = scale;
+    glsl_local_size = 128;
+    omp_set_dynamic(0);
+    for (uint wg = 0; wg < n_heads; wg++) {
+        glsl_wgid = wg;
+#pragma omp parallel num_threads(128)
+        {
+            glsl_lid = static_cast<uint>(omp_get_thread_num());
+            ref_attn::main();
+        }
+    }
+}
+
+// add_flat_f32 (rec_add, moe.rs:1972): push {n}, groups ceil(n/256).
+void ref_add_flat_f32(const float *a, const float *b, float *d, uint n) {
+    ref_add::data_a = const_cast<float *>(a);
+    ref_add::data_b = const_cast<float *>(b);
+    ref_add::data_d = d;
+    ref_add::p.n = n;
+    glsl_local_size = 256;
+    for (uint wg = 0; wg < (n + 255) / 256; wg++) {
+        glsl_wgid = wg;
+        for (uint l = 0; l < 256; l++) {
+            glsl_lid = l;
+            ref_add::main();
         }
     }
 }

@@ -7,7 +7,7 @@ REF ?= /root/reference
 HERE := $(dir $(abspath $(lastword $(MAKEFILE_LIST))))
 OUT := $(HERE)_ref
 CXX := $(firstword $(wildcard /usr/bin/g++) g++)
-SHADERS := matvec_strided_f32 topk_softmax_f32 moe_reduce_f32 gather_slabs_f32
+SHADERS := matvec_strided_f32 topk_softmax_f32 moe_reduce_f32 gather_slabs_f32 attn_decode_f32 add_flat_f32
 INCS := $(addprefix $(OUT)/,$(addsuffix .inc,$(SHADERS)))
 
 all: $(OUT)/libref_glsl.so

@@ -17,6 +17,7 @@
 #include "styx_oracle.h"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 #ifdef _OPENMP
 #include <omp.h>
@@ -609,4 +610,90 @@ void or_moe_block_mt(const float *ffn_norm, float eps, const float *router,
     moe_block_impl(ffn_norm, eps, router, E, H, F, k, renorm, qt_gate, qt_up,
                    qt_down, gate, up, down, NULL, NULL, x, NULL, NULL, NULL,
                    NULL, NULL, NULL, nthreads < 1 ? 1 : nthreads);
+}
+
+/* ------------------------------------------------------------------ attention half */
+
+void or_rope_neox(float *x, int head_dim, int n_heads, int n_tokens,
+                  float freq_base, const int32_t *pos) {
+    const int half = head_dim / 2;
+    const double theta_scale = pow((double)freq_base, -2.0 / (double)head_dim);
+    for (int t = 0; t < n_tokens; t++)
+        for (int h = 0; h < n_heads; h++) {
+            float *b = x + ((size_t)t * n_heads + h) * head_dim;
+            for (int i = 0; i < half; i++) {
+                const double theta = (double)pos[t] * pow(theta_scale, (double)i);
+                const double s = sin(theta), c = cos(theta);
+                const double x0 = b[i], x1 = b[i + half];
+                b[i] = (float)(x0 * c - x1 * s);
+                b[i + half] = (float)(x0 * s + x1 * c);
+            }
+        }
+}
+
+void or_attn_decode(const float *q, const float *kcache, const float *vcache,
+                    float *out, int n_heads, int n_t, int hd, int kv_dim,
+                    int gqa, float scale) {
+    float acc0[128], acc1[128], red[128];
+    for (int h = 0; h < n_heads; h++) {
+        const int kvoff = (h / gqa) * hd, qbase = h * hd;
+        for (int tid = 0; tid < 128; tid++) acc0[tid] = acc1[tid] = 0.f;
+        float m = -INFINITY, l = 0.f;
+        for (int t = 0; t < n_t; t++) {
+            const float *kr = kcache + (size_t)t * kv_dim + kvoff;
+            for (int tid = 0; tid < 128; tid++) {
+                float part = 0.f;
+                for (int i = tid; i < hd; i += 128) part += q[qbase + i] * kr[i];
+                red[tid] = part;
+            }
+            for (int s = 64; s > 0; s >>= 1)
+                for (int tid = 0; tid < s; tid++) red[tid] += red[tid + s];
+            const float sc = red[0] * scale;
+            const float m_new = glsl_max(m, sc);
+            const float corr = expf(m - m_new);
+            const float pr = expf(sc - m_new);
+            l = l * corr + pr;
+            m = m_new;
+            const float *vr = vcache + (size_t)t * kv_dim + kvoff;
+            for (int tid = 0; tid < 128; tid++) {
+                if (tid < hd) acc0[tid] = acc0[tid] * corr + pr * vr[tid];
+                if (tid + 128 < hd) acc1[tid] = acc1[tid] * corr + pr * vr[tid + 128];
+            }
+        }
+        /* 1.0 / l: a float division in GLSL (double-then-float rounds the same) */
+        const float inv_l = 1.0f / l;
+        for (int tid = 0; tid < 128; tid++) {
+            if (tid < hd) out[qbase + tid] = acc0[tid] * inv_l;
+            if (tid + 128 < hd) out[qbase + tid + 128] = acc1[tid] * inv_l;
+        }
+    }
+}
+
+void or_attn_block(float *x, const float *attn_norm, float eps, int H,
+                   int n_heads, int n_kv, int hd, int qk_norm,
+                   const float *q_norm, const float *k_norm, float rope_base,
+                   int qt_q, const uint8_t *wq, int qt_k, const uint8_t *wk,
+                   int qt_v, const uint8_t *wv, int qt_o, const uint8_t *wo,
+                   int pos, float *kcache, float *vcache) {
+    const int qd = n_heads * hd, kvd = n_kv * hd;
+    float *xn = (float *)malloc(sizeof(float) * (size_t)(H + 2 * qd + 2 * kvd + H));
+    float *q = xn + H, *k = q + qd, *v = k + kvd, *att = v + kvd, *proj = att + qd;
+    or_rms_norm(x, attn_norm, H, eps, xn);                       /* moe.rs:1857-1864 */
+    or_matvec_q(qt_q, wq, qd, H, xn, q);                         /* :1865-1885 */
+    or_matvec_q(qt_k, wk, kvd, H, xn, k);
+    or_matvec_q(qt_v, wv, kvd, H, xn, v);
+    if (qk_norm) {                                               /* :1886-1897 */
+        for (int h = 0; h < n_heads; h++) or_rms_norm(q + h * hd, q_norm, hd, eps, q + h * hd);
+        for (int h = 0; h < n_kv; h++) or_rms_norm(k + h * hd, k_norm, hd, eps, k + h * hd);
+    }
+    const int32_t p32 = pos;
+    or_rope_neox(q, hd, n_heads, 1, rope_base, &p32);            /* :1914-1932 */
+    or_rope_neox(k, hd, n_kv, 1, rope_base, &p32);
+    memcpy(kcache + (size_t)pos * kvd, k, sizeof(float) * (size_t)kvd);   /* :1933-1945 */
+    memcpy(vcache + (size_t)pos * kvd, v, sizeof(float) * (size_t)kvd);
+    or_attn_decode(q, kcache, vcache, att, n_heads, pos + 1, hd, kvd, n_heads / n_kv,
+                   1.0f / sqrtf((float)hd));                     /* :1946-1964 */
+    or_matvec_q(qt_o, wo, H, qd, att, proj);                     /* :1965-1971 */
+    for (int i = 0; i < H; i++) x[i] = x[i] + proj[i];          /* :1972 */
+    free(xn);
 }

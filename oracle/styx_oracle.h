@@ -106,6 +106,31 @@ void or_moe_block_mt(const float *ffn_norm, float eps, const float *router,
                      const uint8_t *up, const uint8_t *down, float *x,
                      int nthreads);
 
+/* ---- the attention half of a decode layer (moe.rs:1845-1972) ---- */
+
+/* rope_neox_f32 as crates/vk-backend/tests/ops2.rs:425-440 computes it on the
+ * CPU: x f32[n_tokens][n_heads][head_dim] in place, pairs (i, i + hd/2),
+ * theta = pos[t] * (freq_base^(-2/hd))^i, all in double. */
+void or_rope_neox(float *x, int head_dim, int n_heads, int n_tokens,
+                  float freq_base, const int32_t *pos);
+
+/* shaders/attn_decode_f32.comp:29-75 for every q head: 128 invocations,
+ * strided partial dots reduced by the shared tree s = 64..1, the online
+ * softmax update per token, acc = acc*corr + pr*v, out = acc * (1/l). */
+void or_attn_decode(const float *q, const float *kcache, const float *vcache,
+                    float *out, int n_heads, int n_t, int hd, int kv_dim,
+                    int gqa, float scale);
+
+/* One layer's attention half (moe.rs:1857-1972) for the token at pos:
+ * xn = rms(x)*attn_norm; q,k,v = W xn; per-head rms of q and k (when
+ * q_norm); RoPE; K/V cache row pos; attention over pos+1 rows; x += Wo att. */
+void or_attn_block(float *x, const float *attn_norm, float eps, int H,
+                   int n_heads, int n_kv, int hd, int qk_norm,
+                   const float *q_norm, const float *k_norm, float rope_base,
+                   int qt_q, const uint8_t *wq, int qt_k, const uint8_t *wk,
+                   int qt_v, const uint8_t *wv, int qt_o, const uint8_t *wo,
+                   int pos, float *kcache, float *vcache);
+
 #ifdef __cplusplus
 }
 #endif

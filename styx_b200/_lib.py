@@ -1,5 +1,5 @@
 """ctypes binding of libstyx_moe.so (include/styx_moe.h, include/styx_residency.h,
-include/styx_gguf.h).
+include/styx_gguf.h, include/styx_attn.h).
 
 There is no fallback: if the library is missing, importing the ops raises.
 """
@@ -13,7 +13,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libstyx_moe.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 HEADER = os.path.join(INCLUDE, "styx_moe.h")
-HEADERS = [HEADER, os.path.join(INCLUDE, "styx_residency.h"), os.path.join(INCLUDE, "styx_gguf.h")]
+HEADERS = [HEADER, os.path.join(INCLUDE, "styx_residency.h"), os.path.join(INCLUDE, "styx_gguf.h"),
+           os.path.join(INCLUDE, "styx_attn.h")]
 
 STYX_OK, STYX_EINVAL, STYX_ECUDA, STYX_ENOMEM, STYX_ETIMEOUT, STYX_EUNSUPPORTED = 0, -1, -2, -3, -4, -5
 STYX_EIO, STYX_EEOF, STYX_EDATA = -6, -7, -8
@@ -58,6 +59,20 @@ class RepinSwap(C.Structure):
 class MoeDims(C.Structure):
     _fields_ = [("n_embd", C.c_int32), ("n_ff", C.c_int32), ("n_expert", C.c_int32),
                 ("n_expert_used", C.c_int32), ("norm_topk", C.c_int32), ("rms_eps", C.c_float)]
+
+
+class DenseTensor(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("qtype", C.c_int32)]
+
+
+class AttnDims(C.Structure):
+    _fields_ = [("n_embd", C.c_int32), ("n_heads", C.c_int32), ("n_kv_heads", C.c_int32),
+                ("head_dim", C.c_int32), ("qk_norm", C.c_int32), ("rms_eps", C.c_float), ("rope_base", C.c_float)]
+
+
+class AttnLayer(C.Structure):
+    _fields_ = [("attn_norm", C.c_void_p), ("wq", DenseTensor), ("wk", DenseTensor), ("wv", DenseTensor),
+                ("wo", DenseTensor), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p)]
 
 
 _vp, _i, _f, _u64 = C.c_void_p, C.c_int, C.c_float, C.c_uint64
@@ -145,6 +160,16 @@ _SIGS = {
     "styx_gguf_tensor_bytes": (_i, [C.c_uint32, C.POINTER(_u64), C.c_uint32, C.POINTER(_u64)]),
     "styx_synth_quant": (_i, [_vp, _vp, _i, _vp, _u64, _i, _u64, _f]),
     "styx_synth_f32": (_i, [_vp, _vp, _vp, _u64, _u64, _u64, _f]),
+    # include/styx_attn.h
+    "styx_mul_mat_vec": (_i, [_vp, _vp, _i, _vp, _i, _i, _vp, _vp]),
+    "styx_add_f32": (_i, [_vp, _vp, _vp, _vp, _vp, _i]),
+    "styx_qk_norm_rope_kv": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _f, _vp, _vp, _vp, _i]),
+    "styx_rope_neox": (_i, [_vp, _vp, _vp, _i, _i, _i, _f, _vp]),
+    "styx_attn_workspace_bytes": (_i, [_i, _i, C.POINTER(_u64)]),
+    "styx_attn_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp, _u64]),
+    "styx_attn_block_workspace_bytes": (_i, [C.POINTER(AttnDims), C.POINTER(_u64)]),
+    "styx_attn_block": (_i, [_vp, _vp, C.POINTER(AttnDims), C.POINTER(AttnLayer), _vp, _i, _vp, _vp, _vp, _i,
+                             _vp, _u64]),
 }
 
 _lib = None

@@ -25,7 +25,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
           f"-I{os.path.join(ROOT, 'include')}", "--expt-relaxed-constexpr"]
 # per-source extra flags: the synthetic quantiser must round like the C oracle
 EXTRA = {"synth.cu": ["-fmad=false"]}
-SOURCES = ["moe_kernels.cu", "moe_fused.cu", "synth.cu", "api.cu", "residency.cpp", "gguf.cpp"]
+SOURCES = ["moe_kernels.cu", "moe_fused.cu", "attn.cu", "synth.cu", "api.cu", "residency.cpp", "gguf.cpp"]
 HEADERS = ["common.cuh", "qdot.cuh", "kernels.h"]
 
 
@@ -46,7 +46,8 @@ def _stale(target: str, deps: list[str]) -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(OUT_DIR, exist_ok=True)
     hdrs = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", h)
-                                                         for h in ("styx_moe.h", "styx_residency.h", "styx_gguf.h")]
+                                                         for h in ("styx_moe.h", "styx_residency.h", "styx_gguf.h",
+                                                                   "styx_attn.h")]
     objs = []
     for src in SOURCES:
         sp = os.path.join(CSRC, src)

@@ -12,6 +12,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "../../include/styx_attn.h"
 #include "../../include/styx_moe.h"
 #include "kernels.h"
 
@@ -19,7 +20,7 @@ struct styx_ctx {
     int device = 0;
     int sm_count = 0;
     char name[256] = {0};
-    int *d_err = nullptr;   // device error word of bounded waits
+    int *d_err = nullptr;   // device error word of bounded waits; d_err[4..7]: zeros (a one-expert id row)
     int moe_kernels = 0;    // STYX_OPT_MOE_KERNELS
     int last_path = 0;      // STYX_OPT_MOE_LAST_PATH
     int trace = 0;          // STYX_OPT_TRACE
@@ -290,8 +291,8 @@ int styx_init(int device, styx_ctx **out) {
     c->device = device;
     c->sm_count = prop.multiProcessorCount;
     snprintf(c->name, sizeof(c->name), "%s", prop.name);
-    cudaError_t e = cudaMalloc(&c->d_err, sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
+    cudaError_t e = cudaMalloc(&c->d_err, 8 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, 8 * sizeof(int));
     if (e != cudaSuccess) {
         delete c;
         return fail(STYX_ECUDA, "error word: %s", cudaGetErrorString(e));
@@ -332,6 +333,7 @@ int styx_check_device_error(styx_ctx *ctx, styx_stream stream) {
         CK(cudaMemsetAsync(ctx->d_err, 0, sizeof(int), S(stream)));
         CK(cudaStreamSynchronize(S(stream)));
         if (h == 4) return fail(STYX_EINVAL, "a kernel skipped an out-of-range expert id / hot index / arena slot");
+        if (h == 5) return fail(STYX_EINVAL, "a kernel skipped a KV cache row outside [0, n_ctx)");
         return fail(STYX_ETIMEOUT, "device-side bounded wait gave up (code %d)", h);
     }
     return STYX_OK;
@@ -1213,3 +1215,207 @@ int styx_synth_f32(styx_ctx *ctx, styx_stream stream, float *dst, uint64_t n, ui
 }
 
 }  // extern "C"
+
+// ------------------------------------------------ attention half of a decode layer (styx_attn.h)
+int styx_mul_mat_vec(styx_ctx *ctx, styx_stream stream, int qtype, const void *a, int nrows, int ncols,
+                     const float *x, float *y) {
+    ENTER(ctx);
+    NEED(nrows > 0, "bad nrows %d", nrows);
+    const long long rb = row_bytes(qtype, ncols);
+    NEED(rb > 0, "ncols %d not representable in qtype %d", ncols, qtype);
+    // one expert, one id row of zeros held by the context
+    return styx_mul_mat_vec_id(ctx, stream, qtype, a, static_cast<uint64_t>(rb) * nrows, 1, nrows, ncols,
+                               ctx->d_err + 4, 1, x, ncols, 1, y, nrows);
+}
+
+int styx_add_f32(styx_ctx *ctx, styx_stream stream, const float *a, const float *b, float *d, int n) {
+    ENTER(ctx);
+    NEED(a && b && d && n > 0, "bad add arguments");
+    NEED(extent_ok(a, static_cast<uint64_t>(n) * 4) && extent_ok(b, static_cast<uint64_t>(n) * 4) &&
+             extent_ok(d, static_cast<uint64_t>(n) * 4),
+         "buffer smaller than n");
+    CK(styx::launch_add_f32(a, b, d, n, S(stream)));
+    return STYX_OK;
+}
+
+int styx_qk_norm_rope_kv(styx_ctx *ctx, styx_stream stream, float *q, float *k, const float *v,
+                         const float *q_norm, const float *k_norm, float eps, int n_heads, int n_kv,
+                         int head_dim, int n_tokens, float freq_base, const int32_t *pos, float *kcache,
+                         float *vcache, int n_ctx) {
+    ENTER(ctx);
+    NEED(head_dim > 0 && head_dim % 2 == 0 && head_dim <= 256, "head_dim %d: need even, <= 256", head_dim);
+    NEED(n_heads >= 0 && n_kv >= 0 && n_heads + n_kv > 0 && n_tokens > 0, "bad head / token counts");
+    NEED(pos && (n_heads == 0 || q) && (n_kv == 0 || k), "null pointer");
+    NEED(!(kcache || vcache) || n_ctx > 0, "n_ctx %d with a cache", n_ctx);
+    NEED(!vcache || v, "vcache without v");
+    NEED(freq_base > 0.f, "freq_base must be positive");
+    const uint64_t hd = static_cast<uint64_t>(head_dim), kv_dim = hd * n_kv;
+    NEED(extent_ok(q, hd * n_heads * n_tokens * 4) && extent_ok(k, kv_dim * n_tokens * 4) &&
+             extent_ok(v, kv_dim * n_tokens * 4) && extent_ok(pos, static_cast<uint64_t>(n_tokens) * 4),
+         "q / k / v / pos smaller than their shapes");
+    NEED(extent_ok(q_norm, hd * 4) && extent_ok(k_norm, hd * 4), "q_norm / k_norm smaller than head_dim");
+    NEED(extent_ok(kcache, kv_dim * n_ctx * 4) && extent_ok(vcache, kv_dim * n_ctx * 4), "cache smaller than n_ctx rows");
+    styx::QkRopeArgs a{};
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.q_norm = n_heads ? q_norm : nullptr;
+    a.k_norm = n_kv ? k_norm : nullptr;
+    a.eps = eps;
+    a.pos = pos;
+    // RopePush::neox's theta_scale (ops.rs:428), kept in double as the
+    // reference test's CPU form evaluates it (tests/ops2.rs:427)
+    a.theta_scale = std::pow(static_cast<double>(freq_base), -2.0 / static_cast<double>(head_dim));
+    a.n_heads = n_heads;
+    a.n_kv = n_kv;
+    a.hd = head_dim;
+    a.kv_dim = static_cast<int>(kv_dim);
+    a.n_tokens = n_tokens;
+    a.n_ctx = n_ctx;
+    a.kcache = kcache;
+    a.vcache = vcache;
+    a.err = ctx->d_err;
+    CK(styx::launch_qk_norm_rope_kv(a, S(stream)));
+    return STYX_OK;
+}
+
+int styx_rope_neox(styx_ctx *ctx, styx_stream stream, float *x, int head_dim, int n_heads, int n_tokens,
+                   float freq_base, const int32_t *pos) {
+    return styx_qk_norm_rope_kv(ctx, stream, x, nullptr, nullptr, nullptr, nullptr, 0.f, n_heads, 0, head_dim,
+                                n_tokens, freq_base, pos, nullptr, nullptr, 0);
+}
+
+namespace {
+constexpr int kAttnMaxSplits = 256;
+constexpr int kAttnMinTokensPerSplit = 16;
+
+// splits of the sequence: about two CTAs per SM over the kv heads, at least
+// 16 tokens each, shared memory within the per-CTA limit
+void attn_plan(int sms, int n_kv, int gqa, int hd, int n_t, int &tps, int &n_splits) {
+    int want = std::max(1, (2 * sms + n_kv - 1) / n_kv);
+    want = std::min(want, std::max(1, (n_t + kAttnMinTokensPerSplit - 1) / kAttnMinTokensPerSplit));
+    want = std::min(want, kAttnMaxSplits);
+    tps = (n_t + want - 1) / want;
+    while (styx::attn_smem_bytes(gqa, hd, tps) > 200 * 1024 && want < kAttnMaxSplits) {
+        want = std::min(kAttnMaxSplits, want * 2);
+        tps = (n_t + want - 1) / want;
+    }
+    n_splits = (n_t + tps - 1) / tps;
+}
+}  // namespace
+
+int styx_attn_workspace_bytes(int n_heads, int head_dim, uint64_t *out) {
+    NEED(out && n_heads > 0 && head_dim > 0, "bad arguments");
+    *out = static_cast<uint64_t>(n_heads) * kAttnMaxSplits * (static_cast<uint64_t>(head_dim) + 2) * 4;
+    return STYX_OK;
+}
+
+int styx_attn_decode(styx_ctx *ctx, styx_stream stream, const float *q, const float *kcache,
+                     const float *vcache, float *out, int n_t, int head_dim, int kv_dim, int gqa, float scale,
+                     void *workspace, uint64_t workspace_bytes) {
+    ENTER(ctx);
+    NEED(q && kcache && vcache && out && workspace, "null pointer");
+    NEED(head_dim > 0 && head_dim % 4 == 0 && head_dim <= 256, "head_dim %d: need a multiple of 4, <= 256", head_dim);
+    NEED(kv_dim > 0 && kv_dim % head_dim == 0 && gqa > 0 && n_t > 0, "bad kv_dim / gqa / n_t");
+    NEED(al16(q) && al16(kcache) && al16(vcache) && al16(out), "q, caches and out must be 16-byte aligned");
+    const int n_kv = kv_dim / head_dim, n_heads = n_kv * gqa;
+    uint64_t need = 0;
+    styx_attn_workspace_bytes(n_heads, head_dim, &need);
+    NEED(workspace_bytes >= need && al16(workspace), "workspace: %llu bytes, 16-byte aligned, needed",
+         static_cast<unsigned long long>(need));
+    NEED(extent_ok(q, static_cast<uint64_t>(n_heads) * head_dim * 4) &&
+             extent_ok(out, static_cast<uint64_t>(n_heads) * head_dim * 4),
+         "q / out smaller than n_heads * head_dim");
+    NEED(extent_ok(kcache, static_cast<uint64_t>(n_t) * kv_dim * 4) &&
+             extent_ok(vcache, static_cast<uint64_t>(n_t) * kv_dim * 4),
+         "caches smaller than n_t rows");
+    NEED(extent_ok(workspace, need), "workspace allocation smaller than needed");
+    styx::AttnArgs a{};
+    a.q = q;
+    a.kcache = kcache;
+    a.vcache = vcache;
+    a.out = out;
+    a.n_t = n_t;
+    a.hd = head_dim;
+    a.kv_dim = kv_dim;
+    a.gqa = gqa;
+    a.n_kv = n_kv;
+    a.scale = scale;
+    attn_plan(ctx->sm_count, n_kv, gqa, head_dim, n_t, a.tps, a.n_splits);
+    NEED(styx::attn_smem_bytes(gqa, head_dim, a.tps) <= 227 * 1024, "gqa %d x head_dim %d too large", gqa, head_dim);
+    a.part_acc = static_cast<float *>(workspace);
+    a.part_ml = a.part_acc + static_cast<size_t>(n_heads) * a.n_splits * head_dim;
+    CK(styx::launch_attn_decode(a, S(stream)));
+    return STYX_OK;
+}
+
+namespace {
+struct AttnWs {
+    size_t xnorm, q, k, v, att, proj, part, total;
+};
+AttnWs attn_ws(const styx_attn_dims &d) {
+    AttnWs w{};
+    size_t o = 0;
+    auto take = [&](size_t n) {
+        const size_t r = o;
+        o = (o + n + 255) & ~size_t(255);
+        return r;
+    };
+    const size_t H = d.n_embd, qd = static_cast<size_t>(d.n_heads) * d.head_dim,
+                 kvd = static_cast<size_t>(d.n_kv_heads) * d.head_dim;
+    w.xnorm = take(H * 4);
+    w.q = take(qd * 4);
+    w.k = take(kvd * 4);
+    w.v = take(kvd * 4);
+    w.att = take(qd * 4);
+    w.proj = take(H * 4);
+    uint64_t pb = 0;
+    styx_attn_workspace_bytes(d.n_heads, d.head_dim, &pb);
+    w.part = take(pb);
+    w.total = o;
+    return w;
+}
+}  // namespace
+
+int styx_attn_block_workspace_bytes(const styx_attn_dims *dims, uint64_t *out) {
+    NEED(dims && out && dims->n_embd > 0 && dims->n_heads > 0 && dims->n_kv_heads > 0 && dims->head_dim > 0,
+         "bad dims");
+    *out = attn_ws(*dims).total;
+    return STYX_OK;
+}
+
+int styx_attn_block(styx_ctx *ctx, styx_stream stream, const styx_attn_dims *dims, const styx_attn_layer *lw,
+                    float *x, int pos, const int32_t *pos_dev, float *kcache, float *vcache, int n_ctx,
+                    void *workspace, uint64_t workspace_bytes) {
+    ENTER(ctx);
+    NEED(dims && lw && x && pos_dev && kcache && vcache && workspace, "null pointer");
+    const styx_attn_dims &d = *dims;
+    NEED(d.n_embd > 0 && d.n_heads > 0 && d.n_kv_heads > 0 && d.n_heads % d.n_kv_heads == 0,
+         "n_heads %d must be a multiple of n_kv_heads %d", d.n_heads, d.n_kv_heads);
+    NEED(d.head_dim > 0 && d.head_dim % 4 == 0 && d.head_dim <= 256, "head_dim %d", d.head_dim);
+    NEED(pos >= 0 && pos < n_ctx, "pos %d outside the caches (n_ctx %d)", pos, n_ctx);
+    NEED(lw->attn_norm && lw->wq.data && lw->wk.data && lw->wv.data && lw->wo.data, "null weight");
+    NEED(!d.qk_norm || (lw->q_norm && lw->k_norm), "qk_norm without q_norm / k_norm");
+    const AttnWs w = attn_ws(d);
+    NEED(workspace_bytes >= w.total && al16(workspace), "workspace: %llu bytes, 16-byte aligned, needed",
+         static_cast<unsigned long long>(w.total));
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    float *xn = reinterpret_cast<float *>(ws + w.xnorm), *q = reinterpret_cast<float *>(ws + w.q);
+    float *k = reinterpret_cast<float *>(ws + w.k), *v = reinterpret_cast<float *>(ws + w.v);
+    float *att = reinterpret_cast<float *>(ws + w.att), *proj = reinterpret_cast<float *>(ws + w.proj);
+    const int H = d.n_embd, hd = d.head_dim, qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
+    int rc;
+    if ((rc = styx_rms_norm(ctx, stream, x, lw->attn_norm, d.rms_eps, H, 1, xn))) return rc;
+    if ((rc = styx_mul_mat_vec(ctx, stream, lw->wq.qtype, lw->wq.data, qd, H, xn, q))) return rc;
+    if ((rc = styx_mul_mat_vec(ctx, stream, lw->wk.qtype, lw->wk.data, kvd, H, xn, k))) return rc;
+    if ((rc = styx_mul_mat_vec(ctx, stream, lw->wv.qtype, lw->wv.data, kvd, H, xn, v))) return rc;
+    if ((rc = styx_qk_norm_rope_kv(ctx, stream, q, k, v, d.qk_norm ? lw->q_norm : nullptr,
+                                   d.qk_norm ? lw->k_norm : nullptr, d.rms_eps, d.n_heads, d.n_kv_heads, hd, 1,
+                                   d.rope_base, pos_dev, kcache, vcache, n_ctx)))
+        return rc;
+    if ((rc = styx_attn_decode(ctx, stream, q, kcache, vcache, att, pos + 1, hd, kvd, d.n_heads / d.n_kv_heads,
+                               1.0f / std::sqrt(static_cast<float>(hd)), ws + w.part, workspace_bytes - w.part)))
+        return rc;
+    if ((rc = styx_mul_mat_vec(ctx, stream, lw->wo.qtype, lw->wo.data, H, qd, att, proj))) return rc;
+    return styx_add_f32(ctx, stream, x, proj, x, H);
+}

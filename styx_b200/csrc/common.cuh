@@ -26,6 +26,7 @@ enum : int {
     kErrWaitEmpty = 2,   // producer gave up waiting for a free stage
     kErrWaitRoute = 3,   // route: last-block handoff failed
     kErrBadId = 4,       // an expert id / hot index / arena slot out of range
+    kErrBadPos = 5,      // a token position outside the KV caches
 };
 
 // ~1 s at the B200's 1.9 GHz SM clock

@@ -169,6 +169,31 @@ cudaError_t launch_synth_f32(float *dst, uint64_t n, uint64_t seed, uint64_t off
 // leaves `msg` for styx_last_error() and returns `code` (api.cu)
 int set_error(int code, const char *msg);
 
+// ------------------------------------------------ attention half of a decode layer (attn.cu)
+struct QkRopeArgs {
+    float *q, *k;                  // [n_heads][hd], [n_kv][hd]: normalised and rotated in place
+    const float *v;                // [n_kv][hd]
+    const float *q_norm, *k_norm;  // [hd] or null (no per-head norm)
+    float eps;
+    const int32_t *pos;            // device: the token's position
+    double theta_scale;            // freq_base^(-2/hd)
+    int n_heads, n_kv, hd, kv_dim, n_tokens, n_ctx;
+    float *kcache, *vcache;        // [n_ctx][kv_dim] or null
+    int *err;                      // device error word (a position outside the caches)
+};
+struct AttnArgs {
+    const float *q, *kcache, *vcache;
+    float *out;
+    float *part_acc, *part_ml;     // workspace: [n_heads][n_splits][hd], [n_heads][n_splits][2]
+    int n_t, hd, kv_dim, gqa, n_kv;
+    float scale;
+    int tps, n_splits;             // tokens per split, splits
+};
+size_t attn_smem_bytes(int gqa, int hd, int tps);
+cudaError_t launch_qk_norm_rope_kv(const QkRopeArgs &a, cudaStream_t st);
+cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st);
+cudaError_t launch_add_f32(const float *x, const float *y, float *d, int n, cudaStream_t st);
+
 // coop: a cooperative launch; false when the caller promised the device to
 // itself (STYX_OPT_EXCLUSIVE)
 cudaError_t launch_fused(const FusedArgs &a, const LayerLink &lk, int qg, int qd, int grid, uint32_t smem,

@@ -433,3 +433,111 @@ class Residency:
                                     _stream(stream)))
             if stream is None:
                 torch.cuda.synchronize(remaps[l].device)
+
+
+# ------------------------------------------------------------ attention half of a decode layer
+# include/styx_attn.h: the part of forward_token before each MoE block
+# (crates/model/src/moe.rs:1845-1972).
+
+def mul_mat_vec(qtype: int, a: torch.Tensor, nrows: int, ncols: int, x: torch.Tensor,
+                y: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """y = W x for a quantised row-major W (rec_matvec_b, moe.rs:1523-1551)."""
+    if y is None:
+        y = torch.empty(nrows, dtype=torch.float32, device=x.device)
+    check(lib().styx_mul_mat_vec(ctx(_dev(x)).handle, _stream(stream), qtype, _ptr(a), nrows, ncols, _ptr(x),
+                                 _ptr(y)))
+    return y
+
+
+def add_f32(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """add_flat_f32: out = a + b (out may be a)."""
+    if out is None:
+        out = torch.empty_like(a)
+    check(lib().styx_add_f32(ctx(_dev(a)).handle, _stream(stream), _ptr(a), _ptr(b), _ptr(out), a.numel()))
+    return out
+
+
+def qk_norm_rope_kv(q: torch.Tensor, k: torch.Tensor, v: Optional[torch.Tensor], q_norm, k_norm, eps: float,
+                    n_heads: int, n_kv: int, head_dim: int, freq_base: float, pos: torch.Tensor,
+                    kcache: Optional[torch.Tensor] = None, vcache: Optional[torch.Tensor] = None,
+                    n_ctx: int = 0, n_tokens: int = 1, stream=None) -> None:
+    """Per-head q/k RMSNorm, NEOX RoPE at pos (device int32[n_tokens]) and the
+    K / V cache rows, in place (moe.rs:1880-1945)."""
+    check(lib().styx_qk_norm_rope_kv(ctx(_dev(pos)).handle, _stream(stream), _ptr(q), _ptr(k), _ptr(v),
+                                     _ptr(q_norm), _ptr(k_norm), eps, n_heads, n_kv, head_dim, n_tokens, freq_base,
+                                     _ptr(pos), _ptr(kcache), _ptr(vcache), n_ctx))
+
+
+def rope_neox(x: torch.Tensor, head_dim: int, n_heads: int, n_tokens: int, freq_base: float, pos: torch.Tensor,
+              stream=None) -> torch.Tensor:
+    """rope_neox_f32 in place over x f32[n_tokens][n_heads][head_dim]."""
+    check(lib().styx_rope_neox(ctx(_dev(x)).handle, _stream(stream), _ptr(x), head_dim, n_heads, n_tokens,
+                               freq_base, _ptr(pos)))
+    return x
+
+
+def attn_workspace_bytes(n_heads: int, head_dim: int) -> int:
+    v = C.c_uint64()
+    check(lib().styx_attn_workspace_bytes(n_heads, head_dim, C.byref(v)))
+    return v.value
+
+
+def attn_decode(q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor, n_t: int, head_dim: int,
+                kv_dim: int, gqa: int, scale: float, out: Optional[torch.Tensor] = None,
+                workspace: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """attn_decode_f32: out[h] = softmax(scale q[h].K[:n_t, h/gqa]) V[:n_t, h/gqa]."""
+    n_heads = gqa * (kv_dim // head_dim)
+    if out is None:
+        out = torch.empty(n_heads * head_dim, dtype=torch.float32, device=q.device)
+    nb = attn_workspace_bytes(n_heads, head_dim)
+    if workspace is None:
+        workspace = torch.empty(nb, dtype=torch.uint8, device=q.device)
+    check(lib().styx_attn_decode(ctx(_dev(q)).handle, _stream(stream), _ptr(q), _ptr(kcache), _ptr(vcache),
+                                 _ptr(out), n_t, head_dim, kv_dim, gqa, scale, _ptr(workspace), workspace.numel()))
+    return out
+
+
+@dataclass
+class DenseWeight:
+    qtype: int
+    data: torch.Tensor     # raw blocks, row-major
+
+    def struct(self) -> _lib.DenseTensor:
+        return _lib.DenseTensor(self.data.data_ptr(), self.qtype)
+
+
+@dataclass
+class AttnWeights:
+    attn_norm: torch.Tensor
+    wq: DenseWeight
+    wk: DenseWeight
+    wv: DenseWeight
+    wo: DenseWeight
+    q_norm: Optional[torch.Tensor] = None
+    k_norm: Optional[torch.Tensor] = None
+
+    def struct(self) -> _lib.AttnLayer:
+        return _lib.AttnLayer(self.attn_norm.data_ptr(), self.wq.struct(), self.wk.struct(), self.wv.struct(),
+                              self.wo.struct(), self.q_norm.data_ptr() if self.q_norm is not None else None,
+                              self.k_norm.data_ptr() if self.k_norm is not None else None)
+
+
+class AttnBlock:
+    """One layer's attention half (styx_attn_block) with its workspace."""
+
+    def __init__(self, n_embd: int, n_heads: int, n_kv_heads: int, head_dim: int, qk_norm: bool,
+                 rms_eps: float, rope_base: float, device: int = 0):
+        self.dims = _lib.AttnDims(n_embd, n_heads, n_kv_heads, head_dim, int(qk_norm), rms_eps, rope_base)
+        self.ctx = ctx(device)
+        v = C.c_uint64()
+        check(lib().styx_attn_block_workspace_bytes(C.byref(self.dims), C.byref(v)))
+        self.ws_bytes = v.value
+        self.workspace = torch.empty(self.ws_bytes, dtype=torch.uint8, device=f"cuda:{device}")
+
+    def forward(self, x: torch.Tensor, w: AttnWeights, pos: int, pos_dev: torch.Tensor, kcache: torch.Tensor,
+                vcache: torch.Tensor, n_ctx: int, stream=None) -> torch.Tensor:
+        st = w.struct()
+        check(lib().styx_attn_block(self.ctx.handle, _stream(stream), C.byref(self.dims), C.byref(st), _ptr(x), pos,
+                                    _ptr(pos_dev), _ptr(kcache), _ptr(vcache), n_ctx, _ptr(self.workspace),
+                                    self.ws_bytes))
+        return x

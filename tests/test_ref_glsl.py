@@ -29,6 +29,8 @@ def ref():
     L.ref_topk_softmax_f32.argtypes = [vp, vp, vp, vp, vp, u, u, u]
     L.ref_moe_reduce_f32.argtypes = [vp, vp, vp, u, u]
     L.ref_gather_slabs_f32.argtypes = [vp] * 7 + [u] * 8
+    L.ref_attn_decode_f32.argtypes = [vp, vp, vp, vp, u, u, u, u, u, C.c_float]
+    L.ref_add_flat_f32.argtypes = [vp, vp, vp, u]
     return L
 
 
@@ -107,3 +109,30 @@ def test_gather_slabs_matches_reference_shader(ref):
     O.gather_slabs(srcs, sb, a_or, db, ids, layer, k)
     for x, y in zip(a_ref, a_or):
         assert np.array_equal(x, y)
+
+
+# ------------------------------------------------------------ attention half of a decode layer
+@pytest.mark.parametrize("n_heads,n_kv,hd,n_t", [(8, 2, 128, 1), (8, 2, 128, 37), (4, 4, 64, 9),
+                                                 (6, 2, 256, 5), (32, 4, 128, 12), (2, 1, 96, 3)])
+def test_attn_decode_matches_reference_shader(ref, n_heads, n_kv, hd, n_t):
+    """attn_decode_f32.comp (one workgroup of 128 invocations per q head,
+    online softmax over the cache rows) against its C restatement, bit for bit."""
+    rng = np.random.default_rng(n_heads * 1000 + hd + n_t)
+    kv_dim, gqa = n_kv * hd, n_heads // n_kv
+    q = rng.normal(0, 1, n_heads * hd).astype(np.float32)
+    k = rng.normal(0, 1, (n_t, kv_dim)).astype(np.float32)
+    v = rng.normal(0, 1, (n_t, kv_dim)).astype(np.float32)
+    scale = np.float32(1.0 / np.sqrt(hd))
+    got = np.zeros(n_heads * hd, np.float32)
+    ref.ref_attn_decode_f32(_p(q), _p(k), _p(v), _p(got), n_heads, n_t, hd, kv_dim, gqa, float(scale))
+    exp = O.attn_decode(q, k, v, n_heads, n_t, hd, kv_dim, gqa, float(scale))
+    assert np.array_equal(bits(exp), bits(got))
+
+
+def test_add_flat_matches_reference_shader(ref):
+    rng = np.random.default_rng(5)
+    a = rng.normal(0, 1, 1000).astype(np.float32)
+    b = rng.normal(0, 1, 1000).astype(np.float32)
+    d = np.zeros_like(a)
+    ref.ref_add_flat_f32(_p(a), _p(b), _p(d), a.size)
+    assert np.array_equal(bits(d), bits(a + b))
