@@ -239,6 +239,139 @@ def build_model(dev: int, n_layers: int, unique: int = 4):
     return layers
 
 
+# ---------------------------------------------------------- whole decode step
+N_HEADS, N_KV, HD, N_VOCAB = 32, 4, 128, 151936   # Qwen3-30B-A3B attention and vocabulary
+
+
+def run_decode(args, local: int) -> int:
+    """The whole decode step at the 30B shape: embedding row, 48 x (attention
+    half + MoE block), output norm, LM head (q6_K, 151,936 rows), greedy pick,
+    with args.ctx cache rows already filled; one token recorded as a CUDA graph
+    through the C ABI and replayed, a new token id each step."""
+    import ctypes as C
+
+    import torch
+
+    from styx_b200 import _lib, ops
+    from styx_b200.decode import DecodeLayer, DecodeModel, DecodeParams
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    L, ctx = args.layers, args.ctx
+    qd, kvd = N_HEADS * HD, N_KV * HD
+    moe = build_model(local, L)
+    ones = lambda n: torch.ones(n, dtype=torch.float32, device=dev)   # noqa: E731
+    base = []
+    for u in range(min(4, L)):
+        base.append((ops.synth_quant(Q4_K, qd, H, 2000 + 4 * u, 0.02, device=local),
+                     ops.synth_quant(Q4_K, kvd, H, 2001 + 4 * u, 0.02, device=local),
+                     ops.synth_quant(Q6_K, kvd, H, 2002 + 4 * u, 0.02, device=local),
+                     ops.synth_quant(Q4_K, H, qd, 2003 + 4 * u, 0.02, device=local)))
+    layers = []
+    for li in range(L):
+        wq, wk, wv, wo = base[li] if li < len(base) else (t.clone() for t in base[li % len(base)])
+        attn = ops.AttnWeights(ones(H), ops.DenseWeight(Q4_K, wq), ops.DenseWeight(Q4_K, wk),
+                               ops.DenseWeight(Q6_K, wv), ops.DenseWeight(Q4_K, wo), q_norm=ones(HD), k_norm=ones(HD))
+        layers.append(DecodeLayer(attn, moe[li]))
+    embd = ops.DenseWeight(Q4_K, ops.synth_quant(Q4_K, N_VOCAB, H, 3000, 0.5, device=local))
+    head = ops.DenseWeight(Q6_K, ops.synth_quant(Q6_K, N_VOCAB, H, 3001, 0.02, device=local))
+    p = DecodeParams(L, H, N_HEADS, N_KV, HD, F, E, K_TOP, N_VOCAB)
+    model = DecodeModel(p, embd, layers, ones(H), head, ctx + 1, local)
+    # ctx earlier positions in every layer's caches
+    model.kcache[:, :ctx].copy_(ops.synth_f32(L * ctx * kvd, 4000, 0, 1.0, device=local).view(L, ctx, kvd))
+    model.vcache[:, :ctx].copy_(ops.synth_f32(L * ctx * kvd, 4001, 0, 1.0, device=local).view(L, ctx, kvd))
+    torch.cuda.synchronize()
+    blk_ctx = model.moe.ctx
+    blk_ctx.set_option(_lib.OPT_EXCLUSIVE, 0 if args.shared_device else 1)
+    lib, cx = _lib.lib(), blk_ctx.handle
+    stream = torch.cuda.Stream(device=dev)
+    sp = C.c_void_p(stream.cuda_stream)
+    rng = np.random.default_rng(7)
+    toks = torch.from_numpy(rng.integers(0, N_VOCAB, 4096).astype(np.int32)).to(dev)
+    model.n_past = ctx
+    with torch.cuda.stream(stream):
+        model.tok.copy_(toks[:1])
+        model.pos.fill_(ctx)
+    model.step(stream)                      # eager once
+    stream.synchronize()
+    blk_ctx.check_device_error(stream)
+    graph = C.c_void_p()
+    _lib.check(lib.styx_graph_begin(cx, sp))
+    model.step(stream)
+    _lib.check(lib.styx_graph_end(cx, sp, C.byref(graph)))
+
+    def replay(i):
+        with torch.cuda.stream(stream):
+            model.tok.copy_(toks[i % toks.numel():i % toks.numel() + 1])
+        _lib.check(lib.styx_graph_launch(cx, graph, sp))
+
+    for i in range(args.warmup):
+        replay(i)
+    stream.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            replay(i)
+        ev1.record(stream)
+        stream.synchronize()
+    el_ms = ev0.elapsed_time(ev1)
+    blk_ctx.check_device_error(stream)
+    # e2e: the token id from pinned host memory in, the greedy pick out, every step
+    hin = ops.HostBuffer(4, local)
+    hout = ops.HostBuffer(4, local)
+    n_e2e = args.e2e_steps or args.steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(n_e2e):
+        hin.tensor.view(torch.int32)[0] = int(rng.integers(0, N_VOCAB))
+        _lib.check(lib.styx_upload(cx, C.c_void_p(model.tok.data_ptr()), 0, C.c_void_p(hin.ptr), 4, sp))
+        _lib.check(lib.styx_graph_launch(cx, graph, sp))
+        _lib.check(lib.styx_download(cx, C.c_void_p(hout.ptr), C.c_void_p(model.next.data_ptr()), 0, 4, sp))
+    e1.record(stream)
+    stream.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    _lib.check(lib.styx_graph_destroy(cx, graph))
+    ms = el_ms / args.steps
+    bytes_tok = decode_bytes_per_token(L, ctx)
+    peak, peak_kind = peaks()
+    achieved = bytes_tok / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "decode tok/s (30B-A3B shape, whole decode step)", "value": 1e3 / ms, "unit": "tok/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8-dp4a/f32 (q4_K,q6_K weights)",
+        "data": "synthetic (random weights of the 30B-A3B shapes, random cache rows)",
+        "config": {"workload": f"whole decode step at the 30B-A3B shape: embedding row, {L} x (attention "
+                               f"{N_HEADS}q/{N_KV}kv x {HD} + MoE block), LM head {N_VOCAB} x {H} q6_K, greedy "
+                               f"pick; {ctx} cache rows before the token",
+                   "ctx": ctx, "l2": "inputs larger than L2 (%.2f GB read per token)" % (bytes_tok / 1e9),
+                   "launch": "cooperative" if args.shared_device else
+                   "plain (STYX_OPT_EXCLUSIVE: the bench owns its GPU)"},
+        "e2e": {"value": n_e2e / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+        # embedding; per layer rms, q, k, v, norms+RoPE+cache, attention (2), o, add, MoE; norm, head, pick
+        "gpu_launches": args.steps * (1 + L * 10 + 3),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_kind": peak_kind,
+                     "unit_of_work": "one token: %d algorithmic bytes (expert slabs, router, attention "
+                                     "weights, cache rows, LM head, embedding row)" % bytes_tok},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def decode_bytes_per_token(n_layers: int, ctx: int) -> int:
+    """Algorithmic bytes of one decode step: per layer the MoE block's bytes,
+    the attention weights (q, k, o q4_K; v q6_K), the norms and the cache
+    rows read (ctx + 1 of K and of V) and written (1 each); then the output
+    norm, the LM head (q6_K) and the embedding row (q4_K)."""
+    q4 = lambda r, c: r * (c // 256) * 144   # noqa: E731
+    q6 = lambda r, c: r * (c // 256) * 210   # noqa: E731
+    qd, kvd = N_HEADS * HD, N_KV * HD
+    attn = q4(qd, H) + q4(kvd, H) + q6(kvd, H) + q4(H, qd) + (H + 2 * HD) * 4
+    cache = 2 * (ctx + 1) * kvd * 4 + 2 * kvd * 4
+    return n_layers * (ALG_BYTES_LAYER + attn + cache) + H * 4 + q6(N_VOCAB, H) + q4(1, H)
+
+
 # ---------------------------------------------------------- cfg4 arm
 def zipf_hist(n_layers: int, n_tok: int = 4096):
     """Synthetic (layer, expert, hits) histogram: n_tok * k draws per layer
@@ -368,9 +501,11 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg4"],
+    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg4", "decode"],
                     help="cfg3: all experts in HBM (the headline); cfg4: 6 GiB HBM expert budget, the rest "
-                         "streamed from pinned host memory")
+                         "streamed from pinned host memory; decode: the whole decode step (attention + MoE "
+                         "per layer, LM head, greedy pick)")
+    ap.add_argument("--ctx", type=int, default=1024, help="decode: cache rows before the token")
     ap.add_argument("--tokens", type=int, default=256, help="cfg4: timed decode tokens")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -381,6 +516,8 @@ def main() -> int:
         return run_reference(args, rank)
     if args.workload == "cfg4":
         return run_streaming(args, local)
+    if args.workload == "decode":
+        return run_decode(args, local)
 
     import ctypes as C
 

@@ -81,6 +81,21 @@ int styx_attn_decode(styx_ctx *ctx, styx_stream stream, const float *q, const fl
                      const float *vcache, float *out, int n_t, int head_dim, int kv_dim, int gqa, float scale,
                      void *workspace, uint64_t workspace_bytes);
 
+/* ------------------------------------------------- the ends of a token */
+/* out[r] = deq(W)[rows[r]] for r < n: W row-major [nrows][ncols] of qtype
+ * (STYX_Q8_0 / Q4_K / Q5_K / Q6_K), rows a device int32[n].  The token
+ * embedding (the reference dequantises the q4_K row on the host,
+ * moe.rs:1824-1835); values identical to a CPU decode of the blocks.  A row
+ * index outside [0, nrows) gives zeros and STYX_EINVAL from
+ * styx_check_device_error. */
+int styx_get_rows(styx_ctx *ctx, styx_stream stream, int qtype, const void *w, int nrows, int ncols,
+                  const int32_t *rows, int n, float *out);
+
+/* *out = the index of the largest x[i] under IEEE total order, the last one
+ * among equals: the greedy pick of generate_moe (examples/generate_moe.rs:29,
+ * max_by(total_cmp) over the downloaded logits), on the device. */
+int styx_argmax_f32(styx_ctx *ctx, styx_stream stream, const float *x, int n, int32_t *out);
+
 /* ------------------------------------------------- one layer's attention */
 typedef struct styx_dense_tensor {
     const void *data;          /* row-major [nrows][ncols] of qtype */

@@ -167,6 +167,8 @@ _SIGS = {
     "styx_rope_neox": (_i, [_vp, _vp, _vp, _i, _i, _i, _f, _vp]),
     "styx_attn_workspace_bytes": (_i, [_i, _i, C.POINTER(_u64)]),
     "styx_attn_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp, _u64]),
+    "styx_get_rows": (_i, [_vp, _vp, _i, _vp, _i, _i, _vp, _i, _vp]),
+    "styx_argmax_f32": (_i, [_vp, _vp, _vp, _i, _vp]),
     "styx_attn_block_workspace_bytes": (_i, [C.POINTER(AttnDims), C.POINTER(_u64)]),
     "styx_attn_block": (_i, [_vp, _vp, C.POINTER(AttnDims), C.POINTER(AttnLayer), _vp, _i, _vp, _vp, _vp, _i,
                              _vp, _u64]),

@@ -1419,3 +1419,34 @@ int styx_attn_block(styx_ctx *ctx, styx_stream stream, const styx_attn_dims *dim
     if ((rc = styx_mul_mat_vec(ctx, stream, lw->wo.qtype, lw->wo.data, H, qd, att, proj))) return rc;
     return styx_add_f32(ctx, stream, x, proj, x, H);
 }
+
+int styx_get_rows(styx_ctx *ctx, styx_stream stream, int qtype, const void *w, int nrows, int ncols,
+                  const int32_t *rows, int n, float *out) {
+    ENTER(ctx);
+    NEED(w && rows && out && nrows > 0 && n > 0, "bad get_rows arguments");
+    const long long rb = row_bytes(qtype, ncols);
+    NEED(rb > 0, "ncols %d not representable in qtype %d", ncols, qtype);
+    NEED(extent_ok(w, static_cast<uint64_t>(rb) * nrows), "matrix smaller than nrows rows");
+    NEED(extent_ok(out, static_cast<uint64_t>(n) * ncols * 4) && extent_ok(rows, static_cast<uint64_t>(n) * 4),
+         "rows / out smaller than n");
+    styx::GetRowsArgs a{};
+    a.w = static_cast<const uint8_t *>(w);
+    a.row_bytes = rb;
+    a.qtype = qtype;
+    a.nrows = nrows;
+    a.ncols = ncols;
+    a.rows = rows;
+    a.n = n;
+    a.out = out;
+    a.err = ctx->d_err;
+    CK(styx::launch_get_rows(a, S(stream)));
+    return STYX_OK;
+}
+
+int styx_argmax_f32(styx_ctx *ctx, styx_stream stream, const float *x, int n, int32_t *out) {
+    ENTER(ctx);
+    NEED(x && out && n > 0, "bad argmax arguments");
+    NEED(extent_ok(x, static_cast<uint64_t>(n) * 4), "x smaller than n");
+    CK(styx::launch_argmax(x, n, out, S(stream)));
+    return STYX_OK;
+}

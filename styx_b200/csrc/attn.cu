@@ -14,6 +14,10 @@
 //                       its K and V rows once for all the kv head's q heads
 //   k_attn_combine      merges the splits' (max, sum, acc) per head
 //   k_add_f32           shaders/add_flat_f32.comp
+//   k_get_rows          the token-embedding row (dequant_q4k on the host,
+//                       moe.rs:1824-1836), any of the four block formats
+//   k_argmax            the greedy pick over the logits
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -243,7 +247,106 @@ __global__ void k_add_f32(const float *x, const float *y, float *d, int n) {
     if (i < n) d[i] = x[i] + y[i];
 }
 
+// ------------------------------------------------------------ embedding rows
+// out[r][c] = deq(W)[rows[r]][c]: one thread per element, the block formats
+// decoded with the reference's own expression order (moe.rs:506-533 for
+// q4_K; the published GGUF layouts for q5_K / q6_K / q8_0) and no fused
+// multiply-adds, so the rows are bit-identical to a CPU decode.
+__device__ __forceinline__ float rd_f16(const uint8_t *p) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(p[0] | (p[1] << 8))));
+}
+__device__ __forceinline__ void kq_scale_min(const uint8_t *s, int j, float &sc, float &m) {
+    if (j < 4) {
+        sc = static_cast<float>(s[j] & 63);
+        m = static_cast<float>(s[j + 4] & 63);
+    } else {
+        sc = static_cast<float>((s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4));
+        m = static_cast<float>((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+    }
+}
+
+__global__ void k_get_rows(GetRowsArgs a) {
+    const long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= static_cast<long long>(a.n) * a.ncols) return;
+    const int r = static_cast<int>(e / a.ncols), c = static_cast<int>(e - static_cast<long long>(r) * a.ncols);
+    const int row = a.rows[r];
+    if (row < 0 || row >= a.nrows) {   // skipped and reported
+        a.out[e] = 0.f;
+        if (c == 0) atomicExch(a.err, kErrBadId);
+        return;
+    }
+    const uint8_t *rp = a.w + static_cast<size_t>(row) * a.row_bytes;
+    float v = 0.f;
+    if (a.qtype == STYX_Q8_0) {
+        const uint8_t *b = rp + static_cast<size_t>(c / 32) * 34;
+        v = __fmul_rn(rd_f16(b), static_cast<float>(static_cast<int8_t>(b[2 + c % 32])));
+    } else {
+        const int blk = c / 256, i = c % 256;
+        if (a.qtype == STYX_Q4_K || a.qtype == STYX_Q5_K) {
+            const uint8_t *b = rp + static_cast<size_t>(blk) * (a.qtype == STYX_Q4_K ? 144 : 176);
+            const int j = i / 64, w = i % 64, l = w % 32, hi = w >= 32;
+            float sc, m;
+            kq_scale_min(b + 4, 2 * j + hi, sc, m);
+            int q;
+            if (a.qtype == STYX_Q4_K) {
+                q = (b[16 + 32 * j + l] >> (hi ? 4 : 0)) & 0x0F;
+            } else {
+                q = ((b[48 + 32 * j + l] >> (hi ? 4 : 0)) & 0x0F) + (((b[16 + l] >> (2 * j + hi)) & 1) << 4);
+            }
+            const float d = rd_f16(b), dmin = rd_f16(b + 2);
+            v = __fsub_rn(__fmul_rn(__fmul_rn(d, sc), static_cast<float>(q)), __fmul_rn(dmin, m));
+        } else {   // q6_K
+            const uint8_t *b = rp + static_cast<size_t>(blk) * 210;
+            const int n = i / 128, rr = i % 128, qq = rr / 32, l = rr % 32;
+            const uint8_t h = b[128 + 32 * n + l];
+            const uint8_t lo = b[64 * n + l + ((qq & 1) ? 32 : 0)];
+            const int q = (((qq & 2) ? (lo >> 4) : (lo & 0x0F)) | (((h >> (2 * qq)) & 3) << 4)) - 32;
+            const int8_t sc = static_cast<int8_t>(b[192 + 8 * n + l / 16 + 2 * qq]);
+            v = __fmul_rn(__fmul_rn(rd_f16(b + 208), static_cast<float>(sc)), static_cast<float>(q));
+        }
+    }
+    a.out[e] = v;
+}
+
+// ------------------------------------------------------------ greedy pick
+// The index of the largest value under IEEE total order (f32::total_cmp),
+// the last one among equals (Iterator::max_by, the greedy pick of
+// crates/model/examples/generate_moe.rs:29).  One CTA.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+    int b = __float_as_int(v);
+    b ^= static_cast<int>(static_cast<unsigned>(b >> 31) >> 1);   // total_cmp's key, compared as signed
+    const unsigned u = static_cast<unsigned>(b) ^ 0x80000000u;      // ... as unsigned
+    return (static_cast<unsigned long long>(u) << 32) | static_cast<unsigned>(i);
+}
+
+__global__ void __launch_bounds__(1024) k_argmax(const float *x, int n, int32_t *out) {
+    __shared__ unsigned long long red[32];
+    unsigned long long best = 0;
+    for (int i = threadIdx.x; i < n; i += 1024) best = max(best, argmax_key(x[i], i));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        best = red[threadIdx.x];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+        if (threadIdx.x == 0) *out = static_cast<int32_t>(best & 0xffffffffu);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_get_rows(const GetRowsArgs &a, cudaStream_t st) {
+    const long long total = static_cast<long long>(a.n) * a.ncols;
+    k_get_rows<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float *x, int n, int32_t *out, cudaStream_t st) {
+    k_argmax<<<1, 1024, 0, st>>>(x, n, out);
+    return cudaGetLastError();
+}
 
 size_t attn_smem_bytes(int gqa, int hd, int tps) {
     return (static_cast<size_t>(attn_acc_offset(gqa, hd, tps)) + static_cast<size_t>(kAttnWarps) * kHeadsPerPass * hd) *

@@ -189,6 +189,17 @@ struct AttnArgs {
     float scale;
     int tps, n_splits;             // tokens per split, splits
 };
+struct GetRowsArgs {
+    const uint8_t *w;              // [nrows][row_bytes] blocks of qtype
+    long long row_bytes;
+    int qtype, nrows, ncols;
+    const int32_t *rows;           // device: n row indices
+    int n;
+    float *out;                    // [n][ncols]
+    int *err;
+};
+cudaError_t launch_get_rows(const GetRowsArgs &a, cudaStream_t st);
+cudaError_t launch_argmax(const float *x, int n, int32_t *out, cudaStream_t st);
 size_t attn_smem_bytes(int gqa, int hd, int tps);
 cudaError_t launch_qk_norm_rope_kv(const QkRopeArgs &a, cudaStream_t st);
 cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st);

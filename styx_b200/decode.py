@@ -1,0 +1,112 @@
+"""One decode step of the MoE model on one device: MoeModel::forward_token
+(crates/model/src/moe.rs:1780-2140) and generate_moe's greedy loop
+(crates/model/examples/generate_moe.rs:29-66), composed from the library's
+kernels through the C ABI.
+
+Per token: the embedding row (styx_get_rows), then per layer the attention
+half (styx_attn_block: RMSNorm, q/k/v, per-head norms, RoPE, the KV cache
+row, attention, o, residual) and the MoE block (styx_moe_block), then the
+output norm, the LM head GEMV and the greedy pick on the device
+(styx_argmax_f32).  The KV caches are allocated once for n_ctx positions
+(the reference grows them page by page, moe.rs:1802-1822; the result is the
+same).
+"""
+from __future__ import annotations
+
+import contextlib
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+
+
+@dataclass
+class DecodeParams:
+    """HParams (moe.rs:550-587) of a Qwen3-MoE model."""
+    n_layers: int
+    n_embd: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    n_ff: int
+    n_expert: int
+    n_expert_used: int
+    n_vocab: int
+    rms_eps: float = 1e-6
+    rope_base: float = 1_000_000.0
+    norm_topk: bool = True
+    qk_norm: bool = True
+
+
+@dataclass
+class DecodeLayer:
+    attn: ops.AttnWeights
+    moe: ops.LayerWeights
+
+
+class DecodeModel:
+    def __init__(self, hp: DecodeParams, embd: ops.DenseWeight, layers: list, output_norm: torch.Tensor,
+                 head: ops.DenseWeight, n_ctx: int, device: int = 0):
+        self.hp, self.embd, self.layers, self.output_norm, self.head = hp, embd, layers, output_norm, head
+        self.n_ctx = n_ctx
+        dev = f"cuda:{device}"
+        self.attn = ops.AttnBlock(hp.n_embd, hp.n_heads, hp.n_kv_heads, hp.head_dim, hp.qk_norm, hp.rms_eps,
+                                  hp.rope_base, device)
+        self.moe = ops.MoeBlock(ops.Dims(hp.n_embd, hp.n_ff, hp.n_expert, hp.n_expert_used, hp.norm_topk,
+                                         hp.rms_eps), device)
+        kv_dim = hp.n_kv_heads * hp.head_dim
+        self.kcache = torch.zeros(hp.n_layers, n_ctx, kv_dim, dtype=torch.float32, device=dev)
+        self.vcache = torch.zeros_like(self.kcache)
+        self.x = torch.empty(hp.n_embd, dtype=torch.float32, device=dev)
+        self.xn = torch.empty_like(self.x)
+        self.logits = torch.empty(hp.n_vocab, dtype=torch.float32, device=dev)
+        self.ids = torch.zeros(hp.n_layers * ops.IDS_PER_LAYER, dtype=torch.int32, device=dev)
+        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.next = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.n_past = 0
+
+    def reset(self) -> None:
+        self.n_past = 0
+
+    def forward_token(self, token: int, stream=None) -> torch.Tensor:
+        """Runs one token at position n_past; returns the device logits
+        (and leaves the greedy pick in self.next)."""
+        if self.n_past >= self.n_ctx:
+            raise ValueError(f"KV caches full ({self.n_ctx})")
+        with torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext():
+            self.tok.fill_(token)
+            self.pos.fill_(self.n_past)
+        self.step(stream)
+        self.n_past += 1
+        return self.logits
+
+    def step(self, stream=None) -> None:
+        """The kernels of one token: the token id in self.tok and its position
+        in self.pos (device) and self.n_past (host, the attention's row
+        count) are the caller's; n_past is not advanced.  Everything here is
+        stream-ordered launches, so a graph can record it."""
+        hp, pos = self.hp, self.n_past
+        ops.get_rows(self.embd.qtype, self.embd.data, hp.n_vocab, hp.n_embd, self.tok, out=self.x, stream=stream)
+        for li, ly in enumerate(self.layers):
+            self.attn.forward(self.x, ly.attn, pos, self.pos, self.kcache[li], self.vcache[li], self.n_ctx,
+                              stream=stream)
+            self.moe.forward(self.x, ly.moe, li, self.ids, stream=stream)
+        ops.rms_norm_into(self.x, self.output_norm, hp.rms_eps, self.xn, stream=stream)
+        ops.mul_mat_vec(self.head.qtype, self.head.data, hp.n_vocab, hp.n_embd, self.xn, y=self.logits,
+                        stream=stream)
+        ops.argmax_f32(self.logits, out=self.next, stream=stream)
+
+    def generate(self, prompt: list, n_predict: int, stream=None) -> list:
+        """generate_moe's loop (examples/generate_moe.rs:46-66): the prompt
+        token by token, then n_predict greedy tokens, each the argmax of the
+        previous step's logits (n_predict - 1 further steps)."""
+        assert prompt and n_predict > 0, "empty prompt or nothing to predict"
+        for t in prompt:
+            self.forward_token(t, stream)
+        out = [int(self.next.item())]
+        for _ in range(1, n_predict):
+            self.forward_token(out[-1], stream)
+            out.append(int(self.next.item()))
+        return out

@@ -121,6 +121,15 @@ def rms_norm(x: torch.Tensor, w: Optional[torch.Tensor], eps: float) -> torch.Te
     return out
 
 
+def rms_norm_into(x: torch.Tensor, w: Optional[torch.Tensor], eps: float, out: torch.Tensor,
+                  stream=None) -> torch.Tensor:
+    """rms_norm_f32 over the last dimension into `out` on `stream`."""
+    nrows = 1 if x.dim() == 1 else x.shape[0]
+    check(lib().styx_rms_norm(ctx(_dev(x)).handle, _stream(stream), _ptr(x), _ptr(w), eps, x.shape[-1], nrows,
+                              _ptr(out)))
+    return out
+
+
 def matvec_f32(a: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     d = torch.empty(a.shape[0], dtype=torch.float32, device=a.device)
     check(lib().styx_matvec_f32(ctx(_dev(a)).handle, _stream(), _ptr(a), a.shape[0], a.shape[1], a.stride(0),
@@ -541,3 +550,22 @@ class AttnBlock:
                                     _ptr(pos_dev), _ptr(kcache), _ptr(vcache), n_ctx, _ptr(self.workspace),
                                     self.ws_bytes))
         return x
+
+
+def get_rows(qtype: int, w: torch.Tensor, nrows: int, ncols: int, rows: torch.Tensor,
+             out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Dequantised rows of a quantised matrix (the token embedding)."""
+    n = rows.numel()
+    if out is None:
+        out = torch.empty(n, ncols, dtype=torch.float32, device=rows.device)
+    check(lib().styx_get_rows(ctx(_dev(rows)).handle, _stream(stream), qtype, _ptr(w), nrows, ncols, _ptr(rows), n,
+                              _ptr(out)))
+    return out
+
+
+def argmax_f32(x: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Greedy pick: the last index of the maximum under IEEE total order."""
+    if out is None:
+        out = torch.empty(1, dtype=torch.int32, device=x.device)
+    check(lib().styx_argmax_f32(ctx(_dev(x)).handle, _stream(stream), _ptr(x), x.numel(), _ptr(out)))
+    return out

@@ -1,0 +1,78 @@
+"""A small Qwen3-MoE model with random weights for the decode-step tests,
+and the oracle's forward_token over the same bytes (the CPU restatements of
+moe.rs:1824-2073: embedding row, per layer the attention half and the MoE
+block, output norm, LM head, greedy pick)."""
+from dataclasses import dataclass
+
+import numpy as np
+
+from oracle import oracle as O
+
+Q4_K, Q6_K, Q8_0 = 12, 14, 8
+
+
+@dataclass
+class Model:
+    hp: dict
+    embd: np.ndarray          # q4_K [n_vocab][H]
+    layers: list              # dicts: attn_norm, wq.. (qtype, raw), q_norm, k_norm, ffn_norm, router, gate, up, down
+    output_norm: np.ndarray
+    head: np.ndarray          # q6_K [n_vocab][H]
+
+
+def make_model(seed=0, n_layers=2, H=512, n_heads=8, n_kv=2, hd=64, F=256, E=16, k=4, n_vocab=1024):
+    rng = np.random.default_rng(seed)
+
+    def q(qt, rows, cols, sigma=0.02):
+        return O.quantize(qt, rng.normal(0, sigma, (rows, cols)).astype(np.float32)).reshape(-1)
+
+    hp = dict(n_layers=n_layers, n_embd=H, n_heads=n_heads, n_kv_heads=n_kv, head_dim=hd, n_ff=F, n_expert=E,
+              n_expert_used=k, n_vocab=n_vocab, rms_eps=1e-6, rope_base=1_000_000.0)
+    layers = []
+    for _ in range(n_layers):
+        layers.append(dict(
+            attn_norm=rng.uniform(0.5, 1.5, H).astype(np.float32),
+            wq=(Q4_K, q(Q4_K, n_heads * hd, H)), wk=(Q4_K, q(Q4_K, n_kv * hd, H)),
+            wv=(Q6_K, q(Q6_K, n_kv * hd, H)), wo=(Q4_K, q(Q4_K, H, n_heads * hd)),
+            q_norm=rng.uniform(0.5, 1.5, hd).astype(np.float32), k_norm=rng.uniform(0.5, 1.5, hd).astype(np.float32),
+            ffn_norm=rng.uniform(0.5, 1.5, H).astype(np.float32),
+            router=rng.normal(0, 0.05, (E, H)).astype(np.float32),
+            gate=q(Q4_K, E * F, H), up=q(Q4_K, E * F, H), down=q(Q6_K, E * H, F)))
+    return Model(hp, q(Q4_K, n_vocab, H, 1.0), layers, rng.uniform(0.5, 1.5, H).astype(np.float32),
+                 q(Q6_K, n_vocab, H, 0.05))
+
+
+def total_cmp_argmax_last(v):
+    """max_by(total_cmp) over the indices: the last index of the maximum."""
+    b = np.ascontiguousarray(v, np.float32).view(np.int32).astype(np.int64)
+    key = np.where(b < 0, b ^ 0x7FFFFFFF, b)
+    m = key.max()
+    return int(np.nonzero(key == m)[0][-1])
+
+
+class OracleDecoder:
+    def __init__(self, m: Model, n_ctx: int):
+        self.m, self.n_ctx, self.n_past = m, n_ctx, 0
+        hp = m.hp
+        kvd = hp["n_kv_heads"] * hp["head_dim"]
+        self.kc = [np.zeros((n_ctx, kvd), np.float32) for _ in range(hp["n_layers"])]
+        self.vc = [np.zeros((n_ctx, kvd), np.float32) for _ in range(hp["n_layers"])]
+
+    def forward_token(self, token):
+        m, hp, pos = self.m, self.m.hp, self.n_past
+        H = hp["n_embd"]
+        rb = O.row_bytes(Q4_K, H)
+        x = O.dequantize(Q4_K, m.embd[token * rb:(token + 1) * rb], H).reshape(-1)
+        ids = []
+        for li, ly in enumerate(m.layers):
+            x = O.attn_block(x, ly["attn_norm"], hp["rms_eps"], hp["n_heads"], hp["n_kv_heads"], hp["head_dim"],
+                             ly["q_norm"], ly["k_norm"], hp["rope_base"], [ly["wq"], ly["wk"], ly["wv"], ly["wo"]],
+                             pos, self.kc[li], self.vc[li])
+            r = O.moe_block(x, ly["ffn_norm"], hp["rms_eps"], ly["router"], hp["n_expert_used"], True,
+                            (Q4_K, Q4_K, Q6_K), ly["gate"], ly["up"], ly["down"], hp["n_ff"])
+            x = r["x"]
+            ids.append(r["ids64"][:hp["n_expert_used"]])
+        xn = O.rms_norm(x, m.output_norm, hp["rms_eps"])
+        logits = O.matvec_q(Q6_K, m.head, hp["n_vocab"], H, xn)
+        self.n_past += 1
+        return logits, x, ids
