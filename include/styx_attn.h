@@ -37,9 +37,15 @@ extern "C" {
 /* y[r] = sum_c deq(W)[r][c] * x[c] for r < nrows; W row-major, qtype
  * STYX_Q8_0 / Q4_K / Q5_K / Q6_K (ncols a multiple of 64 for q8_0, 256 for
  * the k-quants; q4_K / q5_K matrices 16-byte aligned, the others 2-byte).
- * The MoE kernels' dot products (styx_mul_mat_vec_id with one expert). */
+ * The MoE kernels' dot products; the rows stream through shared memory by
+ * bulk copies, x is converted once per CTA. */
 int styx_mul_mat_vec(styx_ctx *ctx, styx_stream stream, int qtype, const void *a, int nrows, int ncols,
                      const float *x, float *y);
+
+/* y[r] += sum_c deq(W)[r][c] * x[c]: the GEMV with the residual add fused
+ * (rounds exactly as styx_mul_mat_vec into a temporary, then styx_add_f32). */
+int styx_mul_mat_vec_add(styx_ctx *ctx, styx_stream stream, int qtype, const void *a, int nrows, int ncols,
+                         const float *x, float *y);
 
 /* d[i] = a[i] + b[i], i < n (d may alias a or b). */
 int styx_add_f32(styx_ctx *ctx, styx_stream stream, const float *a, const float *b, float *d, int n);
@@ -93,7 +99,9 @@ int styx_get_rows(styx_ctx *ctx, styx_stream stream, int qtype, const void *w, i
 
 /* *out = the index of the largest x[i] under IEEE total order, the last one
  * among equals: the greedy pick of generate_moe (examples/generate_moe.rs:29,
- * max_by(total_cmp) over the downloaded logits), on the device. */
+ * max_by(total_cmp) over the downloaded logits), on the device.  Uses a
+ * scratch area of the context: calls on one context must not run at the same
+ * time on different streams. */
 int styx_argmax_f32(styx_ctx *ctx, styx_stream stream, const float *x, int n, int32_t *out);
 
 /* ------------------------------------------------- one layer's attention */
@@ -130,7 +138,8 @@ int styx_attn_block_workspace_bytes(const styx_attn_dims *dims, uint64_t *out);
 /* x += o(attention(rope(norm(q, k, v of rms_norm(x) * attn_norm)))) for the
  * token at position `pos` (n_t = pos + 1 cache rows are read; row pos is
  * written first).  pos_dev is the same position as a device int32 (the
- * reference's bpos buffer).  Seven launches, stream-ordered. */
+ * reference's bpos buffer).  Seven launches, stream-ordered (the o GEMV adds
+ * into x). */
 int styx_attn_block(styx_ctx *ctx, styx_stream stream, const styx_attn_dims *dims, const styx_attn_layer *lw,
                     float *x, int pos, const int32_t *pos_dev, float *kcache, float *vcache, int n_ctx,
                     void *workspace, uint64_t workspace_bytes);

@@ -162,6 +162,7 @@ _SIGS = {
     "styx_synth_f32": (_i, [_vp, _vp, _vp, _u64, _u64, _u64, _f]),
     # include/styx_attn.h
     "styx_mul_mat_vec": (_i, [_vp, _vp, _i, _vp, _i, _i, _vp, _vp]),
+    "styx_mul_mat_vec_add": (_i, [_vp, _vp, _i, _vp, _i, _i, _vp, _vp]),
     "styx_add_f32": (_i, [_vp, _vp, _vp, _vp, _vp, _i]),
     "styx_qk_norm_rope_kv": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _f, _vp, _vp, _vp, _i]),
     "styx_rope_neox": (_i, [_vp, _vp, _vp, _i, _i, _i, _f, _vp]),

@@ -16,11 +16,17 @@
 #include "../../include/styx_moe.h"
 #include "kernels.h"
 
+// the context's scratch: styx_argmax_f32's partial maxima and ticket, then
+// the dense GEMV's id block (expert 0 from the full tensor) and its weight 1
+constexpr size_t kScratchDenseIds = 2560, kScratchOne = kScratchDenseIds + 256, kScratchBytes = 4096;
+static_assert(styx::kArgmaxCtas * 8 + 4 <= kScratchDenseIds, "argmax scratch overlaps the id block");
+
 struct styx_ctx {
     int device = 0;
     int sm_count = 0;
     char name[256] = {0};
     int *d_err = nullptr;   // device error word of bounded waits; d_err[4..7]: zeros (a one-expert id row)
+    void *d_scratch = nullptr;   // styx_argmax_f32's partial maxima and ticket (zeroed at init)
     int moe_kernels = 0;    // STYX_OPT_MOE_KERNELS
     int last_path = 0;      // STYX_OPT_MOE_LAST_PATH
     int trace = 0;          // STYX_OPT_TRACE
@@ -230,10 +236,18 @@ styx::ExpSrc to_src(const styx_expert_tensor &t, int n_expert) {
                         t.n_arena};
 }
 
+// rows per CTA of k_matvec_id: about two CTAs per SM over all slots, a whole
+// number of the kernel's passes
+int mv_rows_per_cta(int nrows, int n_ids, int gs, int sms) {
+    const int step = styx::kMvRowStep(gs);
+    const long long want = (static_cast<long long>(nrows) * n_ids + 2LL * sms - 1) / (2LL * sms);
+    return static_cast<int>(std::max<long long>(step, (want + step - 1) / step * step));
+}
+
 // reference-shaped 3-way expert GEMV (rec_matvec_id, moe.rs:1649-1700): hot,
 // arena and full-tensor rows, each a SKIP-gated dispatch over all k slots
 int matvec_id_3way(const styx_expert_tensor &t, int n_expert, const int32_t *ids64, int nrows, int ncols, int k,
-                   const float *x, int ne11, float *y, int *err, cudaStream_t st) {
+                   const float *x, int ne11, float *y, int *err, int sms, cudaStream_t st) {
     const int units = ncols / 64;
     styx::MatVecIdArgs a{};
     a.err = err;
@@ -248,6 +262,7 @@ int matvec_id_3way(const styx_expert_tensor &t, int n_expert, const int32_t *ids
     a.stride_d = nrows;
     a.units = units;
     a.gs = std::min(32, pow2ceil(units));
+    a.rows_per_cta = mv_rows_per_cta(nrows, k, a.gs, sms);
     struct Row { const void *buf; uint64_t stride; int off; int count; } rows[3] = {
         {t.hot, t.slab_bytes, 16, static_cast<int>(t.n_hot)},
         {t.arena, t.arena_slab_bytes, 32, static_cast<int>(t.n_arena)},
@@ -293,9 +308,22 @@ int styx_init(int device, styx_ctx **out) {
     snprintf(c->name, sizeof(c->name), "%s", prop.name);
     cudaError_t e = cudaMalloc(&c->d_err, 8 * sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, 8 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_scratch, kScratchBytes);
+    if (e == cudaSuccess) e = cudaMemset(c->d_scratch, 0, kScratchBytes);
+    if (e == cudaSuccess) {
+        int32_t ids[64];
+        for (int i = 0; i < 64; i++) ids[i] = (i >= 16 && i < 48) ? -1 : 0;   // hot / arena SKIP, full row 0
+        const float one = 1.0f;
+        e = cudaMemcpy(static_cast<uint8_t *>(c->d_scratch) + kScratchDenseIds, ids, sizeof(ids),
+                       cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(static_cast<uint8_t *>(c->d_scratch) + kScratchOne, &one, 4, cudaMemcpyHostToDevice);
+    }
     if (e != cudaSuccess) {
+        cudaFree(c->d_err);
+        cudaFree(c->d_scratch);
         delete c;
-        return fail(STYX_ECUDA, "error word: %s", cudaGetErrorString(e));
+        return fail(STYX_ECUDA, "error word / scratch: %s", cudaGetErrorString(e));
     }
     *out = c;
     return STYX_OK;
@@ -305,6 +333,7 @@ void styx_destroy(styx_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     cudaFree(ctx->d_err);
+    cudaFree(ctx->d_scratch);
     delete ctx;
 }
 
@@ -577,6 +606,7 @@ int styx_mul_mat_vec_id(styx_ctx *ctx, styx_stream stream, int qtype, const void
     m.stride_d = stride_d;
     m.units = ncols / 64;
     m.gs = std::min(32, pow2ceil(m.units));
+    m.rows_per_cta = mv_rows_per_cta(nrows, n_ids, m.gs, ctx->sm_count);
     CK(styx::launch_matvec_id(m, qtype, S(stream)));
     return STYX_OK;
 }
@@ -768,10 +798,10 @@ static int moe_block_host_read(styx_ctx *ctx, cudaStream_t st, const styx_moe_di
     CK(cudaMemsetAsync(u, 0, kF * 4, st));
     CK(cudaMemsetAsync(dd, 0, static_cast<size_t>(k) * H * 4, st));
     int rc;
-    if ((rc = matvec_id_3way(lw.gate, E, ids64, F, H, k, ra.xnorm, 1, g, ctx->d_err, st))) return rc;
-    if ((rc = matvec_id_3way(lw.up, E, ids64, F, H, k, ra.xnorm, 1, u, ctx->d_err, st))) return rc;
+    if ((rc = matvec_id_3way(lw.gate, E, ids64, F, H, k, ra.xnorm, 1, g, ctx->d_err, ctx->sm_count, st))) return rc;
+    if ((rc = matvec_id_3way(lw.up, E, ids64, F, H, k, ra.xnorm, 1, u, ctx->d_err, ctx->sm_count, st))) return rc;
     CK(styx::launch_swiglu(g, u, h, static_cast<int>(kF), st));
-    if ((rc = matvec_id_3way(lw.down, E, ids64, H, F, k, h, k, dd, ctx->d_err, st))) return rc;
+    if ((rc = matvec_id_3way(lw.down, E, ids64, H, F, k, h, k, dd, ctx->d_err, ctx->sm_count, st))) return rc;
     CK(styx::launch_moe_reduce(dd, wts, x, H, k, st));
     return STYX_OK;
 }
@@ -850,8 +880,8 @@ static int moe_block_split(styx_ctx *ctx, cudaStream_t st, const styx_moe_dims &
             CK(cudaMemsetAsync(g, 0, static_cast<size_t>(k) * F * 4, st));
             CK(cudaMemsetAsync(u, 0, static_cast<size_t>(k) * F * 4, st));
         }
-        if ((rc = matvec_id_3way(lw->gate, E, ids64, F, H, k, ra.xnorm, 1, g, ctx->d_err, st))) return rc;
-        if ((rc = matvec_id_3way(lw->up, E, ids64, F, H, k, ra.xnorm, 1, u, ctx->d_err, st))) return rc;
+        if ((rc = matvec_id_3way(lw->gate, E, ids64, F, H, k, ra.xnorm, 1, g, ctx->d_err, ctx->sm_count, st))) return rc;
+        if ((rc = matvec_id_3way(lw->up, E, ids64, F, H, k, ra.xnorm, 1, u, ctx->d_err, ctx->sm_count, st))) return rc;
         CK(styx::launch_swiglu(g, u, h, k * F, st));
     }
 
@@ -1217,15 +1247,73 @@ int styx_synth_f32(styx_ctx *ctx, styx_stream stream, float *dst, uint64_t n, ui
 }  // extern "C"
 
 // ------------------------------------------------ attention half of a decode layer (styx_attn.h)
+// A dense GEMV streamed by the down kernel as a one-slot block: rows in
+// chunks of 16 lane groups' rows through a ring of bulk copies, x as digits
+// in shared memory; y = W x (the kernel's per-slot output) or, with
+// `accumulate`, y += W x (its weighted combine with weight 1, which rounds
+// exactly as a separate add).
+static int dense_gemv(styx_ctx *ctx, cudaStream_t st, int qtype, const void *a, int nrows, int ncols,
+                      const float *x, float *y, bool accumulate) {
+    NEED(a && x && y && nrows > 0, "bad mul_mat_vec arguments");
+    NEED(qtype_ok(qtype), "unsupported qtype %d", qtype);
+    NEED(units_ok(qtype, ncols) && ncols <= 16384, "ncols %d not supported for qtype %d", ncols, qtype);
+    const long long rb = row_bytes(qtype, ncols);
+    if (qtype == STYX_Q4_K || qtype == STYX_Q5_K)
+        NEED(al16(a) && rb % 16 == 0, "q4_K/q5_K matrices must be 16-byte aligned");
+    else
+        NEED((reinterpret_cast<uintptr_t>(a) & 1) == 0, "matrix must be 2-byte aligned");
+    NEED(extent_ok(a, static_cast<uint64_t>(rb) * nrows), "matrix smaller than nrows rows");
+    NEED(extent_ok(x, static_cast<uint64_t>(ncols) * 4) && extent_ok(y, static_cast<uint64_t>(nrows) * 4),
+         "x / y smaller than their lengths");
+    styx_expert_tensor t{};
+    t.full = a;
+    t.slab_bytes = static_cast<uint64_t>(rb) * nrows;
+    t.qtype = qtype;
+    styx::DownArgs da{};
+    da.down = to_src(t, 1);
+    da.ids64 = reinterpret_cast<const int32_t *>(static_cast<uint8_t *>(ctx->d_scratch) + kScratchDenseIds);
+    da.h = x;
+    da.w = reinterpret_cast<const float *>(static_cast<uint8_t *>(ctx->d_scratch) + kScratchOne);
+    da.x = accumulate ? y : nullptr;
+    da.partial = accumulate ? nullptr : y;
+    da.H = nrows;
+    da.F = ncols;
+    da.k = 1;
+    da.rb = static_cast<int>(rb);
+    da.units = ncols / 64;
+    da.gs = std::min(32, pow2ceil(da.units));
+    da.rc = 2 * 8 * (32 / da.gs);   // two rows per lane group per chunk
+    da.slot_stride = static_cast<uint32_t>(a16(static_cast<size_t>(da.rc) * da.rb + 32));
+    da.stage_bytes = da.slot_stride;
+    const int grid = std::max(1, std::min(ctx->sm_count, (nrows + da.rc - 1) / da.rc));
+    const int rows = (nrows + grid - 1) / grid;
+    da.dig_off = 512;
+    const size_t dig_bytes = static_cast<size_t>(ncols) * 3 + ncols / 32 * 4;
+    const int chunks = (rows + da.rc - 1) / da.rc;
+    const size_t fixed = a128(a128(da.dig_off + dig_bytes) + static_cast<size_t>(std::max(2, chunks)) * da.rc * 4);
+    const int nst = std::min({16, chunks, static_cast<int>((227 * 1024 - std::min<size_t>(fixed, 227 * 1024)) /
+                                                            da.stage_bytes)});
+    NEED(nst >= 1, "rows of %d columns too large for shared memory", ncols);
+    da.nst = nst;
+    da.part_off = static_cast<uint32_t>(a128(da.dig_off + dig_bytes));
+    da.stage_off = static_cast<uint32_t>(a128(da.part_off + static_cast<size_t>(std::max(2, nst)) * da.rc * 4));
+    const uint32_t smem = da.stage_off + static_cast<uint32_t>(nst) * da.stage_bytes;
+    NEED(smem <= 227 * 1024, "dense GEMV needs %u bytes of shared memory", smem);
+    da.err = ctx->d_err;
+    CK(styx::launch_down(da, qtype, grid, smem, st));
+    return STYX_OK;
+}
+
 int styx_mul_mat_vec(styx_ctx *ctx, styx_stream stream, int qtype, const void *a, int nrows, int ncols,
                      const float *x, float *y) {
     ENTER(ctx);
-    NEED(nrows > 0, "bad nrows %d", nrows);
-    const long long rb = row_bytes(qtype, ncols);
-    NEED(rb > 0, "ncols %d not representable in qtype %d", ncols, qtype);
-    // one expert, one id row of zeros held by the context
-    return styx_mul_mat_vec_id(ctx, stream, qtype, a, static_cast<uint64_t>(rb) * nrows, 1, nrows, ncols,
-                               ctx->d_err + 4, 1, x, ncols, 1, y, nrows);
+    return dense_gemv(ctx, S(stream), qtype, a, nrows, ncols, x, y, false);
+}
+
+int styx_mul_mat_vec_add(styx_ctx *ctx, styx_stream stream, int qtype, const void *a, int nrows, int ncols,
+                         const float *x, float *y) {
+    ENTER(ctx);
+    return dense_gemv(ctx, S(stream), qtype, a, nrows, ncols, x, y, true);
 }
 
 int styx_add_f32(styx_ctx *ctx, styx_stream stream, const float *a, const float *b, float *d, int n) {
@@ -1351,7 +1439,7 @@ int styx_attn_decode(styx_ctx *ctx, styx_stream stream, const float *q, const fl
 
 namespace {
 struct AttnWs {
-    size_t xnorm, q, k, v, att, proj, part, total;
+    size_t xnorm, q, k, v, att, part, total;
 };
 AttnWs attn_ws(const styx_attn_dims &d) {
     AttnWs w{};
@@ -1368,7 +1456,6 @@ AttnWs attn_ws(const styx_attn_dims &d) {
     w.k = take(kvd * 4);
     w.v = take(kvd * 4);
     w.att = take(qd * 4);
-    w.proj = take(H * 4);
     uint64_t pb = 0;
     styx_attn_workspace_bytes(d.n_heads, d.head_dim, &pb);
     w.part = take(pb);
@@ -1402,7 +1489,7 @@ int styx_attn_block(styx_ctx *ctx, styx_stream stream, const styx_attn_dims *dim
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     float *xn = reinterpret_cast<float *>(ws + w.xnorm), *q = reinterpret_cast<float *>(ws + w.q);
     float *k = reinterpret_cast<float *>(ws + w.k), *v = reinterpret_cast<float *>(ws + w.v);
-    float *att = reinterpret_cast<float *>(ws + w.att), *proj = reinterpret_cast<float *>(ws + w.proj);
+    float *att = reinterpret_cast<float *>(ws + w.att);
     const int H = d.n_embd, hd = d.head_dim, qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
     int rc;
     if ((rc = styx_rms_norm(ctx, stream, x, lw->attn_norm, d.rms_eps, H, 1, xn))) return rc;
@@ -1416,8 +1503,7 @@ int styx_attn_block(styx_ctx *ctx, styx_stream stream, const styx_attn_dims *dim
     if ((rc = styx_attn_decode(ctx, stream, q, kcache, vcache, att, pos + 1, hd, kvd, d.n_heads / d.n_kv_heads,
                                1.0f / std::sqrt(static_cast<float>(hd)), ws + w.part, workspace_bytes - w.part)))
         return rc;
-    if ((rc = styx_mul_mat_vec(ctx, stream, lw->wo.qtype, lw->wo.data, H, qd, att, proj))) return rc;
-    return styx_add_f32(ctx, stream, x, proj, x, H);
+    return styx_mul_mat_vec_add(ctx, stream, lw->wo.qtype, lw->wo.data, H, qd, att, x);   // x += o, rec_add fused
 }
 
 int styx_get_rows(styx_ctx *ctx, styx_stream stream, int qtype, const void *w, int nrows, int ncols,
@@ -1447,6 +1533,6 @@ int styx_argmax_f32(styx_ctx *ctx, styx_stream stream, const float *x, int n, in
     ENTER(ctx);
     NEED(x && out && n > 0, "bad argmax arguments");
     NEED(extent_ok(x, static_cast<uint64_t>(n) * 4), "x smaller than n");
-    CK(styx::launch_argmax(x, n, out, S(stream)));
+    CK(styx::launch_argmax(x, n, out, ctx->d_scratch, S(stream)));
     return STYX_OK;
 }

@@ -20,6 +20,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 
@@ -56,6 +57,8 @@ __device__ __forceinline__ float warp_max(float v) {
 // (in place) and to the K cache row pos[t]; v copied to the V cache row.
 // Thread i < hd/2 owns the NEOX pair (i, i + hd/2).
 __global__ void __launch_bounds__(128) k_qk_norm_rope_kv(QkRopeArgs a) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[4];
     const int rows = a.n_heads + a.n_kv;
     const int t = blockIdx.x / rows, h = blockIdx.x - t * rows;
@@ -113,6 +116,8 @@ __global__ void __launch_bounds__(128) k_qk_norm_rope_kv(QkRopeArgs a) {
 // for up to 8 heads.  Writes per (head, split): m, l and acc[hd] (unnormalised).
 template <int NF4>   // float4s of a row per lane: hd <= 128 * NF4
 __global__ void __launch_bounds__(kAttnThreads) k_attn_split(AttnArgs a) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) float sm[];
     const int gqa = a.gqa, hd = a.hd;
     float *sq = sm;                                   // [gqa][hd] the q heads
@@ -225,24 +230,45 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_split(AttnArgs a) {
     }
 }
 
-// out[h][c] = sum_s e^(m_s - M) acc_s[c] / sum_s e^(m_s - M) l_s
+// out[h][c] = sum_s e^(m_s - M) acc_s[c] / sum_s e^(m_s - M) l_s: the
+// split weights once per head in shared memory, then every column's sum
+// with its loads in flight.
 __global__ void __launch_bounds__(128) k_attn_combine(AttnArgs a) {
-    const int h = blockIdx.x;
-    const float *ml = a.part_ml + static_cast<size_t>(h) * a.n_splits * 2;
-    float M = -INFINITY;
-    for (int s = 0; s < a.n_splits; s++) M = fmaxf(M, ml[2 * s]);
-    float L = 0.f;
-    for (int s = 0; s < a.n_splits; s++) L += expf(ml[2 * s] - M) * ml[2 * s + 1];
-    const float inv = 1.0f / L;
-    for (int c = threadIdx.x; c < a.hd; c += 128) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float w[kAttnMaxSplits];
+    __shared__ float red[8];
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ns = a.n_splits;
+    const float *ml = a.part_ml + static_cast<size_t>(h) * ns * 2;
+    float m = -INFINITY;
+    for (int s = tid; s < ns; s += 128) m = fmaxf(m, ml[2 * s]);
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float l = 0.f;
+    for (int s = tid; s < ns; s += 128) {
+        const float ws = expf(ml[2 * s] - M);
+        w[s] = ws;
+        l += ws * ml[2 * s + 1];
+    }
+    l = warp_sum(l);
+    if (lane == 0) red[4 + warp] = l;
+    __syncthreads();
+    const float inv = 1.0f / (red[4] + red[5] + red[6] + red[7]);
+    const float *acc = a.part_acc + static_cast<size_t>(h) * ns * a.hd;
+    for (int c = tid; c < a.hd; c += 128) {
         float o = 0.f;
-        for (int s = 0; s < a.n_splits; s++)
-            o += expf(ml[2 * s] - M) * a.part_acc[(static_cast<size_t>(h) * a.n_splits + s) * a.hd + c];
+#pragma unroll 8
+        for (int s = 0; s < ns; s++) o += w[s] * acc[static_cast<size_t>(s) * a.hd + c];
         a.out[static_cast<size_t>(h) * a.hd + c] = o * inv;
     }
 }
 
 __global__ void k_add_f32(const float *x, const float *y, float *d, int n) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) d[i] = x[i] + y[i];
 }
@@ -266,6 +292,8 @@ __device__ __forceinline__ void kq_scale_min(const uint8_t *s, int j, float &sc,
 }
 
 __global__ void k_get_rows(GetRowsArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (e >= static_cast<long long>(a.n) * a.ncols) return;
     const int r = static_cast<int>(e / a.ncols), c = static_cast<int>(e - static_cast<long long>(r) * a.ncols);
@@ -319,33 +347,58 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
     return (static_cast<unsigned long long>(u) << 32) | static_cast<unsigned>(i);
 }
 
-__global__ void __launch_bounds__(1024) k_argmax(const float *x, int n, int32_t *out) {
-    __shared__ unsigned long long red[32];
-    unsigned long long best = 0;
-    for (int i = threadIdx.x; i < n; i += 1024) best = max(best, argmax_key(x[i], i));
+__device__ __forceinline__ unsigned long long block_max_u64(unsigned long long v, unsigned long long *red) {
 #pragma unroll
-    for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
+    v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
     if (threadIdx.x < 32) {
-        best = red[threadIdx.x];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
-        if (threadIdx.x == 0) *out = static_cast<int32_t>(best & 0xffffffffu);
+        for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
     }
+    return v;   // valid in thread 0
+}
+
+// Each CTA reduces a stride of x to one key; the last CTA to finish (a
+// ticket counter that wraps back to zero, after a fence) reduces the CTAs'
+// keys.  No CTA waits for another.
+__global__ void __launch_bounds__(256) k_argmax(const float *x, int n, int32_t *out, unsigned long long *part,
+                                                unsigned *ticket) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ unsigned long long red[8];
+    __shared__ bool last;
+    unsigned long long best = 0;
+    for (int i = blockIdx.x * 256 + threadIdx.x; i < n; i += gridDim.x * 256) best = max(best, argmax_key(x[i], i));
+    best = block_max_u64(best, red);
+    if (threadIdx.x == 0) {
+        part[blockIdx.x] = best;
+        __threadfence();
+        last = atomicInc(ticket, gridDim.x - 1) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    best = 0;
+    for (int b = threadIdx.x; b < gridDim.x; b += 256) best = max(best, __ldcg(part + b));
+    __syncthreads();
+    best = block_max_u64(best, red);
+    if (threadIdx.x == 0) *out = static_cast<int32_t>(best & 0xffffffffu);
 }
 
 }  // namespace
 
 cudaError_t launch_get_rows(const GetRowsArgs &a, cudaStream_t st) {
     const long long total = static_cast<long long>(a.n) * a.ncols;
-    k_get_rows<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(k_get_rows, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, st, a);
 }
 
-cudaError_t launch_argmax(const float *x, int n, int32_t *out, cudaStream_t st) {
-    k_argmax<<<1, 1024, 0, st>>>(x, n, out);
-    return cudaGetLastError();
+cudaError_t launch_argmax(const float *x, int n, int32_t *out, void *scratch, cudaStream_t st) {
+    auto *part = static_cast<unsigned long long *>(scratch);
+    auto *ticket = reinterpret_cast<unsigned *>(part + kArgmaxCtas);
+    const int grid = std::min(kArgmaxCtas, std::max(1, (n + 1023) / 1024));
+    return launch_pdl(k_argmax, dim3(grid), dim3(256), 0, st, x, n, out, part, ticket);
 }
 
 size_t attn_smem_bytes(int gqa, int hd, int tps) {
@@ -354,8 +407,7 @@ size_t attn_smem_bytes(int gqa, int hd, int tps) {
 }
 
 cudaError_t launch_qk_norm_rope_kv(const QkRopeArgs &a, cudaStream_t st) {
-    k_qk_norm_rope_kv<<<a.n_tokens * (a.n_heads + a.n_kv), 128, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(k_qk_norm_rope_kv, dim3(a.n_tokens * (a.n_heads + a.n_kv)), dim3(128), 0, st, a);
 }
 
 cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st) {
@@ -365,21 +417,18 @@ cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st) {
     if (a.hd <= 128) {
         e = cudaFuncSetAttribute(k_attn_split<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        k_attn_split<1><<<grid, kAttnThreads, smem, st>>>(a);
+        e = launch_pdl(k_attn_split<1>, grid, dim3(kAttnThreads), smem, st, a);
     } else {
         e = cudaFuncSetAttribute(k_attn_split<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        k_attn_split<2><<<grid, kAttnThreads, smem, st>>>(a);
+        e = launch_pdl(k_attn_split<2>, grid, dim3(kAttnThreads), smem, st, a);
     }
-    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    k_attn_combine<<<a.n_kv * a.gqa, 128, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(k_attn_combine, dim3(a.n_kv * a.gqa), dim3(128), 0, st, a);
 }
 
 cudaError_t launch_add_f32(const float *x, const float *y, float *d, int n, cudaStream_t st) {
-    k_add_f32<<<(n + 255) / 256, 256, 0, st>>>(x, y, d, n);
-    return cudaGetLastError();
+    return launch_pdl(k_add_f32, dim3((n + 255) / 256), dim3(256), 0, st, x, y, d, n);
 }
 
 }  // namespace styx

@@ -132,7 +132,10 @@ struct MatVecIdArgs {
     float *y;
     int stride_d;
     int units, gs;
+    int rows_per_cta;              // a multiple of kMvRowStep(gs)
 };
+// rows a CTA of k_matvec_id covers per pass: 8 warps x (32 / gs) rows x 4 in flight
+constexpr int kMvRowStep(int gs) { return 8 * (32 / gs) * 4; }
 
 struct GatherArgs {
     const uint8_t *src[3];
@@ -199,11 +202,34 @@ struct GetRowsArgs {
     int *err;
 };
 cudaError_t launch_get_rows(const GetRowsArgs &a, cudaStream_t st);
-cudaError_t launch_argmax(const float *x, int n, int32_t *out, cudaStream_t st);
+// scratch: u64[kArgmaxCtas] partial maxima, then a u32 ticket (zero between calls)
+cudaError_t launch_argmax(const float *x, int n, int32_t *out, void *scratch, cudaStream_t st);
+constexpr int kAttnMaxSplits = 256;
+constexpr int kArgmaxCtas = 296;   // partial maxima of styx_argmax_f32
 size_t attn_smem_bytes(int gqa, int hd, int tps);
 cudaError_t launch_qk_norm_rope_kv(const QkRopeArgs &a, cudaStream_t st);
 cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st);
 cudaError_t launch_add_f32(const float *x, const float *y, float *d, int n, cudaStream_t st);
+
+// A launch with programmatic stream serialisation: the kernel may be
+// scheduled while the previous one on the stream drains (its CTAs start once
+// every CTA of the previous kernel has started).  Every kernel launched this
+// way begins with griddepcontrol.launch_dependents + griddepcontrol.wait, so
+// nothing it reads or writes is touched before the previous grid completed.
+template <class Kern, class... Args>
+inline cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 
 // coop: a cooperative launch; false when the caller promised the device to
 // itself (STYX_OPT_EXCLUSIVE)

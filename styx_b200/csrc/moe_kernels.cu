@@ -326,6 +326,8 @@ cudaError_t launch_gate_up(const GateUpArgs &a, int qtype, int grid, cudaStream_
 // moe_reduce_f32.comp:8-13: acc = sum_s w[s]*d[s][i] in slot order, x += acc.
 template <int QT>
 __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + 16;
@@ -403,8 +405,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
     const int slot0 = multi ? cw : cw / nwps;
     const int sub = multi ? 0 : cw % nwps;
     const int sstep = multi ? kConsumerWarps : 1 << 30;
+    // rows of at most 32 units: a lane's unit of h stays in registers; wider
+    // rows (a dense GEMV over more than 2048 columns) reload it per unit
+    const bool preload = p.units <= 32;
     XUnit x;
-    if (!multi && slot0 < p.k && active)
+    if (preload && !multi && slot0 < p.k && active)
         load_xunit<QT>(x, hd1 + slot0 * p.F, hd2 + slot0 * p.F, hd3 + slot0 * p.F, hsc + slot0 * (p.F >> 5), ug);
 
     // After a timed-out wait a warp stops computing but keeps taking part in
@@ -417,7 +422,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
         if (ok) ok = mbar_wait(&full[st], (ci / p.nst) & 1, p.err, kErrWaitFull);
         float *part = dpart + static_cast<size_t>(ci % nparts) * p.k * p.rc;
         for (int s = slot0; ok && s < p.k; s += sstep) {
-            if (multi && active)
+            if (preload && multi && active)
                 load_xunit<QT>(x, hd1 + s * p.F, hd2 + s * p.F, hd3 + s * p.F, hsc + s * (p.F >> 5), ug);
             const uint8_t *src = slot_src(p.down, p.ids64, s, p.err, false, p.quiet);
             const uint8_t *base = stages + static_cast<size_t>(st) * p.stage_bytes +
@@ -426,7 +431,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
             for (int t = sub * rpw; t < n; t += nwps * rpw) {
                 const int row = t + grp;
                 float v = 0.f;
-                if (src && active && row < n) v = unit_dot<QT>(base + static_cast<size_t>(row) * p.rb, ug, x);
+                if (preload) {
+                    if (src && active && row < n) v = unit_dot<QT>(base + static_cast<size_t>(row) * p.rb, ug, x);
+                } else if (src && row < n) {
+                    for (int u = ug; u < p.units; u += p.gs) {
+                        load_xunit<QT>(x, hd1 + s * p.F, hd2 + s * p.F, hd3 + s * p.F, hsc + s * (p.F >> 5), u);
+                        v += unit_dot<QT>(base + static_cast<size_t>(row) * p.rb, u, x);
+                    }
+                }
+                __syncwarp();   // regroup the lanes after the row-bound branches
                 for (int o = p.gs >> 1; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                 if (ug == 0 && row < n) part[s * p.rc + row] = v;
             }
@@ -455,8 +468,7 @@ static cudaError_t launch_down_t(const DownArgs &a, int grid, uint32_t smem, cud
         cudaFuncSetAttribute(k_down<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         attr_done = true;
     }
-    k_down<QT><<<grid, kFusedThreads, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(k_down<QT>, dim3(grid), dim3(kFusedThreads), smem, st, a);
 }
 
 cudaError_t launch_down(const DownArgs &a, int qtype, int grid, uint32_t smem, cudaStream_t st) {
@@ -471,12 +483,13 @@ cudaError_t launch_down(const DownArgs &a, int qtype, int grid, uint32_t smem, c
 
 // ------------------------------------------------ generic id matvec
 // MatVecIdPush semantics (ops.rs:120-147, kernels.rs:124-131).  Grid
-// (row tiles of 64, slots).  Weights are read straight from global memory;
-// x row (slot % ne11) becomes digits in shared memory.
-constexpr int kMvRows = 64;
+// (row tiles of rows_per_cta, slots).  Weights are read straight from global
+// memory; x row (slot % ne11) becomes digits in shared memory.
 
 template <int QT>
 __global__ void __launch_bounds__(256) k_matvec_id(const MatVecIdArgs p) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) uint8_t sm[];
     const int s = blockIdx.y;
     const uint32_t e = static_cast<uint32_t>(p.ids[s]);
@@ -498,21 +511,33 @@ __global__ void __launch_bounds__(256) k_matvec_id(const MatVecIdArgs p) {
     const int rpw = 32 / p.gs;
     const int ug = lane & (p.gs - 1), grp = lane / p.gs;
     const uint8_t *a = p.a + static_cast<uint64_t>(e) * p.expert_bytes;
-    const int r0 = blockIdx.x * kMvRows;
+    const int r0 = blockIdx.x * p.rows_per_cta, r1 = min(p.nrows, r0 + p.rows_per_cta);
     XUnit x;
     const bool preload = p.units <= 32;
     if (preload && ug < p.units) load_xunit<QT>(x, d1, d2, d3, sc, ug);
-    for (int t = warp * rpw; t < kMvRows; t += 8 * rpw) {
-        const int row = r0 + t + grp;
-        float v = 0.f;
-        if (row < p.nrows) {
-            for (int u = ug; u < p.units; u += p.gs) {
-                if (!preload) load_xunit<QT>(x, d1, d2, d3, sc, u);
-                v += unit_dot<QT>(a + static_cast<size_t>(row) * p.rb, u, x);
+    // four rows per lane group in flight; each row's sum (lane order, then
+    // the shuffle tree) is the same whatever the grouping
+    constexpr int R = 4;
+    for (int t = r0 + warp * rpw * R; t < r1; t += 8 * rpw * R) {
+        float v[R];
+#pragma unroll
+        for (int j = 0; j < R; j++) {
+            const int row = t + j * rpw + grp;
+            v[j] = 0.f;
+            if (row < r1) {
+                for (int u = ug; u < p.units; u += p.gs) {
+                    if (!preload) load_xunit<QT>(x, d1, d2, d3, sc, u);
+                    v[j] += unit_dot<QT>(a + static_cast<size_t>(row) * p.rb, u, x);
+                }
             }
         }
-        for (int o = p.gs >> 1; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (ug == 0 && row < p.nrows) p.y[static_cast<size_t>(s) * p.stride_d + row] = v;
+        __syncwarp();   // regroup the lanes after the row-bound branches
+#pragma unroll
+        for (int j = 0; j < R; j++) {
+            const int row = t + j * rpw + grp;
+            for (int o = p.gs >> 1; o; o >>= 1) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+            if (ug == 0 && row < r1) p.y[static_cast<size_t>(s) * p.stride_d + row] = v[j];
+        }
     }
 }
 
@@ -524,9 +549,8 @@ static cudaError_t launch_matvec_id_t(const MatVecIdArgs &a, cudaStream_t st) {
         cudaFuncSetAttribute(k_matvec_id<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         attr_done = true;
     }
-    dim3 grid((a.nrows + kMvRows - 1) / kMvRows, a.n_ids);
-    k_matvec_id<QT><<<grid, 256, smem, st>>>(a);
-    return cudaGetLastError();
+    dim3 grid((a.nrows + a.rows_per_cta - 1) / a.rows_per_cta, a.n_ids);
+    return launch_pdl(k_matvec_id<QT>, grid, dim3(256), smem, st, a);
 }
 
 cudaError_t launch_matvec_id(const MatVecIdArgs &a, int qtype, cudaStream_t st) {
@@ -542,6 +566,8 @@ cudaError_t launch_matvec_id(const MatVecIdArgs &a, int qtype, cudaStream_t st) 
 // ------------------------------------------------------ single ops
 __global__ void __launch_bounds__(256) k_rms_norm(const float *x, const float *w, float eps, int ncols,
                                                   float *out) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[32];
     const float *xr = x + static_cast<size_t>(blockIdx.x) * ncols;
     float *orow = out + static_cast<size_t>(blockIdx.x) * ncols;
@@ -557,8 +583,7 @@ __global__ void __launch_bounds__(256) k_rms_norm(const float *x, const float *w
 
 cudaError_t launch_rms_norm(const float *x, const float *w, float eps, int ncols, int nrows, float *out,
                             cudaStream_t st) {
-    k_rms_norm<<<nrows, 256, 0, st>>>(x, w, eps, ncols, out);
-    return cudaGetLastError();
+    return launch_pdl(k_rms_norm, dim3(nrows), dim3(256), 0, st, x, w, eps, ncols, out);
 }
 
 __global__ void __launch_bounds__(256) k_matvec_f32(const float *a, int ncols, int stride_a, const float *x,

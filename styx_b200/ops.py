@@ -458,6 +458,14 @@ def mul_mat_vec(qtype: int, a: torch.Tensor, nrows: int, ncols: int, x: torch.Te
     return y
 
 
+def mul_mat_vec_add(qtype: int, a: torch.Tensor, nrows: int, ncols: int, x: torch.Tensor, y: torch.Tensor,
+                    stream=None) -> torch.Tensor:
+    """y += W x (the o projection with the residual add fused)."""
+    check(lib().styx_mul_mat_vec_add(ctx(_dev(x)).handle, _stream(stream), qtype, _ptr(a), nrows, ncols, _ptr(x),
+                                     _ptr(y)))
+    return y
+
+
 def add_f32(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
     """add_flat_f32: out = a + b (out may be a)."""
     if out is None:

@@ -127,6 +127,19 @@ def test_mul_mat_vec_matches_oracle(qname, nrows, ncols):
     assert rel_to_max(got, exp) < 1e-5
 
 
+@pytest.mark.parametrize("qname,nrows,ncols", [("q4_K", 2048, 4096), ("q6_K", 700, 2048)])
+def test_mul_mat_vec_add_is_gemv_then_add(qname, nrows, ncols):
+    qt = _lib.QTYPES[qname]
+    rng = np.random.default_rng(nrows)
+    w = T(O.quantize(qt, rng.normal(0, 0.02, (nrows, ncols)).astype(np.float32)).reshape(-1))
+    x = T(rng.normal(0, 1, ncols).astype(np.float32))
+    y0 = rng.normal(0, 1, nrows).astype(np.float32)
+    y = T(y0)
+    ops.mul_mat_vec_add(qt, w, nrows, ncols, x, y)
+    sep = ops.add_f32(T(y0), ops.mul_mat_vec(qt, w, nrows, ncols, x))
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), sep.cpu().numpy().view(np.uint32))
+
+
 def test_add_f32_in_place():
     rng = np.random.default_rng(2)
     a = rng.normal(0, 1, 5000).astype(np.float32)
