@@ -114,6 +114,12 @@ int styx_check_device_error(styx_ctx *ctx, styx_stream stream);
  * promise costs no hang: a wait that cannot finish gives up after about a
  * second with STYX_ETIMEOUT. */
 #define STYX_OPT_EXCLUSIVE 5
+/* STYX_OPT_ATTN_KERNELS: styx_attn_block as one cooperative kernel when the
+ * shape fits (0, default), always (1: STYX_EUNSUPPORTED otherwise) or as
+ * seven kernels (2).  STYX_OPT_ATTN_LAST_PATH (read only): 1 (one kernel) or
+ * 2 (seven), the form the last styx_attn_block used. */
+#define STYX_OPT_ATTN_KERNELS 6
+#define STYX_OPT_ATTN_LAST_PATH 7
 int styx_set_option(styx_ctx *ctx, int option, int64_t value);
 int styx_get_option(styx_ctx *ctx, int option, int64_t *value);
 

@@ -25,6 +25,7 @@ SKIP = 0xFFFFFFFF
 IDS_PER_LAYER = 64
 MEM_DEVICE, MEM_HOST = 0, 1
 OPT_MOE_KERNELS, OPT_MOE_LAST_PATH, OPT_TRACE, OPT_MOE_LAYERS, OPT_EXCLUSIVE = 1, 2, 3, 4, 5
+OPT_ATTN_KERNELS, OPT_ATTN_LAST_PATH = 6, 7
 MOE_AUTO, MOE_FUSED, MOE_SPLIT = 0, 1, 2
 
 
@@ -171,6 +172,7 @@ _SIGS = {
     "styx_get_rows": (_i, [_vp, _vp, _i, _vp, _i, _i, _vp, _i, _vp]),
     "styx_argmax_f32": (_i, [_vp, _vp, _vp, _i, _vp]),
     "styx_attn_block_workspace_bytes": (_i, [C.POINTER(AttnDims), C.POINTER(_u64)]),
+    "styx_attn_block_workspace_init": (_i, [_vp, _vp, _vp, _u64]),
     "styx_attn_block": (_i, [_vp, _vp, C.POINTER(AttnDims), C.POINTER(AttnLayer), _vp, _i, _vp, _vp, _vp, _i,
                              _vp, _u64]),
 }

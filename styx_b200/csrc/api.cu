@@ -32,6 +32,8 @@ struct styx_ctx {
     int trace = 0;          // STYX_OPT_TRACE
     int moe_layers = 0;     // STYX_OPT_MOE_LAYERS
     int exclusive = 0;      // STYX_OPT_EXCLUSIVE
+    int attn_kernels = 0;   // STYX_OPT_ATTN_KERNELS
+    int attn_last_path = 0; // STYX_OPT_ATTN_LAST_PATH
 };
 
 namespace {
@@ -385,6 +387,10 @@ int styx_set_option(styx_ctx *ctx, int option, int64_t value) {
     case STYX_OPT_EXCLUSIVE:
         ctx->exclusive = value ? 1 : 0;
         return STYX_OK;
+    case STYX_OPT_ATTN_KERNELS:
+        NEED(value >= 0 && value <= 2, "STYX_OPT_ATTN_KERNELS: 0, 1 or 2");
+        ctx->attn_kernels = static_cast<int>(value);
+        return STYX_OK;
     default: return fail(STYX_EINVAL, "unknown or read-only option %d", option);
     }
 }
@@ -397,6 +403,8 @@ int styx_get_option(styx_ctx *ctx, int option, int64_t *value) {
     case STYX_OPT_TRACE: *value = ctx->trace; return STYX_OK;
     case STYX_OPT_MOE_LAYERS: *value = ctx->moe_layers; return STYX_OK;
     case STYX_OPT_EXCLUSIVE: *value = ctx->exclusive; return STYX_OK;
+    case STYX_OPT_ATTN_KERNELS: *value = ctx->attn_kernels; return STYX_OK;
+    case STYX_OPT_ATTN_LAST_PATH: *value = ctx->attn_last_path; return STYX_OK;
     default: return fail(STYX_EINVAL, "unknown option %d", option);
     }
 }
@@ -1439,7 +1447,7 @@ int styx_attn_decode(styx_ctx *ctx, styx_stream stream, const float *q, const fl
 
 namespace {
 struct AttnWs {
-    size_t xnorm, q, k, v, att, part, total;
+    size_t cnt, xnorm, qkv, att, part, total;
 };
 AttnWs attn_ws(const styx_attn_dims &d) {
     AttnWs w{};
@@ -1451,10 +1459,11 @@ AttnWs attn_ws(const styx_attn_dims &d) {
     };
     const size_t H = d.n_embd, qd = static_cast<size_t>(d.n_heads) * d.head_dim,
                  kvd = static_cast<size_t>(d.n_kv_heads) * d.head_dim;
+    // the single kernel's counters: launch counter, per-head arrivals (q, k,
+    // v heads), per-kv-head split arrivals, attention-output arrivals
+    w.cnt = take(8 * (1 + static_cast<size_t>(d.n_heads) + 3 * static_cast<size_t>(d.n_kv_heads) + 1));
     w.xnorm = take(H * 4);
-    w.q = take(qd * 4);
-    w.k = take(kvd * 4);
-    w.v = take(kvd * 4);
+    w.qkv = take((qd + 2 * kvd) * 4);   // q | k | v, contiguous
     w.att = take(qd * 4);
     uint64_t pb = 0;
     styx_attn_workspace_bytes(d.n_heads, d.head_dim, &pb);
@@ -1470,6 +1479,49 @@ int styx_attn_block_workspace_bytes(const styx_attn_dims *dims, uint64_t *out) {
     *out = attn_ws(*dims).total;
     return STYX_OK;
 }
+
+int styx_attn_block_workspace_init(styx_ctx *ctx, styx_stream stream, void *workspace, uint64_t workspace_bytes) {
+    ENTER(ctx);
+    NEED(workspace && workspace_bytes > 0, "null workspace");
+    CK(cudaMemsetAsync(workspace, 0, workspace_bytes, S(stream)));
+    return STYX_OK;
+}
+
+namespace {
+// The single-kernel plan (attn_fused.cu) for these dims / formats at n_t
+// cache rows; false when it does not apply (the caller runs seven kernels).
+bool plan_attn_fused(const styx_attn_dims &d, const styx_attn_layer &lw, int sms, int n_t, styx::AttnFusedArgs &a,
+                     uint32_t &smem) {
+    const int H = d.n_embd, hd = d.head_dim, nh = d.n_heads, nkv = d.n_kv_heads;
+    if (hd != 128 || nh > sms || nh % nkv || nh / nkv > 16 || H > 2048 || H % 256) return false;
+    const int qw = lw.wq.qtype, qv = lw.wv.qtype;
+    if (lw.wk.qtype != qw || lw.wo.qtype != qw || !styx::attn_fused_supported(qw, qv)) return false;
+    const int qd = nh * hd, kvd = nkv * hd, gqa = nh / nkv;
+    if (!units_ok(qw, H) || !units_ok(qv, H) || !units_ok(qw, qd)) return false;
+    a.rb_q = static_cast<int>(row_bytes(qw, H));
+    a.rb_v = static_cast<int>(row_bytes(qv, H));
+    a.rb_o = static_cast<int>(row_bytes(qw, qd));
+    // splits of the sequence over the CTAs of each kv head, >= 16 rows each
+    int S = std::max(1, std::min(sms / nkv, (n_t + 15) / 16));
+    a.tps = (n_t + S - 1) / S;
+    S = (n_t + a.tps - 1) / a.tps;
+    a.n_splits = S;
+    const int R = qd + 2 * kvd, dmax = std::max(H, qd);
+    const size_t dig = static_cast<size_t>(dmax) * 3 + dmax / 32 * 4;
+    const size_t w1_rows = static_cast<size_t>((R + sms - 1) / sms) * std::max(a.rb_q, a.rb_v) + 3 * 32;
+    const size_t w1_attn = (static_cast<size_t>(gqa) * hd + 2 * hd) * 4 + 64 * 16 +
+                           (static_cast<size_t>(a.tps) * gqa + ((2 * gqa + 3) & ~3)) * 4 + 8 * 8 * 128 * 4;
+    const size_t w2 = static_cast<size_t>((H + sms - 1) / sms) * a.rb_o + 32;
+    a.off_dig = 256;
+    a.off_f32 = static_cast<uint32_t>(a16(a.off_dig + dig));
+    a.off_w1 = static_cast<uint32_t>(a128(a.off_f32 + static_cast<size_t>(dmax) * 4));
+    a.off_w2 = static_cast<uint32_t>(a128(a.off_w1 + std::max(w1_rows, w1_attn)));
+    const size_t total = a.off_w2 + w2;
+    if (total > 227 * 1024) return false;
+    smem = static_cast<uint32_t>(total);
+    return true;
+}
+}  // namespace
 
 int styx_attn_block(styx_ctx *ctx, styx_stream stream, const styx_attn_dims *dims, const styx_attn_layer *lw,
                     float *x, int pos, const int32_t *pos_dev, float *kcache, float *vcache, int n_ctx,
@@ -1487,11 +1539,63 @@ int styx_attn_block(styx_ctx *ctx, styx_stream stream, const styx_attn_dims *dim
     NEED(workspace_bytes >= w.total && al16(workspace), "workspace: %llu bytes, 16-byte aligned, needed",
          static_cast<unsigned long long>(w.total));
     uint8_t *ws = static_cast<uint8_t *>(workspace);
-    float *xn = reinterpret_cast<float *>(ws + w.xnorm), *q = reinterpret_cast<float *>(ws + w.q);
-    float *k = reinterpret_cast<float *>(ws + w.k), *v = reinterpret_cast<float *>(ws + w.v);
-    float *att = reinterpret_cast<float *>(ws + w.att);
     const int H = d.n_embd, hd = d.head_dim, qd = d.n_heads * hd, kvd = d.n_kv_heads * hd;
+    float *xn = reinterpret_cast<float *>(ws + w.xnorm), *q = reinterpret_cast<float *>(ws + w.qkv);
+    float *k = q + qd, *v = k + kvd;
+    float *att = reinterpret_cast<float *>(ws + w.att);
+    NEED(al16(kcache) && al16(vcache), "caches must be 16-byte aligned");
+    NEED(extent_ok(kcache, static_cast<uint64_t>(n_ctx) * kvd * 4) &&
+             extent_ok(vcache, static_cast<uint64_t>(n_ctx) * kvd * 4),
+         "caches smaller than n_ctx rows");
+    NEED(extent_ok(x, static_cast<uint64_t>(H) * 4) && extent_ok(lw->attn_norm, static_cast<uint64_t>(H) * 4),
+         "x / attn_norm smaller than n_embd");
     int rc;
+    // one cooperative kernel when the shape fits, else seven launches
+    if (ctx->attn_kernels != 2) {
+        styx::AttnFusedArgs a{};
+        uint32_t smem = 0;
+        const bool fits = plan_attn_fused(d, *lw, ctx->sm_count, pos + 1, a, smem);
+        if (!fits && ctx->attn_kernels == 1)
+            return fail(STYX_EUNSUPPORTED, "single-kernel attention does not fit these dims / formats");
+        if (fits) {
+            const int qw = lw->wq.qtype, qv = lw->wv.qtype;
+            NEED(extent_ok(lw->wq.data, static_cast<uint64_t>(a.rb_q) * qd) &&
+                     extent_ok(lw->wk.data, static_cast<uint64_t>(a.rb_q) * kvd) &&
+                     extent_ok(lw->wv.data, static_cast<uint64_t>(a.rb_v) * kvd) &&
+                     extent_ok(lw->wo.data, static_cast<uint64_t>(a.rb_o) * H),
+                 "a weight matrix is smaller than its shape");
+            a.x = x;
+            a.attn_norm = lw->attn_norm;
+            a.eps = d.rms_eps;
+            a.wq = static_cast<const uint8_t *>(lw->wq.data);
+            a.wk = static_cast<const uint8_t *>(lw->wk.data);
+            a.wv = static_cast<const uint8_t *>(lw->wv.data);
+            a.wo = static_cast<const uint8_t *>(lw->wo.data);
+            a.H = H;
+            a.n_heads = d.n_heads;
+            a.n_kv = d.n_kv_heads;
+            a.q_norm = d.qk_norm ? lw->q_norm : nullptr;
+            a.k_norm = d.qk_norm ? lw->k_norm : nullptr;
+            a.theta_scale = std::pow(static_cast<double>(d.rope_base), -2.0 / static_cast<double>(hd));
+            a.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+            a.n_t = pos + 1;
+            a.kcache = kcache;
+            a.vcache = vcache;
+            a.qkv = q;
+            a.part_acc = reinterpret_cast<float *>(ws + w.part);
+            a.part_ml = a.part_acc + static_cast<size_t>(d.n_heads) * a.n_splits * hd;
+            a.att = att;
+            a.gen = reinterpret_cast<unsigned long long *>(ws + w.cnt);
+            a.head_cnt = a.gen + 1;
+            a.split_cnt = a.head_cnt + d.n_heads + 2 * d.n_kv_heads;
+            a.att_cnt = a.split_cnt + d.n_kv_heads;
+            a.err = ctx->d_err;
+            CK(styx::launch_attn_fused(a, qw, qv, ctx->sm_count, smem, !ctx->exclusive, S(stream)));
+            ctx->attn_last_path = 1;
+            return STYX_OK;
+        }
+    }
+    ctx->attn_last_path = 2;
     if ((rc = styx_rms_norm(ctx, stream, x, lw->attn_norm, d.rms_eps, H, 1, xn))) return rc;
     if ((rc = styx_mul_mat_vec(ctx, stream, lw->wq.qtype, lw->wq.data, qd, H, xn, q))) return rc;
     if ((rc = styx_mul_mat_vec(ctx, stream, lw->wk.qtype, lw->wk.data, kvd, H, xn, k))) return rc;

@@ -204,6 +204,34 @@ struct GetRowsArgs {
 cudaError_t launch_get_rows(const GetRowsArgs &a, cudaStream_t st);
 // scratch: u64[kArgmaxCtas] partial maxima, then a u32 ticket (zero between calls)
 cudaError_t launch_argmax(const float *x, int n, int32_t *out, void *scratch, cudaStream_t st);
+// the attention half of a layer in one cooperative kernel (attn_fused.cu);
+// head_dim 128
+struct AttnFusedArgs {
+    float *x;                          // [H] in/out
+    const float *attn_norm;
+    float eps;
+    const uint8_t *wq, *wk, *wv, *wo;  // row-major blocks; q, k, o of one qtype, v of another
+    int rb_q, rb_v, rb_o;              // row bytes (k as q)
+    int H, n_heads, n_kv;
+    const float *q_norm, *k_norm;      // [128] or null
+    double theta_scale;
+    float scale;
+    int n_t;                           // cache rows read; the token's position is n_t - 1
+    float *kcache, *vcache;            // [n_ctx][n_kv * 128]
+    int tps, n_splits;
+    // workspace
+    float *qkv;                        // [n_heads*128 + 2*n_kv*128]
+    float *part_acc, *part_ml;         // [n_heads][n_splits][128], [n_heads][n_splits][2]
+    float *att;                        // [n_heads*128]
+    unsigned long long *gen, *head_cnt, *split_cnt, *att_cnt;   // zero at workspace init
+    int *err;
+    uint32_t off_dig, off_f32, off_w1, off_w2;
+};
+bool attn_fused_supported(int qw, int qv);
+int attn_fused_threads();
+cudaError_t launch_attn_fused(const AttnFusedArgs &a, int qw, int qv, int grid, uint32_t smem, bool coop,
+                              cudaStream_t st);
+
 constexpr int kAttnMaxSplits = 256;
 constexpr int kArgmaxCtas = 296;   // partial maxima of styx_argmax_f32
 size_t attn_smem_bytes(int gqa, int hd, int tps);

@@ -550,6 +550,15 @@ class AttnBlock:
         check(lib().styx_attn_block_workspace_bytes(C.byref(self.dims), C.byref(v)))
         self.ws_bytes = v.value
         self.workspace = torch.empty(self.ws_bytes, dtype=torch.uint8, device=f"cuda:{device}")
+        self.init_workspace()
+
+    def init_workspace(self, stream=None) -> None:
+        check(lib().styx_attn_block_workspace_init(self.ctx.handle, _stream(stream), _ptr(self.workspace),
+                                                   self.ws_bytes))
+
+    def last_path(self) -> int:
+        """1: the last forward ran as one kernel, 2: as seven."""
+        return self.ctx.get_option(_lib.OPT_ATTN_LAST_PATH)
 
     def forward(self, x: torch.Tensor, w: AttnWeights, pos: int, pos_dev: torch.Tensor, kcache: torch.Tensor,
                 vcache: torch.Tensor, n_ctx: int, stream=None) -> torch.Tensor:

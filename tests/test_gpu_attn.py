@@ -161,16 +161,31 @@ def _attn_layer(seed, H, n_heads, n_kv, hd, qts):
     return ws, an, qn, kn
 
 
-@pytest.mark.parametrize("H,n_heads,n_kv,hd,qk", [(2048, 32, 4, 128, True), (512, 8, 2, 64, False)])
-def test_attn_block_decodes_like_the_oracle(H, n_heads, n_kv, hd, qk):
+FUSED, SEPARATE = 0, 2
+
+
+@pytest.mark.parametrize("form", [FUSED, SEPARATE], ids=["one-kernel", "seven-kernels"])
+@pytest.mark.parametrize("H,n_heads,n_kv,hd,qk", [(2048, 32, 4, 128, True), (1024, 16, 4, 128, False),
+                                                 (512, 8, 2, 64, False)])
+def test_attn_block_decodes_like_the_oracle(H, n_heads, n_kv, hd, qk, form):
     """Six tokens through one layer's attention half (the 30B shape: q/k/o
     q4_K, v q6_K), the caches filling up row by row; x and the caches after
-    every token against the oracle's layer."""
+    every token against the oracle's layer.  Both forms: one cooperative
+    kernel (head_dim 128) and seven launches."""
     qts = (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K, _lib.Q4_K)
     ws, an, qn, kn = _attn_layer(H + hd, H, n_heads, n_kv, hd, qts)
     eps, base, n_ctx = 1e-6, 1_000_000.0, 64
     kvd = n_kv * hd
     blk = ops.AttnBlock(H, n_heads, n_kv, hd, qk, eps, base)
+    blk.ctx.set_option(_lib.OPT_ATTN_KERNELS, form)
+    try:
+        _decode_six(blk, H, n_heads, n_kv, hd, qk, ws, an, qn, kn, eps, base, n_ctx, kvd)
+        assert blk.last_path() == (1 if form == FUSED and hd == 128 else 2)
+    finally:
+        blk.ctx.set_option(_lib.OPT_ATTN_KERNELS, 0)
+
+
+def _decode_six(blk, H, n_heads, n_kv, hd, qk, ws, an, qn, kn, eps, base, n_ctx, kvd):
     w = ops.AttnWeights(T(an), *[ops.DenseWeight(qt, T(raw)) for qt, raw in ws],
                         q_norm=T(qn) if qk else None, k_norm=T(kn) if qk else None)
     kc = torch.zeros(n_ctx, kvd, device=DEV)
@@ -193,3 +208,74 @@ def test_attn_block_decodes_like_the_oracle(H, n_heads, n_kv, hd, qk):
         # from the GPU's rows so that differences do not compound
         okc[: pos + 1] = kc.cpu().numpy()[: pos + 1]
         ovc[: pos + 1] = vc.cpu().numpy()[: pos + 1]
+
+
+@pytest.mark.parametrize("pos", [300, 2047])
+def test_one_kernel_attention_at_long_context(pos):
+    """The single kernel with many splits (cache rows filled at random up to
+    pos) against the oracle; and against the seven-kernel form."""
+    H, n_heads, n_kv, hd = 2048, 32, 4, 128
+    qts = (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K, _lib.Q4_K)
+    ws, an, qn, kn = _attn_layer(pos, H, n_heads, n_kv, hd, qts)
+    eps, base, n_ctx = 1e-6, 1_000_000.0, 2048
+    kvd = n_kv * hd
+    rng = np.random.default_rng(pos)
+    kc0 = rng.normal(0, 1, (n_ctx, kvd)).astype(np.float32)
+    vc0 = rng.normal(0, 1, (n_ctx, kvd)).astype(np.float32)
+    x0 = rng.normal(0, 1, H).astype(np.float32)
+    blk = ops.AttnBlock(H, n_heads, n_kv, hd, True, eps, base)
+    w = ops.AttnWeights(T(an), *[ops.DenseWeight(qt, T(raw)) for qt, raw in ws], q_norm=T(qn), k_norm=T(kn))
+    outs = {}
+    try:
+        for form in (FUSED, SEPARATE):
+            blk.ctx.set_option(_lib.OPT_ATTN_KERNELS, form)
+            kc, vc, x = T(kc0), T(vc0), T(x0)
+            blk.forward(x, w, pos, T(np.array([pos], np.int32)), kc, vc, n_ctx)
+            torch.cuda.synchronize()
+            blk.ctx.check_device_error()
+            assert blk.last_path() == (1 if form == FUSED else 2)
+            outs[form] = (x.cpu().numpy(), kc.cpu().numpy()[pos], vc.cpu().numpy()[pos])
+    finally:
+        blk.ctx.set_option(_lib.OPT_ATTN_KERNELS, 0)
+    okc, ovc = kc0.copy(), vc0.copy()
+    exp = O.attn_block(x0, an, eps, n_heads, n_kv, hd, qn, kn, base, ws, pos, okc, ovc)
+    for form in (FUSED, SEPARATE):
+        x, krow, vrow = outs[form]
+        assert rel_to_max(x, exp) < 1e-4, form
+        assert rel_to_max(krow, okc[pos]) < 1e-4 and rel_to_max(vrow, ovc[pos]) < 1e-4
+    assert rel_to_max(outs[FUSED][0], outs[SEPARATE][0]) < 1e-5
+
+
+def test_one_kernel_attention_split_launch_numbers_time_out_and_recover():
+    """As tests/test_gpu_timeout.py for the attention kernel: the workspace's
+    launch counter set to half a grid splits the CTAs over two launch
+    numbers; every wait gives up after about a second, STYX_ETIMEOUT is
+    reported, and after styx_attn_block_workspace_init the layer is exact."""
+    H, n_heads, n_kv, hd = 1024, 16, 4, 128
+    qts = (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K, _lib.Q4_K)
+    ws, an, qn, kn = _attn_layer(7, H, n_heads, n_kv, hd, qts)
+    eps, base, n_ctx, pos = 1e-6, 1_000_000.0, 16, 3
+    blk = ops.AttnBlock(H, n_heads, n_kv, hd, True, eps, base)
+    w = ops.AttnWeights(T(an), *[ops.DenseWeight(qt, T(raw)) for qt, raw in ws], q_norm=T(qn), k_norm=T(kn))
+    kvd = n_kv * hd
+    rng = np.random.default_rng(8)
+    kc0 = rng.normal(0, 1, (n_ctx, kvd)).astype(np.float32)
+    vc0 = rng.normal(0, 1, (n_ctx, kvd)).astype(np.float32)
+    x0 = rng.normal(0, 1, H).astype(np.float32)
+    blk.ctx.check_device_error()
+    blk.workspace[0:8].view(torch.int64).fill_(blk.ctx.sm_count // 2)   # the launch counter
+    x = T(x0)
+    blk.forward(x, w, pos, T(np.array([pos], np.int32)), T(kc0), T(vc0), n_ctx)
+    torch.cuda.synchronize()
+    assert blk.last_path() == 1
+    with pytest.raises(_lib.StyxError) as ei:
+        blk.ctx.check_device_error()
+    assert ei.value.code == _lib.STYX_ETIMEOUT
+    blk.init_workspace()
+    x, kc, vc = T(x0), T(kc0), T(vc0)
+    blk.forward(x, w, pos, T(np.array([pos], np.int32)), kc, vc, n_ctx)
+    torch.cuda.synchronize()
+    blk.ctx.check_device_error()
+    okc, ovc = kc0.copy(), vc0.copy()
+    exp = O.attn_block(x0, an, eps, n_heads, n_kv, hd, qn, kn, base, ws, pos, okc, ovc)
+    assert rel_to_max(x.cpu().numpy(), exp) < 1e-4

@@ -46,9 +46,10 @@ def gpu_model(m, n_ctx):
                        ops.DenseWeight(Q6_K, T(m.head)), n_ctx)
 
 
-@pytest.mark.parametrize("seed", [0, 1])
-def test_greedy_tokens_identical_to_the_oracle(seed):
-    m = make_model(seed)
+@pytest.mark.parametrize("seed,cfg", [(0, {}), (1, {}), (2, dict(hd=128, n_heads=8, n_kv=2))],
+                         ids=["hd64-s0", "hd64-s1", "hd128-one-kernel-attention"])
+def test_greedy_tokens_identical_to_the_oracle(seed, cfg):
+    m = make_model(seed, **cfg)
     prompt, n_predict, n_ctx = [5, 17, 99], 10, 32
     # the oracle's greedy run (generate_moe's loop), keeping every step
     od = OracleDecoder(m, n_ctx)
@@ -72,6 +73,7 @@ def test_greedy_tokens_identical_to_the_oracle(seed):
         got.append(int(g.next.item()))
         checks.append((g.logits.cpu().numpy(), g.x.cpu().numpy()))
     g.moe.ctx.check_device_error()
+    assert g.attn.last_path() == (1 if m.hp["head_dim"] == 128 else 2)
     for (lg, x), (elg, ex) in zip(checks, steps):
         assert rel_to_max(x, ex) < 1e-3
         assert rel_to_max(lg, elg) < 1e-3
