@@ -1447,7 +1447,7 @@ int styx_attn_decode(styx_ctx *ctx, styx_stream stream, const float *q, const fl
 
 namespace {
 struct AttnWs {
-    size_t cnt, xnorm, qkv, att, part, total;
+    size_t cnt, xnorm, qkv, att, part, trace, total;
 };
 AttnWs attn_ws(const styx_attn_dims &d) {
     AttnWs w{};
@@ -1468,6 +1468,7 @@ AttnWs attn_ws(const styx_attn_dims &d) {
     uint64_t pb = 0;
     styx_attn_workspace_bytes(d.n_heads, d.head_dim, &pb);
     w.part = take(pb);
+    w.trace = take(kTraceCtas * styx::kAttnTraceStamps * 8);   // last: STYX_OPT_TRACE stamps
     w.total = o;
     return w;
 }
@@ -1516,7 +1517,8 @@ bool plan_attn_fused(const styx_attn_dims &d, const styx_attn_layer &lw, int sms
     a.off_f32 = static_cast<uint32_t>(a16(a.off_dig + dig));
     a.off_w1 = static_cast<uint32_t>(a128(a.off_f32 + static_cast<size_t>(dmax) * 4));
     a.off_w2 = static_cast<uint32_t>(a128(a.off_w1 + std::max(w1_rows, w1_attn)));
-    const size_t total = a.off_w2 + w2;
+    a.off_kv = static_cast<uint32_t>(a128(a.off_w2 + w2));
+    const size_t total = a.off_kv + 2 * static_cast<size_t>(styx::kPreRows) * hd * 4;
     if (total > 227 * 1024) return false;
     smem = static_cast<uint32_t>(total);
     return true;
@@ -1584,12 +1586,19 @@ int styx_attn_block(styx_ctx *ctx, styx_stream stream, const styx_attn_dims *dim
             a.qkv = q;
             a.part_acc = reinterpret_cast<float *>(ws + w.part);
             a.part_ml = a.part_acc + static_cast<size_t>(d.n_heads) * a.n_splits * hd;
-            a.att = att;
+            // att as digits, in the att region (3 bytes + 1/8 float per element)
+            a.att_d1 = reinterpret_cast<int8_t *>(att);
+            a.att_d2 = reinterpret_cast<uint8_t *>(att) + qd;
+            a.att_d3 = a.att_d2 + qd;
+            a.att_sc = reinterpret_cast<float *>(a.att_d3 + qd);
             a.gen = reinterpret_cast<unsigned long long *>(ws + w.cnt);
             a.head_cnt = a.gen + 1;
             a.split_cnt = a.head_cnt + d.n_heads + 2 * d.n_kv_heads;
             a.att_cnt = a.split_cnt + d.n_kv_heads;
             a.err = ctx->d_err;
+            a.trace = ctx->trace && ctx->sm_count <= static_cast<int>(kTraceCtas)
+                          ? reinterpret_cast<long long *>(ws + w.trace)
+                          : nullptr;
             CK(styx::launch_attn_fused(a, qw, qv, ctx->sm_count, smem, !ctx->exclusive, S(stream)));
             ctx->attn_last_path = 1;
             return STYX_OK;

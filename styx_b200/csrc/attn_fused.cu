@@ -40,6 +40,13 @@ constexpr int kHD = 128;                 // head_dim of the fused form
 constexpr int kAFHeadsPerPass = 8;
 constexpr long long kAFPollFree = 100000;   // cycles of tight polling before backing off
 
+// 16-byte asynchronous copies global -> shared (no registers held while in flight)
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned long long ld_acq(const unsigned long long *p) {
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -134,6 +141,11 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
     const int o1 = static_cast<int>(static_cast<long long>(H) * (b + 1) / G);
     Seg seg[3];
     const int nseg = qkv_segments(p, r0, r1, seg);
+#define AF_STAMP(i_)                                                           \
+    do {                                                                       \
+        if (tid == 0 && p.trace) p.trace[b * kAttnTraceStamps + (i_)] = clock64(); \
+    } while (0)
+    AF_STAMP(0);
 
     // ------------------------------------------------ phase 0
     if (tid == 0) {
@@ -191,6 +203,23 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
     pdl_wait();
     __syncthreads();
     const unsigned long long tag = *s_tag;
+    AF_STAMP(1);
+    // this CTA's first cache rows of K and V (before row pos), in flight
+    // while phases A and B run: warp w copies rows w and w + 16
+    float *kpre = reinterpret_cast<float *>(smem + p.off_kv);   // [kPreRows][128]
+    float *vpre = kpre + kPreRows * kHD;
+    const int S = p.n_splits;
+    const bool attn_cta = b < p.n_kv * S;
+    const int kvh = attn_cta ? b / S : 0, split = attn_cta ? b % S : 0;
+    const int t0 = split * p.tps, t1 = attn_cta ? min(p.n_t, t0 + p.tps) : 0, nt = t1 - t0;
+    const int pos = p.n_t - 1;
+    for (int t = warp; t < min(nt, kPreRows); t += kAFWarps) {
+        if (t0 + t == pos) continue;
+        const size_t off = static_cast<size_t>(t0 + t) * kvd + kvh * kHD + 4 * lane;
+        cp_async16(kpre + t * kHD + 4 * lane, p.kcache + off);
+        cp_async16(vpre + t * kHD + 4 * lane, p.vcache + off);
+    }
+    cp_async_commit();
 
     // ------------------------------------------------ phase A: x -> RMSNorm -> digits
     float ss = 0.f;
@@ -208,10 +237,12 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
         for (int g = warp; g < (H >> 5); g += kAFWarps) digits_group_warp(fst[g * 32 + lane], lane, dv, g);
     }
     __syncthreads();
+    AF_STAMP(2);
 
     // ------------------------------------------------ phase B: q|k|v rows
     {
         bool ok = mbar_wait(&bar[0], 0, p.err, kErrWaitFull);
+        AF_STAMP(3);
         const int units = H >> 6, gs = units >= 32 ? 32 : units >= 16 ? 16 : units >= 8 ? 8 : units >= 4 ? 4 : 2;
         const int rpw = 32 / gs, ug = lane & (gs - 1), grp = lane / gs;
         const bool active = ug < units;
@@ -224,16 +255,26 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
             } else {
                 if (active) load_xunit<QW>(x, dg1, dg2, dg3, dsc, ug);
             }
-            for (int t = warp * rpw; t < n; t += kAFWarps * rpw) {
-                const int row = t + grp;
-                float v = 0.f;
-                if (ok && active && row < n) {
-                    if (seg[i].m == 2) v = unit_dot<QV>(base + static_cast<size_t>(row) * p.rb_v, ug, x);
-                    else v = unit_dot<QW>(base + static_cast<size_t>(row) * p.rb_q, ug, x);
+            const int rb = seg[i].m == 2 ? p.rb_v : p.rb_q;
+            for (int t = warp * rpw * 2; t < n; t += kAFWarps * rpw * 2) {   // two rows in flight
+                const int ra = t + grp, rc = t + rpw + grp;
+                float va = 0.f, vc = 0.f;
+                if (ok && active) {
+                    if (seg[i].m == 2) {
+                        if (ra < n) va = unit_dot<QV>(base + static_cast<size_t>(ra) * rb, ug, x);
+                        if (rc < n) vc = unit_dot<QV>(base + static_cast<size_t>(rc) * rb, ug, x);
+                    } else {
+                        if (ra < n) va = unit_dot<QW>(base + static_cast<size_t>(ra) * rb, ug, x);
+                        if (rc < n) vc = unit_dot<QW>(base + static_cast<size_t>(rc) * rb, ug, x);
+                    }
                 }
                 __syncwarp();
-                for (int o = gs >> 1; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (ug == 0 && row < n) p.qkv[seg[i].out0 + row] = v;
+                for (int o = gs >> 1; o; o >>= 1) {
+                    va += __shfl_xor_sync(0xffffffffu, va, o);
+                    vc += __shfl_xor_sync(0xffffffffu, vc, o);
+                }
+                if (ug == 0 && ra < n) p.qkv[seg[i].out0 + ra] = va;
+                if (ug == 0 && rc < n) p.qkv[seg[i].out0 + rc] = vc;
             }
         }
         __syncthreads();
@@ -248,12 +289,11 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
             }
         }
     }
+    AF_STAMP(4);
 
     // ------------------------------------------------ phase C: attention partials
-    const int S = p.n_splits;
-    if (b < p.n_kv * S) {
-        const int kvh = b / S, split = b % S;
-        const int t0 = split * p.tps, t1 = min(p.n_t, t0 + p.tps), nt = t1 - t0;
+    cp_async_wait_all();
+    if (attn_cta) {
         float *sq = reinterpret_cast<float *>(w1);                 // [gqa][128] q heads
         float *sk = sq + gqa * kHD;                                // [128] k (row pos)
         float *sv = sk + kHD;                                      // [128] v (row pos)
@@ -278,6 +318,7 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
             rope[tid] = make_double2(cs, sn);
         }
         __syncthreads();
+        AF_STAMP(5);
         const bool ok = *s_ok;
         for (int i = tid; i < gqa * kHD; i += kAF) sq[i] = __ldcg(p.qkv + kvh * gqa * kHD + i);
         for (int i = tid; i < kHD; i += kAF) {
@@ -307,7 +348,6 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
             hv[lane + 96] = static_cast<float>(a1 * rb.y + a3 * rb.x);
         }
         __syncthreads();
-        const int pos = p.n_t - 1;
         if (split == 0) {   // the cache rows of this token
             float *kr = p.kcache + static_cast<size_t>(pos) * kvd + kvh * kHD;
             float *vr = p.vcache + static_cast<size_t>(pos) * kvd + kvh * kHD;
@@ -319,9 +359,10 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
         // scores: one token per warp pass, lane c holds elements 4c..4c+3
         for (int t = warp; t < nt; t += kAFWarps) {
             const int tt = t0 + t;
-            const float4 kv = tt == pos ? *reinterpret_cast<const float4 *>(sk + 4 * lane)
-                                        : __ldg(reinterpret_cast<const float4 *>(
-                                              p.kcache + static_cast<size_t>(tt) * kvd + kvh * kHD) + lane);
+            const float4 kv = tt == pos       ? *reinterpret_cast<const float4 *>(sk + 4 * lane)
+                              : t < kPreRows ? *reinterpret_cast<const float4 *>(kpre + t * kHD + 4 * lane)
+                                             : __ldg(reinterpret_cast<const float4 *>(
+                                                   p.kcache + static_cast<size_t>(tt) * kvd + kvh * kHD) + lane);
             for (int g = 0; g < gqa; g++) {
                 const float4 qv = *reinterpret_cast<const float4 *>(sq + g * kHD + 4 * lane);
                 float d = qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
@@ -330,6 +371,7 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
             }
         }
         __syncthreads();
+        AF_STAMP(6);
         for (int g = warp; g < gqa; g += kAFWarps) {
             float m = -INFINITY;
             for (int t = lane; t < nt; t += 32) m = fmaxf(m, ssc[t * gqa + g]);
@@ -354,9 +396,10 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
             for (int g = 0; g < kAFHeadsPerPass; g++) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int t = warp; t < nt; t += kAFWarps) {
                 const int tt = t0 + t;
-                const float4 vv = tt == pos ? *reinterpret_cast<const float4 *>(sv + 4 * lane)
-                                            : __ldg(reinterpret_cast<const float4 *>(
-                                                  p.vcache + static_cast<size_t>(tt) * kvd + kvh * kHD) + lane);
+                const float4 vv = tt == pos       ? *reinterpret_cast<const float4 *>(sv + 4 * lane)
+                                  : t < kPreRows ? *reinterpret_cast<const float4 *>(vpre + t * kHD + 4 * lane)
+                                                 : __ldg(reinterpret_cast<const float4 *>(
+                                                       p.vcache + static_cast<size_t>(tt) * kvd + kvh * kHD) + lane);
 #pragma unroll
                 for (int g = 0; g < kAFHeadsPerPass; g++) {
                     if (g < ng) {
@@ -403,6 +446,7 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
             atomicAdd(p.split_cnt + kvh, 1ull);
         }
     }
+    AF_STAMP(7);
 
     // ------------------------------------------------ phase D: merge head b's splits
     if (b < p.n_heads) {
@@ -410,6 +454,7 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
         if (tid == 0 && !wait_count(p.split_cnt + b / gqa, tag * static_cast<unsigned long long>(S), p.err))
             *s_ok = 0;
         __syncthreads();
+        AF_STAMP(8);
         const float *ml = p.part_ml + static_cast<size_t>(b) * S * 2;
         float m = -INFINITY;
         for (int s = tid; s < S; s += kAF) m = fmaxf(m, __ldcg(ml + 2 * s));
@@ -427,11 +472,22 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
         }
         const float L = af_block_sum(l, red);
         const float inv = 1.0f / L;
+        // column c = tid % 128 summed by four threads (splits q, q+4, ..),
+        // then the four partials in order
         const float *acc = p.part_acc + static_cast<size_t>(b) * S * kHD;
-        for (int c = tid; c < kHD; c += kAF) {
+        {
+            const int c = tid & (kHD - 1), q = tid >> 7;
             float o = 0.f;
-            for (int s = 0; s < S; s++) o += w[s] * __ldcg(acc + static_cast<size_t>(s) * kHD + c);
-            p.att[b * kHD + c] = o * inv;
+#pragma unroll 4
+            for (int s = q; s < S; s += kAF / kHD) o += w[s] * __ldcg(acc + static_cast<size_t>(s) * kHD + c);
+            fst[q * kHD + c] = o;
+        }
+        __syncthreads();
+        if (warp < kHD / 32) {   // head b's 4 groups of 32 -> digits, published for phase E
+            const int c = warp * 32 + lane;
+            const float o = (fst[c] + fst[kHD + c] + fst[2 * kHD + c] + fst[3 * kHD + c]) * inv;
+            const DigitsView dv{p.att_d1 + b * kHD, p.att_d2 + b * kHD, p.att_d3 + b * kHD, p.att_sc + b * (kHD / 32)};
+            digits_group_warp(o, lane, dv, warp);
         }
         __syncthreads();
         if (tid == 0) {
@@ -441,14 +497,20 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
     }
 
     // ------------------------------------------------ phase E: x += Wo . att
+    AF_STAMP(9);
     if (tid == 0 && !wait_count(p.att_cnt, tag * static_cast<unsigned long long>(p.n_heads), p.err)) *s_ok = 0;
     __syncthreads();
+    AF_STAMP(10);
     {
-        for (int i = tid; i < qd; i += kAF) fst[i] = __ldcg(p.att + i);
+        // att's digits, as the merging CTAs published them
+        for (int i = tid; i < qd / 16; i += kAF) {
+            reinterpret_cast<uint4 *>(dg1)[i] = __ldcg(reinterpret_cast<const uint4 *>(p.att_d1) + i);
+            reinterpret_cast<uint4 *>(dg2)[i] = __ldcg(reinterpret_cast<const uint4 *>(p.att_d2) + i);
+            reinterpret_cast<uint4 *>(dg3)[i] = __ldcg(reinterpret_cast<const uint4 *>(p.att_d3) + i);
+        }
+        for (int i = tid; i < qd / 32; i += kAF) dsc[i] = __ldcg(p.att_sc + i);
         __syncthreads();
-        const DigitsView dv{dg1, dg2, dg3, dsc};
-        for (int g = warp; g < (qd >> 5); g += kAFWarps) digits_group_warp(fst[g * 32 + lane], lane, dv, g);
-        __syncthreads();
+        AF_STAMP(11);
         const bool ok = mbar_wait(&bar[1], 0, p.err, kErrWaitFull) && *s_ok;
         const int units = qd >> 6, gs = 32, ug = lane;   // qd >= 2048: every lane has units
         const int n = o1 - o0;
@@ -467,6 +529,8 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
             if (lane == 0 && ok) p.x[o0 + row] = p.x[o0 + row] + v;
         }
     }
+    AF_STAMP(12);
+#undef AF_STAMP
     // no copies in flight at exit (both barriers completed above on the
     // normal path; after a timed-out wait, wait for them, bounded)
     if (tid == 0) {

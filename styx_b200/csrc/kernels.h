@@ -222,11 +222,16 @@ struct AttnFusedArgs {
     // workspace
     float *qkv;                        // [n_heads*128 + 2*n_kv*128]
     float *part_acc, *part_ml;         // [n_heads][n_splits][128], [n_heads][n_splits][2]
-    float *att;                        // [n_heads*128]
+    int8_t *att_d1;                    // att as digits ([n_heads*128] each, scales [n_heads*4])
+    uint8_t *att_d2, *att_d3;
+    float *att_sc;
     unsigned long long *gen, *head_cnt, *split_cnt, *att_cnt;   // zero at workspace init
     int *err;
-    uint32_t off_dig, off_f32, off_w1, off_w2;
+    long long *trace;                  // STYX_OPT_TRACE: clock64 stamps [CTA][16], else null
+    uint32_t off_dig, off_f32, off_w1, off_w2, off_kv;
 };
+constexpr int kAttnTraceStamps = 16;
+constexpr int kPreRows = 32;   // cache rows of K and of V a CTA prefetches (async copies)
 bool attn_fused_supported(int qw, int qv);
 int attn_fused_threads();
 cudaError_t launch_attn_fused(const AttnFusedArgs &a, int qw, int qv, int grid, uint32_t smem, bool coop,
