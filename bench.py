@@ -294,6 +294,7 @@ def run_decode(args, local: int) -> int:
     model.step(stream)                      # eager once
     stream.synchronize()
     blk_ctx.check_device_error(stream)
+    attn_path = model.attn.last_path()
     graph = C.c_void_p()
     _lib.check(lib.styx_graph_begin(cx, sp))
     model.step(stream)
@@ -345,10 +346,12 @@ def run_decode(args, local: int) -> int:
                                f"pick; {ctx} cache rows before the token",
                    "ctx": ctx, "l2": "inputs larger than L2 (%.2f GB read per token)" % (bytes_tok / 1e9),
                    "launch": "cooperative" if args.shared_device else
-                   "plain (STYX_OPT_EXCLUSIVE: the bench owns its GPU)"},
+                   "plain (STYX_OPT_EXCLUSIVE: the bench owns its GPU)",
+                   "attention": "one kernel per layer" if attn_path == 1 else "eight kernels per layer"},
         "e2e": {"value": n_e2e / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-        # embedding; per layer rms, q, k, v, norms+RoPE+cache, attention (2), o, add, MoE; norm, head, pick
-        "gpu_launches": args.steps * (1 + L * 10 + 3),
+        # embedding; per layer the attention half (one kernel, or rms, q, k, v, norms+RoPE+cache,
+        # attention (2), o+add) and the MoE block; output norm, head, pick
+        "gpu_launches": args.steps * (1 + L * ((1 if attn_path == 1 else 8) + 1) + 3),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None, "peak_kind": peak_kind,
                      "unit_of_work": "one token: %d algorithmic bytes (expert slabs, router, attention "
