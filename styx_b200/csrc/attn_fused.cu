@@ -278,6 +278,7 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
             }
         }
         __syncthreads();
+        AF_STAMP(13);
         if (tid == 0) {   // publish: rows of each head this CTA wrote
             __threadfence();
             for (int i = 0; i < nseg; i++) {
@@ -512,21 +513,28 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
         __syncthreads();
         AF_STAMP(11);
         const bool ok = mbar_wait(&bar[1], 0, p.err, kErrWaitFull) && *s_ok;
-        const int units = qd >> 6, gs = 32, ug = lane;   // qd >= 2048: every lane has units
+        // the row's units in groups of 32 (one unit per lane, its digits
+        // loaded once), each group on kAFWarps / ngrp warps that walk the
+        // rows; the groups' sums are added in group order
+        const int units = qd >> 6, ngrp = (units + 31) >> 5, wpg = kAFWarps / ngrp;
+        const int grp = warp / wpg, u = grp * 32 + lane;
         const int n = o1 - o0;
         const uint8_t *base = w2 + s_soff[3];
-        for (int row = warp; row < n; row += kAFWarps) {
+        float *opart = fst;   // [ngrp][n]
+        XUnit x;
+        if (grp < ngrp && u < units) load_xunit<QW>(x, dg1, dg2, dg3, dsc, u);
+        for (int row = warp % wpg; grp < ngrp && row < n; row += wpg) {
             float v = 0.f;
-            if (ok) {
-                for (int u = ug; u < units; u += gs) {
-                    XUnit x;
-                    load_xunit<QW>(x, dg1, dg2, dg3, dsc, u);
-                    v += unit_dot<QW>(base + static_cast<size_t>(row) * p.rb_o, u, x);
-                }
-            }
+            if (ok && u < units) v = unit_dot<QW>(base + static_cast<size_t>(row) * p.rb_o, u, x);
             __syncwarp();
             v = af_warp_sum(v);
-            if (lane == 0 && ok) p.x[o0 + row] = p.x[o0 + row] + v;
+            if (lane == 0) opart[grp * n + row] = v;
+        }
+        __syncthreads();
+        if (tid < n && ok) {
+            float v = 0.f;
+            for (int g = 0; g < ngrp; g++) v += opart[g * n + tid];
+            p.x[o0 + tid] = p.x[o0 + tid] + v;
         }
     }
     AF_STAMP(12);
