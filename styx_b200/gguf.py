@@ -15,6 +15,9 @@ the way MoeModel::load reads them (crates/model/src/moe.rs:538-599,
 856-892, 1056-1078): the architecture's metadata keys, ffn_norm (or
 post_attention_norm), the f32 router ffn_gate_inp and the three expert
 tensors ffn_{gate,up,down}_exps, each one buffer of n_expert contiguous slabs.
+`load_decode_model` adds the rest of MoeModel::load (moe.rs:996-1108): the
+embedding, the attention tensors and norms of every layer, output_norm and
+the LM head, into a `styx_b200.decode.DecodeModel`.
 """
 from __future__ import annotations
 
@@ -419,4 +422,109 @@ def write_moe_gguf(path, arch: str, n_embd: int, n_ff: int, n_expert: int, n_exp
         w.add_tensor(f"blk.{l}.ffn_gate_exps.weight", [n_embd, n_ff, n_expert], qg, ly["gate"])
         w.add_tensor(f"blk.{l}.ffn_up_exps.weight", [n_embd, n_ff, n_expert], qu, ly["up"])
         w.add_tensor(f"blk.{l}.ffn_down_exps.weight", [n_ff, n_embd, n_expert], qd, ly["down"])
+    w.write(path)
+
+
+# ------------------------------------------------------------ the whole decode model
+def decode_params(g: Gguf):
+    """DecodeParams from a model file's metadata (MoeModel::load,
+    moe.rs:550-590): the MoE keys, attention.head_count / head_count_kv,
+    attention.key_length (else n_embd / n_heads), rope.freq_base, and
+    n_vocab from token_embd's dims."""
+    from .decode import DecodeParams
+    arch, n_layers, dims = moe_dims(g)
+    n_heads = g.get_u32(f"{arch}.attention.head_count")
+    n_kv = g.get_u32(f"{arch}.attention.head_count_kv")
+    key = f"{arch}.attention.key_length"
+    head_dim = g.get_u32(key) if g.value_types.get(key) == U32 else dims.n_embd // n_heads
+    rope_base = g.get_f32(f"{arch}.rope.freq_base")
+    n_vocab = g.tensor("token_embd.weight").dims[1]
+    return DecodeParams(n_layers, dims.n_embd, n_heads, n_kv, head_dim, dims.n_ff, dims.n_expert,
+                        dims.n_expert_used, n_vocab, dims.rms_eps, rope_base, dims.norm_topk,
+                        g.has_tensor("blk.0.attn_q_norm.weight"))
+
+
+def load_decode_model(g: Gguf, n_ctx: int, device: int = 0, experts_in_host: bool = False):
+    """A DecodeModel (styx_b200.decode) from a model file, as MoeModel::load
+    uploads it (moe.rs:996-1108): token_embd (the embedding rows), per layer
+    attn_norm, attn_q / attn_k / attn_v / attn_output, attn_q_norm /
+    attn_k_norm when present and the MoE block's tensors, then output_norm
+    and output (the LM head).  Returns (model, host buffers to keep)."""
+    import torch
+
+    from . import ops
+    from .decode import DecodeLayer, DecodeModel
+    hp = decode_params(g)
+    dev = f"cuda:{device}"
+    H, qd, kvd = hp.n_embd, hp.n_heads * hp.head_dim, hp.n_kv_heads * hp.head_dim
+
+    def f32(name, n):
+        t = g.tensor(name)
+        if t.ggml_type != _lib.F32 or t.dims != [n]:
+            raise ValueError(f"{name}: f32 [{n}] expected, got type {t.ggml_type} dims {t.dims}")
+        return torch.from_numpy(g.tensor_data(name).view(np.float32).copy()).to(dev)
+
+    def dense(name, rows, cols):
+        t = g.tensor(name)
+        if t.ggml_type not in _lib.BLOCK:
+            raise ValueError(f"{name}: ggml type {t.ggml_type} is not a supported block format")
+        if t.dims != [cols, rows]:
+            raise ValueError(f"{name}: dims {t.dims}, expected {[cols, rows]}")
+        return ops.DenseWeight(t.ggml_type, torch.from_numpy(g.tensor_data(name).copy()).to(dev))
+
+    _, moe_layers, keep = load_moe_layers(g, device, experts_in_host=experts_in_host)
+    layers = []
+    for l, moe in enumerate(moe_layers):
+        n = lambda s: f"blk.{l}.{s}.weight"   # noqa: E731
+        attn = ops.AttnWeights(f32(n("attn_norm"), H), dense(n("attn_q"), qd, H), dense(n("attn_k"), kvd, H),
+                               dense(n("attn_v"), kvd, H), dense(n("attn_output"), H, qd),
+                               q_norm=f32(n("attn_q_norm"), hp.head_dim) if hp.qk_norm else None,
+                               k_norm=f32(n("attn_k_norm"), hp.head_dim) if hp.qk_norm else None)
+        layers.append(DecodeLayer(attn, moe))
+    model = DecodeModel(hp, dense("token_embd.weight", hp.n_vocab, H), layers, f32("output_norm.weight", H),
+                        dense("output.weight", hp.n_vocab, H), n_ctx, device)
+    return model, keep
+
+
+def write_decode_gguf(path, arch: str, hp: dict, embd, layers: Sequence[dict], output_norm, head,
+                      qtypes: dict) -> None:
+    """A whole Qwen3-MoE model file: the keys decode_params reads and the
+    tensors load_decode_model uploads.  hp: n_layers, n_embd, n_heads,
+    n_kv_heads, head_dim, n_ff, n_expert, n_expert_used, n_vocab, rms_eps,
+    rope_base.  layers: dicts of numpy arrays (attn_norm, wq, wk, wv, wo raw
+    bytes, q_norm, k_norm or None, ffn_norm, router, gate, up, down raw
+    bytes); qtypes: the ggml types of embd, head, wq, wk, wv, wo, gate, up,
+    down."""
+    H, E, F = hp["n_embd"], hp["n_expert"], hp["n_ff"]
+    qd, kvd = hp["n_heads"] * hp["head_dim"], hp["n_kv_heads"] * hp["head_dim"]
+    w = GgufWriter()
+    w.add_string("general.architecture", arch)
+    w.add_u32(f"{arch}.block_count", len(layers))
+    w.add_u32(f"{arch}.embedding_length", H)
+    w.add_u32(f"{arch}.attention.head_count", hp["n_heads"])
+    w.add_u32(f"{arch}.attention.head_count_kv", hp["n_kv_heads"])
+    w.add_u32(f"{arch}.attention.key_length", hp["head_dim"])
+    w.add_u32(f"{arch}.expert_count", E)
+    w.add_u32(f"{arch}.expert_used_count", hp["n_expert_used"])
+    w.add_u32(f"{arch}.expert_feed_forward_length", F)
+    w.add_f32(f"{arch}.attention.layer_norm_rms_epsilon", hp["rms_eps"])
+    w.add_f32(f"{arch}.rope.freq_base", hp["rope_base"])
+    w.add_tensor("token_embd.weight", [H, hp["n_vocab"]], qtypes["embd"], embd)
+    for l, ly in enumerate(layers):
+        n = lambda s: f"blk.{l}.{s}.weight"   # noqa: E731
+        w.add_tensor(n("attn_norm"), [H], _lib.F32, np.asarray(ly["attn_norm"], np.float32))
+        w.add_tensor(n("attn_q"), [H, qd], qtypes["wq"], ly["wq"])
+        w.add_tensor(n("attn_k"), [H, kvd], qtypes["wk"], ly["wk"])
+        w.add_tensor(n("attn_v"), [H, kvd], qtypes["wv"], ly["wv"])
+        w.add_tensor(n("attn_output"), [qd, H], qtypes["wo"], ly["wo"])
+        if ly.get("q_norm") is not None:
+            w.add_tensor(n("attn_q_norm"), [hp["head_dim"]], _lib.F32, np.asarray(ly["q_norm"], np.float32))
+            w.add_tensor(n("attn_k_norm"), [hp["head_dim"]], _lib.F32, np.asarray(ly["k_norm"], np.float32))
+        w.add_tensor(n("ffn_norm"), [H], _lib.F32, np.asarray(ly["ffn_norm"], np.float32))
+        w.add_tensor(n("ffn_gate_inp"), [H, E], _lib.F32, np.asarray(ly["router"], np.float32))
+        w.add_tensor(n("ffn_gate_exps"), [H, F, E], qtypes["gate"], ly["gate"])
+        w.add_tensor(n("ffn_up_exps"), [H, F, E], qtypes["up"], ly["up"])
+        w.add_tensor(n("ffn_down_exps"), [F, H, E], qtypes["down"], ly["down"])
+    w.add_tensor("output_norm.weight", [H], _lib.F32, np.asarray(output_norm, np.float32))
+    w.add_tensor("output.weight", [H, hp["n_vocab"]], qtypes["head"], head)
     w.write(path)

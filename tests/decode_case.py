@@ -76,3 +76,26 @@ class OracleDecoder:
         logits = O.matvec_q(Q6_K, m.head, hp["n_vocab"], H, xn)
         self.n_past += 1
         return logits, x, ids
+
+
+def write_gguf(m: Model, path) -> None:
+    """The model as a qwen3moe GGUF file (styx_b200.gguf.write_decode_gguf)."""
+    from styx_b200 import gguf as G
+    layers = [dict(attn_norm=ly["attn_norm"], wq=ly["wq"][1], wk=ly["wk"][1], wv=ly["wv"][1], wo=ly["wo"][1],
+                   q_norm=ly["q_norm"], k_norm=ly["k_norm"], ffn_norm=ly["ffn_norm"], router=ly["router"],
+                   gate=ly["gate"], up=ly["up"], down=ly["down"]) for ly in m.layers]
+    ly0 = m.layers[0]
+    qtypes = dict(embd=Q4_K, head=Q6_K, wq=ly0["wq"][0], wk=ly0["wk"][0], wv=ly0["wv"][0], wo=ly0["wo"][0],
+                  gate=Q4_K, up=Q4_K, down=Q6_K)
+    G.write_decode_gguf(path, "qwen3moe", m.hp, m.embd, layers, m.output_norm, m.head, qtypes)
+
+
+def oracle_greedy(m: Model, prompt, n_predict, n_ctx=64):
+    od = OracleDecoder(m, n_ctx)
+    for t in prompt:
+        lg, _, _ = od.forward_token(t)
+    toks = [total_cmp_argmax_last(lg)]
+    for _ in range(1, n_predict):
+        lg, _, _ = od.forward_token(toks[-1])
+        toks.append(total_cmp_argmax_last(lg))
+    return toks

@@ -302,3 +302,22 @@ def test_gguf_py_reads_a_file_written_here(tmp_path):
     assert np.array_equal(np.asarray(t["a"].data).reshape(-1), np.arange(32, dtype=np.float32))
     assert int(t["b"].tensor_type) == 12 and list(t["b"].shape) == [256, 2]
     assert np.array_equal(np.asarray(t["b"].data).reshape(-1), np.arange(288, dtype=np.uint8))
+
+
+def test_decode_model_keys_round_trip(tmp_path):
+    """A whole model file (write_decode_gguf) gives back the hyper-parameters
+    MoeModel::load reads (moe.rs:550-590) and every tensor it uploads."""
+    from tests.decode_case import make_model, write_gguf
+    m = make_model(3, n_layers=2, H=512, n_heads=8, n_kv=2, hd=128, F=256, E=8, k=2, n_vocab=300)
+    path = tmp_path / "model.gguf"
+    write_gguf(m, path)
+    g = G.Gguf.open(path)
+    hp = G.decode_params(g)
+    assert (hp.n_layers, hp.n_embd, hp.n_heads, hp.n_kv_heads, hp.head_dim) == (2, 512, 8, 2, 128)
+    assert (hp.n_ff, hp.n_expert, hp.n_expert_used, hp.n_vocab) == (256, 8, 2, 300)
+    assert hp.qk_norm and hp.norm_topk and hp.rope_base == 1_000_000.0
+    assert np.array_equal(g.tensor_data("token_embd.weight"), m.embd)
+    assert np.array_equal(g.tensor_data("blk.1.attn_v.weight"), m.layers[1]["wv"][1])
+    assert np.array_equal(g.tensor_data("output.weight"), m.head)
+    assert g.tensor("blk.0.attn_output.weight").dims == [8 * 128, 512]
+    g.close()

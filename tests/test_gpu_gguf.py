@@ -59,3 +59,20 @@ def test_moe_layers_from_a_gguf_match_the_oracle(tmp_path, experts_in_host):
     g.close()
     for hb in keep:
         hb.free()
+
+
+def test_whole_model_from_a_gguf_decodes_greedy_identical(tmp_path):
+    """A model file through the reader and load_decode_model into the decode
+    step (single-kernel attention, head_dim 128): generate() gives the
+    oracle's greedy tokens for the same bytes (generate_moe's loop)."""
+    from tests.decode_case import make_model, oracle_greedy, write_gguf
+    m = make_model(5, n_layers=2, H=512, n_heads=8, n_kv=2, hd=128)
+    path = tmp_path / "model.gguf"
+    write_gguf(m, path)
+    g = G.Gguf.open(path)
+    model, keep = G.load_decode_model(g, n_ctx=32)
+    g.close()
+    prompt, n_predict = [11, 250, 3], 8
+    assert model.generate(prompt, n_predict) == oracle_greedy(m, prompt, n_predict)
+    assert model.attn.last_path() == 1
+    model.moe.ctx.check_device_error()
