@@ -358,8 +358,50 @@ def run_decode(args, local: int) -> int:
                                      "weights, cache rows, LM head, embedding row)" % bytes_tok},
         "clocks": clk.summary(),
     }
+    if not args.no_cpu:
+        try:
+            nth = os.cpu_count() or 1
+            v, desc = time_cpu_decode(args.cpu_seconds, nth, ctx)
+            line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": nth, "kind": "port", "sample": desc}
+        except Exception as e:  # the CPU leg must not sink the GPU number
+            line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": 0, "kind": "port",
+                                    "sample": f"failed: {e}"}
     print(json.dumps(line))
     return 0
+
+
+def time_cpu_decode(budget_s: float, nthreads: int, ctx: int):
+    """The decode step's CPU leg on the oracle: the MoE block (C, OpenMP over
+    rows, time_cpu), the attention half of a layer (C, one thread; 30B shapes,
+    ctx cache rows) and a 4,096-row sample of the LM head (C, one thread),
+    scaled to 48 layers + the whole head.  Returns (tok/s, description)."""
+    from oracle import oracle as O
+    _, moe_layer, reps = time_cpu(budget_s * 0.6, nthreads)
+    rng = np.random.default_rng(11)
+    qd, kvd = N_HEADS * HD, N_KV * HD
+
+    def q(qt, r, c):
+        return O.quantize(qt, rng.standard_normal((r, c), np.float32) * np.float32(0.02)).reshape(-1)
+    ws = [(Q4_K, q(Q4_K, qd, H)), (Q4_K, q(Q4_K, kvd, H)), (Q6_K, q(Q6_K, kvd, H)), (Q4_K, q(Q4_K, H, qd))]
+    kc = rng.standard_normal((ctx + 1, kvd), np.float32)
+    vc = rng.standard_normal((ctx + 1, kvd), np.float32)
+    x = rng.standard_normal(H, np.float32)
+    ones_h, ones_d = np.ones(H, np.float32), np.ones(HD, np.float32)
+    t0 = time.perf_counter()
+    n_attn = 0
+    while n_attn < 3 or time.perf_counter() - t0 < budget_s * 0.2:
+        O.attn_block(x, ones_h, 1e-6, N_HEADS, N_KV, HD, ones_d, ones_d, 1e6, ws, ctx, kc, vc)
+        n_attn += 1
+    attn_layer = (time.perf_counter() - t0) / n_attn
+    rows = 4096
+    head = q(Q6_K, rows, H)
+    t0 = time.perf_counter()
+    O.matvec_q(Q6_K, head, rows, H, x)
+    head_s = (time.perf_counter() - t0) * N_VOCAB / rows
+    per_tok = N_LAYERS * (moe_layer + attn_layer) + head_s
+    return 1.0 / per_tok, (f"oracle: MoE block {moe_layer * 1e3:.2f} ms/layer ({reps} runs, {nthreads} threads), "
+                           f"attention half {attn_layer * 1e3:.2f} ms/layer at {ctx} rows ({n_attn} runs, 1 thread), "
+                           f"LM head {head_s * 1e3:.1f} ms (4,096-row sample, 1 thread); scaled to 48 layers")
 
 
 def decode_bytes_per_token(n_layers: int, ctx: int) -> int:
