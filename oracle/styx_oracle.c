@@ -1,5 +1,7 @@
 /*
- * styx_oracle.c -- CPU oracle for the Qwen3-MoE block hot path.
+ * styx_oracle.c -- CPU oracle for the Qwen3-MoE block hot path, and for the
+ * attention half of a decode layer (or_rope_neox, or_attn_decode,
+ * or_attn_block: moe.rs:1857-1972, shaders/attn_decode_f32.comp).
  *
  * TEST INFRASTRUCTURE ONLY: loaded by tests/, __graft_entry__.smoke() and the
  * CPU legs of bench.py as the checker; never by the product library.

@@ -279,3 +279,13 @@ def test_one_kernel_attention_split_launch_numbers_time_out_and_recover():
     okc, ovc = kc0.copy(), vc0.copy()
     exp = O.attn_block(x0, an, eps, n_heads, n_kv, hd, qn, kn, base, ws, pos, okc, ovc)
     assert rel_to_max(x.cpu().numpy(), exp) < 1e-4
+
+
+def test_attention_options_are_checked():
+    c = ops.ctx(0)
+    with pytest.raises(_lib.StyxError) as ei:
+        c.set_option(_lib.OPT_ATTN_KERNELS, 3)
+    assert ei.value.code == _lib.STYX_EINVAL
+    with pytest.raises(_lib.StyxError):
+        c.set_option(_lib.OPT_ATTN_LAST_PATH, 1)     # read only
+    assert c.get_option(_lib.OPT_ATTN_KERNELS) == 0
