@@ -247,7 +247,9 @@ int mv_rows_per_cta(int nrows, int n_ids, int gs, int sms) {
 }
 
 // reference-shaped 3-way expert GEMV (rec_matvec_id, moe.rs:1649-1700): hot,
-// arena and full-tensor rows, each a SKIP-gated dispatch over all k slots
+// arena and full-tensor rows in one launch, each slot reading from the last
+// of its three sources whose id is set and in range -- the output the
+// reference's three SKIP-gated dispatches, in that order, leave
 int matvec_id_3way(const styx_expert_tensor &t, int n_expert, const int32_t *ids64, int nrows, int ncols, int k,
                    const float *x, int ne11, float *y, int *err, int sms, cudaStream_t st) {
     const int units = ncols / 64;
@@ -265,18 +267,18 @@ int matvec_id_3way(const styx_expert_tensor &t, int n_expert, const int32_t *ids
     a.units = units;
     a.gs = std::min(32, pow2ceil(units));
     a.rows_per_cta = mv_rows_per_cta(nrows, k, a.gs, sms);
-    struct Row { const void *buf; uint64_t stride; int off; int count; } rows[3] = {
-        {t.hot, t.slab_bytes, 16, static_cast<int>(t.n_hot)},
-        {t.arena, t.arena_slab_bytes, 32, static_cast<int>(t.n_arena)},
-        {t.full, t.slab_bytes, 48, n_expert}};
-    for (auto &r : rows) {
-        if (!r.buf) continue;
-        a.a = static_cast<const uint8_t *>(r.buf);
-        a.expert_bytes = r.stride;
-        a.n_expert = r.count;
-        a.ids = ids64 + r.off;
-        CK(styx::launch_matvec_id(a, t.qtype, st));
-    }
+    a.src3[0] = static_cast<const uint8_t *>(t.hot);
+    a.src3[1] = static_cast<const uint8_t *>(t.arena);
+    a.src3[2] = static_cast<const uint8_t *>(t.full);
+    a.stride3[0] = t.slab_bytes;
+    a.stride3[1] = t.arena_slab_bytes;
+    a.stride3[2] = t.slab_bytes;
+    a.count3[0] = static_cast<int>(t.n_hot);
+    a.count3[1] = static_cast<int>(t.n_arena);
+    a.count3[2] = n_expert;
+    a.ids = ids64;
+    if (!t.hot && !t.arena && !t.full) return STYX_OK;
+    CK(styx::launch_matvec_id(a, t.qtype, st));
     return STYX_OK;
 }
 

@@ -133,6 +133,12 @@ struct MatVecIdArgs {
     int stride_d;
     int units, gs;
     int rows_per_cta;              // a multiple of kMvRowStep(gs)
+    // three-source form (src3[0] non-null): ids is a 64-int id block and slot
+    // s reads from the last of hot (row 16), arena (32), full (48) whose id is
+    // set and in range -- what one launch per source, in that order, leaves
+    const uint8_t *src3[3];
+    uint64_t stride3[3];
+    int count3[3];
 };
 // rows a CTA of k_matvec_id covers per pass: 8 warps x (32 / gs) rows x 4 in flight
 constexpr int kMvRowStep(int gs) { return 8 * (32 / gs) * 4; }

@@ -492,11 +492,27 @@ __global__ void __launch_bounds__(256) k_matvec_id(const MatVecIdArgs p) {
     pdl_wait();
     extern __shared__ __align__(16) uint8_t sm[];
     const int s = blockIdx.y;
-    const uint32_t e = static_cast<uint32_t>(p.ids[s]);
-    if (e == kSkip) return;
-    if (e >= static_cast<uint32_t>(p.n_expert)) {
-        if (threadIdx.x == 0 && blockIdx.x == 0 && p.err) atomicExch(p.err, kErrBadId);
-        return;
+    const uint8_t *a = nullptr;
+    if (p.src3[0] || p.src3[1] || p.src3[2]) {   // hot, arena, full: the last source set and in range
+        for (int i = 0; i < 3; i++) {
+            if (!p.src3[i]) continue;
+            const uint32_t e = static_cast<uint32_t>(p.ids[16 * (i + 1) + s]);
+            if (e == kSkip) continue;
+            if (e >= static_cast<uint32_t>(p.count3[i])) {
+                if (threadIdx.x == 0 && blockIdx.x == 0 && p.err) atomicExch(p.err, kErrBadId);
+                continue;
+            }
+            a = p.src3[i] + static_cast<uint64_t>(e) * p.stride3[i];
+        }
+        if (!a) return;   // the slot's output is left as it is
+    } else {
+        const uint32_t e = static_cast<uint32_t>(p.ids[s]);
+        if (e == kSkip) return;
+        if (e >= static_cast<uint32_t>(p.n_expert)) {
+            if (threadIdx.x == 0 && blockIdx.x == 0 && p.err) atomicExch(p.err, kErrBadId);
+            return;
+        }
+        a = p.a + static_cast<uint64_t>(e) * p.expert_bytes;
     }
     int8_t *d1 = reinterpret_cast<int8_t *>(sm);
     uint8_t *d2 = reinterpret_cast<uint8_t *>(sm) + p.ncols;
@@ -510,7 +526,6 @@ __global__ void __launch_bounds__(256) k_matvec_id(const MatVecIdArgs p) {
 
     const int rpw = 32 / p.gs;
     const int ug = lane & (p.gs - 1), grp = lane / p.gs;
-    const uint8_t *a = p.a + static_cast<uint64_t>(e) * p.expert_bytes;
     const int r0 = blockIdx.x * p.rows_per_cta, r1 = min(p.nrows, r0 + p.rows_per_cta);
     XUnit x;
     const bool preload = p.units <= 32;
