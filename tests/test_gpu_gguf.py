@@ -76,3 +76,22 @@ def test_whole_model_from_a_gguf_decodes_greedy_identical(tmp_path):
     assert model.generate(prompt, n_predict) == oracle_greedy(m, prompt, n_predict)
     assert model.attn.last_path() == 1
     model.moe.ctx.check_device_error()
+
+
+def test_c_host_decodes_like_the_oracle(tmp_path):
+    """The same model file through the plain-C host (generate_moe.c: the GGUF
+    reader, uploads, styx_attn_block / styx_moe_block per layer, head and
+    greedy pick, all through the C ABI): the oracle's greedy tokens."""
+    import subprocess
+
+    from tests.decode_case import make_model, oracle_greedy, write_gguf
+    from tests.host_c import build
+    m = make_model(5, n_layers=2, H=512, n_heads=8, n_kv=2, hd=128)
+    path = tmp_path / "model.gguf"
+    write_gguf(m, path)
+    exe = build(tmp_path)
+    prompt, n_predict = [11, 250, 3], 8
+    r = subprocess.run([exe, str(path), str(n_predict), ",".join(map(str, prompt)), "64"], capture_output=True,
+                       text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert [int(t) for t in r.stdout.strip().split(",")] == oracle_greedy(m, prompt, n_predict)
