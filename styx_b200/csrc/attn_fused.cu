@@ -558,15 +558,8 @@ int attn_fused_threads() { return kAF; }
 
 template <class Kern>
 static cudaError_t launch_af(Kern kern, const AttnFusedArgs &a, int grid, uint32_t smem, bool coop, cudaStream_t st) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    const cudaError_t e = resident_fit(reinterpret_cast<const void *>(kern), kAF, smem, grid);
     if (e != cudaSuccess) return e;
-    int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kAF, smem);
-    if (e != cudaSuccess) return e;
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (occ < 1 || grid > occ * sms) return cudaErrorCooperativeLaunchTooLarge;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kAF);

@@ -270,6 +270,13 @@ inline cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cud
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// Whether `grid` CTAs of `kern` (threads, smem bytes each) can all be
+// resident on the current device: cudaSuccess or
+// cudaErrorCooperativeLaunchTooLarge.  The function attribute and the
+// occupancy query run once per (kernel, device, smem) and are cached, so an
+// eager caller does not pay them on every launch.
+cudaError_t resident_fit(const void *kern, int threads, uint32_t smem, int grid);
+
 // coop: a cooperative launch; false when the caller promised the device to
 // itself (STYX_OPT_EXCLUSIVE)
 cudaError_t launch_fused(const FusedArgs &a, const LayerLink &lk, int qg, int qd, int grid, uint32_t smem,

@@ -32,6 +32,8 @@
 // reset either: nothing in the workspace needs clearing between launches.
 // Every wait is bounded (~1 s) and reports through the device error word.
 #include <cfloat>
+#include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -888,6 +890,42 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused_layers(const __gri
     }
 }
 
+cudaError_t resident_fit(const void *kern, int threads, uint32_t smem, int grid) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    struct Fit {
+        const void *kern;
+        int dev;
+        uint32_t smem;
+        int threads, grid_max;
+    };
+    static std::mutex mu;
+    static std::vector<Fit> fits;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const Fit &f : fits)
+            if (f.kern == kern && f.dev == dev && f.smem == smem && f.threads == threads)
+                return grid <= f.grid_max ? cudaSuccess : cudaErrorCooperativeLaunchTooLarge;
+    }
+    // the attribute goes to the largest opt-in size (the launch's own smem
+    // is what counts for residency), so a later, larger launch of the same
+    // kernel never finds it set lower
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    int occ = 0, sms = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+    if (e != cudaSuccess) return e;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    const int grid_max = occ * sms;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        fits.push_back(Fit{kern, dev, smem, threads, grid_max});
+    }
+    return grid <= grid_max ? cudaSuccess : cudaErrorCooperativeLaunchTooLarge;
+}
+
 // Launch with programmatic stream serialisation: the kernel lets the next
 // one launch at entry and waits for the previous grid before it touches the
 // workspace or x.  Every CTA must be resident at once (the tagged-slot reads
@@ -900,15 +938,8 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_fused_layers(const __gri
 template <class Kern, class... Args>
 static cudaError_t launch_coop_pdl(Kern kern, bool coop, int grid, uint32_t smem, cudaStream_t st,
                                    const Args &...a) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    cudaError_t e = resident_fit(reinterpret_cast<const void *>(kern), kFusedBlock, smem, grid);
     if (e != cudaSuccess) return e;
-    int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kFusedBlock, smem);
-    if (e != cudaSuccess) return e;
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (occ < 1 || grid > occ * sms) return cudaErrorCooperativeLaunchTooLarge;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kFusedBlock);
