@@ -487,14 +487,17 @@ def load_decode_model(g: Gguf, n_ctx: int, device: int = 0, experts_in_host: boo
 
 
 def write_decode_gguf(path, arch: str, hp: dict, embd, layers: Sequence[dict], output_norm, head,
-                      qtypes: dict) -> None:
+                      qtypes: dict, key_length: bool = True, ff_length: bool = True) -> None:
     """A whole Qwen3-MoE model file: the keys decode_params reads and the
     tensors load_decode_model uploads.  hp: n_layers, n_embd, n_heads,
     n_kv_heads, head_dim, n_ff, n_expert, n_expert_used, n_vocab, rms_eps,
     rope_base.  layers: dicts of numpy arrays (attn_norm, wq, wk, wv, wo raw
     bytes, q_norm, k_norm or None, ffn_norm, router, gate, up, down raw
     bytes); qtypes: the ggml types of embd, head, wq, wk, wv, wo, gate, up,
-    down."""
+    down.  key_length / ff_length False leave out attention.key_length and
+    expert_feed_forward_length, as files of architectures whose head size is
+    n_embd / n_heads and whose expert width is read from ffn_gate_exps do
+    (olmoe, qwen2moe; moe.rs:567-583)."""
     H, E, F = hp["n_embd"], hp["n_expert"], hp["n_ff"]
     qd, kvd = hp["n_heads"] * hp["head_dim"], hp["n_kv_heads"] * hp["head_dim"]
     w = GgufWriter()
@@ -503,10 +506,12 @@ def write_decode_gguf(path, arch: str, hp: dict, embd, layers: Sequence[dict], o
     w.add_u32(f"{arch}.embedding_length", H)
     w.add_u32(f"{arch}.attention.head_count", hp["n_heads"])
     w.add_u32(f"{arch}.attention.head_count_kv", hp["n_kv_heads"])
-    w.add_u32(f"{arch}.attention.key_length", hp["head_dim"])
+    if key_length:
+        w.add_u32(f"{arch}.attention.key_length", hp["head_dim"])
     w.add_u32(f"{arch}.expert_count", E)
     w.add_u32(f"{arch}.expert_used_count", hp["n_expert_used"])
-    w.add_u32(f"{arch}.expert_feed_forward_length", F)
+    if ff_length:
+        w.add_u32(f"{arch}.expert_feed_forward_length", F)
     w.add_f32(f"{arch}.attention.layer_norm_rms_epsilon", hp["rms_eps"])
     w.add_f32(f"{arch}.rope.freq_base", hp["rope_base"])
     w.add_tensor("token_embd.weight", [H, hp["n_vocab"]], qtypes["embd"], embd)

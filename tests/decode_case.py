@@ -78,7 +78,7 @@ class OracleDecoder:
         return logits, x, ids
 
 
-def write_gguf(m: Model, path) -> None:
+def write_gguf(m: Model, path, arch: str = "qwen3moe", **keys) -> None:
     """The model as a qwen3moe GGUF file (styx_b200.gguf.write_decode_gguf)."""
     from styx_b200 import gguf as G
     layers = [dict(attn_norm=ly["attn_norm"], wq=ly["wq"][1], wk=ly["wk"][1], wv=ly["wv"][1], wo=ly["wo"][1],
@@ -87,7 +87,7 @@ def write_gguf(m: Model, path) -> None:
     ly0 = m.layers[0]
     qtypes = dict(embd=Q4_K, head=Q6_K, wq=ly0["wq"][0], wk=ly0["wk"][0], wv=ly0["wv"][0], wo=ly0["wo"][0],
                   gate=Q4_K, up=Q4_K, down=Q6_K)
-    G.write_decode_gguf(path, "qwen3moe", m.hp, m.embd, layers, m.output_norm, m.head, qtypes)
+    G.write_decode_gguf(path, arch, m.hp, m.embd, layers, m.output_norm, m.head, qtypes, **keys)
 
 
 def oracle_greedy(m: Model, prompt, n_predict, n_ctx=64):

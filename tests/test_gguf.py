@@ -321,3 +321,19 @@ def test_decode_model_keys_round_trip(tmp_path):
     assert np.array_equal(g.tensor_data("output.weight"), m.head)
     assert g.tensor("blk.0.attn_output.weight").dims == [8 * 128, 512]
     g.close()
+
+
+def test_decode_params_fallbacks(tmp_path):
+    """Without attention.key_length the head size is n_embd / n_heads, without
+    expert_feed_forward_length the expert width comes from ffn_gate_exps'
+    dims (moe.rs:567-583); qwen2moe does not renormalise the top-k weights
+    (ArchCfg.norm_topk, moe.rs:324-361)."""
+    from tests.decode_case import make_model, write_gguf
+    m = make_model(4, n_layers=1, H=512, n_heads=8, n_kv=2, hd=64, F=256, E=8, k=2, n_vocab=64)
+    path = tmp_path / "model.gguf"
+    write_gguf(m, path, arch="qwen2moe", key_length=False, ff_length=False)
+    g = G.Gguf.open(path)
+    assert "qwen2moe.attention.key_length" not in g.value_types
+    hp = G.decode_params(g)
+    assert hp.head_dim == 512 // 8 and hp.n_ff == 256 and not hp.norm_topk
+    g.close()
