@@ -343,9 +343,14 @@ int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial,
  * array of STYX_NOALLOC_SCRATCH_BYTES per device, and nothing is allocated.
  *   - Dims whose styx_moe_workspace_bytes exceeds that size are rejected
  *     (STYX_EINVAL).
- *   - The first call on a device looks up the array and zeroes it; make it
- *     before any stream capture (it fails while the stream is capturing).
- *   - Every call zeroes the scratch's counter words on `stream` first.
+ *   - The first call on a device looks up the array's device address; make
+ *     it before any stream capture (it fails while the stream is capturing).
+ *     The address is looked up again once every context on that device has
+ *     been destroyed.
+ *   - Every call first clears, on `stream`, all the words one call leaves for
+ *     the next (launch and arrival counters, tagged logit and x words), so
+ *     a call after one with other dims, or after one whose bounded wait ran
+ *     out (STYX_ETIMEOUT), starts clean; no reset call is needed.
  *   - All calls on one device share the one scratch: calls that overlap (on
  *     different streams or host threads) race.  Serialise them.
  *   - styx_moe_workspace_view does not apply to it. */

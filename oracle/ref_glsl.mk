@@ -2,9 +2,10 @@
 #   make -C oracle -f ref_glsl.mk [REF=/path/to/reference]
 # Reads shaders/*.comp from the reference tree where they lie, preprocesses
 # them with ref_glsl.sed into _ref/*.inc and builds _ref/libref_glsl.so.
-# Output goes only to oracle/_ref/ (git-ignored).
-REF ?= /root/reference
+# Output goes only to oracle/_ref/ (git-ignored).  The reference tree is
+# $STYX_REFERENCE_ROOT, else a "reference" folder beside this repository.
 HERE := $(dir $(abspath $(lastword $(MAKEFILE_LIST))))
+REF ?= $(or $(STYX_REFERENCE_ROOT),$(abspath $(HERE)../../reference))
 OUT := $(HERE)_ref
 CXX := $(firstword $(wildcard /usr/bin/g++) g++)
 SHADERS := matvec_strided_f32 topk_softmax_f32 moe_reduce_f32 gather_slabs_f32 attn_decode_f32 add_flat_f32

@@ -290,6 +290,52 @@ int styx::set_error(int code, const char *msg) {
     return code;
 }
 
+// Scratch of styx_moe_block_noalloc: one statically sized array per device
+// (module global memory, zero at module load), shared by every call on that
+// device.  Its address is looked up once per device with the device current,
+// and forgotten when the last context on that device is destroyed (so a
+// context made after a device reset looks it up again).
+static __device__ __align__(256) uint8_t g_noalloc_scratch[STYX_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kMaxDevices] = {};
+int g_noalloc_ctxs[kMaxDevices] = {};
+
+void noalloc_ctx_made(int device) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (device >= 0 && device < kMaxDevices) g_noalloc_ctxs[device]++;
+}
+void noalloc_ctx_gone(int device) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (device >= 0 && device < kMaxDevices && --g_noalloc_ctxs[device] <= 0) {
+        g_noalloc_ctxs[device] = 0;
+        g_noalloc_ptr[device] = nullptr;
+    }
+}
+
+// first call on a device: resolve the symbol's device address (the array's
+// name in host code is only a host-side stand-in)
+int noalloc_scratch(styx_ctx *ctx, cudaStream_t st, void **out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NEED(ctx->device >= 0 && ctx->device < kMaxDevices, "device %d out of range", ctx->device);
+    void *&p = g_noalloc_ptr[ctx->device];
+    if (!p) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        CK(cudaStreamIsCapturing(st, &cs));
+        NEED(cs == cudaStreamCaptureStatusNone,
+             "styx_moe_block_noalloc: the first call on a device sets up its scratch and must not be "
+             "made while the stream is being captured");
+        void *q = nullptr;
+        CK(cudaGetSymbolAddress(&q, g_noalloc_scratch));
+        p = q;
+    }
+    *out = p;
+    return STYX_OK;
+}
+}  // namespace
+
 extern "C" {
 
 const char *styx_last_error(void) { return g_err.c_str(); }
@@ -329,6 +375,7 @@ int styx_init(int device, styx_ctx **out) {
         delete c;
         return fail(STYX_ECUDA, "error word / scratch: %s", cudaGetErrorString(e));
     }
+    noalloc_ctx_made(device);
     *out = c;
     return STYX_OK;
 }
@@ -338,6 +385,7 @@ void styx_destroy(styx_ctx *ctx) {
     cudaSetDevice(ctx->device);
     cudaFree(ctx->d_err);
     cudaFree(ctx->d_scratch);
+    noalloc_ctx_gone(ctx->device);
     delete ctx;
 }
 
@@ -1192,37 +1240,6 @@ int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial, fl
 }
 
 // ------------------------------------------------ MoE block, no allocation
-// Scratch of styx_moe_block_noalloc: one statically sized array per device
-// (module global memory, zero at module load), shared by every call on that
-// device.  Its address is looked up once per device with the device current.
-static __device__ __align__(256) uint8_t g_noalloc_scratch[STYX_NOALLOC_SCRATCH_BYTES];
-
-namespace {
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-void *g_noalloc_ptr[kMaxDevices] = {};
-
-// first call on a device: resolve the symbol and zero the whole scratch
-int noalloc_scratch(styx_ctx *ctx, cudaStream_t st, void **out) {
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    NEED(ctx->device >= 0 && ctx->device < kMaxDevices, "device %d out of range", ctx->device);
-    void *&p = g_noalloc_ptr[ctx->device];
-    if (!p) {
-        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        CK(cudaStreamIsCapturing(st, &cs));
-        NEED(cs == cudaStreamCaptureStatusNone,
-             "styx_moe_block_noalloc: the first call on a device sets up its scratch and must not be "
-             "made while the stream is being captured");
-        void *q = nullptr;
-        CK(cudaGetSymbolAddress(&q, g_noalloc_scratch));
-        CK(cudaMemset(q, 0, STYX_NOALLOC_SCRATCH_BYTES));
-        p = q;
-    }
-    *out = p;
-    return STYX_OK;
-}
-}  // namespace
-
 int styx_moe_block_noalloc(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims, const styx_moe_layer *lw,
                            int layer, float *x, int32_t *ids, float *weights_out) {
     ENTER(ctx);
@@ -1235,10 +1252,13 @@ int styx_moe_block_noalloc(styx_ctx *ctx, styx_stream stream, const styx_moe_dim
          (unsigned long long)L.total, (unsigned long long)STYX_NOALLOC_SCRATCH_BYTES);
     void *scratch = nullptr;
     if ((rc = noalloc_scratch(ctx, S(stream), &scratch))) return rc;
-    // the hand-off counter must be zero when the block starts (a timed-out
-    // wait of an earlier call can leave it set); the launch counter after it
-    // must keep counting
-    CK(cudaMemsetAsync(static_cast<uint8_t *>(scratch) + L.counter, 0, kGenOffset, S(stream)));
+    // Every call starts from a clean scratch: the counter block (the hand-off
+    // counter, the launch counter, the h-arrival counts) and the tagged logit
+    // and x words are cleared on `stream` first.  Their places depend on the
+    // dims, and a call whose bounded wait ran out leaves them part-advanced;
+    // cleared, neither an earlier call with other dims nor a timed-out one
+    // leaves a word this call could take for its own.
+    CK(cudaMemsetAsync(scratch, 0, L.trace, S(stream)));
     return styx_moe_block(ctx, stream, dims, lw, layer, x, ids, weights_out, scratch, STYX_NOALLOC_SCRATCH_BYTES);
 }
 

@@ -14,13 +14,14 @@ from oracle import oracle as O
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_DIR = os.path.join(os.path.dirname(HERE), "oracle")
 REF_SO = os.path.join(ORACLE_DIR, "_ref", "libref_glsl.so")
-REF_TREE = "/root/reference/shaders"
+REF_ROOT = os.environ.get("STYX_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+REF_TREE = os.path.join(REF_ROOT, "shaders")
 
 
 @pytest.fixture(scope="module")
 def ref():
     if os.path.isdir(REF_TREE):
-        subprocess.run(["make", "-s", "-C", ORACLE_DIR, "-f", "ref_glsl.mk"], check=True)
+        subprocess.run(["make", "-s", "-C", ORACLE_DIR, "-f", "ref_glsl.mk", "REF=" + REF_ROOT], check=True)
     if not os.path.exists(REF_SO):
         pytest.skip("reference shaders not built (reference tree absent)")
     L = C.CDLL(REF_SO)

@@ -18,8 +18,9 @@ from oracle import residency as R
 from styx_b200 import _lib, ops
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "residency_golden.json")
-REF_HIST = os.path.join(os.environ.get("STYX_REFERENCE_ROOT", "/root/reference"), "tests", "golden",
-                        "route_hist_30b.csv")
+REF_ROOT = os.environ.get("STYX_REFERENCE_ROOT") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference")
+REF_HIST = os.path.join(REF_ROOT, "tests", "golden", "route_hist_30b.csv")
 COST_30B = 884736 + 884736 + 1290240
 
 

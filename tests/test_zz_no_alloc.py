@@ -68,6 +68,34 @@ def test_noalloc_matches_workspace_entry(mode, path):
         blk.ctx.set_moe_kernels(_lib.MOE_AUTO)
 
 
+def test_noalloc_alternating_dims_match_fresh_workspaces():
+    """Two shapes (other F, k and E) in turn through the one shared scratch:
+    each call clears the words an earlier call with other dims left behind,
+    so every result equals styx_moe_block on that shape's own workspace."""
+    cases = [make_case(31, 2048, 768, 16, 8, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K)),
+             make_case(32, 1024, 512, 32, 4, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K))]
+    lws = [_layer(c) for c in cases]
+    blks = [ops.MoeBlock(ops.Dims(c.H, c.F, c.E, c.k), 0) for c in cases]
+    for turn in range(4):
+        i = turn % 2
+        c, lw, blk = cases[i], lws[i], blks[i]
+        x_ws, x_na = _t(c.x), _t(c.x)
+        ids_ws = torch.full((64,), -7, dtype=torch.int32, device=DEV)
+        ids_na = ids_ws.clone()
+        w_ws = torch.zeros(c.k, dtype=torch.float32, device=DEV)
+        w_na = torch.zeros_like(w_ws)
+        blk.forward(x_ws, lw, 0, ids_ws, weights_out=w_ws)
+        torch.cuda.synchronize()
+        blk.ctx.check_device_error()
+        _noalloc(blk.ctx, blk._dims, lw.struct(), 0, x_na, ids_na, w_na)
+        torch.cuda.synchronize()
+        blk.ctx.check_device_error()
+        a, b = x_ws.cpu().numpy(), x_na.cpu().numpy()
+        assert np.all(np.isfinite(b))
+        assert np.max(np.abs(a - b)) <= 1e-6 * np.max(np.abs(a)), f"turn {turn}"
+        np.testing.assert_array_equal(ids_ws.cpu().numpy(), ids_na.cpu().numpy())
+
+
 def test_noalloc_rejects_dims_above_its_scratch():
     dims = ops.Dims(16384, 2048, 64, 16).struct()
     need = C.c_uint64()
