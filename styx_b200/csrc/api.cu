@@ -1050,8 +1050,9 @@ static bool plan_pipe(const styx_moe_dims &d, const styx_moe_layer &lw, int sms,
     if (lw.up.qtype != qg || !styx::fused_supported(qg, qd)) return false;
     const int units_g = H / 64, units_d = F / 64;
     if (units_g > 32 || units_d > 32 || k > 16 || sms <= 0) return false;
-    // the down warps hold the h words of every slot in registers: 24 per thread
-    if (static_cast<long long>(k) * F > 24 * 256) return false;
+    // a warp of a slot group converts at most 12 of the slot's 32-element
+    // groups of h: F / 32 <= 12 * (16 / k)
+    if (k > 16 || F / 32 > 12 * (16 / k)) return false;
     const int G = sms;
     a.units_g = units_g;
     a.gs_g = pow2ceil(units_g);

@@ -260,7 +260,39 @@ __device__ __forceinline__ void digits_group_warp(float v, int lane, const Digit
     dv.d1[i] = static_cast<int8_t>(d1);
     dv.d2[i] = static_cast<uint8_t>(d2);
     dv.d3[i] = static_cast<uint8_t>(d3);
-    if (lane == 0) dv.scale[g] = s;
+    // every lane stores the (same) scale: a lane-0 branch here would leave the
+    // warp split, and each shuffle of the next group would pay for regrouping
+    // it (~10x its cost on B200)
+    dv.scale[g] = s;
+}
+
+// N independent 32-element groups at once, one element of each per lane,
+// group j at index gidx[j] (< 0: skipped): the same digits as N calls of
+// digits_group_warp, but the N shuffle chains of the group maxima run in
+// lockstep, so their latencies overlap instead of adding up.
+template <int N>
+__device__ __forceinline__ void digits_groups_warp(const float (&v)[N], const int (&gidx)[N], int lane,
+                                                   const DigitsView &dv) {
+    float a[N];
+#pragma unroll
+    for (int j = 0; j < N; j++) a[j] = fabsf(v[j]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+#pragma unroll
+        for (int j = 0; j < N; j++) a[j] = fmaxf(a[j], __shfl_xor_sync(0xffffffffu, a[j], o));
+#pragma unroll
+    for (int j = 0; j < N; j++) {
+        if (gidx[j] < 0) continue;
+        float inv;
+        const float s = digits_scale(a[j], inv);
+        int d1, d2, d3;
+        digits_of(v[j], inv, d1, d2, d3);
+        const int i = gidx[j] * 32 + lane;
+        dv.d1[i] = static_cast<int8_t>(d1);
+        dv.d2[i] = static_cast<uint8_t>(d2);
+        dv.d3[i] = static_cast<uint8_t>(d3);
+        dv.scale[gidx[j]] = s;
+    }
 }
 
 // Digits of a whole vector v[n] (n % 32 == 0) by a group of `nthreads`
@@ -310,7 +342,7 @@ __device__ __forceinline__ void digits_part(const float (&x)[EPT], bool on, int 
             *reinterpret_cast<uint2 *>(pd2 + o) = make_uint2(w2[0], w2[1]);
             *reinterpret_cast<uint2 *>(pd3 + o) = make_uint2(w3[0], w3[1]);
         }
-        if (pidx % TPG == 0) scale[pidx / TPG] = s;
+        scale[pidx / TPG] = s;   // the group's threads store the same value (no branch)
     }
 }
 

@@ -21,6 +21,13 @@ __device__ __forceinline__ void st_slot(uint64_t *p, float v, uint32_t tag) {
     const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
     atomicExch(reinterpret_cast<unsigned long long *>(p), w);
 }
+// the same word written with one plain 64-bit store (single-copy atomic for
+// an aligned 64-bit access: a reader sees the value with its tag or the old
+// word, never a mix), not an atomic read-modify-write at L2
+__device__ __forceinline__ void st_slot_plain(uint64_t *p, float v, uint32_t tag) {
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
 __device__ __forceinline__ uint64_t ld_slot(const uint64_t *p) {
     uint64_t w;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");

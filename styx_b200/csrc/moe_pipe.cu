@@ -20,14 +20,14 @@
 //   3  gate/up warps (0-7): the CTA's row pairs slot by slot as their bytes
 //      land; h = SiLU(g) * u is published per row as a tagged word, and the
 //      CTA's last row of a slot adds the CTA's rows to the slot's counter;
-//   4  down warps (8-15): poll the counters of the slots still pending; a
-//      slot whose counter reached this launch's target has its h words read
-//      (tags checked), each warp turns its 32-element groups into digits and
-//      flags them; a slot whose groups are all flagged gets its down rows
-//      computed from shared memory -- slot s's down work overlaps the later
-//      slots' gate/up work.  Then the slot-ordered combine x[r] += sum_s
-//      w[s] d[s][r] (moe_reduce_f32.comp), or, for expert parallelism,
-//      partial[s][r] = w[s] d[s][r].
+//   4  slot groups of 16 / k warps: warps 8-15 (idle during phase 3) take
+//      the first slots, whose h completes first, warps 0-7 the later ones
+//      after their gate/up rows; a group waits for its slot's counter, reads
+//      the slot's h words (tags checked), turns them into digits and runs
+//      the CTA's down rows of the slot from shared memory -- the first slots'
+//      down work overlaps the later slots' gate/up work.  Then the
+//      slot-ordered combine x[r] += sum_s w[s] d[s][r] (moe_reduce_f32.comp),
+//      or, for expert parallelism, partial[s][r] = w[s] d[s][r].
 // Tags: launch number + 1, from the workspace's never-reset launch counter
 // (bumped once by every CTA after the grid dependency resolved, so launches
 // never interleave their numbers).  Logit and h words carry the tag and the
@@ -52,7 +52,6 @@ constexpr int kPBarMaps = 264;    // remap / pmap
 constexpr int kPRed = 320;        // 32 floats of block-reduction scratch
 constexpr int kPWts = 448;        // 16 floats: slot logits, then weights
 constexpr int kPMisc = 512;       // ints: [0] tag, [1] active-slot mask, [2] a down wait gave up
-constexpr int kPReady = 528;      // 16 words: bit w = down warp w has its digits of slot s in place
 constexpr int kPGcnt = 592;       // 16 ints: h rows of slot s this CTA has stored
 constexpr int kPSrc = 656;        // 3 x 16 slab pointers
 constexpr int kPXown = 1040;      // the CTA's raw x rows (<= 128 floats)
@@ -64,12 +63,16 @@ static_assert(kPArgs + static_cast<int>(sizeof(PipeArgs)) <= kPHeader, "PipeArgs
 static_assert(sizeof(PipeArgs) % 8 == 0, "PipeArgs size");
 
 constexpr int kGuWarps = 8;                 // warps 0-7: gate/up; 8-15: down
-constexpr int kDnWarps = kFusedWarps - kGuWarps;
-constexpr int kDnThreads = 32 * kDnWarps;
-constexpr uint32_t kAllDn = (1u << kDnWarps) - 1u;
-constexpr int kBarDown = 1;                 // named barrier of the down warps
-constexpr int kBarW0 = 15;                  // warps 0-2 alone: 15, 14, 13
-constexpr int kHWords = 24;                 // h words a down thread holds: k * F <= 24 * 256
+constexpr int kBarW0 = 15;                  // 32-thread barriers 15, 14, 13 of warps 0-2 (phase 2)
+constexpr int kHGroups = 12;                // 32-element groups of h[s] a warp converts: F / 32 / (16 / k)
+
+// slot s's h digits (planes d1, d2, d3 of F bytes, then F / 32 scales)
+__device__ __forceinline__ DigitsView hd_view_of(uint8_t *smem, const PipeArgs &p, int s, int F) {
+    int8_t *d1 = reinterpret_cast<int8_t *>(smem + p.off_hd + static_cast<size_t>(s) * p.hd_stride);
+    uint8_t *d2 = reinterpret_cast<uint8_t *>(d1) + F;
+    uint8_t *d3 = d2 + F;
+    return DigitsView{d1, d2, d3, reinterpret_cast<float *>(d3 + F)};
+}
 
 template <int QG, int QD>
 __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_pipe(const __grid_constant__ PipeArgs pa) {
@@ -85,7 +88,6 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_pipe(const __grid_consta
     float *red = reinterpret_cast<float *>(smem + kPRed);
     float *wts = reinterpret_cast<float *>(smem + kPWts);
     int *misc = reinterpret_cast<int *>(smem + kPMisc);
-    uint32_t *ready = reinterpret_cast<uint32_t *>(smem + kPReady);
     int *gcnt = reinterpret_cast<int *>(smem + kPGcnt);
     const uint8_t **src_g = reinterpret_cast<const uint8_t **>(smem + kPSrc);
     const uint8_t **src_u = src_g + 16;
@@ -114,7 +116,6 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_pipe(const __grid_consta
         mbar_init(bar_pre, 1);
         mbar_init(bar_maps, 1);
     } else if (tid >= 32 && tid < 48) {
-        ready[tid - 32] = 0u;
         gcnt[tid - 32] = 0;
     } else if (tid == 48) {
         misc[2] = 0;
@@ -330,7 +331,17 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_pipe(const __grid_consta
         STYX_PSTAMP(7);
     } else {
         const DigitsView dv{xd1, xd2, xd3, xsc};
-        for (int g = warp - 3; g < (H >> 5); g += kFusedWarps - 3) digits_group_warp(xn[g * 32 + lane], lane, dv, g);
+        for (int g0 = warp - 3; g0 < (H >> 5); g0 += 4 * (kFusedWarps - 3)) {
+            float v[4];
+            int gi[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int g = g0 + j * (kFusedWarps - 3);
+                gi[j] = g < (H >> 5) ? g : -1;
+                v[j] = g < (H >> 5) ? xn[g * 32 + lane] : 0.f;
+            }
+            digits_groups_warp<4>(v, gi, lane, dv);
+        }
         if (b == 0)
             for (int i = tid - 96; i < H; i += kFusedBlock - 96) p.xnorm[i] = xn[i];   // debug view
     }
@@ -394,7 +405,7 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_pipe(const __grid_consta
             // swiglu split (ops2.rs:305-308): g / (1 + exp(-g)) * u
             if (ug == 0 && s >= 0) {
                 const float hv = g / (1.0f + expf(-g)) * u;
-                st_slot(p.hslot + static_cast<size_t>(s) * F + gbeg + i, hv, tag);
+                st_slot_plain(p.hslot + static_cast<size_t>(s) * F + gbeg + i, hv, tag);
                 __stcg(p.h + static_cast<size_t>(s) * F + gbeg + i, hv);   // debug view
                 // the CTA's last row of slot s counts all n_g of them at once: a
                 // hint for the readers, which check the tags
@@ -403,28 +414,24 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_pipe(const __grid_consta
             }
         }
         STYX_PSTAMP(9);
-    } else {
-        // ------------------------------------------------ phase 4: down, slots as they complete
-        // Each down warp polls the counters of its pending slots; a slot whose
-        // counter reached this launch's target has its h words read in one
-        // pass (thread dt holds words j*256 + dt, so warp dw holds whole
-        // 32-element groups and turns them into digits from its registers; a
-        // word without this launch's tag is read again on the next pass).  A
-        // warp that has its groups of slot s in place sets its bit in
-        // ready[s]; a slot with every bit set is complete and each warp
-        // computes its rows of it, in any order (each slot's results have
-        // their own place).  No block barrier until the combine.
-        const int dt = tid - 32 * kGuWarps, dw = warp - kGuWarps;   // thread / warp inside the down group
-        const int wps = F / kDnThreads;                              // words of one slot per thread
-        const int kw = k * wps;                                      // words per thread, all slots
+    }
+    // ------------------------------------------------ phase 4: down, by slot groups
+    // Every warp joins a slot group of nw = 16 / k warps (slot s: group s,
+    // then s + 16 / nw, ...).  Warps 8-15, free while the gate/up warps work,
+    // form the groups of the first slots, whose h is complete first; warps
+    // 0-7 take the later slots once their gate/up rows are done.  A group
+    // polls its slot's counter, reads the slot's h words (tags checked, a
+    // missing word read again), turns them into digits (warp `sub` of the
+    // group holds 32-element groups sub, sub + nw, ...), then runs the CTA's
+    // down rows of the slot, two rows per lane group in flight.
+    {
+        const int nw = k >= kFusedWarps ? 1 : kFusedWarps / k;     // warps per slot group
+        const int ngroups = kFusedWarps / nw;
+        const int wr = (warp + kGuWarps) % kFusedWarps;             // warps 8-15 first
+        const int grp_id = wr / nw, sub = wr % nw;
+        const int gthreads = nw * 32;
         float *dpart = reinterpret_cast<float *>(smem + p.off_dpart);
-        auto hd_view = [&](int s) {
-            int8_t *d1 = reinterpret_cast<int8_t *>(smem + p.off_hd + static_cast<size_t>(s) * p.hd_stride);
-            uint8_t *d2 = reinterpret_cast<uint8_t *>(d1) + F;
-            uint8_t *d3 = d2 + F;
-            return DigitsView{d1, d2, d3, reinterpret_cast<float *>(d3 + F)};
-        };
-        if (dw == 0) {
+        if (wr == 0) {
             // softmax statistics over all E logits and the slot weights
             // (topk_softmax_f32.comp:47-52); wts[s] holds slot s's logit until here
             float mx = -INFINITY, sum = 0.f;
@@ -438,118 +445,113 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_pipe(const __grid_consta
             float wsum = 0.f;
             for (int t = 0; t < k; t++) wsum += __shfl_sync(0xffffffffu, w, t);
             if (lane < k) {
-                const float wr = p.renorm ? w / wsum : w;
-                wts[lane] = wr;
-                if (b == 0) p.weights[lane] = wr;
+                const float wv = p.renorm ? w / wsum : w;
+                wts[lane] = wv;
+                if (b == 0) p.weights[lane] = wv;
             }
         }
-        for (int s = 0; s < k; s++)
-            if (!(amask >> s & 1u))
-                for (int r = dt; r < n_d; r += kDnThreads) dpart[s * p.rows_d + r] = 0.f;
         const int gs = p.gs_d, rpw = 32 / gs;
-        const int ug = lane & (gs - 1), grp = lane / gs;
+        const int ug = lane & (gs - 1), lgrp = lane / gs;
         const bool on = ug < p.units_d;
-        uint32_t pending = amask;   // slots whose words this warp still lacks
-        uint32_t todo = amask;      // slots whose rows this warp still has to compute
-        bool stamped = false;
         const unsigned long long target = static_cast<unsigned long long>(tag) * static_cast<unsigned long long>(F);
-        const long long t0 = clock64();
-        while (todo) {
-            bool progressed = false;
-            if (pending) {
-                const unsigned long long c =
-                    (lane < k && (pending >> lane & 1u)) ? ld_relaxed_u64(p.hcount + lane * kHcStride) : 0ull;
-                const uint32_t hint = __ballot_sync(0xffffffffu, lane < k && (pending >> lane & 1u) && c >= target);
-                if (hint) {
-                    float v[kHWords];
-                    uint32_t got = 0;
-#pragma unroll
-                    for (int j = 0; j < kHWords; j++) {
-                        v[j] = 0.f;
-                        if (j < kw && (hint >> (j / wps) & 1u)) {
-                            const uint64_t w = ld_slot(p.hslot + static_cast<size_t>(j) * kDnThreads + dt);
-                            if (slot_tag(w) == tag) {
-                                v[j] = slot_val(w);
-                                got |= 1u << j;
-                            }
-                        }
-                    }
-                    uint32_t complete = 0;   // slots whose words this warp now has (warp-uniform)
-                    for (int s = 0; s < k; s++) {
-                        if (!(hint >> s & 1u)) continue;
-                        const uint32_t m = ((1u << wps) - 1u) << (s * wps);
-                        if (__all_sync(0xffffffffu, (got & m) == m)) complete |= 1u << s;
-                    }
-                    if (complete) {
-#pragma unroll
-                        for (int j = 0; j < kHWords; j++) {
-                            if (j < kw) {
-                                const int s = j / wps;
-                                if (complete >> s & 1u)
-                                    digits_group_warp(v[j], lane, hd_view(s), (j - s * wps) * 8 + dw);
-                            }
-                        }
-                        __syncwarp();
+        const int ngrp32 = F >> 5;   // 32-element groups of h[s]
+        bool ok = true;              // one value per warp
+        for (int s = grp_id; s < k; s += ngroups) {
+            if (!(amask >> s & 1u)) {
+                for (int r = sub * 32 + lane; r < n_d; r += gthreads) dpart[s * p.rows_d + r] = 0.f;
+                continue;
+            }
+            const long long t0 = clock64();
+            // the slot's counter: every CTA has stored its rows of h[s]
+            if (ok) {
+                for (;;) {
+                    const unsigned long long c = lane == 0 ? ld_relaxed_u64(p.hcount + s * kHcStride) : 0ull;
+                    if (__shfl_sync(0xffffffffu, c >= target ? 1 : 0, 0)) break;
+                    const long long el = __shfl_sync(0xffffffffu, clock64() - t0, 0);
+                    if (el > kSpinCycles) {
                         if (lane == 0) {
-                            __threadfence_block();
-                            for (int s = 0; s < k; s++)
-                                if (complete >> s & 1u) atomicOr(ready + s, 1u << dw);
+                            atomicExch(p.err, kErrWaitRoute);
+                            atomicOr(misc + 2, 1);
                         }
-                        pending &= ~complete;
-                        progressed = true;
-                        if (!pending && p.trace && lane == 0) p.trace[b * kTraceStamps + 14 + dw] = clock64();
+                        ok = false;
+                        break;
+                    }
+                    if (el > kPollFreeCycles) __nanosleep(256);
+                }
+            }
+            if (p.trace && sub == 0 && lane == 0 && s < 8) p.trace[b * kTraceStamps + 14 + s] = clock64();
+            // every word of this warp's 32-element groups (sub, sub + nw, ...:
+            // at most kHGroups) read in one pass, then their digits in one
+            // interleaved batch
+            const DigitsView hv = hd_view_of(smem, p, s, F);
+            {
+                float v[kHGroups];
+                int gi[kHGroups];
+                uint32_t need = 0;
+#pragma unroll
+                for (int j = 0; j < kHGroups; j++) {
+                    const int g = sub + j * nw;
+                    gi[j] = g < ngrp32 ? g : -1;
+                    v[j] = 0.f;
+                    if (g < ngrp32) need |= 1u << j;
+                }
+                while (ok) {
+                    uint64_t w[kHGroups];
+#pragma unroll
+                    for (int j = 0; j < kHGroups; j++)
+                        w[j] = (need >> j & 1u) ? ld_slot(p.hslot + static_cast<size_t>(s) * F + gi[j] * 32 + lane) : 0ull;
+#pragma unroll
+                    for (int j = 0; j < kHGroups; j++) {
+                        const bool hit = (need >> j & 1u) && slot_tag(w[j]) == tag;
+                        v[j] = hit ? slot_val(w[j]) : v[j];
+                        need = hit ? need & ~(1u << j) : need;
+                    }
+                    if (!__any_sync(0xffffffffu, need != 0)) break;
+                    const long long el = __shfl_sync(0xffffffffu, clock64() - t0, 0);
+                    if (el > kSpinCycles) {
+                        if (lane == 0) {
+                            atomicExch(p.err, kErrWaitRoute);
+                            atomicOr(misc + 2, 1);
+                        }
+                        ok = false;
                     }
                 }
+                __syncwarp();   // regroup after the poll before the digits' shuffles
+                digits_groups_warp<kHGroups>(v, gi, lane, hv);
             }
-            // every complete slot this warp has not computed yet
-            for (int s = 0; s < k; s++) {
-                if (!(todo >> s & 1u)) continue;
-                const uint32_t rd =
-                    __shfl_sync(0xffffffffu, lane == 0 ? *reinterpret_cast<volatile uint32_t *>(ready + s) : 0u, 0);
-                if (rd != kAllDn) continue;
-                __threadfence_block();
-                if (!stamped && dw == 0) {
-                    STYX_PSTAMP_T(32 * kGuWarps, 10);
-                    stamped = true;
+            if (nw > 1) asm volatile("bar.sync %0, %1;" ::"r"(1 + grp_id), "r"(gthreads) : "memory");
+            else __syncwarp();
+            if (s == 0) STYX_PSTAMP_T(32 * kGuWarps, 10);
+            XUnit x;
+            if (on) load_xunit<QD>(x, hv.d1, hv.d2, hv.d3, hv.scale, ug);
+            const bool got_rows = ok && mbar_wait(&bar_d[s], 0, p.err, kErrWaitFull);
+            const uint8_t *base = dbuf + static_cast<size_t>(s) * p.d_slot +
+                                  (reinterpret_cast<uintptr_t>(src_d[s] + static_cast<size_t>(dbeg) * p.rb_d) & 15);
+            // four rows per lane group per pass: independent dot products in flight
+            for (int t = sub * 4 * rpw; t < n_d; t += nw * 4 * rpw) {
+                float vr[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int r = t + q * rpw + lgrp;
+                    vr[q] = (got_rows && on && r < n_d) ? unit_dot<QD>(base + static_cast<size_t>(r) * p.rb_d, ug, x)
+                                                         : 0.f;
                 }
-                XUnit x;
-                const DigitsView hv = hd_view(s);
-                if (on) load_xunit<QD>(x, hv.d1, hv.d2, hv.d3, hv.scale, ug);
-                const bool got_rows = mbar_wait(&bar_d[s], 0, p.err, kErrWaitFull);
-                const uint8_t *base = dbuf + static_cast<size_t>(s) * p.d_slot +
-                                      (reinterpret_cast<uintptr_t>(src_d[s] + static_cast<size_t>(dbeg) * p.rb_d) & 15);
-                for (int t = dw * rpw; t < n_d; t += kDnWarps * rpw) {
-                    const int r = t + grp;
-                    float val = 0.f;
-                    if (got_rows && on && r < n_d) val = unit_dot<QD>(base + static_cast<size_t>(r) * p.rb_d, ug, x);
-                    __syncwarp();
-                    for (int o = gs >> 1; o; o >>= 1) val += __shfl_xor_sync(0xffffffffu, val, o);
-                    if (ug == 0 && r < n_d) dpart[s * p.rows_d + r] = val;
+                __syncwarp();
+                for (int o = gs >> 1; o; o >>= 1)
+#pragma unroll
+                    for (int q = 0; q < 4; q++) vr[q] += __shfl_xor_sync(0xffffffffu, vr[q], o);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int r = t + q * rpw + lgrp;
+                    if (ug == 0 && r < n_d) dpart[s * p.rows_d + r] = vr[q];
                 }
-                todo &= ~(1u << s);
-                progressed = true;
             }
-            if (!todo) break;
-            const long long el = __shfl_sync(0xffffffffu, clock64() - t0, 0);
-            if (el > kSpinCycles) {   // give up: the slots left contribute 0, x stays
-                if (lane == 0) {
-                    atomicExch(p.err, kErrWaitRoute);
-                    atomicOr(misc + 2, 1);
-                }
-                for (int s = 0; s < k; s++)
-                    if (todo >> s & 1u)
-                        for (int t = dw * rpw; t < n_d; t += kDnWarps * rpw)
-                            if (ug == 0 && t + grp < n_d) dpart[s * p.rows_d + t + grp] = 0.f;
-                break;
-            }
-            // short waits spin: a sleep, however short it is asked to be, can
-            // keep the warp off the SM for microseconds
-            if (!progressed && el > kPollFreeCycles) __nanosleep(256);
+            if (p.trace && sub == 0 && lane == 0 && s < 8) p.trace[b * kTraceStamps + 22 + s] = clock64();
         }
-        asm volatile("bar.sync %0, %1;" ::"r"(kBarDown), "r"(kDnThreads) : "memory");
-        STYX_PSTAMP_T(32 * kGuWarps, 11);
+        __syncthreads();   // every slot's rows and the weights
+        STYX_PSTAMP(11);
         const bool fine = misc[2] == 0;
-        for (int r = dt; r < n_d; r += kDnThreads) {
+        for (int r = tid; r < n_d; r += kFusedBlock) {
             if (p.partial) {
                 for (int s = 0; s < k; s++)
                     p.partial[static_cast<size_t>(s) * H + dbeg + r] =
@@ -560,7 +562,7 @@ __global__ void __launch_bounds__(kFusedBlock, 1) k_moe_pipe(const __grid_consta
                 p.x[dbeg + r] = __fadd_rn(xown[r], acc);
             }
         }
-        STYX_PSTAMP_T(32 * kGuWarps, 12);
+        STYX_PSTAMP(12);
     }
     // No CTA leaves with copies in flight into its shared memory, even after
     // a wait above gave up: thread 0 waits (bounded) on every armed barrier.
