@@ -85,17 +85,13 @@ int styx_device_info(styx_ctx *ctx, int *sm_count, char *name, int name_len);
 int styx_check_device_error(styx_ctx *ctx, styx_stream stream);
 
 /* Options.  STYX_OPT_MOE_KERNELS selects how styx_moe_block runs: 0 = auto
- * (a single kernel when the shape and formats fit -- the pipelined one, whose
- * down projection runs slot by slot behind the gate/up projection, else the
- * earlier single kernel -- else three kernels), 1 = single kernel only
- * (STYX_EUNSUPPORTED if neither fits), 2 = three kernels, 3 = the earlier
- * single kernel (down after every slot's gate/up; else three kernels).
- * STYX_OPT_MOE_LAST_PATH (read only) = 1 (single kernel), 2 (three kernels),
- * 3 (host-read form: some full tensor is in STYX_MEM_HOST memory), 4 (single
- * kernel, several layers per launch, styx_moe_blocks), 5 (single kernel, one
- * chained launch per layer, styx_moe_blocks) or 6 (the earlier single kernel,
- * asked for by option 3), the form the last styx_moe_block[s] call used.
- * STYX_OPT_TRACE = 1 makes the single
+ * (the single cooperative kernel when the shape and formats fit, else three
+ * kernels), 1 = single kernel only (STYX_EUNSUPPORTED if it does not fit),
+ * 2 = three kernels.  STYX_OPT_MOE_LAST_PATH (read only) = 1 (single
+ * kernel), 2 (three kernels), 3 (host-read form: some full tensor is in
+ * STYX_MEM_HOST memory), 4 (single kernel, several layers per launch,
+ * styx_moe_blocks) or 5 (single kernel, one chained launch per layer,
+ * styx_moe_blocks), the form the last styx_moe_block[s] call used.  STYX_OPT_TRACE = 1 makes the single
  * kernel record 32 clock64 stamps per CTA at its phase boundaries into the
  * workspace (styx_moe_workspace_view 4: int64[CTAs][32]).
  * STYX_OPT_MOE_LAYERS picks how styx_moe_blocks runs single-kernel layers:

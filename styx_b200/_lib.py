@@ -26,7 +26,7 @@ IDS_PER_LAYER = 64
 MEM_DEVICE, MEM_HOST = 0, 1
 OPT_MOE_KERNELS, OPT_MOE_LAST_PATH, OPT_TRACE, OPT_MOE_LAYERS, OPT_EXCLUSIVE = 1, 2, 3, 4, 5
 OPT_ATTN_KERNELS, OPT_ATTN_LAST_PATH = 6, 7
-MOE_AUTO, MOE_FUSED, MOE_SPLIT, MOE_EARLIER = 0, 1, 2, 3
+MOE_AUTO, MOE_FUSED, MOE_SPLIT = 0, 1, 2
 
 
 class StyxError(RuntimeError):

@@ -134,7 +134,7 @@ constexpr size_t kTraceCtas = 256;   // phase stamps: styx::kTraceStamps per CTA
 // styx_moe_workspace_init (which also clears the tagged words they guard).
 constexpr size_t kGenOffset = 128;
 struct WsLayout {
-    size_t counter, hcnt, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, d, lgslot, xslot, hslot, trace, total;
+    size_t counter, hcnt, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, d, lgslot, xslot, trace, total;
 };
 
 WsLayout ws_layout(const styx_moe_dims &d) {
@@ -161,7 +161,6 @@ WsLayout ws_layout(const styx_moe_dims &d) {
     L.d = take(static_cast<size_t>(d.n_expert_used) * H * 4);   // down outputs of the host-read form
     L.lgslot = take(2 * E * 8);   // two banks of logit words, by launch-tag parity
     L.xslot = take(H * 8);        // x rows passed from one layer to the next
-    L.hslot = take(kF * 8);       // h rows as tagged words (the pipelined single kernel)
     L.trace = take(kTraceCtas * styx::kTraceStamps * 8);
     L.total = o;
     return L;
@@ -426,7 +425,7 @@ int styx_set_option(styx_ctx *ctx, int option, int64_t value) {
     NEED(ctx, "null ctx");
     switch (option) {
     case STYX_OPT_MOE_KERNELS:
-        NEED(value >= 0 && value <= 3, "STYX_OPT_MOE_KERNELS: 0, 1, 2 or 3");
+        NEED(value >= 0 && value <= 2, "STYX_OPT_MOE_KERNELS: 0, 1 or 2");
         ctx->moe_kernels = static_cast<int>(value);
         return STYX_OK;
     case STYX_OPT_TRACE:
@@ -1040,92 +1039,6 @@ static bool plan_fused(const styx_moe_dims &d, const styx_moe_layer &lw, int sms
     return true;
 }
 
-// Shared-memory plan of the pipelined single kernel (moe_pipe.cu) for these
-// dims on `sms` CTAs; false if a CTA's share does not fit (or the formats
-// are not instantiated), and the caller falls back.
-static bool plan_pipe(const styx_moe_dims &d, const styx_moe_layer &lw, int sms, styx::PipeArgs &a,
-                      uint32_t &smem) {
-    const int H = d.n_embd, F = d.n_ff, k = d.n_expert_used, E = d.n_expert;
-    const int qg = lw.gate.qtype, qd = lw.down.qtype;
-    if (lw.up.qtype != qg || !styx::fused_supported(qg, qd)) return false;
-    const int units_g = H / 64, units_d = F / 64;
-    if (units_g > 32 || units_d > 32 || k > 16 || sms <= 0) return false;
-    // a warp of a slot group converts at most 12 of the slot's 32-element
-    // groups of h: F / 32 <= 12 * (16 / k)
-    if (k > 16 || F / 32 > 12 * (16 / k)) return false;
-    const int G = sms;
-    a.units_g = units_g;
-    a.gs_g = pow2ceil(units_g);
-    a.units_d = units_d;
-    a.gs_d = pow2ceil(units_d);
-    a.rb_g = static_cast<int>(row_bytes(qg, H));
-    a.rb_d = static_cast<int>(row_bytes(qd, F));
-    const int rows_g = (F + G - 1) / G, rows_d = (H + G - 1) / G;
-    if (rows_d > 128) return false;   // the CTA's raw x rows live in the header
-    a.rows_d = rows_d;
-    const int n_router = E > G ? (E + G - 1) / G : 1;
-    size_t o = styx::kPipeHeader;
-    auto take = [&](size_t n) {
-        const size_t r = o;
-        o = a128(o + n);
-        return static_cast<uint32_t>(r);
-    };
-    a.maps_half = static_cast<uint32_t>(a16(static_cast<size_t>(E) * 4 + 32));
-    a.off_maps = take(2 * static_cast<size_t>(a.maps_half));
-    a.off_xd = take(3 * static_cast<size_t>(H) + H / 32 * 4);
-    // route-phase regions, dead once phase 2 ends: then the h digits of
-    // every slot live there (or after them, when they do not fit)
-    a.off_norm = take(static_cast<size_t>(H) * 4);
-    a.off_router = take(static_cast<size_t>(n_router) * H * 4);
-    a.off_x = take(static_cast<size_t>(H) * 4);
-    a.hd_stride = static_cast<uint32_t>(a16(3 * static_cast<size_t>(F) + F / 32 * 4));
-    if (static_cast<size_t>(k) * a.hd_stride <= o - a.off_norm) a.off_hd = a.off_norm;
-    else a.off_hd = take(static_cast<size_t>(k) * a.hd_stride);
-    a.off_lgs = take(static_cast<size_t>(E) * 4);
-    a.off_dpart = take(static_cast<size_t>(k) * rows_d * 4);
-    a.gu_up_off = static_cast<uint32_t>(a16(static_cast<size_t>(rows_g) * a.rb_g + 32));
-    a.gu_slot = 2 * a.gu_up_off;
-    a.off_gu = take(static_cast<size_t>(k) * a.gu_slot);
-    a.d_slot = static_cast<uint32_t>(a16(static_cast<size_t>(rows_d) * a.rb_d + 32));
-    a.off_d = take(static_cast<size_t>(k) * a.d_slot);
-    if (o > 227 * 1024) return false;
-    smem = static_cast<uint32_t>(o);
-    return true;
-}
-
-static void fill_pipe(styx::PipeArgs &pa, const styx_ctx *ctx, const styx_moe_dims &d, const styx_moe_layer &lw,
-                      float *x, int32_t *ids64, float *wts, uint8_t *ws, const WsLayout &L, float *partial,
-                      bool quiet) {
-    const int E = d.n_expert;
-    pa.x = x;
-    pa.norm_w = lw.ffn_norm;
-    pa.router = lw.router;
-    pa.remap = lw.remap;
-    pa.pmap = lw.pmap;
-    pa.gate = to_src(lw.gate, E);
-    pa.up = to_src(lw.up, E);
-    pa.down = to_src(lw.down, E);
-    pa.ids64 = ids64;
-    pa.weights = wts;
-    pa.logits = reinterpret_cast<float *>(ws + L.logits);
-    pa.xnorm = reinterpret_cast<float *>(ws + L.xnorm);
-    pa.h = reinterpret_cast<float *>(ws + L.h);
-    pa.partial = partial;
-    pa.lgslot = reinterpret_cast<uint64_t *>(ws + L.lgslot);
-    pa.hslot = reinterpret_cast<uint64_t *>(ws + L.hslot);
-    pa.gen = reinterpret_cast<unsigned long long *>(ws + L.counter + kGenOffset);
-    pa.hcount = reinterpret_cast<unsigned long long *>(ws + L.hcnt);
-    pa.err = ctx->d_err;
-    pa.trace = ctx->trace ? reinterpret_cast<long long *>(ws + L.trace) : nullptr;
-    pa.eps = d.rms_eps;
-    pa.E = E;
-    pa.H = d.n_embd;
-    pa.F = d.n_ff;
-    pa.k = d.n_expert_used;
-    pa.renorm = d.norm_topk;
-    pa.quiet = quiet ? 1 : 0;
-}
-
 // The per-layer part of the single kernel's arguments (the plan part comes
 // from plan_fused).
 static void fill_fused(styx::FusedArgs &fa, const styx_ctx *ctx, const styx_moe_dims &d, const styx_moe_layer &lw,
@@ -1203,19 +1116,7 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
         return moe_block_host_read(ctx, st, *dims, *lw, x, ids64, wts, ws, L);
     }
 
-    // the single kernel when the shape fits (the pipelined form first; option
-    // 3 asks for the earlier form), else three kernels
-    if (ctx->moe_kernels != 2 && ctx->moe_kernels != 3 && al16(lw->ffn_norm)) {
-        styx::PipeArgs pa{};
-        uint32_t smem = 0;
-        if (plan_pipe(*dims, *lw, ctx->sm_count, pa, smem)) {
-            NEED(!ctx->trace || ctx->sm_count <= static_cast<int>(kTraceCtas), "too many CTAs to trace");
-            fill_pipe(pa, ctx, *dims, *lw, x, ids64, wts, ws, L, nullptr, false);
-            CK(styx::launch_pipe(pa, lw->gate.qtype, lw->down.qtype, ctx->sm_count, smem, !ctx->exclusive, st));
-            ctx->last_path = 1;
-            return STYX_OK;
-        }
-    }
+    // the single cooperative kernel when the shape fits, else three kernels
     if (ctx->moe_kernels != 2) {
         styx::FusedArgs fa{};
         uint32_t smem = 0;
@@ -1228,7 +1129,7 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
             const styx::LayerLink alone{0, false, false, true, nullptr, nullptr, nullptr};
             CK(styx::launch_fused(fa, alone, lw->gate.qtype, lw->down.qtype, ctx->sm_count, smem, !ctx->exclusive,
                                   st));
-            ctx->last_path = ctx->moe_kernels == 3 ? 6 : 1;
+            ctx->last_path = 1;
             return STYX_OK;
         }
     }

@@ -99,43 +99,9 @@ struct FusedArgs {
     int units_g, gs_g, units_d, gs_d;
 };
 
-// the single-kernel MoE block with the down projection pipelined behind the
-// gate/up projection slot by slot (moe_pipe.cu)
-struct PipeArgs {
-    float *x;                // residual f32[H], += the block (unless partial)
-    const float *norm_w;
-    const float *router;     // f32[E][H]
-    const uint32_t *remap, *pmap;
-    ExpSrc gate, up, down;
-    int32_t *ids64;
-    float *weights;
-    float *logits;           // workspace f32[E] (debug view)
-    float *xnorm;            // workspace f32[H] (debug view, written by CTA 0)
-    float *h;                // workspace f32[k][F] (debug view)
-    float *partial;          // optional f32[k][H]: w[s]*d[s][r] per slot, written instead of the combine into x
-    uint64_t *lgslot;        // workspace u64[2][E]: tagged logit words
-    uint64_t *hslot;         // workspace u64[k][F]: tagged h words
-    unsigned long long *gen; // workspace launch counter (never reset)
-    unsigned long long *hcount; // workspace: h rows stored per slot, slot s at s * kHcStride (F per launch)
-    int *err;
-    long long *trace;        // optional: kTraceStamps clock64 stamps per CTA
-    float eps;
-    int E, H, F, k, renorm;
-    int quiet;               // a slot with no source is another rank's expert: no error
-    int rb_g, rb_d;          // row bytes of gate/up and of down
-    int units_g, gs_g, units_d, gs_d;
-    int rows_d;              // dpart row stride (>= the CTA's down rows)
-    // shared-memory plan
-    uint32_t off_norm, off_router, off_maps, maps_half, off_x, off_xd, off_lgs, off_dpart;
-    uint32_t off_hd, hd_stride;   // h digits of every slot (over the route-phase regions when they fit)
-    uint32_t off_gu, gu_slot, gu_up_off, off_d, d_slot;
-    uint32_t pad_;
-};
-constexpr uint32_t kPipeHeader = 2048;
 // the per-slot h counters sit one 128-byte line apart (u64 stride), so the
 // adds of different slots do not queue at one L2 slice
 constexpr int kHcStride = 16;
-cudaError_t launch_pipe(const PipeArgs &a, int qg, int qd, int grid, uint32_t smem, bool coop, cudaStream_t st);
 
 // How a single-kernel layer connects to the layers before and after it (see
 // moe_fused.cu): chain flags and the x exchange words.

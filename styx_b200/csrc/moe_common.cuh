@@ -1,6 +1,6 @@
-// moe_common.cuh -- device helpers shared by the single-kernel MoE block
-// forms (moe_fused.cu, moe_pipe.cu): tagged exchange words, slab sources,
-// the warp-wide top-k selection, deterministic block sums, 16-byte covers.
+// moe_common.cuh -- device helpers of the single-kernel MoE block
+// (moe_fused.cu): tagged exchange words, slab sources, the warp-wide top-k
+// selection, deterministic block sums, 16-byte covers.
 #pragma once
 
 #include <cfloat>
@@ -21,13 +21,6 @@ __device__ __forceinline__ void st_slot(uint64_t *p, float v, uint32_t tag) {
     const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
     atomicExch(reinterpret_cast<unsigned long long *>(p), w);
 }
-// the same word written with one plain 64-bit store (single-copy atomic for
-// an aligned 64-bit access: a reader sees the value with its tag or the old
-// word, never a mix), not an atomic read-modify-write at L2
-__device__ __forceinline__ void st_slot_plain(uint64_t *p, float v, uint32_t tag) {
-    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
 __device__ __forceinline__ uint64_t ld_slot(const uint64_t *p) {
     uint64_t w;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
@@ -37,15 +30,6 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
-}
-__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-// a relaxed atomic add whose result is not needed (no fence, no wait)
-__device__ __forceinline__ void red_add_u64(unsigned long long *p, unsigned long long v) {
-    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 // two adjacent tagged words (16-byte aligned), each read whole
 __device__ __forceinline__ void ld_slot2(const uint64_t *p, uint64_t &a, uint64_t &b) {

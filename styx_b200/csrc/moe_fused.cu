@@ -175,9 +175,12 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
     }
     if (lk.index == 0) {
         pdl_trigger();
+        // router rows and norms are read every token: kept in L2 (evict
+        // last) while the expert slabs stream through it (evict first)
+        const uint64_t keep = l2_evict_last();
         for (int j = tid; j < n_rows_mine; j += kFusedBlock)
-            prefetch_l2(p.router + static_cast<size_t>(b + G * j) * H, static_cast<uint32_t>(H) * 4u);
-        if (tid == kFusedBlock - 1) prefetch_l2(p.norm_w, static_cast<uint32_t>(H) * 4u);
+            prefetch_l2_hint(p.router + static_cast<size_t>(b + G * j) * H, static_cast<uint32_t>(H) * 4u, keep);
+        if (tid == kFusedBlock - 1) prefetch_l2_hint(p.norm_w, static_cast<uint32_t>(H) * 4u, keep);
     }
     // this launch's tag (published to the block by the barriers in phase 1).
     // Safe before the grid dependency resolves: every CTA of the previous
@@ -312,7 +315,17 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
     // shuffles and reductions were several times slower.)
     {
         const DigitsView dv{xd1, xd2, xd3, xsc};
-        for (int g = warp; g < (H >> 5); g += kFusedWarps) digits_group_warp(xn[g * 32 + lane], lane, dv, g);
+        for (int g0 = warp; g0 < (H >> 5); g0 += 4 * kFusedWarps) {   // four groups' shuffle chains together
+            float v[4];
+            int gi[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int g = g0 + j * kFusedWarps;
+                gi[j] = g < (H >> 5) ? g : -1;
+                v[j] = g < (H >> 5) ? xn[g * 32 + lane] : 0.f;
+            }
+            digits_groups_warp<4>(v, gi, lane, dv);
+        }
         if (b == 0)   // test / debug view of x_norm
             for (int i = tid; i < H; i += kFusedBlock) p.xnorm[i] = xn[i];
     }
@@ -432,9 +445,11 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
                 mbar_arrive(&full_gu[lane]);
             } else {
                 mbar_arrive_expect_tx(&full_gu[lane], total);
+                const uint64_t once = l2_evict_first();   // expert bytes are read once per token
 #pragma unroll
                 for (int i = 0; i < 4; i++)
-                    if (lens[i]) bulk_g2s(dst[i], reinterpret_cast<const void *>(addr[i]), lens[i], &full_gu[lane]);
+                    if (lens[i])
+                        bulk_g2s_hint(dst[i], reinterpret_cast<const void *>(addr[i]), lens[i], &full_gu[lane], once);
             }
         }
         STYX_STAMP(20);
@@ -454,8 +469,8 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
             }
             __syncwarp();
             if (len)
-                bulk_g2s(dbuf + static_cast<size_t>(s) * p.dslot_stride, reinterpret_cast<const void *>(a), len,
-                         &full_d[0]);
+                bulk_g2s_hint(dbuf + static_cast<size_t>(s) * p.dslot_stride, reinterpret_cast<const void *>(a), len,
+                              &full_d[0], l2_evict_first());
         }
         STYX_STAMP(21);
         // the logits and the picked ones stay in shared memory for the
@@ -557,9 +572,10 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
     STYX_STAMP(10);
 
     if (lk.next_router) {   // warm L2 with the next layer's router rows and norm while h travels
+        const uint64_t keep = l2_evict_last();
         for (int j = tid; j < n_rows_mine; j += kFusedBlock)
-            prefetch_l2(lk.next_router + static_cast<size_t>(b + G * j) * H, static_cast<uint32_t>(H) * 4u);
-        if (tid == kFusedBlock - 1) prefetch_l2(lk.next_norm, static_cast<uint32_t>(H) * 4u);
+            prefetch_l2_hint(lk.next_router + static_cast<size_t>(b + G * j) * H, static_cast<uint32_t>(H) * 4u, keep);
+        if (tid == kFusedBlock - 1) prefetch_l2_hint(lk.next_norm, static_cast<uint32_t>(H) * 4u, keep);
     }
 
     // ------------------------------------------------ phase 4: down + combine

@@ -59,21 +59,12 @@ def _run_both(cases, first_layer, reps, lws, c0, n, k, one, many, total, exclusi
         ib = ia.clone()
         wa = torch.zeros(n * k, dtype=torch.float32, device=DEV)
         wb = torch.zeros_like(wa)
+        many.ctx.set_option(_lib.OPT_EXCLUSIVE, 0)   # the reference: cooperative launches
+        for i, lw in enumerate(lws):
+            one.forward(xa, lw, first_layer + i, ia, weights_out=wa[i * k:(i + 1) * k])
         many.ctx.set_option(_lib.OPT_EXCLUSIVE, exclusive)
         many.forward_layers(xb, lws, first_layer, ib, weights_out=wb)
         torch.cuda.synchronize()
-        # the reference: one cooperative styx_moe_block call per layer, in the
-        # kernel body the linked form runs (linked layers run the earlier
-        # single kernel; a fallback, the pipelined one)
-        path = many.path = many.ctx.last_moe_path()
-        many.ctx.set_option(_lib.OPT_EXCLUSIVE, 0)
-        one.ctx.set_moe_kernels(_lib.MOE_EARLIER if path in (4, 5) else _lib.MOE_AUTO)
-        try:
-            for i, lw in enumerate(lws):
-                one.forward(xa, lw, first_layer + i, ia, weights_out=wa[i * k:(i + 1) * k])
-            torch.cuda.synchronize()
-        finally:
-            one.ctx.set_moe_kernels(_lib.MOE_AUTO)
         one.ctx.check_device_error()
         assert np.array_equal(xa.cpu().numpy().view(np.uint32), xb.cpu().numpy().view(np.uint32)), rep
         assert np.array_equal(ia.cpu().numpy(), ib.cpu().numpy()), rep
@@ -85,7 +76,7 @@ def _run_both(cases, first_layer, reps, lws, c0, n, k, one, many, total, exclusi
 def test_linked_layers_equal_one_call_per_layer_and_the_oracle(mode):
     cases = [make_case(90 + l, 1024, 512, 32, 8, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K)) for l in range(5)]
     many, x, _ = run_both(cases, first_layer=3, mode=mode)
-    assert many.path == PATH[mode]
+    assert many.ctx.last_moe_path() == PATH[mode]
     xr = cases[0].x.copy()
     for c in cases:
         xr = oracle_block(dataclasses.replace(c, x=xr))["x"]
@@ -98,7 +89,7 @@ def test_plain_launches_equal_cooperative_ones(mode):
     attribute give the same bits."""
     cases = [make_case(150 + l, 2048, 768, 128, 8, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K)) for l in range(3)]
     many, _, _ = run_both(cases, mode=mode, exclusive=1)
-    assert many.path == PATH[mode]
+    assert many.ctx.last_moe_path() == PATH[mode]
 
 
 @MODES
@@ -107,7 +98,7 @@ def test_more_layers_than_one_launch_holds(mode):
     cases = [make_case(200 + l, 512, 256, 8, 2, (_lib.Q8_0, _lib.Q8_0, _lib.Q8_0), sigma=0.01)
              for l in range(83)]
     many, _, _ = run_both(cases, reps=1, mode=mode)
-    assert many.path == PATH[mode]
+    assert many.ctx.last_moe_path() == PATH[mode]
 
 
 @MODES
@@ -118,7 +109,7 @@ def test_mixed_formats(mode):
              make_case(301, 1024, 512, 16, 4, (_lib.Q4_K, _lib.Q4_K, _lib.Q4_K)),
              make_case(302, 1024, 512, 16, 4, (_lib.Q5_K, _lib.Q5_K, _lib.Q5_K))]
     many, _, _ = run_both(cases, reps=1, mode=mode)
-    assert many.path == (5 if mode == CHAIN else 1)
+    assert many.ctx.last_moe_path() == (5 if mode == CHAIN else 1)
 
 
 def test_chained_layers_replayed_from_a_graph():
@@ -156,13 +147,9 @@ def test_chained_layers_replayed_from_a_graph():
             many.ctx.check_device_error(stream)
             xa = T(t)
             ia = torch.zeros_like(ids)
-            one.ctx.set_moe_kernels(_lib.MOE_EARLIER)   # the kernel body the chained launches run
-            try:
-                for i, lw in enumerate(lws):
-                    one.forward(xa, lw, i, ia)
-                torch.cuda.synchronize()
-            finally:
-                one.ctx.set_moe_kernels(_lib.MOE_AUTO)
+            for i, lw in enumerate(lws):
+                one.forward(xa, lw, i, ia)
+            torch.cuda.synchronize()
             assert np.array_equal(xa.cpu().numpy().view(np.uint32), x.cpu().numpy().view(np.uint32))
             assert np.array_equal(ia.cpu().numpy(), ids.cpu().numpy())
     finally:
