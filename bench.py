@@ -1,23 +1,29 @@
 #!/usr/bin/env python
-"""Benchmark: decode tok/s of the Qwen3-30B-A3B MoE stack on B200.
+"""Benchmark: decode tok/s at the Qwen3-30B-A3B shape on B200.
 
-Workload (BASELINE.json configs[1] shape, stacked to the 48 layers of
-configs[2]): hidden 2048, 128 experts, top-8, expert FFN 768; gate/up q4_K,
-down q6_K, N(0, 0.02) weights quantised per block; every expert resident in
-HBM (48 x 128 x 3.06 MB = 18.8 GB per GPU).  Router rows carry a Zipf(1.1)
-popularity bias.  One step = one decode token through the 48 MoE blocks
-(RMSNorm -> router -> top-k -> gate/up+SiLU -> down -> combine), i.e. the
-north-star path; attention is not on the path.  Synthetic data, generated on
-the device.
+Default workload (the metric's config): one decode
+token of the 48-layer 30B-A3B-shaped model with random weights -- embedding
+row, 48 x (attention half, 32 q / 4 kv heads of 128, + MoE block: hidden
+2048, 128 experts, top-8, expert FFN 768, gate/up q4_K, down q6_K), output
+norm, LM head (151,936 x 2048 q6_K), greedy pick -- with --ctx cache rows
+already filled, batch 1.  Every expert resident in HBM (18.8 GB); router
+rows carry a Zipf(1.1) popularity bias.  Synthetic data, generated on the
+device.  At N > 1 (torchrun) the same sequence runs with its experts split
+over the ranks (expert parallelism, e % N == rank) and one NCCL all-reduce
+of the k x H slot buffer per layer: strong scaling of one sequence.
 
-`value`: tokens/s over all ranks with inputs resident (device-timed CUDA
-graph replays, CUDA events).  `e2e`: the same through the C ABI with host
-buffers (upload token, replay, download hidden state + ids every step).
-`roofline`: one MoE block (3 kernels) = 25,550,848 algorithmic bytes against
-the measured HBM copy bandwidth.  Multi-GPU: independent replicas (the
-30B shape fits one GPU), weak scaling.
+`value`: tokens/s, device-timed with CUDA events (a CUDA graph at N = 1).
+`e2e`: a greedy chain through the C ABI with host buffers (token id in,
+pick out, fed back).  `roofline`: the MoE block (25,550,848 algorithmic
+bytes) over its own time measured in the same run, against the measured HBM
+copy bandwidth; `step_roofline`: the whole token's bytes.  `check`: the
+greedy picks, equal at every N (expert parallelism is bit-exact).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+Other workloads: --workload cfg3 (the 48 MoE blocks alone; replicas at
+N > 1), --workload cfg4 (6 GiB expert budget, the rest streamed from pinned
+host memory).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload ...]
 """
 from __future__ import annotations
 
@@ -169,7 +175,10 @@ def time_cpu(budget_s: float, nthreads: int):
 
 def run_reference(args, rank: int) -> int:
     """--impl reference: the reference's CPU implementation of the path (the
-    C restatement in oracle/, all host threads) on the same workload."""
+    C restatement in oracle/, all host threads) on the same workload, each
+    step a bounded sample of it scaled to one token.  decode: one layer's
+    attention half (args.ctx cache rows) and MoE block plus 1/48 of
+    the LM head per step, i.e. 1/48 of a token; cfg3: two MoE layers."""
     if rank != 0:
         return 0
     from oracle import oracle as O
@@ -178,22 +187,50 @@ def run_reference(args, rank: int) -> int:
     router, norm, gate, up, down = cpu_layer()
     toks = token_bank(16)
     qts = (Q4_K, Q4_K, Q6_K)
-    layers_per_step = 2
+    if args.workload == "decode":
+        rng = np.random.default_rng(11)
+        qd, kvd, ctx = N_HEADS * HD, N_KV * HD, args.ctx
+
+        def q(qt, r, c):
+            return O.quantize(qt, rng.standard_normal((r, c), np.float32) * np.float32(0.02)).reshape(-1)
+        ws = [(Q4_K, q(Q4_K, qd, H)), (Q4_K, q(Q4_K, kvd, H)), (Q6_K, q(Q6_K, kvd, H)), (Q4_K, q(Q4_K, H, qd))]
+        kc = rng.standard_normal((ctx + 1, kvd), np.float32)
+        vc = rng.standard_normal((ctx + 1, kvd), np.float32)
+        ones_h, ones_d = np.ones(H, np.float32), np.ones(HD, np.float32)
+        head_rows = -(-N_VOCAB // N_LAYERS)
+        head = q(Q6_K, head_rows, H)
+
+        def step(i):
+            x = toks[i % 16].copy()
+            x = O.attn_block(x, ones_h, 1e-6, N_HEADS, N_KV, HD, ones_d, ones_d, 1e6, ws, ctx, kc, vc)
+            x = O.moe_block_mt(x, norm, 1e-6, router, K_TOP, True, qts, gate, up, down, F, nth)
+            O.matvec_q(Q6_K, head, head_rows, H, x)
+        per_step_tokens = 1.0 / N_LAYERS
+        sample = (f"per step one layer of the whole decode step (attention half at {ctx} cache rows, one thread; "
+                  f"MoE block, {nth} threads) and 1/48 of the LM head ({head_rows} q6_K rows), i.e. 1/48 of a "
+                  f"token; scaled to the token")
+        workload = decode_config(args.layers, ctx, int(os.environ.get("WORLD_SIZE", "1")))
+        metric = METRIC
+    else:
+        def step(i):
+            for j in range(2):
+                O.moe_block_mt(toks[(i + j) % 16], norm, 1e-6, router, K_TOP, True, qts, gate, up, down, F, nth)
+        per_step_tokens = 2.0 / N_LAYERS
+        sample = "2 of the 48 MoE layers per step (one 30B-shaped layer re-run), scaled to the 48-layer token"
+        workload = workload_config(args.gpus)
+        metric = METRIC
     for i in range(args.warmup):
-        O.moe_block_mt(toks[i % 16], norm, 1e-6, router, K_TOP, True, qts, gate, up, down, F, nth)
+        step(i)
     t0 = time.perf_counter()
     for i in range(args.steps):
-        for j in range(layers_per_step):
-            O.moe_block_mt(toks[(i + j) % 16], norm, 1e-6, router, K_TOP, True, qts, gate, up, down, F, nth)
+        step(i)
     el = time.perf_counter() - t0
-    per_layer = el / (args.steps * layers_per_step)
-    v = 1.0 / (N_LAYERS * per_layer)
-    sample = (f"{layers_per_step} of the 48 MoE layers per step (one 30B-shaped layer re-run), "
-              f"scaled to the 48-layer token; {per_layer * 1e3:.2f} ms per layer")
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * N_LAYERS * 1e3,
+    v = args.steps * per_step_tokens / el
+    line = {"impl": "reference", "metric": metric, "value": v, "unit": "tok/s",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", str(args.gpus))),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / v,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": workload_config(args.gpus),
+            "data": "synthetic", "config": workload,
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": nth, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "reference = C restatement of the reference CPU path (oracle/); the reference itself is "
@@ -243,22 +280,65 @@ def build_model(dev: int, n_layers: int, unique: int = 4):
 N_HEADS, N_KV, HD, N_VOCAB = 32, 4, 128, 151936   # Qwen3-30B-A3B attention and vocabulary
 
 
-def run_decode(args, local: int) -> int:
-    """The whole decode step at the 30B shape: embedding row, 48 x (attention
-    half + MoE block), output norm, LM head (q6_K, 151,936 rows), greedy pick,
-    with args.ctx cache rows already filled; one token recorded as a CUDA graph
-    through the C ABI and replayed, a new token id each step."""
-    import ctypes as C
-
+def ep_moe_layers(dev: int, n_layers: int, world: int, rank: int, unique: int = 4):
+    """This rank's MoE layers under expert parallelism: the experts e with
+    e % world == rank of each layer as dense hot buffers in ascending id
+    order (remap: expert -> local slot, SKIP for the others), no full tensor.
+    The bytes are the ones build_model generates for world 1."""
     import torch
 
-    from styx_b200 import _lib, ops
+    from styx_b200 import ops
+    d = f"cuda:{dev}"
+    owned = [e for e in range(E) if e % world == rank]
+    remap = torch.full((E,), -1, dtype=torch.int32)
+    remap[owned] = torch.arange(len(owned), dtype=torch.int32)
+    remap = remap.to(d)
+    base = []
+    for u in range(min(unique, n_layers)):
+        base.append((ops.synth_quant(Q4_K, E * F, H, 1000 + 3 * u, 0.02, device=dev),
+                     ops.synth_quant(Q4_K, E * F, H, 1001 + 3 * u, 0.02, device=dev),
+                     ops.synth_quant(Q6_K, E * H, F, 1002 + 3 * u, 0.02, device=dev)))
+    torch.cuda.synchronize()
+    norm = torch.ones(H, dtype=torch.float32, device=d)
+
+    def mine(t, slab):
+        return torch.cat([t[e * slab:(e + 1) * slab] for e in owned])
+    layers = []
+    for layer in range(n_layers):
+        g, up, dn = base[layer % len(base)]
+        router = torch.from_numpy(router_host(layer)).to(d)
+        layers.append(ops.LayerWeights(norm, router, ops.Experts(Q4_K, None, SG, hot=mine(g, SG)),
+                                       ops.Experts(Q4_K, None, SG, hot=mine(up, SG)),
+                                       ops.Experts(Q6_K, None, SD, hot=mine(dn, SD)), remap=remap))
+    del base
+    torch.cuda.synchronize()
+    return layers
+
+
+def decode_config(L: int, ctx: int, world: int) -> dict:
+    """The decode workload's config (both arms)."""
+    return {"workload": f"whole decode step at the 30B-A3B shape (configs[2]): embedding row, {L} x "
+                        f"(attention {N_HEADS}q/{N_KV}kv x {HD} + MoE block H{H} E{E} top{K_TOP} F{F}, "
+                        f"gate/up q4_K, down q6_K), LM head {N_VOCAB} x {H} q6_K, greedy pick; batch 1; "
+                        f"{ctx} cache rows before the token",
+            "ctx": ctx, "global_batch": 1,
+            "parallelism": (f"expert-parallel x{world}: experts e % {world} == rank, one NCCL all-reduce "
+                            f"of the {K_TOP} x {H} slot buffer per layer" if world > 1 else "single"),
+            "l2": "inputs larger than L2 (%.2f GB read per token)" % (decode_bytes_per_token(L, ctx) / 1e9)}
+
+
+def decode_model(local: int, L: int, ctx: int, world: int, rank: int, allreduce=None):
+    """The 30B-shaped decode model with random weights: attention q/k/o q4_K,
+    v q6_K (four generated layer bases, copied to every layer), the MoE
+    layers (every expert at world 1, this rank's experts under expert
+    parallelism), embedding q4_K, LM head q6_K; ctx cache rows filled."""
+    import torch
+
+    from styx_b200 import ops
     from styx_b200.decode import DecodeLayer, DecodeModel, DecodeParams
-    torch.cuda.set_device(local)
     dev = f"cuda:{local}"
-    L, ctx = args.layers, args.ctx
     qd, kvd = N_HEADS * HD, N_KV * HD
-    moe = build_model(local, L)
+    moe = build_model(local, L) if world == 1 else ep_moe_layers(local, L, world, rank)
     ones = lambda n: torch.ones(n, dtype=torch.float32, device=dev)   # noqa: E731
     base = []
     for u in range(min(4, L)):
@@ -275,11 +355,43 @@ def run_decode(args, local: int) -> int:
     embd = ops.DenseWeight(Q4_K, ops.synth_quant(Q4_K, N_VOCAB, H, 3000, 0.5, device=local))
     head = ops.DenseWeight(Q6_K, ops.synth_quant(Q6_K, N_VOCAB, H, 3001, 0.02, device=local))
     p = DecodeParams(L, H, N_HEADS, N_KV, HD, F, E, K_TOP, N_VOCAB)
-    model = DecodeModel(p, embd, layers, ones(H), head, ctx + 1, local)
-    # ctx earlier positions in every layer's caches
+    model = DecodeModel(p, embd, layers, ones(H), head, ctx + 1, local, allreduce=allreduce)
     model.kcache[:, :ctx].copy_(ops.synth_f32(L * ctx * kvd, 4000, 0, 1.0, device=local).view(L, ctx, kvd))
     model.vcache[:, :ctx].copy_(ops.synth_f32(L * ctx * kvd, 4001, 0, 1.0, device=local).view(L, ctx, kvd))
+    model.n_past = ctx
     torch.cuda.synchronize()
+    return model
+
+
+def run_decode(args, local: int, rank: int, world: int) -> int:
+    """The whole decode step at the 30B shape: embedding row,
+    48 x (attention half + MoE block), output norm, LM head (q6_K, 151,936
+    rows), greedy pick, with args.ctx cache rows already filled.  One
+    sequence; at N > 1 its experts are split over the ranks (expert
+    parallelism: every rank runs the step on the same token, holds the
+    experts e % N == rank, and one NCCL all-reduce per layer sums the slot
+    contributions), so the scaling is strong.  At N = 1 the token is a CUDA
+    graph recorded through the C ABI; at N > 1 the step runs eagerly (its
+    all-reduces go through torch.distributed)."""
+    import ctypes as C
+    import zlib
+
+    import torch
+
+    from styx_b200 import _lib, ops
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device(dev))
+        pg = dist
+    L, ctx = args.layers, args.ctx
+    allreduce = (lambda t: pg.all_reduce(t)) if pg else None
+    model = decode_model(local, L, ctx, world, rank, allreduce)
     blk_ctx = model.moe.ctx
     blk_ctx.set_option(_lib.OPT_EXCLUSIVE, 0 if args.shared_device else 1)
     lib, cx = _lib.lib(), blk_ctx.handle
@@ -287,78 +399,176 @@ def run_decode(args, local: int) -> int:
     sp = C.c_void_p(stream.cuda_stream)
     rng = np.random.default_rng(7)
     toks = torch.from_numpy(rng.integers(0, N_VOCAB, 4096).astype(np.int32)).to(dev)
-    model.n_past = ctx
     with torch.cuda.stream(stream):
         model.tok.copy_(toks[:1])
         model.pos.fill_(ctx)
     model.step(stream)                      # eager once
     stream.synchronize()
     blk_ctx.check_device_error(stream)
-    attn_path = model.attn.last_path()
-    graph = C.c_void_p()
-    _lib.check(lib.styx_graph_begin(cx, sp))
-    model.step(stream)
-    _lib.check(lib.styx_graph_end(cx, sp, C.byref(graph)))
+    attn_path, moe_path = model.attn.last_path(), blk_ctx.last_moe_path()
+    graph = None
+    if world == 1:
+        graph = C.c_void_p()
+        _lib.check(lib.styx_graph_begin(cx, sp))
+        model.step(stream)
+        _lib.check(lib.styx_graph_end(cx, sp, C.byref(graph)))
+
+    def run_step():
+        if graph is not None:
+            _lib.check(lib.styx_graph_launch(cx, graph, sp))
+        else:
+            model.step(stream)
 
     def replay(i):
         with torch.cuda.stream(stream):
             model.tok.copy_(toks[i % toks.numel():i % toks.numel() + 1])
-        _lib.check(lib.styx_graph_launch(cx, graph, sp))
+        run_step()
+
+    def barrier():
+        if pg:
+            pg.barrier()
+
+    def max_over_ranks(v):
+        if not pg:
+            return v
+        t = torch.tensor([v], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
 
     for i in range(args.warmup):
         replay(i)
     stream.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
     with Clocks(local) as clk:
         ev0.record(stream)
         for i in range(args.steps):
             replay(i)
         ev1.record(stream)
         stream.synchronize()
-    el_ms = ev0.elapsed_time(ev1)
+    barrier()
+    el_ms = max_over_ranks(ev0.elapsed_time(ev1))
     blk_ctx.check_device_error(stream)
-    # e2e: the token id from pinned host memory in, the greedy pick out, every step
-    hin = ops.HostBuffer(4, local)
-    hout = ops.HostBuffer(4, local)
+    ms = el_ms / args.steps
+
+    # e2e: a real greedy chain through the C ABI with host buffers -- the
+    # token id uploaded from pinned memory, the step, the greedy pick read
+    # back into pinned memory and fed in as the next token; the picks are
+    # also the cross-N identity check (expert parallelism is bit-exact)
+    hin, hout = ops.HostBuffer(4, local), ops.HostBuffer(4, local)
     n_e2e = args.e2e_steps or args.steps
+    tok_host = 1234
+    picks = []
+    barrier()
+    torch.cuda.synchronize()
+    t_wall = time.perf_counter()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(n_e2e):
-        hin.tensor.view(torch.int32)[0] = int(rng.integers(0, N_VOCAB))
+        hin.tensor.view(torch.int32)[0] = tok_host
         _lib.check(lib.styx_upload(cx, C.c_void_p(model.tok.data_ptr()), 0, C.c_void_p(hin.ptr), 4, sp))
-        _lib.check(lib.styx_graph_launch(cx, graph, sp))
+        run_step()
         _lib.check(lib.styx_download(cx, C.c_void_p(hout.ptr), C.c_void_p(model.next.data_ptr()), 0, 4, sp))
+        stream.synchronize()
+        tok_host = int(hout.tensor.view(torch.int32)[0])
+        picks.append(tok_host)
     e1.record(stream)
     stream.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    _lib.check(lib.styx_graph_destroy(cx, graph))
-    ms = el_ms / args.steps
-    bytes_tok = decode_bytes_per_token(L, ctx)
+    t_wall = time.perf_counter() - t_wall
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    x_bytes = model.x.cpu().numpy().tobytes()
+    check = {"greedy_tokens": picks[:8], "greedy_crc32": zlib.crc32(np.array(picks, np.int32).tobytes()),
+             "x_crc32": zlib.crc32(x_bytes), "steps": n_e2e}
+    if graph is not None:
+        _lib.check(lib.styx_graph_destroy(cx, graph))
+        graph = None
+
+    # the MoE block's roofline, measured in the same run: at N = 1 the 48
+    # blocks alone as a graph (the kernel the block runs, nothing else); at
+    # N > 1 the per-layer compute (styx_moe_block_ep) and all-reduce apart
+    def timed(fn, reps):
+        fn()
+        stream.synchronize()
+        barrier()
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            fn()
+        z.record(stream)
+        stream.synchronize()
+        barrier()
+        return max_over_ranks(a.elapsed_time(z)) / reps
+
     peak, peak_kind = peaks()
-    achieved = bytes_tok / (ms * 1e-3) / 1e9
+    reps = max(3, args.steps // 4)
+    ep = None
+    if world == 1:
+        g2 = C.c_void_p()
+        _lib.check(lib.styx_graph_begin(cx, sp))
+        for li, ly in enumerate(model.layers):
+            model.moe.forward(model.x, ly.moe, li, model.ids, stream=stream)
+        _lib.check(lib.styx_graph_end(cx, sp, C.byref(g2)))
+        t_layer = timed(lambda: _lib.check(lib.styx_graph_launch(cx, g2, sp)), reps) / L * 1e-3
+        _lib.check(lib.styx_graph_destroy(cx, g2))
+        achieved = ALG_BYTES_LAYER / t_layer / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_kind": peak_kind, "alg_bytes": ALG_BYTES_LAYER, "us_per_layer": t_layer * 1e6,
+                "unit_of_work": "one MoE block (one k_moe_fused launch), timed as 48 blocks in a graph in this run"}
+    else:
+        def moe_ep_only():
+            for li, ly in enumerate(model.layers):
+                model.moe.forward_ep(model.x, ly.moe, li, model.ids, model.partial, stream=stream)
+
+        def allreduce_only():
+            with torch.cuda.stream(stream):
+                for _ in range(L):
+                    pg.all_reduce(model.partial)
+        t_moe = timed(moe_ep_only, reps) / L
+        t_ar = timed(allreduce_only, reps) / L
+        t_layer = (t_moe + t_ar) * 1e-3
+        achieved = ALG_BYTES_LAYER / t_layer / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
+                "frac": achieved / (peak * world), "peak_kind": peak_kind + f" x{world}",
+                "alg_bytes": ALG_BYTES_LAYER, "us_per_layer": t_layer * 1e6,
+                "unit_of_work": "one MoE layer over all ranks: styx_moe_block_ep on every rank + one all-reduce "
+                                "of the k x H slot buffer"}
+        ep = {"moe_ep_us_per_layer": t_moe * 1e3, "allreduce_us_per_layer": t_ar * 1e3,
+              "allreduce_bytes": K_TOP * H * 4, "limiter": "all-reduce latency" if t_ar > t_moe else
+              "the block's compute", "nccl_ranks": world}
+    bytes_tok = decode_bytes_per_token(L, ctx)
+    step_achieved = bytes_tok / (ms * 1e-3) / 1e9
+    launches = 1 + L * ((1 if attn_path == 1 else 8) + (1 if moe_path == 1 else 3) + (1 if world > 1 else 0)) + 3
     line = {
-        "metric": "decode tok/s (30B-A3B shape, whole decode step)", "value": 1e3 / ms, "unit": "tok/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8-dp4a/f32 (q4_K,q6_K weights)",
+        "metric": METRIC, "value": 1e3 / ms, "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "int8-dp4a/f32 (q4_K,q6_K weights)",
         "data": "synthetic (random weights of the 30B-A3B shapes, random cache rows)",
-        "config": {"workload": f"whole decode step at the 30B-A3B shape: embedding row, {L} x (attention "
-                               f"{N_HEADS}q/{N_KV}kv x {HD} + MoE block), LM head {N_VOCAB} x {H} q6_K, greedy "
-                               f"pick; {ctx} cache rows before the token",
-                   "ctx": ctx, "l2": "inputs larger than L2 (%.2f GB read per token)" % (bytes_tok / 1e9),
-                   "launch": "cooperative" if args.shared_device else
-                   "plain (STYX_OPT_EXCLUSIVE: the bench owns its GPU)",
-                   "attention": "one kernel per layer" if attn_path == 1 else "eight kernels per layer"},
-        "e2e": {"value": n_e2e / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-        # embedding; per layer the attention half (one kernel, or rms, q, k, v, norms+RoPE+cache,
-        # attention (2), o+add) and the MoE block; output norm, head, pick
-        "gpu_launches": args.steps * (1 + L * ((1 if attn_path == 1 else 8) + 1) + 3),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "peak_kind": peak_kind,
-                     "unit_of_work": "one token: %d algorithmic bytes (expert slabs, router, attention "
-                                     "weights, cache rows, LM head, embedding row)" % bytes_tok},
+        "config": decode_config(L, ctx, world),
+        "kernels": {"launch": ("CUDA graph" if world == 1 else "eager (NCCL all-reduces between the kernels)") +
+                              (", cooperative" if args.shared_device else
+                               ", plain single kernels (STYX_OPT_EXCLUSIVE: the bench owns its GPU)"),
+                    "attention": "one kernel per layer" if attn_path == 1 else "eight kernels per layer",
+                    "moe": "single kernel per layer" if moe_path == 1 else "three kernels per layer"},
+        "e2e": {"value": n_e2e / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                "wall_s": t_wall, "form": "greedy chain: each step's pick read back and fed in as the next token"},
+        "gpu_launches": args.steps * launches,
+        "roofline": roof,
+        "step_roofline": {"bytes": bytes_tok, "achieved": step_achieved, "peak": peak * world, "unit": "GB/s",
+                          "frac": step_achieved / (peak * world)},
+        "check": check,
         "clocks": clk.summary(),
     }
-    if not args.no_cpu:
+    if ep:
+        line["ep"] = ep
+    tp = os.path.join(ROOT, "profiles", "moe_layer_traffic.json")
+    if world == 1 and os.path.exists(tp):
+        try:
+            roof["traffic"] = json.load(open(tp)).get("dram_bytes_per_layer")
+        except Exception:
+            roof["traffic"] = None
+    if rank == 0 and world == 1 and not args.no_cpu:
         try:
             nth = os.cpu_count() or 1
             v, desc = time_cpu_decode(args.cpu_seconds, nth, ctx)
@@ -366,7 +576,13 @@ def run_decode(args, local: int) -> int:
         except Exception as e:  # the CPU leg must not sink the GPU number
             line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": 0, "kind": "port",
                                     "sample": f"failed: {e}"}
-    print(json.dumps(line))
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    hin.free()
+    hout.free()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
     return 0
 
 
@@ -546,11 +762,14 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg4", "decode"],
-                    help="cfg3: all experts in HBM (the headline); cfg4: 6 GiB HBM expert budget, the rest "
-                         "streamed from pinned host memory; decode: the whole decode step (attention + MoE "
-                         "per layer, LM head, greedy pick)")
-    ap.add_argument("--ctx", type=int, default=1024, help="decode: cache rows before the token")
+    ap.add_argument("--workload", default="decode", choices=["decode", "cfg3", "cfg4"],
+                    help="decode (default): the whole decode step at the 30B shape (attention + MoE per layer, LM "
+                         "head, greedy pick; experts split over the ranks at N > 1); cfg3: the 48 MoE blocks "
+                         "alone (replicas at N > 1); cfg4: 6 GiB HBM expert budget, the rest streamed from "
+                         "pinned host memory")
+    ap.add_argument("--ctx", type=int, default=640,
+                    help="decode: cache rows before the token (640: the mean over configs[2]'s 256 decode "
+                         "tokens after its 512-token prompt)")
     ap.add_argument("--tokens", type=int, default=256, help="cfg4: timed decode tokens")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -562,7 +781,7 @@ def main() -> int:
     if args.workload == "cfg4":
         return run_streaming(args, local)
     if args.workload == "decode":
-        return run_decode(args, local)
+        return run_decode(args, local, rank, world)
 
     import ctypes as C
 
@@ -655,11 +874,15 @@ def main() -> int:
     ms_step = el_ms / args.steps
     value = world * args.steps / (el_ms / 1e3)
 
-    # e2e: C ABI with host buffers -- upload the token, replay, download the
-    # hidden state and the ids every step
+    # e2e: C ABI with host buffers -- every step uploads its own token from a
+    # pinned buffer and downloads its hidden state + ids into its own pinned
+    # buffer: a ring of RING slots, the host refilling a slot only after the
+    # event recorded after that slot's last download has completed
+    RING = 4
     n_e2e = args.e2e_steps or args.steps
-    hx = ops.HostBuffer(H * 4, local)
-    hout = ops.HostBuffer(H * 4 + L * 256, local)
+    hxs = [ops.HostBuffer(H * 4, local) for _ in range(RING)]
+    houts = [ops.HostBuffer(H * 4 + L * 256, local) for _ in range(RING)]
+    done = [None] * RING
     hbank = token_bank(64)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     xp, idp = C.c_void_p(x.data_ptr()), C.c_void_p(ids.data_ptr())
@@ -668,11 +891,17 @@ def main() -> int:
     t_wall = time.perf_counter()
     e0.record(stream)
     for i in range(n_e2e):
-        hx.tensor.view(torch.float32).copy_(torch.from_numpy(hbank[i % 64]))
-        _lib.check(lib.styx_upload(cx, xp, 0, C.c_void_p(hx.ptr), H * 4, sp))
+        r = i % RING
+        if done[r] is not None:
+            done[r].synchronize()
+        hxs[r].tensor.view(torch.float32).copy_(torch.from_numpy(hbank[i % 64]))
+        _lib.check(lib.styx_upload(cx, xp, 0, C.c_void_p(hxs[r].ptr), H * 4, sp))
         _lib.check(lib.styx_graph_launch(cx, graph, sp))
-        _lib.check(lib.styx_download(cx, C.c_void_p(hout.ptr), xp, 0, H * 4, sp))
-        _lib.check(lib.styx_download(cx, C.c_void_p(hout.ptr + H * 4), idp, 0, L * 256, sp))
+        _lib.check(lib.styx_download(cx, C.c_void_p(houts[r].ptr), xp, 0, H * 4, sp))
+        _lib.check(lib.styx_download(cx, C.c_void_p(houts[r].ptr + H * 4), idp, 0, L * 256, sp))
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        done[r] = ev
     e1.record(stream)
     stream.synchronize()
     t_wall = time.perf_counter() - t_wall
@@ -683,6 +912,9 @@ def main() -> int:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e_val = world * n_e2e / (e2e_ms / 1e3)
+    # the last step's result, read on the host
+    last_x = houts[(n_e2e - 1) % RING].tensor[:H * 4].view(torch.float32)
+    e2e_finite = bool(torch.isfinite(last_x).all())
 
     peak, peak_kind = peaks()
     t_layer = ms_step / L * 1e-3
@@ -717,7 +949,8 @@ def main() -> int:
                            launch="cooperative" if args.shared_device else
                            "plain (STYX_OPT_EXCLUSIVE: the bench owns its GPU)"),
             "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": H * 4,
-                    "d2h_bytes_per_step": H * 4 + L * 256, "wall_s": t_wall},
+                    "d2h_bytes_per_step": H * 4 + L * 256, "wall_s": t_wall, "ring": RING,
+                    "last_hidden_state_finite": e2e_finite},
             "gpu_launches": args.steps * launches_per_token,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -730,8 +963,8 @@ def main() -> int:
         }
         print(json.dumps(line), flush=True)
     _lib.check(lib.styx_graph_destroy(cx, graph))
-    hx.free()
-    hout.free()
+    for hb in hxs + houts:
+        hb.free()
     if pg:
         pg.barrier()
         pg.destroy_process_group()

@@ -323,7 +323,9 @@ int styx_moe_blocks(styx_ctx *ctx, styx_stream stream,
  * partial[s*n_embd + r] = w[s] * d[s][r] for the slots held here and 0 for
  * the others; x is read (RMSNorm, router), not updated.  Sum `partial` over
  * the ranks (one all-reduce per layer, e.g. NCCL), then styx_moe_combine
- * adds it into x.  Runs the three-kernel form. */
+ * adds it into x.  Runs the single kernel (its partial-output epilogue)
+ * when the shape fits and STYX_OPT_MOE_KERNELS is not 2, else the
+ * three-kernel form (STYX_OPT_MOE_LAST_PATH says which). */
 int styx_moe_block_ep(styx_ctx *ctx, styx_stream stream,
                       const styx_moe_dims *dims, const styx_moe_layer *layer_w,
                       int layer, const float *x, int32_t *ids,

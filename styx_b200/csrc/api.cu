@@ -1226,8 +1226,25 @@ int styx_moe_block_ep(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *di
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     int32_t *ids64 = ids + static_cast<size_t>(layer) * STYX_IDS_PER_LAYER;
     float *wts = weights_out ? weights_out : reinterpret_cast<float *>(ws + L.weights);
+    const cudaStream_t st = S(stream);
+    // the single kernel with its partial-output epilogue when the shape fits
+    if (ctx->moe_kernels != 2 && !full_in_host(lw->gate) && !full_in_host(lw->up) && !full_in_host(lw->down)) {
+        styx::FusedArgs fa{};
+        uint32_t smem = 0;
+        if (al16(lw->ffn_norm) && plan_fused(*dims, *lw, ctx->sm_count, fa, smem)) {
+            NEED(!ctx->trace || ctx->sm_count <= static_cast<int>(kTraceCtas), "too many CTAs to trace");
+            fill_fused(fa, ctx, *dims, *lw, const_cast<float *>(x), ids64, wts, ws, L);
+            fa.partial = partial;
+            fa.quiet = 1;
+            const styx::LayerLink alone{0, false, false, true, nullptr, nullptr, nullptr};
+            CK(styx::launch_fused(fa, alone, lw->gate.qtype, lw->down.qtype, ctx->sm_count, smem, !ctx->exclusive,
+                                  st));
+            ctx->last_path = 1;
+            return STYX_OK;
+        }
+    }
     ctx->last_path = 2;
-    return moe_block_split(ctx, S(stream), *dims, *lw, const_cast<float *>(x), ids64, wts, ws, L, partial, true);
+    return moe_block_split(ctx, st, *dims, *lw, const_cast<float *>(x), ids64, wts, ws, L, partial, true);
 }
 
 int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial, float *x, int ne, int k) {

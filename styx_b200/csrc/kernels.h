@@ -88,6 +88,11 @@ struct FusedArgs {
     unsigned long long *hcount; // workspace: rows of h stored per slot (slot s at s * kHcStride), never reset
     int *err;
     long long *trace;        // optional: kTraceStamps clock64 stamps per CTA (phase boundaries)
+    // expert parallelism (single-layer launches only): when set, the block
+    // writes partial[s][r] = w[s] * d[s][r] instead of adding into x, and a
+    // slot whose expert has no source here is another rank's (contributes 0)
+    float *partial;
+    int quiet;
     // shared-memory plan (every chunk of a CTA is resident at once)
     uint32_t off_a, off_part, off_ring, off_down;
     int ch;                  // gate/up rows per chunk (<= 16 chunks per CTA, a multiple of 32 / gs_g)

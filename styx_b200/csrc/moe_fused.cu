@@ -404,7 +404,7 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
             src_u[lane] = fused_slot_src(p.up, hi, ai, fi);
             src_d[lane] = fused_slot_src(p.down, hi, ai, fi);
             if (b == 0) {
-                if (e >= 0 && (!src_g[lane] || !src_u[lane] || !src_d[lane])) atomicExch(p.err, kErrBadId);
+                if (e >= 0 && !p.quiet && (!src_g[lane] || !src_u[lane] || !src_d[lane])) atomicExch(p.err, kErrBadId);
                 p.ids64[lane] = e;
                 p.ids64[16 + lane] = hi;
                 p.ids64[32 + lane] = ai;
@@ -658,7 +658,13 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
         }
         __syncthreads();
         STYX_STAMP(13);
-        if (tid < n) {
+        if (tid < n && p.partial) {
+            // expert parallelism: each slot's weighted rows; the ranks' sum
+            // (one non-zero contributor per slot) then goes through the combine
+            for (int s = 0; s < k; s++)
+                p.partial[static_cast<size_t>(s) * H + dbeg + tid] =
+                    ok ? __fmul_rn(wts[s], dpart[s * p.rc + tid]) : 0.f;
+        } else if (tid < n) {
             // the residual: the row as read from the tagged words when x came
             // that way (written by another CTA, perhaps still draining)
             float xv = lk.x_from_slot ? wts[16 + tid] : p.x[dbeg + tid];

@@ -10,6 +10,13 @@ output norm, the LM head GEMV and the greedy pick on the device
 (styx_argmax_f32).  The KV caches are allocated once for n_ctx positions
 (the reference grows them page by page, moe.rs:1802-1822; the result is the
 same).
+
+Expert parallelism (`allreduce` given): every rank runs the whole step on
+the same token with the same dense weights, but holds only its own experts
+(its layers' hot buffers, remap -> local slot); each MoE block writes its
+slot contributions (styx_moe_block_ep), `allreduce` sums them over the
+ranks in place on the stream, and styx_moe_combine adds the slot-ordered
+sum into x -- bit-identical to one device holding every expert.
 """
 from __future__ import annotations
 
@@ -47,7 +54,7 @@ class DecodeLayer:
 
 class DecodeModel:
     def __init__(self, hp: DecodeParams, embd: ops.DenseWeight, layers: list, output_norm: torch.Tensor,
-                 head: ops.DenseWeight, n_ctx: int, device: int = 0):
+                 head: ops.DenseWeight, n_ctx: int, device: int = 0, allreduce=None):
         self.hp, self.embd, self.layers, self.output_norm, self.head = hp, embd, layers, output_norm, head
         self.n_ctx = n_ctx
         dev = f"cuda:{device}"
@@ -66,6 +73,10 @@ class DecodeModel:
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.next = torch.zeros(1, dtype=torch.int32, device=dev)
         self.n_past = 0
+        # expert parallelism: a callable summing a tensor over the ranks in
+        # place, on the current stream (e.g. torch.distributed.all_reduce)
+        self.allreduce = allreduce
+        self.partial = torch.zeros(hp.n_expert_used * hp.n_embd, dtype=torch.float32, device=dev)
 
     def reset(self) -> None:
         self.n_past = 0
@@ -92,7 +103,13 @@ class DecodeModel:
         for li, ly in enumerate(self.layers):
             self.attn.forward(self.x, ly.attn, pos, self.pos, self.kcache[li], self.vcache[li], self.n_ctx,
                               stream=stream)
-            self.moe.forward(self.x, ly.moe, li, self.ids, stream=stream)
+            if self.allreduce is None:
+                self.moe.forward(self.x, ly.moe, li, self.ids, stream=stream)
+            else:
+                self.moe.forward_ep(self.x, ly.moe, li, self.ids, self.partial, stream=stream)
+                with torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext():
+                    self.allreduce(self.partial)
+                self.moe.combine(self.partial, self.x, stream=stream)
         ops.rms_norm_into(self.x, self.output_norm, hp.rms_eps, self.xn, stream=stream)
         ops.mul_mat_vec(self.head.qtype, self.head.data, hp.n_vocab, hp.n_embd, self.xn, y=self.logits,
                         stream=stream)

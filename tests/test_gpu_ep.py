@@ -2,9 +2,10 @@
 only the experts e with e % R == r (a dense hot buffer, remap -> local slot,
 no full tensor), styx_moe_block_ep writes its slot contributions, the
 partials are summed as an all-reduce would, and styx_moe_combine must give
-the single-device styx_moe_block (three-kernel form) bit for bit.  Both the
-k_gate_up shape (H 1024) and the 235B-like shape that runs gate/up as
-mul_mat_vec_id dispatches (H 4096) are covered.
+the single-device styx_moe_block bit for bit, in both kernel forms: the
+single kernel (its partial-output epilogue; the H 1024 shape) and three
+kernels (the H 1024 shape, and the 235B-like shape that runs gate/up as
+mul_mat_vec_id dispatches, H 4096, which the single kernel does not take).
 """
 import numpy as np
 import pytest
@@ -47,18 +48,21 @@ def _rank_layer(c, owned):
                                    (4096, 1536, 8, 4, (_lib.Q4_K, _lib.Q4_K, _lib.Q4_K))],
                          ids=["gate_up-kernel", "235B-like"])
 @pytest.mark.parametrize("R", [2, 3])
-def test_ep_ranks_sum_to_single_device(shape, R):
+@pytest.mark.parametrize("mode", [_lib.MOE_SPLIT, _lib.MOE_AUTO], ids=["three-kernel", "single-kernel"])
+def test_ep_ranks_sum_to_single_device(shape, R, mode):
     H, F, E, k, qts = shape
     c = make_case(51, H, F, E, k, qts)
     ref = oracle_block(c)
     blk = ops.MoeBlock(ops.Dims(H, F, E, k), 0)
-    blk.ctx.set_moe_kernels(_lib.MOE_SPLIT)
+    blk.ctx.set_moe_kernels(mode)
+    want_path = 1 if (mode == _lib.MOE_AUTO and H == 1024) else 2
     try:
         x1 = _t(c.x)
         ids1 = torch.full((64,), -7, dtype=torch.int32, device=DEV)
         blk.forward(x1, _full_layer(c), 0, ids1)
         torch.cuda.synchronize()
         blk.ctx.check_device_error()
+        assert blk.ctx.last_moe_path() == want_path
         total = torch.zeros(k * H, dtype=torch.float32, device=DEV)
         for r in range(R):
             owned = [e for e in range(E) if e % R == r]
@@ -70,6 +74,7 @@ def test_ep_ranks_sum_to_single_device(shape, R):
             blk.forward_ep(xr, lw, 0, ids, partial, weights_out=w)
             torch.cuda.synchronize()
             blk.ctx.check_device_error()           # experts held elsewhere are not errors
+            assert blk.ctx.last_moe_path() == want_path
             assert torch.equal(xr, _t(c.x))          # x is read, not updated
             assert torch.equal(ids[:k], ids1[:k])    # every rank routes the same
             p = partial.view(k, H).cpu().numpy()

@@ -59,11 +59,12 @@ def _rank_main(rank, port, out_dir):
         torch.cuda.synchronize()
         blk.ctx.check_device_error()
         np.save(os.path.join(out_dir, f"x{rank}.npy"), x.cpu().numpy())
-        if rank == 0:   # the single-device block with every expert, three-kernel form
+        path = blk.ctx.last_moe_path()
+        if rank == 0:   # the single-device block with every expert, in the same kernel form
             full = ops.LayerWeights(ffn_norm=t(c.norm), router=t(c.router),
                                     gate=ops.Experts(c.qts[0], t(c.gate), sg), up=ops.Experts(c.qts[1], t(c.up), su),
                                     down=ops.Experts(c.qts[2], t(c.down), sd))
-            blk.ctx.set_moe_kernels(_lib.MOE_SPLIT)
+            assert path == 1   # this shape runs the single kernel's expert-parallel form
             x1 = t(c.x)
             blk.forward(x1, full, 0, torch.full((64,), -7, dtype=torch.int32, device=dev))
             torch.cuda.synchronize()
