@@ -331,6 +331,27 @@ int styx_moe_block_ep(styx_ctx *ctx, styx_stream stream,
                       int layer, const float *x, int32_t *ids,
                       float *weights_out, float *partial, void *workspace,
                       uint64_t workspace_bytes);
+/* ------------------------------------------------- batched decode
+ * The MoE block for a batch of n_tokens (1..STYX_MAX_BATCH) tokens of one
+ * layer; no counterpart in the reference, which decodes one token at a time
+ * (examples/generate_moe.rs:46-53).  x: f32[n_tokens][n_embd], updated in
+ * place as n_tokens separate styx_moe_block calls would; ids: n_tokens id
+ * blocks (STYX_IDS_PER_LAYER ints each, layout of topk_softmax_f32.comp);
+ * weights_out: f32[n_tokens][k].  The tokens routed to one expert share its
+ * bytes: per used expert a grouped GEMM on the tensor cores (tcgen05, f16
+ * operands dequantised from the blocks, f32 accumulation in TMEM), M = 128
+ * weight rows per tile, N = the expert's tokens.  Operands rounded to f16:
+ * within 1e-3 of max|dx| of the f32 path.  Gate and up share one format;
+ * experts must be in device memory (hot / arena / full).  The workspace:
+ * styx_moe_batch_workspace_bytes(dims, n_tokens), no initialisation. */
+#define STYX_MAX_BATCH 64
+int styx_moe_batch_workspace_bytes(const styx_moe_dims *dims, int n_tokens, uint64_t *out);
+int styx_moe_block_batch(styx_ctx *ctx, styx_stream stream,
+                         const styx_moe_dims *dims, const styx_moe_layer *layer_w,
+                         int n_tokens, float *x, int32_t *ids,
+                         float *weights_out, void *workspace,
+                         uint64_t workspace_bytes);
+
 /* x[i] += sum_{s<k} partial[s*ne + i], summed in slot order
  * (moe_reduce_f32.comp:8-13 with the weights already applied).  With one
  * non-zero contributor per slot the cross-rank sum is exact, so the result

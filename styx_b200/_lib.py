@@ -123,6 +123,9 @@ _SIGS = {
     "styx_moe_block_ep": (_i, [_vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp, _vp, _vp,
                                _vp, _u64]),
     "styx_moe_combine": (_i, [_vp, _vp, _vp, _vp, _i, _i]),
+    "styx_moe_batch_workspace_bytes": (_i, [C.POINTER(MoeDims), _i, C.POINTER(C.c_uint64)]),
+    "styx_moe_block_batch": (_i, [_vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp, _vp, _vp,
+                                  C.c_uint64]),
     # include/styx_residency.h
     "styx_expert_budget": (_u64, [_u64, _u64, _u64, _u64, _u64, _i, _u64, _i]),
     "styx_arena_bytes": (_u64, [_i, _i, C.POINTER(_u64)]),

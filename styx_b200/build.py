@@ -25,7 +25,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
           f"-I{os.path.join(ROOT, 'include')}", "--expt-relaxed-constexpr"]
 # per-source extra flags: the synthetic quantiser must round like the C oracle
 EXTRA = {"synth.cu": ["-fmad=false"]}
-SOURCES = ["moe_kernels.cu", "moe_fused.cu", "attn.cu", "attn_fused.cu", "synth.cu", "api.cu", "residency.cpp", "gguf.cpp"]
+SOURCES = ["moe_kernels.cu", "moe_fused.cu", "batch.cu", "attn.cu", "attn_fused.cu", "synth.cu", "api.cu", "residency.cpp", "gguf.cpp"]
 HEADERS = ["common.cuh", "qdot.cuh", "kernels.h", "moe_common.cuh"]
 
 

@@ -1247,6 +1247,110 @@ int styx_moe_block_ep(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *di
     return moe_block_split(ctx, st, *dims, *lw, const_cast<float *>(x), ids64, wts, ws, L, partial, true);
 }
 
+// ------------------------------------------------ MoE block, a batch of tokens (tensor cores)
+namespace {
+struct BatchLayout {
+    size_t xh, n_used, used_e, cnt, off, pair, pv, srcs, h, d, total;
+};
+BatchLayout batch_layout(const styx_moe_dims &d, int B) {
+    BatchLayout L{};
+    size_t o = 0;
+    auto take = [&](size_t n) {
+        const size_t r = o;
+        o = (o + n + 255) & ~size_t(255);
+        return r;
+    };
+    const size_t H = d.n_embd, E = d.n_expert, F = d.n_ff, P = static_cast<size_t>(B) * d.n_expert_used;
+    L.xh = take(static_cast<size_t>(B) * H * 2);
+    L.n_used = take(16);
+    L.used_e = take(E * 4);
+    L.cnt = take(E * 4);
+    L.off = take((E + 1) * 4);
+    L.pair = take(P * 4);
+    L.pv = take(P * 4);
+    L.srcs = take(E * 3 * 8);
+    L.h = take(P * F * 2);
+    L.d = take(P * H * 4);
+    L.total = o;
+    return L;
+}
+}  // namespace
+
+int styx_moe_batch_workspace_bytes(const styx_moe_dims *dims, int n_tokens, uint64_t *out) {
+    int rc = check_dims(dims);
+    if (rc) return rc;
+    NEED(out, "null out");
+    NEED(n_tokens >= 1 && n_tokens <= STYX_MAX_BATCH, "n_tokens %d: 1..%d", n_tokens, STYX_MAX_BATCH);
+    *out = batch_layout(*dims, n_tokens).total;
+    return STYX_OK;
+}
+
+int styx_moe_block_batch(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims, const styx_moe_layer *lw,
+                         int n_tokens, float *x, int32_t *ids, float *weights_out, void *workspace,
+                         uint64_t workspace_bytes) {
+    ENTER(ctx);
+    int rc = check_dims(dims);
+    if (rc) return rc;
+    NEED(lw && x && ids && weights_out && workspace, "null pointer");
+    NEED(n_tokens >= 1 && n_tokens <= STYX_MAX_BATCH, "n_tokens %d: 1..%d", n_tokens, STYX_MAX_BATCH);
+    NEED(lw->router && lw->ffn_norm, "router and ffn_norm are required");
+    const int H = dims->n_embd, F = dims->n_ff, E = dims->n_expert, k = dims->n_expert_used, B = n_tokens;
+    if ((rc = check_tensor(lw->gate, "gate", F, H, E))) return rc;
+    if ((rc = check_tensor(lw->up, "up", F, H, E))) return rc;
+    if ((rc = check_tensor(lw->down, "down", H, F, E))) return rc;
+    NEED(lw->up.qtype == lw->gate.qtype, "gate and up must share one format");
+    NEED(styx::batch_supported(lw->gate.qtype, lw->down.qtype), "formats %d / %d not supported by the batch path",
+         lw->gate.qtype, lw->down.qtype);
+    NEED(!full_in_host(lw->gate) && !full_in_host(lw->up) && !full_in_host(lw->down),
+         "the batch path reads experts from device memory only");
+    const BatchLayout L = batch_layout(*dims, B);
+    NEED(workspace_bytes >= L.total, "workspace %llu bytes < %llu", (unsigned long long)workspace_bytes,
+         (unsigned long long)L.total);
+    NEED(al16(workspace) && extent_ok(workspace, L.total), "workspace: 16-byte aligned, workspace_bytes long");
+    NEED(extent_ok(x, static_cast<uint64_t>(B) * H * 4), "x smaller than n_tokens x n_embd");
+    NEED(extent_ok(ids, static_cast<uint64_t>(B) * STYX_IDS_PER_LAYER * 4), "ids smaller than n_tokens id blocks");
+    NEED(extent_ok(weights_out, static_cast<uint64_t>(B) * k * 4), "weights_out smaller than n_tokens x k");
+    NEED(extent_ok(lw->router, static_cast<uint64_t>(E) * H * 4), "router smaller than n_expert x n_embd");
+    NEED(extent_ok(lw->ffn_norm, static_cast<uint64_t>(H) * 4), "ffn_norm smaller than n_embd");
+    NEED(!lw->remap || extent_ok(lw->remap, static_cast<uint64_t>(E) * 4), "remap smaller than n_expert");
+    NEED(!lw->pmap || extent_ok(lw->pmap, static_cast<uint64_t>(E) * 4), "pmap smaller than n_expert");
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    styx::BatchArgs a{};
+    a.x = x;
+    a.norm_w = lw->ffn_norm;
+    a.eps = dims->rms_eps;
+    a.router = lw->router;
+    a.E = E;
+    a.H = H;
+    a.F = F;
+    a.k = k;
+    a.renorm = dims->norm_topk;
+    a.B = B;
+    a.rb_g = static_cast<int>(row_bytes(lw->gate.qtype, H));
+    a.rb_d = static_cast<int>(row_bytes(lw->down.qtype, F));
+    a.remap = lw->remap;
+    a.pmap = lw->pmap;
+    a.gate = to_src(lw->gate, E);
+    a.up = to_src(lw->up, E);
+    a.down = to_src(lw->down, E);
+    a.ids = ids;
+    a.weights = weights_out;
+    a.xh = reinterpret_cast<__half *>(ws + L.xh);
+    a.n_used = reinterpret_cast<int *>(ws + L.n_used);
+    a.used_e = reinterpret_cast<int *>(ws + L.used_e);
+    a.cnt = reinterpret_cast<int *>(ws + L.cnt);
+    a.off = reinterpret_cast<int *>(ws + L.off);
+    a.pair = reinterpret_cast<int *>(ws + L.pair);
+    a.pv = reinterpret_cast<int *>(ws + L.pv);
+    a.srcs = reinterpret_cast<const uint8_t **>(ws + L.srcs);
+    a.h = reinterpret_cast<__half *>(ws + L.h);
+    a.d = reinterpret_cast<float *>(ws + L.d);
+    a.quiet = 0;
+    a.err = ctx->d_err;
+    CK(styx::launch_batch(a, lw->gate.qtype, lw->down.qtype, S(stream)));
+    return STYX_OK;
+}
+
 int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial, float *x, int ne, int k) {
     ENTER(ctx);
     NEED(partial && x, "null pointer");

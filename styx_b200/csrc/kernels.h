@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace styx {
@@ -107,6 +108,32 @@ struct FusedArgs {
 // the per-slot h counters sit one 128-byte line apart (u64 stride), so the
 // adds of different slots do not queue at one L2 slice
 constexpr int kHcStride = 16;
+
+// the MoE block of a batch of tokens on the tensor cores (batch.cu)
+struct BatchArgs {
+    float *x;                    // [B][H] residuals, += the block
+    const float *norm_w;
+    float eps;
+    const float *router;         // f32[E][H]
+    int E, H, F, k, renorm, B;
+    int rb_g, rb_d;              // row bytes of gate/up and of down
+    const uint32_t *remap, *pmap;
+    ExpSrc gate, up, down;
+    int32_t *ids;                // [B][64] id blocks
+    float *weights;              // [B][k]
+    __half *xh;                  // workspace [B][H]: x_norm as f16
+    int *n_used;                 // workspace: used experts
+    int *used_e, *cnt, *off;     // workspace [E], [E], [E + 1]: per used expert its id, pairs, first pair
+    int *pair;                   // workspace [B * k]: pairs b * k + s grouped by expert
+    int *pv;                     // workspace [B * k]: the pair has an expert here
+    const uint8_t **srcs;        // workspace [E][3]: gate, up, down slab of each used expert
+    __half *h;                   // workspace [B * k][F]: SiLU(g) * u per pair, f16
+    float *d;                    // workspace [B * k][H]: down output per pair
+    int quiet;                   // a slot with no source here is not an error
+    int *err;
+};
+bool batch_supported(int qg, int qd);
+cudaError_t launch_batch(const BatchArgs &a, int qg, int qd, cudaStream_t st);
 
 // How a single-kernel layer connects to the layers before and after it (see
 // moe_fused.cu): chain flags and the x exchange words.

@@ -324,6 +324,30 @@ class MoeBlock:
         return self.workspace[off: off + 4 * n].view(torch.float32)
 
 
+class MoeBatch:
+    """The MoE block of a batch of up to 64 tokens of one layer
+    (styx_moe_block_batch: grouped expert GEMMs on the tensor cores)."""
+
+    def __init__(self, dims: Dims, n_tokens: int, device: int = 0):
+        self.dims, self.n_tokens, self.device = dims, n_tokens, device
+        self._dims = dims.struct()
+        n = C.c_uint64()
+        check(lib().styx_moe_batch_workspace_bytes(C.byref(self._dims), n_tokens, C.byref(n)))
+        self.ws_bytes = n.value
+        self.workspace = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=f"cuda:{device}")
+        self.ctx = ctx(device)
+
+    def forward(self, x: torch.Tensor, layer_w: LayerWeights, ids: torch.Tensor, weights_out: torch.Tensor,
+                stream=None) -> torch.Tensor:
+        """x: f32[n_tokens][n_embd] (in place); ids: int32[n_tokens * 64];
+        weights_out: f32[n_tokens * k]."""
+        st = layer_w.struct()
+        check(lib().styx_moe_block_batch(self.ctx.handle, _stream(stream), C.byref(self._dims), C.byref(st),
+                                         self.n_tokens, _ptr(x), _ptr(ids), _ptr(weights_out),
+                                         _ptr(self.workspace), self.ws_bytes))
+        return x
+
+
 # ---------------------------------------------------------------- residency
 def expert_budget(device_vram: int, headroom: int = 1024 << 20, pinned: int = 0, kv_max: int = 0,
                   arena: int = 0, explicit: Optional[int] = None, all_vram: bool = False) -> int:
