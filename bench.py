@@ -21,7 +21,8 @@ greedy picks, equal at every N (expert parallelism is bit-exact).
 
 Other workloads: --workload cfg3 (the 48 MoE blocks alone; replicas at
 N > 1), --workload cfg4 (6 GiB expert budget, the rest streamed from pinned
-host memory).
+host memory), --workload batch (--batch B tokens per step through the 48 MoE
+blocks on the tensor-core batch path).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload ...]
 """
@@ -745,6 +746,146 @@ def run_streaming(args, local: int) -> int:
     return 0
 
 
+def run_batch(args, local: int) -> int:
+    """A batch of B decode tokens through the 48 MoE layers of the cfg3 stack
+    (styx_moe_block_batch: per used expert a grouped GEMM on the tensor
+    cores).  Step i takes tokens bank[(i * B + j) % 64].  Algorithmic bytes of
+    a layer: the union of the experts the B tokens route to (each slab read
+    once), the router, the norm, and x read and written; the union sizes come
+    from an untimed pass over every phase of the token bank."""
+    import ctypes as C
+    from math import gcd
+
+    import torch
+
+    from styx_b200 import _lib, ops
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    L, B = args.layers, args.batch
+    layers = build_model(local, L)
+    blk = ops.MoeBatch(ops.Dims(H, F, E, K_TOP), B, local)
+    lib, cx = _lib.lib(), blk.ctx.handle
+    bank = torch.from_numpy(token_bank(64)).to(dev)
+    x = torch.empty(B, H, dtype=torch.float32, device=dev)
+    ids = torch.zeros(L, B * 64, dtype=torch.int32, device=dev)
+    wts = torch.zeros(L, B * K_TOP, dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    phases = 64 // gcd(64, B)
+    sel = [torch.tensor([(p * B + j) % 64 for j in range(B)], device=dev) for p in range(phases)]
+
+    def layers_pass():
+        for l in range(L):
+            blk.forward(x, layers[l], ids[l], wts[l])
+
+    # union sizes per phase and layer (untimed), from the ids the kernels wrote
+    uniq = []
+    with torch.cuda.stream(stream):
+        for p in range(phases):
+            x.copy_(bank[sel[p]])
+            layers_pass()
+            stream.synchronize()
+            got = ids.view(L, B, 64)[:, :, :K_TOP].cpu().numpy()
+            uniq.append([len(np.unique(got[l])) for l in range(L)])
+    blk.ctx.check_device_error(stream)
+
+    graph = C.c_void_p()
+    sp = C.c_void_p(stream.cuda_stream)
+    _lib.check(lib.styx_graph_begin(cx, sp))
+    with torch.cuda.stream(stream):
+        layers_pass()
+    _lib.check(lib.styx_graph_end(cx, sp, C.byref(graph)))
+
+    def replay(i):
+        with torch.cuda.stream(stream):
+            x.copy_(bank[sel[i % phases]])
+        _lib.check(lib.styx_graph_launch(cx, graph, sp))
+
+    for i in range(args.warmup):
+        replay(i)
+    stream.synchronize()
+    blk.ctx.check_device_error(stream)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            replay(i)
+        ev1.record(stream)
+        stream.synchronize()
+    el_ms = ev0.elapsed_time(ev1)
+    blk.ctx.check_device_error(stream)
+    clocks = clk.summary()
+    ms_step = el_ms / args.steps
+    value = B * args.steps / (el_ms / 1e3)
+
+    # e2e through the C ABI with host buffers: the batch's tokens up, the
+    # hidden states and id blocks down, a ring of pinned buffers
+    RING = 4
+    hbank = token_bank(64)
+    hxs = [ops.HostBuffer(B * H * 4, local) for _ in range(RING)]
+    houts = [ops.HostBuffer(B * H * 4 + L * B * 256, local) for _ in range(RING)]
+    done = [None] * RING
+    xp, idp = C.c_void_p(x.data_ptr()), C.c_void_p(ids.data_ptr())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t_wall = time.perf_counter()
+    e0.record(stream)
+    for i in range(args.steps):
+        r = i % RING
+        if done[r] is not None:
+            done[r].synchronize()
+        rows = [(i % phases * B + j) % 64 for j in range(B)]
+        hxs[r].tensor.view(torch.float32).view(B, H).copy_(torch.from_numpy(hbank[rows]))
+        _lib.check(lib.styx_upload(cx, xp, 0, C.c_void_p(hxs[r].ptr), B * H * 4, sp))
+        _lib.check(lib.styx_graph_launch(cx, graph, sp))
+        _lib.check(lib.styx_download(cx, C.c_void_p(houts[r].ptr), xp, 0, B * H * 4, sp))
+        _lib.check(lib.styx_download(cx, C.c_void_p(houts[r].ptr + B * H * 4), idp, 0, L * B * 256, sp))
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        done[r] = ev
+    e1.record(stream)
+    stream.synchronize()
+    t_wall = time.perf_counter() - t_wall
+    e2e_val = B * args.steps / (e0.elapsed_time(e1) / 1e3)
+    last_x = houts[(args.steps - 1) % RING].tensor[:B * H * 4].view(torch.float32)
+    finite = bool(torch.isfinite(last_x).all())
+
+    # algorithmic bytes per layer: the mean over the timed steps' phases
+    counts = [0] * phases
+    for i in range(args.steps):
+        counts[i % phases] += 1
+    mean_union = sum(counts[p] * sum(uniq[p]) for p in range(phases)) / (args.steps * L)
+    alg = mean_union * (2 * SG + SD) + E * H * 4 + H * 4 + 2 * B * H * 4
+    peak, peak_kind = peaks()
+    t_layer = ms_step / L * 1e-3
+    achieved = alg / t_layer / 1e9
+    line = {
+        "metric": f"decode tok/s at batch {B} (30B-A3B MoE stack, q4_K/q6_K experts)", "value": value,
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 tensor-core operands (dequantised q4_K/q6_K), f32 accumulate", "data": "synthetic",
+        "config": {"workload": f"batch {B}: the cfg3 stack ({L} MoE layers H{H} E{E} top{K_TOP} F{F}) for {B} "
+                               f"tokens per step, grouped expert GEMMs (tcgen05)", "global_batch": B,
+                   "n_layers": L, "parallelism": "single",
+                   "l2": "inputs larger than L2 (every layer's used experts stream from HBM)",
+                   "mean_union_experts_per_layer": mean_union},
+        "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": B * H * 4,
+                "d2h_bytes_per_step": B * H * 4 + L * B * 256, "wall_s": t_wall, "ring": RING,
+                "last_hidden_state_finite": finite},
+        "gpu_launches": args.steps * 5 * L,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "unit_of_work": "one batched MoE layer (5 kernels); time = step / layers",
+                     "alg_bytes": alg, "peak_kind": peak_kind, "us_per_layer": t_layer * 1e6},
+        "cpu_baseline": None,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    _lib.check(lib.styx_graph_destroy(cx, graph))
+    for hb in hxs + houts:
+        hb.free()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -762,15 +903,17 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "cfg3", "cfg4"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "cfg3", "cfg4", "batch"],
                     help="decode (default): the whole decode step at the 30B shape (attention + MoE per layer, LM "
                          "head, greedy pick; experts split over the ranks at N > 1); cfg3: the 48 MoE blocks "
                          "alone (replicas at N > 1); cfg4: 6 GiB HBM expert budget, the rest streamed from "
-                         "pinned host memory")
+                         "pinned host memory; batch: --batch tokens per step through the cfg3 stack on the "
+                         "tensor-core batch path")
     ap.add_argument("--ctx", type=int, default=640,
                     help="decode: cache rows before the token (640: the mean over configs[2]'s 256 decode "
                          "tokens after its 512-token prompt)")
     ap.add_argument("--tokens", type=int, default=256, help="cfg4: timed decode tokens")
+    ap.add_argument("--batch", type=int, default=8, help="batch: tokens per step (1..64)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -782,6 +925,8 @@ def main() -> int:
         return run_streaming(args, local)
     if args.workload == "decode":
         return run_decode(args, local, rank, world)
+    if args.workload == "batch":
+        return run_batch(args, local)
 
     import ctypes as C
 

@@ -341,8 +341,11 @@ int styx_moe_block_ep(styx_ctx *ctx, styx_stream stream,
  * bytes: per used expert a grouped GEMM on the tensor cores (tcgen05, f16
  * operands dequantised from the blocks, f32 accumulation in TMEM), M = 128
  * weight rows per tile, N = the expert's tokens.  Operands rounded to f16:
- * within 1e-3 of max|dx| of the f32 path.  Gate and up share one format;
- * experts must be in device memory (hot / arena / full).  The workspace:
+ * within 1e-3 of max|dx| of the f32 path.  Formats q4_K, q5_K, q6_K (q8_0
+ * is rejected with STYX_EINVAL); gate and up share one format; experts must
+ * be in device memory (hot / arena / full), x, router and ffn_norm 16-byte
+ * aligned.  The result is a function of the inputs alone (bit-identical on
+ * repeat and for any expert placement).  The workspace:
  * styx_moe_batch_workspace_bytes(dims, n_tokens), no initialisation. */
 #define STYX_MAX_BATCH 64
 int styx_moe_batch_workspace_bytes(const styx_moe_dims *dims, int n_tokens, uint64_t *out);

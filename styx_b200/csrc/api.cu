@@ -1250,7 +1250,7 @@ int styx_moe_block_ep(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *di
 // ------------------------------------------------ MoE block, a batch of tokens (tensor cores)
 namespace {
 struct BatchLayout {
-    size_t xh, n_used, used_e, cnt, off, pair, pv, srcs, h, d, total;
+    size_t xh, n_used, used_e, cnt, off, pair, pv, srcs, h, d, logits, gpart, upart, item_cnt, split, total;
 };
 BatchLayout batch_layout(const styx_moe_dims &d, int B) {
     BatchLayout L{};
@@ -1270,7 +1270,12 @@ BatchLayout batch_layout(const styx_moe_dims &d, int B) {
     L.pv = take(P * 4);
     L.srcs = take(E * 3 * 8);
     L.h = take(P * F * 2);
-    L.d = take(P * H * 4);
+    L.d = take(static_cast<size_t>(styx::batch_split_max(d.n_ff)) * P * H * 4);
+    L.logits = take(static_cast<size_t>(B) * E * 4);
+    L.gpart = take(static_cast<size_t>(styx::batch_split_max(d.n_embd)) * P * F * 4);
+    L.upart = take(static_cast<size_t>(styx::batch_split_max(d.n_embd)) * P * F * 4);
+    L.item_cnt = take(E * (F / 128) * 4);
+    L.split = take(16);
     L.total = o;
     return L;
 }
@@ -1307,6 +1312,7 @@ int styx_moe_block_batch(styx_ctx *ctx, styx_stream stream, const styx_moe_dims 
     NEED(workspace_bytes >= L.total, "workspace %llu bytes < %llu", (unsigned long long)workspace_bytes,
          (unsigned long long)L.total);
     NEED(al16(workspace) && extent_ok(workspace, L.total), "workspace: 16-byte aligned, workspace_bytes long");
+    NEED(al16(x) && al16(lw->router) && al16(lw->ffn_norm), "x, router and ffn_norm must be 16-byte aligned");
     NEED(extent_ok(x, static_cast<uint64_t>(B) * H * 4), "x smaller than n_tokens x n_embd");
     NEED(extent_ok(ids, static_cast<uint64_t>(B) * STYX_IDS_PER_LAYER * 4), "ids smaller than n_tokens id blocks");
     NEED(extent_ok(weights_out, static_cast<uint64_t>(B) * k * 4), "weights_out smaller than n_tokens x k");
@@ -1345,6 +1351,13 @@ int styx_moe_block_batch(styx_ctx *ctx, styx_stream stream, const styx_moe_dims 
     a.srcs = reinterpret_cast<const uint8_t **>(ws + L.srcs);
     a.h = reinterpret_cast<__half *>(ws + L.h);
     a.d = reinterpret_cast<float *>(ws + L.d);
+    a.logits = reinterpret_cast<float *>(ws + L.logits);
+    a.gpart = reinterpret_cast<float *>(ws + L.gpart);
+    a.upart = reinterpret_cast<float *>(ws + L.upart);
+    a.item_cnt = reinterpret_cast<int *>(ws + L.item_cnt);
+    a.n_item_cnt = E * (F / 128);
+    a.split_d = reinterpret_cast<int *>(ws + L.split);
+    a.sms = ctx->sm_count;
     a.quiet = 0;
     a.err = ctx->d_err;
     CK(styx::launch_batch(a, lw->gate.qtype, lw->down.qtype, S(stream)));

@@ -127,11 +127,18 @@ struct BatchArgs {
     int *pair;                   // workspace [B * k]: pairs b * k + s grouped by expert
     int *pv;                     // workspace [B * k]: the pair has an expert here
     const uint8_t **srcs;        // workspace [E][3]: gate, up, down slab of each used expert
-    __half *h;                   // workspace [B * k][F]: SiLU(g) * u per pair, f16
-    float *d;                    // workspace [B * k][H]: down output per pair
+    __half *h;                   // workspace [B * k][F]: SiLU(g) * u per pair, f16 (element order 0,2,1,3 per 4)
+    float *d;                    // workspace [smax_d][B * k][H]: down output per pair, per K piece
+    float *logits;               // workspace [B][E]
+    float *gpart, *upart;        // workspace [smax_g][B * k][F]: gate / up per K piece
+    int *item_cnt;               // workspace [n_item_cnt]: pieces done per (expert, tile)
+    int n_item_cnt;
+    int *split_d;                // workspace [2]: the K pieces of down (0) and gate/up (1)
+    int sms;                     // CTAs of a GEMM launch: the SM count
     int quiet;                   // a slot with no source here is not an error
     int *err;
 };
+int batch_split_max(int K);
 bool batch_supported(int qg, int qd);
 cudaError_t launch_batch(const BatchArgs &a, int qg, int qd, cudaStream_t st);
 

@@ -4,7 +4,8 @@ run token by token (the reference's block, moe.rs:1974-2062): routing ids
 bit-exact wherever the top-k margin exceeds 1e-4, weights within 1e-5, and
 each token's update dx within 1e-3 of max|dx| (the operands are rounded to
 f16); at batch 1, 8 and 64 and at the 30B and 235B-like shapes.  The result
-must not depend on where an expert lives (hot buffer, or full tensor)."""
+must not depend on where an expert lives (hot buffer, or full tensor).
+q8_0 is rejected by this path (its kernel stays off the GPU)."""
 import dataclasses
 
 import numpy as np
@@ -20,7 +21,6 @@ DEV = "cuda:0"
 CASES = [
     ("30B-shape-E32", 11, 2048, 768, 32, 8, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K)),
     ("H1024-q5K", 12, 1024, 512, 16, 6, (_lib.Q5_K, _lib.Q5_K, _lib.Q5_K)),
-    ("cfg1-q8_0", 13, 512, 256, 32, 4, (_lib.Q8_0, _lib.Q8_0, _lib.Q8_0)),
     ("235B-like-E6", 14, 4096, 1536, 6, 4, (_lib.Q4_K, _lib.Q4_K, _lib.Q4_K)),
 ]
 
@@ -92,6 +92,11 @@ def test_batch_rejects_bad_arguments():
     with pytest.raises(_lib.StyxError):
         blk.forward(x, _layer(c), torch.zeros(128, dtype=torch.int32, device=DEV),
                     torch.zeros(4, dtype=torch.float32, device=DEV))
+    c8 = make_case(23, 512, 256, 8, 2, (_lib.Q8_0, _lib.Q8_0, _lib.Q8_0))   # not a batch-path format
+    blk8 = ops.MoeBatch(ops.Dims(c8.H, c8.F, c8.E, c8.k), 2)
+    with pytest.raises(_lib.StyxError):
+        blk8.forward(torch.zeros(2 * c8.H, dtype=torch.float32, device=DEV), _layer(c8),
+                     torch.zeros(128, dtype=torch.int32, device=DEV), torch.zeros(4, dtype=torch.float32, device=DEV))
     import ctypes as C
     n = C.c_uint64()
     rc = _lib.lib().styx_moe_batch_workspace_bytes(C.byref(ops.Dims(512, 256, 8, 2).struct()), 65, C.byref(n))
