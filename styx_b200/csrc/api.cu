@@ -1250,7 +1250,8 @@ int styx_moe_block_ep(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *di
 // ------------------------------------------------ MoE block, a batch of tokens (tensor cores)
 namespace {
 struct BatchLayout {
-    size_t xh, n_used, used_e, cnt, off, pair, pv, srcs, h, d, logits, gpart, upart, item_cnt, split, total;
+    size_t xh, n_used, used_e, cnt, off, pair, pv, srcs, panel_x, panel_h, d, logits, gpart, upart, item_cnt, split,
+        src_sel, total;
 };
 BatchLayout batch_layout(const styx_moe_dims &d, int B) {
     BatchLayout L{};
@@ -1269,15 +1270,59 @@ BatchLayout batch_layout(const styx_moe_dims &d, int B) {
     L.pair = take(P * 4);
     L.pv = take(P * 4);
     L.srcs = take(E * 3 * 8);
-    L.h = take(P * F * 2);
+    const size_t npm = static_cast<size_t>((B + 15) & ~15);
+    L.panel_x = take(E * npm * H * 2);
+    L.panel_h = take(E * npm * F * 2);
     L.d = take(static_cast<size_t>(styx::batch_split_max(d.n_ff)) * P * H * 4);
     L.logits = take(static_cast<size_t>(B) * E * 4);
     L.gpart = take(static_cast<size_t>(styx::batch_split_max(d.n_embd)) * P * F * 4);
     L.upart = take(static_cast<size_t>(styx::batch_split_max(d.n_embd)) * P * F * 4);
     L.item_cnt = take(E * (F / 128) * 4);
     L.split = take(16);
+    L.src_sel = take(E * 4);
     L.total = o;
     return L;
+}
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+// The TMA descriptors of one expert matrix: for each source present (hot,
+// arena, full) a 3-D byte tensor {row bytes, rows, slabs} with strides {row
+// bytes, slab stride}, box {one 256-element chunk of a row, 128 rows, 1}.
+int encode_expert_maps(const styx_expert_tensor &t, int nrows, int ncols, int n_expert, CUtensorMap out[3]) {
+    EncodeTiledFn fn = encode_tiled();
+    NEED(fn, "cuTensorMapEncodeTiled is not available");
+    const uint64_t rb = static_cast<uint64_t>(row_bytes(t.qtype, ncols));
+    const uint32_t bb = static_cast<uint32_t>(row_bytes(t.qtype, 256));
+    const void *base[3] = {t.hot, t.arena, t.full};
+    const uint64_t n[3] = {t.n_hot, t.n_arena, static_cast<uint64_t>(n_expert)};
+    const uint64_t stride[3] = {t.slab_bytes, t.arena_slab_bytes, t.slab_bytes};
+    for (int i = 0; i < 3; i++) {
+        memset(&out[i], 0, sizeof(CUtensorMap));
+        if (!base[i] || !n[i]) continue;
+        const cuuint64_t dims[3] = {rb, static_cast<cuuint64_t>(nrows), n[i]};
+        const cuuint64_t strides[2] = {rb, stride[i]};
+        const cuuint32_t box[3] = {bb, 128, 1}, es[3] = {1, 1, 1};
+        const CUresult r = fn(&out[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base[i]), dims, strides, box,
+                              es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        NEED(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    }
+    return STYX_OK;
 }
 }  // namespace
 
@@ -1349,7 +1394,9 @@ int styx_moe_block_batch(styx_ctx *ctx, styx_stream stream, const styx_moe_dims 
     a.pair = reinterpret_cast<int *>(ws + L.pair);
     a.pv = reinterpret_cast<int *>(ws + L.pv);
     a.srcs = reinterpret_cast<const uint8_t **>(ws + L.srcs);
-    a.h = reinterpret_cast<__half *>(ws + L.h);
+    a.panel_x = reinterpret_cast<__half *>(ws + L.panel_x);
+    a.panel_h = reinterpret_cast<__half *>(ws + L.panel_h);
+    a.npm = (B + 15) & ~15;
     a.d = reinterpret_cast<float *>(ws + L.d);
     a.logits = reinterpret_cast<float *>(ws + L.logits);
     a.gpart = reinterpret_cast<float *>(ws + L.gpart);
@@ -1358,9 +1405,18 @@ int styx_moe_block_batch(styx_ctx *ctx, styx_stream stream, const styx_moe_dims 
     a.n_item_cnt = E * (F / 128);
     a.split_d = reinterpret_cast<int *>(ws + L.split);
     a.sms = ctx->sm_count;
+    a.src_sel = reinterpret_cast<uint32_t *>(ws + L.src_sel);
     a.quiet = 0;
     a.err = ctx->d_err;
-    CK(styx::launch_batch(a, lw->gate.qtype, lw->down.qtype, S(stream)));
+    styx::TmaSet tgu, tdn;
+    memset(&tgu, 0, sizeof(tgu));
+    memset(&tdn, 0, sizeof(tdn));
+    if (styx::batch_uses_tma(lw->gate.qtype)) {
+        if ((rc = encode_expert_maps(lw->gate, F, H, E, tgu.m[0]))) return rc;
+        if ((rc = encode_expert_maps(lw->up, F, H, E, tgu.m[1]))) return rc;
+    }
+    if (styx::batch_uses_tma(lw->down.qtype) && (rc = encode_expert_maps(lw->down, H, F, E, tdn.m[0]))) return rc;
+    CK(styx::launch_batch(a, lw->gate.qtype, lw->down.qtype, tgu, tdn, S(stream)));
     return STYX_OK;
 }
 

@@ -12,7 +12,9 @@
 //                      (a warp each), the softmax weights and the id block;
 //                      per used expert its (token, slot) pairs in token
 //                      order and its slab sources
-//   3  k_bgemm<Q, 2>   gate and up: persistent, one CTA per SM
+//   2b k_batch_panels  per used expert its tokens' x_norm rows as B panels
+//   3  k_bgemm<Q, 2>   gate and up: persistent, one CTA per SM; h goes
+//                      straight into the down kernel's B panels
 //   4  k_bgemm<Q, 1>   down: the same kernel with one matrix
 //   5  k_batch_combine x[b][r] += sum_s w[b][s] d[b][s][r], slot order
 //                      (moe_reduce_f32.comp)
@@ -20,27 +22,33 @@
 // The GEMM kernel.  A work unit is (used expert, 128-row tile, K piece):
 // the K range of a tile is cut into S pieces when that spreads the units
 // more evenly over the SMs (S is a function of the used-expert count only,
-// the same in every CTA).  The CTA walks its units' K chunks (one quant
-// super-block per row: 256 elements) through a ring of R raw
-// stages filled with cp.async (the 128 rows' quant bytes of the chunk and
-// the B rows of the unit's tokens, f16, in the canonical K-major layout):
-// chunk q + R - 1 is requested while chunk q is consumed.  Each chunk is
-// consumed in 64-wide K slices: all threads dequantise the slice's weight
-// rows into one of two A slots (f16, canonical K-major layout), then thread
-// 0 issues the slice's tcgen05.mma (M 128, N = the unit's tokens rounded to
-// 16, K 64) into the TMEM accumulator and commits them to the slot's
-// mbarrier, which the slot's next writer waits on.  At a unit's last chunk
-// the accumulator goes out: h = SiLU(g) * u as f16 (gate/up) or d as f32
-// (down) when S == 1, else f32 partials per piece, which the CTA that
-// finishes an item's last piece sums in piece order (gate/up) or the combine
-// kernel sums (down): the result does not depend on which CTA ran what.
+// the same in every CTA).  Warp roles, linked by mbarriers (no block barrier
+// in the loop):
+//   copies      the unit's K chunks (one quant super-block per row, 256
+//               elements) into a ring of R stages: one TMA tensor copy per
+//               matrix (a 128-row x chunk box of a 3-D map over the source
+//               buffer) for q4_K / q5_K, cp.async from 16-byte aligned row
+//               windows for q6_K; plus the unit's B panel chunk (bulk copy)
+//   dequant     two groups taking alternate 64-wide K slices; a thread
+//               turns one row's slice into f16 in an A slot (2 or 4 slots,
+//               canonical K-major layout)
+//   MMA         one thread: tcgen05.mma (M 128, N = the unit's tokens
+//               rounded to 16, K 16) into a TMEM accumulator, commits to the
+//               slot, stage and accumulator barriers
+//   epilogue    four warps: TMEM -> h = SiLU(g) * u as f16 straight into the
+//               down kernel's B panel (gate/up) or d as f32 (down) when
+//               S == 1, else f32 partials per piece, which the CTA that
+//               finishes an item's last piece sums in piece order (gate/up)
+//               or the combine kernel sums (down); two accumulator buffers
+// The result does not depend on which CTA ran what.
 //
 // Dequantisation stays in packed f16 arithmetic: a quant byte q becomes the
-// half 1024 + q by OR-ing it into the bits of 1024, then q = that - 1024
-// exactly, then d * sc * q - dmin * m in one fused multiply-add.  Splitting a
-// 32-bit word of four bytes into two half2 gives the element order
-// (0, 2, 1, 3) in every group of four; the B rows (x_norm and h) are stored
-// in the same order, so the dot products are unchanged.
+// half 1024 + q by OR-ing it into the bits of 1024, t = sc * q exactly by one
+// fused multiply-add, then round(round(d * t - c_hi) - c_lo) with the min
+// term split in two halves.  Splitting a 32-bit word of four bytes into two
+// half2 gives the element order (0, 2, 1, 3) in every group of four; the B
+// rows (x_norm and h) are stored in the same order, so the dot products are
+// unchanged.
 //
 // Precision: operands are rounded to f16 (11-bit significand), products and
 // sums are f32 in TMEM; the block stays within 1e-3 of max|dx| of the f32
@@ -48,6 +56,7 @@
 // TMEM columns; every wait is bounded.
 #include <cfloat>
 #include <cstring>
+#include <type_traits>
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -112,25 +121,6 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src, uint64_t 
                  "l"(pol)
                  : "memory");
 }
-__device__ __forceinline__ void cp_async8(void *dst, const void *src, uint64_t pol) {
-    asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 8, %2;" ::"r"(smem_addr(dst)), "l"(src),
-                 "l"(pol)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-// wait until at most n of this thread's groups are pending (n = 0 .. 6)
-__device__ __forceinline__ void cp_async_wait(int n) {
-    switch (n) {
-    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
-    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
-    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
-    case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
-    case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
-    case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
-    default: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
-    }
-}
-
 // position of element i of a B row (x_norm, h) in memory: positions 1 and
 // 2 of every group of four swapped, the order the dequantisation produces
 __host__ __device__ __forceinline__ int kperm(int i) { return (i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1); }
@@ -321,6 +311,9 @@ __global__ void __launch_bounds__(kListThreads) k_batch_lists(BatchArgs a) {
         a.pair[a.off[u] + rank] = p;
         if (rank == 0) {
             const int32_t *ids = a.ids + static_cast<size_t>(b) * kIdsPerLayer;
+            const int hi = ids[16 + s], ai = ids[32 + s], fi = ids[48 + s];
+            a.src_sel[u] = hi >= 0 ? static_cast<uint32_t>(hi)
+                                   : ai >= 0 ? (1u << 28) | static_cast<uint32_t>(ai) : (2u << 28) | static_cast<uint32_t>(fi);
             a.srcs[3 * u + 0] = fused_slot_src(a.gate, ids[16 + s], ids[32 + s], ids[48 + s]);
             a.srcs[3 * u + 1] = fused_slot_src(a.up, ids[16 + s], ids[32 + s], ids[48 + s]);
             a.srcs[3 * u + 2] = fused_slot_src(a.down, ids[16 + s], ids[32 + s], ids[48 + s]);
@@ -328,16 +321,38 @@ __global__ void __launch_bounds__(kListThreads) k_batch_lists(BatchArgs a) {
     }
 }
 
+// ------------------------------------------------------------ 2b: x_norm panels
+// Per used expert u and K chunk kc: the f16 x_norm rows of u's tokens (list
+// order), Np = its token count rounded up to 16 rows (zero rows past it), in
+// the canonical K-major core-matrix layout the MMA reads; one contiguous
+// Np x 512-byte block, so the GEMM brings it with a single bulk copy.
+__global__ void __launch_bounds__(256) k_batch_panels(BatchArgs a) {
+    const int u = blockIdx.x, kc = blockIdx.y;
+    if (u >= *a.n_used) return;
+    const int N = a.cnt[u], p0 = a.off[u], Np = max(16, (N + 15) & ~15);
+    __half *dst = a.panel_x + static_cast<size_t>(u) * a.npm * a.H + static_cast<size_t>(kc) * Np * 256;
+    for (int i = threadIdx.x; i < Np * 32; i += blockDim.x) {
+        const int n = i >> 5, kp = i & 31;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (n < N) {
+            const int b = a.pair[p0 + n] / a.k;
+            v = *reinterpret_cast<const uint4 *>(a.xh + static_cast<size_t>(b) * a.H + kc * 256 + kp * 8);
+        }
+        *reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(dst) + kmaj_off(n, kp * 8, Np)) = v;
+    }
+}
+
 // ------------------------------------------------------------ quant formats
-// per format: elements of one K chunk (one super-block per row), its bytes
-// per row, the stage row stride (a multiple of 16 whose quotient by 16 is
-// odd: 16-byte reads of 32 consecutive rows are free of bank conflicts), the
-// cp.async size (16 where every row chunk starts on a 16-byte boundary; 8
-// for q6_K, whose 210-byte blocks start on 2-byte boundaries)
-__host__ __device__ constexpr int q_kch(int) { return 256; }
+// Per format: bytes of one K chunk of a row (one 256-element super-block),
+// the bulk copy that brings it (a 16-byte aligned window: q4_K / q5_K row
+// chunks start on 16-byte boundaries; q6_K's 210-byte blocks on 2-byte ones,
+// so its window is the chunk rounded down to 16, 224 bytes, never past the
+// 16-byte block that holds the chunk's last byte), and the stage row stride
+// (a multiple of 16 whose quotient by 16 is odd: 16-byte reads of 32
+// consecutive rows are free of bank conflicts).
 __host__ __device__ constexpr int q_bb(int qt) { return qt == STYX_Q4_K ? 144 : qt == STYX_Q5_K ? 176 : 210; }
+__host__ __device__ constexpr int q_win(int qt) { return qt == STYX_Q6_K ? 224 : q_bb(qt); }
 __host__ __device__ constexpr int q_rsb(int qt) { return qt == STYX_Q4_K ? 144 : qt == STYX_Q5_K ? 176 : 240; }
-__host__ __device__ constexpr int q_cpb(int qt) { return qt == STYX_Q6_K ? 8 : 16; }
 
 __device__ __forceinline__ __half2 u2h2(uint32_t u) {
     __half2 h;
@@ -350,121 +365,117 @@ __device__ __forceinline__ uint32_t h22u(__half2 h) {
     return u;
 }
 constexpr uint32_t kHalf1024x2 = 0x64006400u;   // the half 1024.0, twice
-// four bytes v = (b0, b1, b2, b3), each < 256, as the halves of
-// (b0 + 1024 - bias, b2 + ...) and (b1 + ..., b3 + ...) scaled: fma(q, s, c)
-__device__ __forceinline__ void bytes4_fma(uint32_t v, __half2 bias, __half2 s, __half2 c, uint32_t &lo,
-                                           uint32_t &hi) {
-    const uint32_t e02 = (v & 0x00FF00FFu) | kHalf1024x2;
-    const uint32_t e13 = ((v >> 8) & 0x00FF00FFu) | kHalf1024x2;
-    lo = h22u(__hfma2(__hsub2(u2h2(e02), bias), s, c));
-    hi = h22u(__hfma2(__hsub2(u2h2(e13), bias), s, c));
+__device__ __forceinline__ uint32_t lop_or(uint32_t v, uint32_t mask) { return (v & mask) | kHalf1024x2; }
+// the 6-bit scale and min of sub-block j (0..7) of a q4_K / q5_K super-block
+// from its 12 packed bytes in three words (get_scale_min_k4, moe.rs:506-533)
+template <int J>
+__device__ __forceinline__ void scale_min_k4(uint32_t s0, uint32_t s1, uint32_t s2, float &sc, float &m) {
+    auto byte = [&](int i) -> uint32_t { return ((i < 4 ? s0 : i < 8 ? s1 : s2) >> (8 * (i & 3))) & 0xFFu; };
+    if constexpr (J < 4) {
+        sc = static_cast<float>(byte(J) & 63);
+        m = static_cast<float>(byte(J + 4) & 63);
+    } else {
+        sc = static_cast<float>((byte(J + 4) & 0xF) | ((byte(J - 4) >> 6) << 4));
+        m = static_cast<float>((byte(J + 4) >> 4) | ((byte(J) >> 6) << 4));
+    }
 }
-// 32 bytes at byte `off` (even) of a stage row, as eight words; the row is
-// read with 16-byte loads from off rounded down to 16
-__device__ __forceinline__ void run32(const uint8_t *row, int off, uint32_t (&w)[8]) {
-    const uint4 *p = reinterpret_cast<const uint4 *>(row + (off & ~15));
-    const uint4 A = p[0], B = p[1], C = p[2];
+
+// the 32 bytes at base + o (base 16-byte aligned, o even, 0..14) as eight
+// words: three 16-byte reads, then a shift by o in 8-, 4- and 2-byte steps
+__device__ __forceinline__ void run32_at(const uint8_t *base, int o, uint32_t (&w)[8]) {
+    const uint4 A = *reinterpret_cast<const uint4 *>(base);
+    const uint4 B = *reinterpret_cast<const uint4 *>(base + 16);
+    const uint4 C = *reinterpret_cast<const uint4 *>(base + 32);
     const uint32_t V[12] = {A.x, A.y, A.z, A.w, B.x, B.y, B.z, B.w, C.x, C.y, C.z, C.w};
-    const int bo = off & 15;
-    const uint32_t s1 = static_cast<uint32_t>(bo & 4) << 3, sh = static_cast<uint32_t>(bo & 3) << 3;
-    const bool two = (bo & 8) != 0;
-    uint32_t T1[11];
+    const bool s8 = (o & 8) != 0, s4 = (o & 4) != 0;
+    const uint32_t sh = static_cast<uint32_t>(o & 2) << 3;
+    uint32_t T1[10], T2[9];
 #pragma unroll
-    for (int i = 0; i < 11; i++) T1[i] = __funnelshift_rc(V[i], V[i + 1], s1);
-    uint32_t T2[9];
+    for (int i = 0; i < 10; i++) T1[i] = s8 ? V[i + 2] : V[i];
 #pragma unroll
-    for (int i = 0; i < 9; i++) T2[i] = two ? T1[i + 2] : T1[i];
+    for (int i = 0; i < 9; i++) T2[i] = s4 ? T1[i + 1] : T1[i];
 #pragma unroll
     for (int i = 0; i < 8; i++) w[i] = __funnelshift_r(T2[i], T2[i + 1], sh);
 }
-// the 6-bit scale and min of sub-block j of a q4_K / q5_K super-block
-// (the packing of get_scale_min_k4, moe.rs:506-533)
-__device__ __forceinline__ void scale_min_k4(const uint8_t *s, int j, float &sc, float &m) {
-    if (j < 4) {
-        sc = static_cast<float>(s[j] & 63);
-        m = static_cast<float>(s[j + 4] & 63);
-    } else {
-        sc = static_cast<float>((s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4));
-        m = static_cast<float>((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
-    }
-}
-__device__ __forceinline__ float half_at(const uint8_t *p) {   // 2-byte aligned
-    return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(p)));
-}
 
-// Elements e0 .. e0 + 31 (e0 % 32 == 0) of a K chunk of one weight row, from
-// its stage row (quant data at byte `o`), dequantised to f16 and written as
-// four 16-byte groups of eight to `dst` (the A slot, rows 128 apart per K
-// group: kmaj_off(r, k0 + 8 i, 128)); element order (0, 2, 1, 3) per four.
-// The value of each element is the reference's d * sc * q - dmin * m
+// 32 elements of K slice J (64 wide) of one weight row, half H: elements
+// 64 J + 32 H .. + 31 of the row's 256-element chunk, from its stage row
+// (quant data at byte `o`: 0 but for q6_K), as f16 in sixteen words, element order
+// (0, 2, 1, 3) in every four.  Values: the reference's d * sc * q - dmin * m
 // (q4_K / q5_K), d * sc * (q - 32) (q6_K).
-template <int QT>
-__device__ __forceinline__ void deq32(const uint8_t *row, int o, int e0, uint8_t *slot, int r, int k0) {
-    uint32_t out[16];
+//
+// q4_K / q5_K keep the error per element: t = sc * q is an integer below
+// 2048, exact in f16, from one fused multiply-add on the half 1024 + q (the
+// quant bits OR-ed into 1024's, exact); high nibbles are taken in place, as
+// 1024 + 16 q, with sc / 16 and 64 sc (exact too); d is the stored half; the
+// min term c = dmin * m (exact in f32) goes in as c_hi + c_lo.  So an element
+// is round(round(d * t - c_hi) - c_lo), and no rounding is shared by the 32
+// elements of a sub-block.
+template <int QT, int J, int H>
+__device__ __forceinline__ void deq_run(const uint8_t *row, int o, uint32_t (&out)[16]) {
     if constexpr (QT == STYX_Q4_K || QT == STYX_Q5_K) {
-        // d * sc * q - dmin * m with one systematic error removed: t = sc * q
-        // is an integer below 2048, exact in f16; d is the stored half; the
-        // min term c = dmin * m (exact in f32) goes in as c_hi + c_lo, so
-        // the element is round(round(d * t - c_hi) - c_lo) and no rounding
-        // is shared by the 32 elements of a sub-block
-        const int sb = e0 >> 5, j = sb >> 1, hi = sb & 1;
-        const uint32_t hd = *reinterpret_cast<const uint32_t *>(row);
-        const __half dh = __ushort_as_half(static_cast<unsigned short>(hd & 0xFFFFu));
-        const float dm = __half2float(__ushort_as_half(static_cast<unsigned short>(hd >> 16)));
+        constexpr int SB = 2 * J + H;
+        const uint4 hdr = *reinterpret_cast<const uint4 *>(row);   // d, dmin, 12 scale bytes
+        const __half dh = __ushort_as_half(static_cast<unsigned short>(hdr.x & 0xFFFFu));
+        const float dm = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr.x >> 16)));
         float sc, mn;
-        scale_min_k4(row + 4, sb, sc, mn);
+        scale_min_k4<SB>(hdr.y, hdr.z, hdr.w, sc, mn);
         const float c = dm * mn;
         const __half chi = __float2half_rn(c);
         const __half clo = __float2half_rn(c - __half2float(chi));
         const __half2 d2 = __half2half2(dh), nchi2 = __half2half2(__hneg(chi)), clo2 = __half2half2(clo);
-        const __half2 sc2 = __float2half2_rn(sc), nsc1024 = __float2half2_rn(-1024.0f * sc);
-        const __half2 k1024 = u2h2(kHalf1024x2);
         constexpr int QS = QT == STYX_Q4_K ? 16 : 48;
-        const uint4 q0 = *reinterpret_cast<const uint4 *>(row + QS + 32 * j);
-        const uint4 q1 = *reinterpret_cast<const uint4 *>(row + QS + 32 * j + 16);
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(row + QS + 32 * J);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(row + QS + 32 * J + 16);
         const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        uint32_t h5[8];
-        if constexpr (QT == STYX_Q5_K) {
+        if constexpr (QT == STYX_Q4_K) {
+            // H = 0: 1024 + q, t = e sc - 1024 sc; H = 1: 1024 + 16 q, t = e sc/16 - 64 sc
+            const __half2 sc2 = __float2half2_rn(H ? sc * 0.0625f : sc);
+            const __half2 nb2 = __float2half2_rn(H ? -64.0f * sc : -1024.0f * sc);
+            constexpr uint32_t M = H ? 0x00F000F0u : 0x000F000Fu;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const __half2 t02 = __hfma2(u2h2(lop_or(w[i], M)), sc2, nb2);
+                const __half2 t13 = __hfma2(u2h2(lop_or(w[i] >> 8, M)), sc2, nb2);
+                out[2 * i] = h22u(__hsub2(__hfma2(t02, d2, nchi2), clo2));
+                out[2 * i + 1] = h22u(__hsub2(__hfma2(t13, d2, nchi2), clo2));
+            }
+        } else {   // q5_K: the fifth bit from qh (bit SB of each byte); q up to 31
             const uint4 h0 = *reinterpret_cast<const uint4 *>(row + 16);
             const uint4 h1 = *reinterpret_cast<const uint4 *>(row + 32);
             const uint32_t hb[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            const __half2 sc2 = __float2half2_rn(sc), k1024 = u2h2(kHalf1024x2);
 #pragma unroll
-            for (int i = 0; i < 8; i++) h5[i] = ((hb[i] >> sb) & 0x01010101u) << 4;
-        }
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            uint32_t v = (w[i] >> (4 * hi)) & 0x0F0F0F0Fu;
-            if constexpr (QT == STYX_Q5_K) v |= h5[i];
-            const uint32_t e02 = (v & 0x00FF00FFu) | kHalf1024x2, e13 = ((v >> 8) & 0x00FF00FFu) | kHalf1024x2;
-            __half2 t02, t13;
-            if constexpr (QT == STYX_Q4_K) {   // (1024 + q) * sc - 1024 * sc: below 65504 throughout
-                t02 = __hfma2(u2h2(e02), sc2, nsc1024);
-                t13 = __hfma2(u2h2(e13), sc2, nsc1024);
-            } else {                           // q up to 31: subtract first
-                t02 = __hmul2(__hsub2(u2h2(e02), k1024), sc2);
-                t13 = __hmul2(__hsub2(u2h2(e13), k1024), sc2);
+            for (int i = 0; i < 8; i++) {
+                const uint32_t v = ((w[i] >> (4 * H)) & 0x0F0F0F0Fu) | (((hb[i] >> SB) & 0x01010101u) << 4);
+                const __half2 t02 = __hmul2(__hsub2(u2h2(lop_or(v, 0x00FF00FFu)), k1024), sc2);
+                const __half2 t13 = __hmul2(__hsub2(u2h2(lop_or(v >> 8, 0x00FF00FFu)), k1024), sc2);
+                out[2 * i] = h22u(__hsub2(__hfma2(t02, d2, nchi2), clo2));
+                out[2 * i + 1] = h22u(__hsub2(__hfma2(t13, d2, nchi2), clo2));
             }
-            out[2 * i] = h22u(__hsub2(__hfma2(t02, d2, nchi2), clo2));
-            out[2 * i + 1] = h22u(__hsub2(__hfma2(t13, d2, nchi2), clo2));
         }
-    } else if constexpr (QT == STYX_Q6_K) {
-        const int n = e0 >> 7, qd = (e0 & 127) >> 5;
+    } else {   // q6_K: quadrant QD = 2 (J & 1) + H of the 128-element half N = J / 2; data at byte o (0..14)
+        constexpr int N = J >> 1, QD = 2 * (J & 1) + H;
         uint32_t ql[8], qh[8];
-        run32(row, o + 64 * n + 32 * (qd & 1), ql);
-        run32(row, o + 128 + 32 * n, qh);
-        const float d = half_at(row + o + 208);
-        const int8_t *scp = reinterpret_cast<const int8_t *>(row + o + 192 + 8 * n + 2 * qd);
-        const __half2 s0 = __float2half2_rn(d * static_cast<float>(scp[0]));
-        const __half2 s1 = __float2half2_rn(d * static_cast<float>(scp[1]));
+        run32_at(row + 64 * N + 32 * (QD & 1), o, ql);
+        run32_at(row + 128 + 32 * N, o, qh);
+        // the quadrant's two int8 scales (l < 16, l >= 16) and d: 2-byte aligned pairs
+        const uint32_t sc_pair = *reinterpret_cast<const unsigned short *>(row + o + 192 + 8 * N + 2 * QD);
+        const float d = __half2float(*reinterpret_cast<const __half *>(row + o + 208));
+        const __half2 s0 = __float2half2_rn(d * static_cast<float>(static_cast<int8_t>(sc_pair & 0xFFu)));
+        const __half2 s1 = __float2half2_rn(d * static_cast<float>(static_cast<int8_t>(sc_pair >> 8)));
         const __half2 bias = u2h2(0x64206420u);   // 1024 + 32
-        const __half2 zero = u2h2(0u);
-        const int s4 = 4 * (qd >> 1), sq = 2 * qd;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            const uint32_t v = ((ql[i] >> s4) & 0x0F0F0F0Fu) | (((qh[i] >> sq) & 0x03030303u) << 4);
-            bytes4_fma(v, bias, i < 4 ? s0 : s1, zero, out[2 * i], out[2 * i + 1]);
+            const uint32_t v = ((ql[i] >> (4 * (QD >> 1))) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * QD)) & 0x03030303u) << 4);
+            const __half2 sc = i < 4 ? s0 : s1;
+            out[2 * i] = h22u(__hmul2(__hsub2(u2h2(lop_or(v, 0x00FF00FFu)), bias), sc));
+            out[2 * i + 1] = h22u(__hmul2(__hsub2(u2h2(lop_or(v >> 8, 0x00FF00FFu)), bias), sc));
         }
     }
+}
+// the sixteen words of a run into the A slot (row r, K offset k0 of the slice)
+__device__ __forceinline__ void store_run(uint8_t *slot, int r, int k0, const uint32_t (&out)[16]) {
 #pragma unroll
     for (int i = 0; i < 4; i++)
         *reinterpret_cast<uint4 *>(slot + kmaj_off(r, k0 + 8 * i, 128)) =
@@ -491,46 +502,92 @@ __host__ __device__ inline int choose_split(int n_items, int nk, int G, int smax
     return best;
 }
 
-__host__ __device__ constexpr uint32_t tmem_cols_for(int n) { return n <= 32 ? 32u : n <= 64 ? 64u : 128u; }
+__host__ __device__ constexpr uint32_t tmem_cols_for(int n) {
+    return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : 256u;
+}
 
 // One side of the block: gate + up (NM = 2) or down (NM = 1).
 struct GemmSide {
     int K, M, rb;            // row length, rows of one expert matrix, bytes of a row
     int mat0;                // srcs index of the first matrix (0: gate, up; 2: down)
-    const __half *bsrc;      // B rows: x_norm [B][K] (by token) or h [P][K] (by pair)
-    int by_token;
+    const __half *panel;     // B panels: per used expert npm * K halves, chunk kc at kc * Np * 256
     float *part0, *part1;    // f32 partials [smax][P][M] per matrix (down: part0 piece 0 = d)
-    int npm;                 // B rows a stage holds (tokens of one expert, padded to 16)
+    int npm;                 // largest Np (tokens of one expert, padded to 16)
     int stages;              // R
+    int nslot;               // A slots: 2 or 4
     int smax;
     int *split_out;          // the S this launch used
 };
 
-// What a stage's chunk is: written by thread 0 when the chunk's copies are
-// issued, read by every thread after the chunk-start barrier.
-struct ChunkMeta {
-    const uint8_t *src0, *src1;   // the unit's matrices (row 0 of the tile, chunk 0)
-    int N, p0, u, tile, piece, kc, first, last;
+// Warp roles of a GEMM CTA: copies (one warp issuing TMA tensor copies for
+// q4_K / q5_K; four warps of cp.async for q6_K, whose rows are not 16-byte
+// multiples), dequantisation (two groups of 4 warps per matrix taking
+// alternate 64-wide slices, a whole row's slice per thread), the MMA thread
+// (one warp), the epilogue (four consecutive warps, whose ids mod 4 cover the
+// four TMEM lane quarters).
+constexpr int kEpiWarps = 4;
+constexpr int kMaxStages = 4;
+template <int QT, int NM>
+struct GemmRoles {
+    static constexpr bool kTma = QT != STYX_Q6_K;
+    static constexpr int kProd = kTma ? 1 : 4;
+    static constexpr int kDeq = 8 * NM;
+    static constexpr int kMma = kProd + kDeq;
+    static constexpr int kEpi0 = kMma + 1;
+    static constexpr int kThreads = 32 * (kEpi0 + kEpiWarps);
+};
+bool batch_uses_tma(int qt) { return qt == STYX_Q4_K || qt == STYX_Q5_K; }
+
+struct GemmBars {
+    uint64_t full[kMaxStages];    // a stage's copies landed (expect_tx arrival, or one cp.async arrival per copy thread)
+    uint64_t empty[kMaxStages];   // a stage's MMAs done (tcgen05.commit)
+    uint64_t afull[4];            // an A slot dequantised (one arrival per warp of its dequant group)
+    uint64_t aempty[4];           // an A slot's MMAs done
+    uint64_t accf[2];             // an accumulator buffer complete
+    uint64_t acce[2];             // an accumulator buffer read out (one arrival per epilogue warp)
+    uint64_t drain;               // the MMA thread's last commit
 };
 
+__device__ __forceinline__ void tma_load3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar,
+                                           uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+        "%3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar)), "l"(pol)
+        : "memory");
+}
+// the mbarrier counts one arrival when all of this thread's earlier cp.async are done
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory"); }
+// every epilogue thread arrives (whatever its wait returned), so this barrier
+// always completes; true when all of them passed their wait
+__device__ __forceinline__ bool epi_all(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+        "barrier.cta.red.and.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(ok)), "n"(32 * kEpiWarps)
+        : "memory");
+    return r != 0;
+}
+
 template <int QT, int NM>
-__global__ void __launch_bounds__(256 * NM, 1) k_bgemm(BatchArgs a, GemmSide g) {
-    constexpr int T = 256 * NM;
-    constexpr int KCH = q_kch(QT), BB = q_bb(QT), RSB = q_rsb(QT), CPB = q_cpb(QT);
-    constexpr int NPC = CPB == 16 ? BB / 16 : (BB + 6 + 7) / 8;   // copies per stage row, at most
-    constexpr int SLICES = KCH / 64;
-    constexpr int JB = SLICES > 2 ? 2 : 1;                       // slice that issues the B rows
+__global__ void __launch_bounds__(GemmRoles<QT, NM>::kThreads, 1)
+    k_bgemm(BatchArgs a, GemmSide g, const __grid_constant__ TmaSet tm) {
+    using RL = GemmRoles<QT, NM>;
+    constexpr int BB = q_bb(QT), RSB = q_rsb(QT);
     constexpr int ASLOT = NM * 128 * 64 * 2;
-    constexpr int BITEMS = (64 * (KCH / 8) + T - 1) / T;         // B copies per thread, at most
-    extern __shared__ __align__(128) uint8_t sm[];
-    __shared__ uint64_t bar[2];
+    extern __shared__ __align__(1024) uint8_t sm[];
+    __shared__ GemmBars bars;
     __shared__ uint32_t tbase;
-    __shared__ int s_fin;
-    __shared__ ChunkMeta meta[4];
+    __shared__ int s_abort, s_fin;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
     const int n_used = *a.n_used;
-    const int tiles = g.M / 128, nk = g.K / KCH, P = a.B * a.k;
+    const int tiles = g.M / 128, nk = g.K / 256, P = a.B * a.k;
     const int n_items = n_used * tiles;
     const int S = choose_split(n_items, nk, G, g.smax);
     if (cta == 0 && tid == 0) *g.split_out = S;
@@ -539,13 +596,26 @@ __global__ void __launch_bounds__(256 * NM, 1) k_bgemm(BatchArgs a, GemmSide g) 
     const int my_units = cta < n_units ? (n_units - 1 - cta) / G + 1 : 0;
     if (my_units == 0) return;   // the whole CTA, before any barrier or TMEM use
     const int Q = my_units * CPU;
-    const int Npm = g.npm, R = g.stages;
-    const int stage_w = NM * 128 * RSB, stage_bytes = stage_w + Npm * KCH * 2;
-    uint8_t *slots = sm, *stages = sm + 2 * ASLOT;
-    const uint32_t tcols = tmem_cols_for(NM * Npm);
+    const int Npm = g.npm, R = g.stages, NS = g.nslot;
+    const int stage_w = NM * 128 * RSB, stage_bytes = stage_w + Npm * 512;
+    uint8_t *slots = sm, *stages = sm + NS * ASLOT;
+    const int acc_cols = NM * Npm;   // one accumulator buffer; two of them
+    const uint32_t tcols = tmem_cols_for(2 * acc_cols);
     if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+        for (int i = 0; i < R; i++) {
+            mbar_init(&bars.full[i], RL::kTma ? 1 : 32 * RL::kProd);
+            mbar_init(&bars.empty[i], 1);
+        }
+        for (int i = 0; i < NS; i++) {
+            mbar_init(&bars.afull[i], RL::kDeq / 2);
+            mbar_init(&bars.aempty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&bars.accf[i], 1);
+            mbar_init(&bars.acce[i], kEpiWarps);
+        }
+        mbar_init(&bars.drain, 1);
+        s_abort = 0;
         fence_mbar_init();
     }
     __syncwarp();   // lane 0 of warp 0 took the branch above; .sync.aligned needs the whole warp
@@ -556,195 +626,256 @@ __global__ void __launch_bounds__(256 * NM, 1) k_bgemm(BatchArgs a, GemmSide g) 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tbase;
-    const uint64_t pol_w = l2_evict_first(), pol_b = l2_evict_last();
 
-    // ---- chunk q -> its unit; the unit's tables (read-only in this kernel)
-    auto meta_of = [&](int q) {
-        ChunkMeta x;
-        const int vi = q / CPU, cq = q - vi * CPU;
-        const int v = cta + vi * G, item = v / S;
-        x.piece = v - item * S;
-        x.u = item / tiles;
-        x.tile = item - x.u * tiles;
-        x.kc = x.piece * CPU + cq;
-        x.first = cq == 0;
-        x.last = cq == CPU - 1;
-        x.N = __ldg(a.cnt + x.u);
-        x.p0 = __ldg(a.off + x.u);
-        const size_t at = static_cast<size_t>(x.tile) * 128 * g.rb;
-        x.src0 = a.srcs[3 * x.u + g.mat0] + at;
-        x.src1 = NM == 2 ? a.srcs[3 * x.u + g.mat0 + 1] + at : x.src0;
-        return x;
+    // unit i of this CTA: v = cta + i G -> (item, piece) -> (used expert, tile)
+    auto unit_of = [&](int i, int &u, int &tile, int &piece) {
+        const int v = cta + i * G, item = v / S;
+        piece = v - item * S;
+        u = item / tiles;
+        tile = item - u * tiles;
     };
-    // the weight rows of chunk x into stage st (no loads besides the copies)
-    auto issue_w = [&](const ChunkMeta &x, uint8_t *st) {
-        const size_t kb = static_cast<size_t>(x.kc) * BB;
-        for (int i = tid; i < NM * 128 * NPC; i += T) {
-            const int m = i / (128 * NPC), rem = i - m * (128 * NPC), r = rem / NPC, pc = rem - r * NPC;
-            const uint8_t *rs = (m ? x.src1 : x.src0) + static_cast<size_t>(r) * g.rb + kb;
-            uint8_t *dst = st + (m * 128 + r) * RSB + pc * CPB;
-            if constexpr (CPB == 16) {
-                cp_async16(dst, rs + pc * 16, pol_w);
-            } else {
-                const int o = static_cast<int>(reinterpret_cast<uintptr_t>(rs) & 7);
-                if (pc * 8 < o + BB) cp_async8(dst, rs - o + pc * 8, pol_w);
-            }
-        }
-    };
-    // this thread's B-row pairs of chunk x (loads issued early, used by issue_b)
-    auto b_pairs = [&](const ChunkMeta &x, int (&pr)[BITEMS]) {
-#pragma unroll
-        for (int t = 0; t < BITEMS; t++) {
-            const int n = (tid + t * T) / (KCH / 8);
-            pr[t] = n < x.N ? __ldg(a.pair + x.p0 + n) : -1;
-        }
-    };
-    auto issue_b = [&](const ChunkMeta &x, uint8_t *st, const int (&pr)[BITEMS]) {
-        const int Np = max(16, (x.N + 15) & ~15);
-        uint8_t *sb = st + stage_w;
-#pragma unroll
-        for (int t = 0; t < BITEMS; t++) {
-            const int i = tid + t * T, n = i / (KCH / 8), kp = i - n * (KCH / 8);
-            if (n >= Np) continue;
-            uint8_t *dst = sb + kmaj_off(n, kp * 8, Npm);
-            if (pr[t] >= 0) {
-                const int row = g.by_token ? pr[t] / a.k : pr[t];
-                cp_async16(dst, g.bsrc + static_cast<size_t>(row) * g.K + static_cast<size_t>(x.kc) * KCH + kp * 8,
-                           pol_b);
-            } else {
-                *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    // bounded wait; false once any role of the CTA gave up
+    auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {
+        if (mbar_try_wait(bar, parity)) return true;
+        const long long t0 = clock64();
+        while (true) {
+            if (mbar_try_wait_suspend(bar, parity)) return true;
+            if (*reinterpret_cast<volatile int *>(&s_abort)) return false;
+            if (clock64() - t0 > kSpinCycles) {
+                atomicExch(a.err, kErrWaitFull);
+                *reinterpret_cast<volatile int *>(&s_abort) = 1;
+                return false;
             }
         }
     };
 
-    // prologue: chunks 0 .. R - 2, one group each
-    for (int q = 0; q < R - 1; q++) {
-        if (q < Q) {
-            const ChunkMeta x = meta_of(q);
-            uint8_t *st = stages + (q % R) * stage_bytes;
-            int pr[BITEMS];
-            b_pairs(x, pr);
-            issue_w(x, st);
-            issue_b(x, st, pr);
-            if (tid == 0) meta[q % R] = x;
+    if (warp < RL::kProd) {
+        // ---------------- copies: chunk q into stage q % R once its MMAs are done
+        const uint64_t pol_w = l2_evict_first(), pol_b = l2_evict_last();
+        int cu, ct, cpc;
+        unit_of(0, cu, ct, cpc);
+        int N = __ldg(a.cnt + cu);
+        uint32_t sel = __ldg(a.src_sel + cu);
+        const uint8_t *s0 = a.srcs[3 * cu + g.mat0], *s1 = a.srcs[3 * cu + g.mat0 + (NM - 1)];
+        for (int q = 0; q < Q; q++) {
+            const int ui = q / CPU, kc = cpc * CPU + (q - ui * CPU);
+            const bool unit_end = q - ui * CPU == CPU - 1;
+            int u = cu, tile = ct, piece = cpc, nN = N;
+            uint32_t nsel = sel;
+            const uint8_t *ns0 = s0, *ns1 = s1;
+            if (unit_end && ui + 1 < my_units) {   // the next unit's tables, loaded early
+                unit_of(ui + 1, u, tile, piece);
+                nN = __ldg(a.cnt + u);
+                nsel = __ldg(a.src_sel + u);
+                ns0 = a.srcs[3 * u + g.mat0];
+                ns1 = a.srcs[3 * u + g.mat0 + (NM - 1)];
+            }
+            const int st_i = q % R, use = q / R;
+            const int Np = max(16, (N + 15) & ~15);
+            if (use > 0 && !wait(&bars.empty[st_i], static_cast<uint32_t>((use - 1) & 1))) break;
+            uint8_t *st = stages + st_i * stage_bytes;
+            const __half *pan = g.panel + static_cast<size_t>(cu) * Npm * g.K + static_cast<size_t>(kc) * Np * 256;
+            if constexpr (RL::kTma) {
+                // one tensor copy per matrix: the chunk's 128 rows x BB bytes; one bulk copy for the panel
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&bars.full[st_i], static_cast<uint32_t>(NM * 128 * BB + Np * 512));
+                    const int kind = static_cast<int>(sel >> 28), slot = static_cast<int>(sel & 0x0FFFFFFFu);
+#pragma unroll
+                    for (int mm = 0; mm < NM; mm++)
+                        tma_load3d(st + mm * 128 * RSB, &tm.m[mm][kind], kc * BB, ct * 128, slot, &bars.full[st_i], pol_w);
+                    bulk_g2s_hint(st + stage_w, pan, static_cast<uint32_t>(Np * 512), &bars.full[st_i], pol_b);
+                }
+            } else {
+                // cp.async from each row's 16-byte aligned window of the chunk, then the panel
+                const int pt = tid;   // 0 .. 32 * kProd - 1
+                const size_t at = static_cast<size_t>(ct) * 128 * g.rb + static_cast<size_t>(kc) * BB;
+                constexpr int PCS = q_win(QT) / 16;
+                for (int i = pt; i < NM * 128 * PCS; i += 32 * RL::kProd) {
+                    const int rr = i / PCS, pc = i - rr * PCS;
+                    const uint8_t *rs = ((rr >> 7) ? s1 : s0) + at + static_cast<size_t>(rr & 127) * g.rb;
+                    cp_async16(st + rr * RSB + pc * 16, rs - (reinterpret_cast<uintptr_t>(rs) & 15) + pc * 16, pol_w);
+                }
+                for (int i = pt; i < Np * 32; i += 32 * RL::kProd)
+                    cp_async16(st + stage_w + i * 16, reinterpret_cast<const uint8_t *>(pan) + i * 16, pol_b);
+                cp_async_arrive(&bars.full[st_i]);
+            }
+            if (unit_end && ui + 1 < my_units) {
+                N = nN;
+                sel = nsel;
+                s0 = ns0;
+                s1 = ns1;
+                cu = u;
+                ct = tile;
+                cpc = piece;
+            }
         }
-        cp_async_commit();
-    }
-    bool ok = true;
-    int gs = 0;   // slices issued so far
-    // dequantisation: thread -> (matrix, row, half of the 64-wide slice)
-    const int dm = (tid >> 7) % NM, dr = tid & 127, dh = tid / (128 * NM);
-    for (int q = 0; q < Q; q++) {
-        cp_async_wait(R - 2);
-        __syncthreads();
-        const ChunkMeta x = meta[q % R];
-        // the chunk R - 1 ahead: its tables now, its copies from slice 1 on
-        const int qn = q + R - 1;
-        const bool have_n = qn < Q;
-        ChunkMeta xn{};
-        if (have_n) xn = meta_of(qn);
-        int prn[BITEMS];
-        const int Np = max(16, (x.N + 15) & ~15);
-        const uint8_t *st = stages + (q % R) * stage_bytes;
-        uint8_t *stn = stages + (qn % R) * stage_bytes;
-        const uint8_t *drow = st + (dm * 128 + dr) * RSB;
-        int o = 0;
-        if constexpr (CPB == 8)
-            o = static_cast<int>((reinterpret_cast<uintptr_t>(dm ? x.src1 : x.src0) + static_cast<size_t>(dr) * g.rb +
-                                  static_cast<size_t>(x.kc) * BB) & 7);
-        const uint32_t sB = smem_addr(st + stage_w);
-#pragma unroll 1
-        for (int j = 0; j < SLICES; j++, gs++) {
-            const int slot = gs & 1;
-            // the slot's previous MMAs (slice gs - 2, and all before it) done
-            if (gs >= 2 && ok) ok = mbar_wait(&bar[slot], static_cast<uint32_t>(((gs >> 1) - 1) & 1), a.err, kErrWaitFull);
-            if (j == 1 && have_n) {   // into chunk q - 1's stage: its MMAs are done
-                issue_w(xn, stn);
-                b_pairs(xn, prn);
-                if (tid == 0) meta[qn % R] = xn;
+        if constexpr (!RL::kTma) asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp < RL::kMma) {
+        // ---------------- dequantisation: group grp takes the slices of its parity;
+        // thread -> (matrix, row): the row's whole 64-wide slice
+        const int dt = tid - 32 * RL::kProd;
+        const int grp = dt / (128 * NM), idx = dt - grp * 128 * NM;
+        const int m = idx >> 7, r = idx & 127;
+        bool live = true;
+        for (int q = 0; q < Q && live; q++) {
+            const int st_i = q % R;
+            if (!wait(&bars.full[st_i], static_cast<uint32_t>((q / R) & 1))) break;
+            __syncwarp();
+            const uint8_t *row = stages + st_i * stage_bytes + (m * 128 + r) * RSB;
+            int o = 0;
+            if constexpr (!RL::kTma) {   // where the chunk starts in its 16-byte window (slabs are 16-byte aligned)
+                int u, tile, piece;
+                const int ui = q / CPU;
+                unit_of(ui, u, tile, piece);
+                const int kc = piece * CPU + (q - ui * CPU);
+                o = static_cast<int>((static_cast<size_t>(tile * 128 + r) * g.rb + static_cast<size_t>(kc) * BB) & 15);
             }
-            if (j == JB) {
-                if (have_n) issue_b(xn, stn, prn);
-                cp_async_commit();
+            auto slice = [&](auto jc) {
+                constexpr int J = decltype(jc)::value;
+                const int gsl = 4 * q + J, slot = gsl % NS, use = gsl / NS;
+                if (use > 0 && !wait(&bars.aempty[slot], static_cast<uint32_t>((use - 1) & 1))) {
+                    live = false;
+                    return;
+                }
+                __syncwarp();
+                uint32_t o0[16], o1[16];
+                deq_run<QT, J, 0>(row, o, o0);
+                deq_run<QT, J, 1>(row, o, o1);
+                uint8_t *sA = slots + slot * ASLOT + m * (128 * 64 * 2);
+                store_run(sA, r, 0, o0);
+                store_run(sA, r, 32, o1);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars.afull[slot]);
+            };
+            if (grp == 0) {
+                slice(std::integral_constant<int, 0>{});
+                if (live) slice(std::integral_constant<int, 2>{});
+            } else {
+                slice(std::integral_constant<int, 1>{});
+                if (live) slice(std::integral_constant<int, 3>{});
             }
-            deq32<QT>(drow, o, 64 * j + 32 * dh, slots + slot * ASLOT + dm * (128 * 64 * 2), dr, 32 * dh);
-            fence_async_smem();
-            __syncthreads();
-            if (tid == 0) {
+        }
+    } else if (warp == RL::kMma) {
+        // ---------------- one thread issues the MMAs
+        if (lane == 0) {
+            int gsl = 0;
+            bool live = true;
+            for (int ui = 0; ui < my_units && live; ui++) {
+                int u, tile, piece;
+                unit_of(ui, u, tile, piece);
+                const int N = __ldg(a.cnt + u), Np = max(16, (N + 15) & ~15);
+                const int ab = ui & 1;
+                if (ui >= 2 && !wait(&bars.acce[ab], static_cast<uint32_t>(((ui >> 1) - 1) & 1))) break;
                 tc_fence_after();
+                const uint32_t dacc = tmem + static_cast<uint32_t>(ab * acc_cols);
                 const uint32_t idesc = umma_idesc_f16(128, Np);
-                const uint32_t sA = smem_addr(slots + slot * ASLOT);
-#pragma unroll
-                for (int m = 0; m < NM; m++)
-#pragma unroll
-                    for (int kk = 0; kk < 4; kk++) {
-                        const uint64_t da = umma_desc(sA + m * (128 * 64 * 2) + kk * 2 * 2048, 2048, 128);
-                        const uint64_t db = umma_desc(sB + (j * 8 + kk * 2) * Npm * 16, Npm * 16, 128);
-                        umma_f16(tmem + m * Npm, da, db, idesc, (x.first && j == 0 && kk == 0) ? 0u : 1u);
+                for (int c = 0; c < CPU && live; c++) {
+                    const int q = ui * CPU + c, st_i = q % R;
+                    if (!wait(&bars.full[st_i], static_cast<uint32_t>((q / R) & 1))) {
+                        live = false;
+                        break;
                     }
-                umma_commit(&bar[slot]);
-            }
-        }
-        if (!x.last) continue;
-        // ---- the unit's accumulator out
-        {
-            const int lg = gs - 1;
-            if (ok) ok = mbar_wait(&bar[lg & 1], static_cast<uint32_t>((lg >> 1) & 1), a.err, kErrWaitFull);
-        }
-        // the lanes of a warp may leave the (suspending) wait at different
-        // times: reconverge before the .sync.aligned TMEM loads
-        __syncwarp();
-        tc_fence_after();
-        const int N = x.N, p0 = x.p0;
-        const int row = x.tile * 128 + 32 * (warp & 3) + lane;   // TMEM lane = weight row
-        const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-        for (int c = (warp >> 2) * 8; c < Np; c += (T / 128) * 8) {
-            float v0[8], v1[8];
-            tmem_ld8(tmem + lane_base + c, v0);
-            if constexpr (NM == 2) tmem_ld8(tmem + lane_base + Npm + c, v1);
-#pragma unroll
-            for (int jj = 0; jj < 8; jj++) {
-                const int n = c + jj;
-                if (n >= N) continue;
-                const int p = __ldg(a.pair + p0 + n);
-                if constexpr (NM == 2) {
-                    if (S == 1) {
-                        // swiglu split (ops2.rs:305-308): g / (1 + exp(-g)) * u
-                        const float hv = ok ? v0[jj] / (1.0f + expf(-v0[jj])) * v1[jj] : 0.f;
-                        a.h[static_cast<size_t>(p) * g.M + kperm(row)] = __float2half_rn(hv);
-                    } else {
-                        const size_t at = (static_cast<size_t>(x.piece) * P + p) * g.M + row;
-                        g.part0[at] = ok ? v0[jj] : 0.f;
-                        g.part1[at] = ok ? v1[jj] : 0.f;
-                    }
-                } else {
-                    g.part0[(static_cast<size_t>(x.piece) * P + p) * g.M + row] = ok ? v0[jj] : 0.f;
-                }
-            }
-        }
-        tc_fence_before();
-        if constexpr (NM == 2) {
-            if (S > 1) {   // the item's last piece sums the pieces in order
-                __syncthreads();   // every partial of this piece stored
-                if (tid == 0) {
-                    __threadfence();
-                    s_fin = atomicAdd(&a.item_cnt[x.u * tiles + x.tile], 1) == S - 1;
-                    __threadfence();
-                }
-                __syncthreads();
-                if (s_fin) {
-                    for (int i = tid; i < 128 * N; i += T) {
-                        const int n = i >> 7, rr = x.tile * 128 + (i & 127);
-                        const int p = __ldg(a.pair + p0 + n);
-                        float gsum = 0.f, usum = 0.f;
-                        for (int s = 0; s < S; s++) {
-                            const size_t at = (static_cast<size_t>(s) * P + p) * g.M + rr;
-                            gsum += __ldcg(g.part0 + at);
-                            usum += __ldcg(g.part1 + at);
+                    fence_async_smem();   // the copied B rows, seen by the tensor core
+                    const uint32_t sB = smem_addr(stages + st_i * stage_bytes + stage_w);
+                    for (int j = 0; j < 4; j++, gsl++) {
+                        const int slot = gsl % NS;
+                        if (!wait(&bars.afull[slot], static_cast<uint32_t>((gsl / NS) & 1))) {
+                            live = false;
+                            break;
                         }
-                        a.h[static_cast<size_t>(p) * g.M + kperm(rr)] =
-                            __float2half_rn(gsum / (1.0f + expf(-gsum)) * usum);
+                        tc_fence_after();
+                        const uint32_t sA = smem_addr(slots + slot * ASLOT);
+#pragma unroll
+                        for (int mm = 0; mm < NM; mm++)
+#pragma unroll
+                            for (int kk = 0; kk < 4; kk++) {
+                                const uint64_t da = umma_desc(sA + mm * (128 * 64 * 2) + kk * 2 * 2048, 2048, 128);
+                                const uint64_t db = umma_desc(sB + (j * 8 + kk * 2) * Np * 16, Np * 16, 128);
+                                umma_f16(dacc + mm * Npm, da, db, idesc, (c == 0 && j == 0 && kk == 0) ? 0u : 1u);
+                            }
+                        umma_commit(&bars.aempty[slot]);
                     }
+                    if (live) umma_commit(&bars.empty[st_i]);
+                }
+                if (live) umma_commit(&bars.accf[ab]);
+            }
+            // every MMA this thread issued has completed before TMEM is freed
+            umma_commit(&bars.drain);
+            const long long t0 = clock64();
+            while (!mbar_try_wait(&bars.drain, 0u) && clock64() - t0 < kSpinCycles) {
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: TMEM lane quarter ew = warp mod 4, row = 32 ew + lane
+        const int ew = warp & 3, et = tid - 32 * RL::kEpi0;
+        const uint32_t lane_base = static_cast<uint32_t>(32 * ew) << 16;
+        for (int ui = 0; ui < my_units; ui++) {
+            int u, tile, piece;
+            unit_of(ui, u, tile, piece);
+            const int N = __ldg(a.cnt + u), p0 = __ldg(a.off + u), Np = max(16, (N + 15) & ~15);
+            const int pr0 = lane < N ? __ldg(a.pair + p0 + lane) : 0;
+            const int pr1 = lane + 32 < N ? __ldg(a.pair + p0 + 32 + lane) : 0;
+            const int ab = ui & 1;
+            const bool ok = epi_all(wait(&bars.accf[ab], static_cast<uint32_t>((ui >> 1) & 1)));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t dacc = tmem + static_cast<uint32_t>(ab * acc_cols) + lane_base;
+            const int row = tile * 128 + 32 * ew + lane;
+            const size_t hpan = static_cast<size_t>(u) * Npm * g.M;   // gate/up: this expert's down panel
+            for (int c = 0; c < Np; c += 8) {
+                float v0[8], v1[8];
+                tmem_ld8(dacc + c, v0);
+                if constexpr (NM == 2) tmem_ld8(dacc + Npm + c, v1);
+#pragma unroll
+                for (int jj = 0; jj < 8; jj++) {
+                    const int n = c + jj;
+                    const int p = __shfl_sync(0xffffffffu, n < 32 ? pr0 : pr1, n & 31);
+                    if (n >= N) continue;
+                    if constexpr (NM == 2) {
+                        if (S == 1) {
+                            // swiglu split (ops2.rs:305-308): g / (1 + exp(-g)) * u
+                            const float hv = v0[jj] / (1.0f + expf(-v0[jj])) * v1[jj];
+                            a.panel_h[hpan + static_cast<size_t>(row >> 8) * Np * 256 +
+                                      kmaj_off(n, kperm(row & 255), Np) / 2] = __float2half_rn(hv);
+                        } else {
+                            const size_t at = (static_cast<size_t>(piece) * P + p) * g.M + row;
+                            g.part0[at] = v0[jj];
+                            g.part1[at] = v1[jj];
+                        }
+                    } else {
+                        g.part0[(static_cast<size_t>(piece) * P + p) * g.M + row] = v0[jj];
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.acce[ab]);
+            if constexpr (NM == 2) {
+                if (S > 1) {   // the item's last piece sums the pieces in piece order
+                    epi_bar_sync();   // every partial of this piece stored
+                    if (et == 0) {
+                        __threadfence();
+                        s_fin = atomicAdd(&a.item_cnt[u * tiles + tile], 1) == S - 1;
+                        __threadfence();
+                    }
+                    epi_bar_sync();
+                    if (s_fin) {
+                        for (int i = et; i < 128 * N; i += 32 * kEpiWarps) {
+                            const int n = i >> 7, rr = tile * 128 + (i & 127);
+                            const int p = __ldg(a.pair + p0 + n);
+                            const size_t hat = hpan + static_cast<size_t>(rr >> 8) * Np * 256 + kmaj_off(n, kperm(rr & 255), Np) / 2;
+                            float gsum = 0.f, usum = 0.f;
+                            for (int sp = 0; sp < S; sp++) {
+                                const size_t at = (static_cast<size_t>(sp) * P + p) * g.M + rr;
+                                gsum += __ldcg(g.part0 + at);
+                                usum += __ldcg(g.part1 + at);
+                            }
+                            a.panel_h[hat] = __float2half_rn(gsum / (1.0f + expf(-gsum)) * usum);
+                        }
+                    }
+                    epi_bar_sync();   // s_fin read by all before the next unit writes it
                 }
             }
         }
@@ -788,64 +919,65 @@ int batch_split_max(int K) { return K / 128 < 8 ? K / 128 : 8; }
 constexpr int kSmemCap = 232448 - 1024;   // 227 KB per CTA, less the static barriers
 
 template <int QT, int NM>
-static cudaError_t launch_bgemm(const BatchArgs &a, GemmSide g, cudaStream_t st) {
-    constexpr int KCH = q_kch(QT), RSB = q_rsb(QT);
-    const int stage_bytes = NM * 128 * RSB + g.npm * KCH * 2;
-    const int slots = 2 * NM * 128 * 64 * 2;
-    int R = (kSmemCap - slots) / stage_bytes;
-    if (R > 4) R = 4;
+static cudaError_t launch_bgemm(const BatchArgs &a, GemmSide g, const TmaSet &tm, cudaStream_t st) {
+    // four A slots when two stages still fit beside them, else two
+    const int stage_bytes = NM * 128 * q_rsb(QT) + g.npm * 512;
+    const int slot_bytes = NM * 128 * 64 * 2;
+    g.nslot = (kSmemCap - 4 * slot_bytes) / stage_bytes >= 2 ? 4 : 2;
+    int R = (kSmemCap - g.nslot * slot_bytes) / stage_bytes;
+    if (R > kMaxStages) R = kMaxStages;
     if (R < 2) return cudaErrorInvalidValue;
     g.stages = R;
-    const int smem = slots + R * stage_bytes;
+    const int smem = g.nslot * slot_bytes + R * stage_bytes;
     cudaError_t e = cudaFuncSetAttribute(k_bgemm<QT, NM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    k_bgemm<QT, NM><<<a.sms, 256 * NM, smem, st>>>(a, g);
+    k_bgemm<QT, NM><<<a.sms, GemmRoles<QT, NM>::kThreads, smem, st>>>(a, g, tm);
     return cudaGetLastError();
 }
 
 template <int NM>
-static cudaError_t launch_bgemm_q(int qt, const BatchArgs &a, const GemmSide &g, cudaStream_t st) {
+static cudaError_t launch_bgemm_q(int qt, const BatchArgs &a, const GemmSide &g, const TmaSet &tm, cudaStream_t st) {
     switch (qt) {
-    case STYX_Q4_K: return launch_bgemm<STYX_Q4_K, NM>(a, g, st);
-    case STYX_Q5_K: return launch_bgemm<STYX_Q5_K, NM>(a, g, st);
-    case STYX_Q6_K: return launch_bgemm<STYX_Q6_K, NM>(a, g, st);
+    case STYX_Q4_K: return launch_bgemm<STYX_Q4_K, NM>(a, g, tm, st);
+    case STYX_Q5_K: return launch_bgemm<STYX_Q5_K, NM>(a, g, tm, st);
+    case STYX_Q6_K: return launch_bgemm<STYX_Q6_K, NM>(a, g, tm, st);
     default: return cudaErrorInvalidValue;
     }
 }
 
-cudaError_t launch_batch(const BatchArgs &a, int qg, int qd, cudaStream_t st) {
+cudaError_t launch_batch(const BatchArgs &a, int qg, int qd, const TmaSet &tgu, const TmaSet &tdn, cudaStream_t st) {
     k_batch_logits<<<dim3(a.B, (a.E + kLogitRows - 1) / kLogitRows), kLogitThreads, static_cast<size_t>(a.H) * 4, st>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     k_batch_lists<<<1, kListThreads, 0, st>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const int npm = a.B >= 64 ? 64 : ((a.B + 15) & ~15);
+    k_batch_panels<<<dim3(a.E, a.H / 256), 256, 0, st>>>(a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const int npm = a.npm;
     GemmSide gu{};
     gu.K = a.H;
     gu.M = a.F;
     gu.rb = a.rb_g;
     gu.mat0 = 0;
-    gu.bsrc = a.xh;
-    gu.by_token = 1;
+    gu.panel = a.panel_x;
     gu.part0 = a.gpart;
     gu.part1 = a.upart;
     gu.npm = npm;
     gu.smax = batch_split_max(a.H);
     gu.split_out = a.split_d + 1;
-    if ((e = launch_bgemm_q<2>(qg, a, gu, st)) != cudaSuccess) return e;
+    if ((e = launch_bgemm_q<2>(qg, a, gu, tgu, st)) != cudaSuccess) return e;
     GemmSide dn{};
     dn.K = a.F;
     dn.M = a.H;
     dn.rb = a.rb_d;
     dn.mat0 = 2;
-    dn.bsrc = a.h;
-    dn.by_token = 0;
+    dn.panel = a.panel_h;
     dn.part0 = a.d;
     dn.part1 = nullptr;
     dn.npm = npm;
     dn.smax = batch_split_max(a.F);
     dn.split_out = a.split_d;
-    if ((e = launch_bgemm_q<1>(qd, a, dn, st)) != cudaSuccess) return e;
+    if ((e = launch_bgemm_q<1>(qd, a, dn, tdn, st)) != cudaSuccess) return e;
     k_batch_combine<<<dim3((a.H + 255) / 256, a.B), 256, 0, st>>>(a);
     return cudaGetLastError();
 }

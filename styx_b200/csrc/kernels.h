@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -127,7 +128,9 @@ struct BatchArgs {
     int *pair;                   // workspace [B * k]: pairs b * k + s grouped by expert
     int *pv;                     // workspace [B * k]: the pair has an expert here
     const uint8_t **srcs;        // workspace [E][3]: gate, up, down slab of each used expert
-    __half *h;                   // workspace [B * k][F]: SiLU(g) * u per pair, f16 (element order 0,2,1,3 per 4)
+    __half *panel_x;             // workspace [E][npm][H]: per used expert its tokens' x_norm, B-panel layout
+    __half *panel_h;             // workspace [E][npm][F]: per used expert its pairs' SiLU(g) * u, B-panel layout
+    int npm;                     // rows of a panel at most: n_tokens rounded up to 16
     float *d;                    // workspace [smax_d][B * k][H]: down output per pair, per K piece
     float *logits;               // workspace [B][E]
     float *gpart, *upart;        // workspace [smax_g][B * k][F]: gate / up per K piece
@@ -135,12 +138,20 @@ struct BatchArgs {
     int n_item_cnt;
     int *split_d;                // workspace [2]: the K pieces of down (0) and gate/up (1)
     int sms;                     // CTAs of a GEMM launch: the SM count
+    uint32_t *src_sel;           // workspace [E]: per used expert its source (kind << 28 | slot; 0 hot, 1 arena, 2 full)
     int quiet;                   // a slot with no source here is not an error
     int *err;
 };
+// TMA descriptors of the expert matrices of one GEMM side (q4_K / q5_K: row
+// chunks on 16-byte boundaries): per matrix and source (hot, arena, full) a
+// 3-D map {row bytes, rows, slabs} with a box of one chunk x 128 rows
+struct TmaSet {
+    CUtensorMap m[2][3];
+};
 int batch_split_max(int K);
 bool batch_supported(int qg, int qd);
-cudaError_t launch_batch(const BatchArgs &a, int qg, int qd, cudaStream_t st);
+bool batch_uses_tma(int qt);
+cudaError_t launch_batch(const BatchArgs &a, int qg, int qd, const TmaSet &gu, const TmaSet &dn, cudaStream_t st);
 
 // How a single-kernel layer connects to the layers before and after it (see
 // moe_fused.cu): chain flags and the x exchange words.
