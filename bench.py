@@ -539,7 +539,12 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
               "the block's compute", "nccl_ranks": world}
     bytes_tok = decode_bytes_per_token(L, ctx)
     step_achieved = bytes_tok / (ms * 1e-3) / 1e9
-    launches = 1 + L * ((1 if attn_path == 1 else 8) + (1 if moe_path == 1 else 3) + (1 if world > 1 else 0)) + 3
+    one_attn, one_moe = attn_path in (1, 3), moe_path in (1, 6)
+    launches = 1 + L * ((1 if one_attn else 8) + (1 if one_moe else 3) + (1 if world > 1 else 0)) + 3
+    attn_form = {1: "one cooperative kernel per layer", 3: "one launch of thread-block clusters per layer "
+                 "(a cluster per kv head)"}.get(attn_path, "eight kernels per layer")
+    moe_form = {1: "single cooperative kernel per layer", 6: "one launch of thread-block clusters per layer "
+                "(a cluster per selected slot)"}.get(moe_path, "three kernels per layer")
     line = {
         "metric": METRIC, "value": 1e3 / ms, "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -550,8 +555,7 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
         "kernels": {"launch": ("CUDA graph" if world == 1 else "eager (NCCL all-reduces between the kernels)") +
                               (", cooperative" if args.shared_device else
                                ", plain single kernels (STYX_OPT_EXCLUSIVE: the bench owns its GPU)"),
-                    "attention": "one kernel per layer" if attn_path == 1 else "eight kernels per layer",
-                    "moe": "single kernel per layer" if moe_path == 1 else "three kernels per layer"},
+                    "attention": attn_form, "moe": moe_form},
         "e2e": {"value": n_e2e / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                 "wall_s": t_wall, "form": "greedy chain: each step's pick read back and fed in as the next token"},
         "gpu_launches": args.steps * launches,
@@ -991,9 +995,10 @@ def main() -> int:
     path = blk.ctx.last_moe_path()
     kernel_path = {1: "single cooperative kernel per MoE block", 2: "three kernels per MoE block",
                    4: "single cooperative kernel running every MoE layer of a token per launch",
-                   5: "single cooperative kernel per MoE block, launches chained (x passed as tagged words)"
+                   5: "single cooperative kernel per MoE block, launches chained (x passed as tagged words)",
+                   6: "one launch of thread-block clusters per MoE block (a cluster per selected slot)"
                    }.get(path, "unknown")
-    launches_per_token = {1: L, 2: 3 * L, 4: -(-L // 80), 5: L}.get(path, 0)
+    launches_per_token = {1: L, 2: 3 * L, 4: -(-L // 80), 5: L, 6: L}.get(path, 0)
 
     def barrier():
         if pg:

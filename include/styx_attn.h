@@ -141,11 +141,12 @@ int styx_attn_block_workspace_init(styx_ctx *ctx, styx_stream stream, void *work
 /* x += o(attention(rope(norm(q, k, v of rms_norm(x) * attn_norm)))) for the
  * token at position `pos` (n_t = pos + 1 cache rows are read; row pos is
  * written first).  pos_dev is the same position as a device int32 (the
- * reference's bpos buffer).  One cooperative kernel when the shape fits
+ * reference's bpos buffer).  One cooperative kernel or one launch of
+ * thread-block clusters (one cluster per kv head) when the shape fits
  * (head_dim 128, n_embd <= 2048, q/k/o of one format, STYX_OPT_ATTN_KERNELS;
- * it reads the position from `pos`), else seven launches, stream-ordered
- * (the o GEMV adds into x).  The workspace keeps launch counters: initialise
- * it once with styx_attn_block_workspace_init. */
+ * both read the position from `pos`), else seven launches, stream-ordered
+ * (the o GEMV adds into x).  The workspace keeps counters: initialise it
+ * once with styx_attn_block_workspace_init. */
 int styx_attn_block(styx_ctx *ctx, styx_stream stream, const styx_attn_dims *dims, const styx_attn_layer *lw,
                     float *x, int pos, const int32_t *pos_dev, float *kcache, float *vcache, int n_ctx,
                     void *workspace, uint64_t workspace_bytes);

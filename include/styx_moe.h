@@ -84,16 +84,21 @@ int styx_device_info(styx_ctx *ctx, int *sm_count, char *name, int name_len);
  * styx_moe_workspace_init on the workspaces in use. */
 int styx_check_device_error(styx_ctx *ctx, styx_stream stream);
 
-/* Options.  STYX_OPT_MOE_KERNELS selects how styx_moe_block runs: 0 = auto
- * (the single cooperative kernel when the shape and formats fit, else three
+/* Options.  STYX_OPT_MOE_KERNELS selects how styx_moe_block (and
+ * styx_moe_block_ep) runs: 0 = auto (the cluster form when the shape and
+ * formats fit, else the single cooperative kernel when they fit, else three
  * kernels), 1 = single kernel only (STYX_EUNSUPPORTED if it does not fit),
- * 2 = three kernels.  STYX_OPT_MOE_LAST_PATH (read only) = 1 (single
- * kernel), 2 (three kernels), 3 (host-read form: some full tensor is in
- * STYX_MEM_HOST memory), 4 (single kernel, several layers per launch,
- * styx_moe_blocks) or 5 (single kernel, one chained launch per layer,
- * styx_moe_blocks), the form the last styx_moe_block[s] call used.  STYX_OPT_TRACE = 1 makes the single
- * kernel record 32 clock64 stamps per CTA at its phase boundaries into the
- * workspace (styx_moe_workspace_view 4: int64[CTAs][32]).
+ * 2 = three kernels, 3 = cluster form only (STYX_EUNSUPPORTED if it does not
+ * fit).  The cluster form is one launch of thread-block clusters, one
+ * cluster per selected slot; it needs no co-resident grid.
+ * STYX_OPT_MOE_LAST_PATH (read only) = 1 (single kernel), 2 (three kernels),
+ * 3 (host-read form: some full tensor is in STYX_MEM_HOST memory), 4 (single
+ * kernel, several layers per launch, styx_moe_blocks), 5 (single kernel, one
+ * chained launch per layer, styx_moe_blocks) or 6 (cluster form), the form
+ * the last styx_moe_block[s] call used.  STYX_OPT_TRACE = 1 makes the single
+ * kernel and the cluster form record 32 clock64 stamps per CTA at their
+ * phase boundaries into the workspace (styx_moe_workspace_view 4:
+ * int64[CTAs][32]).
  * STYX_OPT_MOE_LAYERS picks how styx_moe_blocks runs single-kernel layers:
  * 0 (default) one independent styx_moe_block call per layer, 1 up to 80
  * layers in one persistent launch (its layer loop spills registers), 2 one
@@ -114,12 +119,19 @@ int styx_check_device_error(styx_ctx *ctx, styx_stream stream);
  * promise costs no hang: a wait that cannot finish gives up after about a
  * second with STYX_ETIMEOUT. */
 #define STYX_OPT_EXCLUSIVE 5
-/* STYX_OPT_ATTN_KERNELS: styx_attn_block as one cooperative kernel when the
- * shape fits (0, default), always (1: STYX_EUNSUPPORTED otherwise) or as
- * seven kernels (2).  STYX_OPT_ATTN_LAST_PATH (read only): 1 (one kernel) or
- * 2 (seven), the form the last styx_attn_block used. */
+/* STYX_OPT_ATTN_KERNELS: styx_attn_block as one cooperative kernel, else as
+ * one launch of thread-block clusters (one cluster per kv head), when the
+ * shape fits (0, default); the cooperative kernel always (1:
+ * STYX_EUNSUPPORTED otherwise); seven kernels (2); the cluster form always
+ * (3: STYX_EUNSUPPORTED otherwise).  STYX_OPT_ATTN_LAST_PATH (read only): 1
+ * (one cooperative kernel), 2 (seven) or 3 (cluster form), the form the last
+ * styx_attn_block used. */
 #define STYX_OPT_ATTN_KERNELS 6
 #define STYX_OPT_ATTN_LAST_PATH 7
+/* STYX_OPT_MOE_LAST_CLUSTER (read only): CTAs per cluster of the last
+ * cluster-form launch (16 when the device holds k such clusters at once, else
+ * the largest smaller size that it does). */
+#define STYX_OPT_MOE_LAST_CLUSTER 8
 int styx_set_option(styx_ctx *ctx, int option, int64_t value);
 int styx_get_option(styx_ctx *ctx, int option, int64_t *value);
 

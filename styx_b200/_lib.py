@@ -25,8 +25,8 @@ SKIP = 0xFFFFFFFF
 IDS_PER_LAYER = 64
 MEM_DEVICE, MEM_HOST = 0, 1
 OPT_MOE_KERNELS, OPT_MOE_LAST_PATH, OPT_TRACE, OPT_MOE_LAYERS, OPT_EXCLUSIVE = 1, 2, 3, 4, 5
-OPT_ATTN_KERNELS, OPT_ATTN_LAST_PATH = 6, 7
-MOE_AUTO, MOE_FUSED, MOE_SPLIT = 0, 1, 2
+OPT_ATTN_KERNELS, OPT_ATTN_LAST_PATH, OPT_MOE_LAST_CLUSTER = 6, 7, 8
+MOE_AUTO, MOE_FUSED, MOE_SPLIT, MOE_CLUSTER = 0, 1, 2, 3
 
 
 class StyxError(RuntimeError):

@@ -25,8 +25,8 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
           f"-I{os.path.join(ROOT, 'include')}", "--expt-relaxed-constexpr"]
 # per-source extra flags: the synthetic quantiser must round like the C oracle
 EXTRA = {"synth.cu": ["-fmad=false"]}
-SOURCES = ["moe_kernels.cu", "moe_fused.cu", "batch.cu", "attn.cu", "attn_fused.cu", "synth.cu", "api.cu", "residency.cpp", "gguf.cpp"]
-HEADERS = ["common.cuh", "qdot.cuh", "kernels.h", "moe_common.cuh"]
+SOURCES = ["moe_kernels.cu", "moe_fused.cu", "moe_cluster.cu", "batch.cu", "attn.cu", "attn_fused.cu", "attn_cluster.cu", "synth.cu", "api.cu", "residency.cpp", "gguf.cpp"]
+HEADERS = ["common.cuh", "qdot.cuh", "kernels.h", "moe_common.cuh", "cluster.cuh"]
 
 
 def nvcc() -> str:

@@ -34,6 +34,7 @@ struct styx_ctx {
     int exclusive = 0;      // STYX_OPT_EXCLUSIVE
     int attn_kernels = 0;   // STYX_OPT_ATTN_KERNELS
     int attn_last_path = 0; // STYX_OPT_ATTN_LAST_PATH
+    int last_cluster = 0;   // STYX_OPT_MOE_LAST_CLUSTER
 };
 
 namespace {
@@ -134,7 +135,7 @@ constexpr size_t kTraceCtas = 256;   // phase stamps: styx::kTraceStamps per CTA
 // styx_moe_workspace_init (which also clears the tagged words they guard).
 constexpr size_t kGenOffset = 128;
 struct WsLayout {
-    size_t counter, hcnt, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, d, lgslot, xslot, trace, total;
+    size_t counter, hcnt, xnorm, xd1, xd2, xd3, xscale, logits, weights, h, g, u, d, lgslot, xslot, ccnt, trace, total;
 };
 
 WsLayout ws_layout(const styx_moe_dims &d) {
@@ -161,6 +162,7 @@ WsLayout ws_layout(const styx_moe_dims &d) {
     L.d = take(static_cast<size_t>(d.n_expert_used) * H * 4);   // down outputs of the host-read form
     L.lgslot = take(2 * E * 8);   // two banks of logit words, by launch-tag parity
     L.xslot = take(H * 8);        // x rows passed from one layer to the next
+    L.ccnt = take(styx::kClusterMaxC * styx::kCntStride * 4);   // cluster form: row-block counters
     L.trace = take(kTraceCtas * styx::kTraceStamps * 8);
     L.total = o;
     return L;
@@ -425,7 +427,7 @@ int styx_set_option(styx_ctx *ctx, int option, int64_t value) {
     NEED(ctx, "null ctx");
     switch (option) {
     case STYX_OPT_MOE_KERNELS:
-        NEED(value >= 0 && value <= 2, "STYX_OPT_MOE_KERNELS: 0, 1 or 2");
+        NEED(value >= 0 && value <= 3, "STYX_OPT_MOE_KERNELS: 0, 1, 2 or 3");
         ctx->moe_kernels = static_cast<int>(value);
         return STYX_OK;
     case STYX_OPT_TRACE:
@@ -439,7 +441,7 @@ int styx_set_option(styx_ctx *ctx, int option, int64_t value) {
         ctx->exclusive = value ? 1 : 0;
         return STYX_OK;
     case STYX_OPT_ATTN_KERNELS:
-        NEED(value >= 0 && value <= 2, "STYX_OPT_ATTN_KERNELS: 0, 1 or 2");
+        NEED(value >= 0 && value <= 3, "STYX_OPT_ATTN_KERNELS: 0, 1, 2 or 3");
         ctx->attn_kernels = static_cast<int>(value);
         return STYX_OK;
     default: return fail(STYX_EINVAL, "unknown or read-only option %d", option);
@@ -456,6 +458,7 @@ int styx_get_option(styx_ctx *ctx, int option, int64_t *value) {
     case STYX_OPT_EXCLUSIVE: *value = ctx->exclusive; return STYX_OK;
     case STYX_OPT_ATTN_KERNELS: *value = ctx->attn_kernels; return STYX_OK;
     case STYX_OPT_ATTN_LAST_PATH: *value = ctx->attn_last_path; return STYX_OK;
+    case STYX_OPT_MOE_LAST_CLUSTER: *value = ctx->last_cluster; return STYX_OK;
     default: return fail(STYX_EINVAL, "unknown option %d", option);
     }
 }
@@ -1070,6 +1073,131 @@ static void fill_fused(styx::FusedArgs &fa, const styx_ctx *ctx, const styx_moe_
     fa.trace = ctx->trace ? reinterpret_cast<long long *>(ws + L.trace) : nullptr;
 }
 
+// Shared-memory plan of the cluster form for these dims; false if no cluster
+// size fits (the caller then takes the single kernel or three kernels).  The
+// largest cluster (16 CTAs, else 8, 4, 2, 1) whose per-CTA share of slot s's
+// rows fits in shared memory and of which the device holds k at once; with
+// `waves`, failing that, the largest that fits at all (its clusters then run
+// in waves: correct, but slower than the single kernel).  On B200 at most 7
+// clusters of 16 CTAs of ~210 KB are resident at once, so the 30B-A3B layer
+// (k 8, whose rows need 16 CTAs per slot) takes the single kernel in auto.
+static bool plan_cluster(const styx_moe_dims &d, const styx_moe_layer &lw, int sms, bool waves, styx::ClusterArgs &a,
+                         uint32_t &smem) {
+    const int H = d.n_embd, F = d.n_ff, E = d.n_expert, k = d.n_expert_used;
+    const int qg = lw.gate.qtype, qd = lw.down.qtype;
+    if (lw.up.qtype != qg || !styx::cluster_supported(qg, qd)) return false;
+    if (H % 64 || F % 64 || H / 4 > styx::fused_block_threads() || F / 64 > 32 || k > 16 || E > 512) return false;
+    a.units_g = H / 64;
+    a.gs_g = pow2ceil(a.units_g);
+    a.units_d = F / 64;
+    a.gs_d = pow2ceil(a.units_d);
+    a.rb_g = static_cast<int>(row_bytes(qg, H));
+    a.rb_u = static_cast<int>(row_bytes(lw.up.qtype, H));
+    a.rb_d = static_cast<int>(row_bytes(qd, F));
+    const int rpw_g = 32 / a.gs_g;
+    const size_t kLimit = 227 * 1024;
+    styx::ClusterArgs fallback{};
+    uint32_t fallback_smem = 0;
+    for (int C = styx::kClusterMaxC; C >= 1; C >>= 1) {
+        if (k * C > sms) continue;
+        const int ngr = (F + C - 1) / C, ndr = (H + C - 1) / C, nrr = (E + C - 1) / C;
+        // gate/up chunks of about 16 row pairs (at most 8; a multiple of the rows a warp takes at once)
+        int ng = std::min(8, std::max(1, (ngr + 15) / 16));
+        const int chg = ((ngr + ng - 1) / ng + rpw_g - 1) / rpw_g * rpw_g;
+        ng = (ngr + chg - 1) / chg;
+        a.C = C;
+        a.ng = ng;
+        a.chg = chg;
+        a.gu_up_off = static_cast<uint32_t>(a16(static_cast<size_t>(chg) * a.rb_g + 32));
+        a.gu_stride = a.gu_up_off + static_cast<uint32_t>(a16(static_cast<size_t>(chg) * a.rb_u + 32));
+        size_t o = styx::kClusterHeader;
+        a.off_lg = static_cast<uint32_t>(o);   // logits, keys, ranks, remap, pmap
+        o = a128(o + 5 * static_cast<size_t>(E) * 4);
+        a.off_x = static_cast<uint32_t>(o);
+        o = a128(o + static_cast<size_t>(H) * 4);
+        a.off_xd = static_cast<uint32_t>(o);
+        o = a128(o + 3 * static_cast<size_t>(H) + H / 32 * 4);
+        a.off_hf = static_cast<uint32_t>(o);
+        o = a128(o + static_cast<size_t>(F) * 4);
+        a.off_hd = static_cast<uint32_t>(o);
+        o = a128(o + 3 * static_cast<size_t>(F) + F / 32 * 4);
+        a.off_y = static_cast<uint32_t>(o);
+        o = a128(o + static_cast<size_t>(ndr) * 4);
+        a.off_gu = static_cast<uint32_t>(o);
+        o = a128(o + static_cast<size_t>(ng) * a.gu_stride);
+        a.off_dn = static_cast<uint32_t>(o);   // the router rows, then the down rows
+        o += std::max(a16(static_cast<size_t>(ndr) * a.rb_d + 32), static_cast<size_t>(nrr) * H * 4);
+        if (o > kLimit) continue;
+        const int n = styx::cluster_max_active(qg, qd, C, static_cast<uint32_t>(o));
+        if (n >= k) {
+            smem = static_cast<uint32_t>(o);
+            return true;
+        }
+        if (n >= 1 && !fallback_smem) {
+            fallback = a;
+            fallback_smem = static_cast<uint32_t>(o);
+        }
+    }
+    if (!fallback_smem || !waves) return false;
+    a = fallback;
+    smem = fallback_smem;
+    return true;
+}
+
+static void fill_cluster(styx::ClusterArgs &ca, const styx_ctx *ctx, const styx_moe_dims &d,
+                         const styx_moe_layer &lw, float *x, int32_t *ids64, float *wts, uint8_t *ws,
+                         const WsLayout &L) {
+    const int E = d.n_expert;
+    ca.x = x;
+    ca.norm_w = lw.ffn_norm;
+    ca.eps = d.rms_eps;
+    ca.router = lw.router;
+    ca.E = E;
+    ca.H = d.n_embd;
+    ca.F = d.n_ff;
+    ca.k = d.n_expert_used;
+    ca.renorm = d.norm_topk;
+    ca.remap = lw.remap;
+    ca.pmap = lw.pmap;
+    ca.gate = to_src(lw.gate, E);
+    ca.up = to_src(lw.up, E);
+    ca.down = to_src(lw.down, E);
+    ca.ids64 = ids64;
+    ca.weights = wts;
+    ca.logits = reinterpret_cast<float *>(ws + L.logits);
+    ca.xnorm = reinterpret_cast<float *>(ws + L.xnorm);
+    ca.h = reinterpret_cast<float *>(ws + L.h);
+    ca.y = reinterpret_cast<float *>(ws + L.d);
+    ca.cnt = reinterpret_cast<unsigned *>(ws + L.ccnt);
+    ca.err = ctx->d_err;
+    ca.trace = ctx->trace ? reinterpret_cast<long long *>(ws + L.trace) : nullptr;
+    ca.partial = nullptr;
+    ca.quiet = 0;
+}
+
+// The cluster form when it fits and the option allows it: STYX_OK after the
+// launch, 1 when the caller should take another form, or an error.
+static int try_cluster(styx_ctx *ctx, cudaStream_t st, const styx_moe_dims &d, const styx_moe_layer &lw, float *x,
+                       int32_t *ids64, float *wts, uint8_t *ws, const WsLayout &L, float *partial) {
+    if (ctx->moe_kernels != 0 && ctx->moe_kernels != 3) return 1;
+    styx::ClusterArgs ca{};
+    uint32_t smem = 0;
+    const bool fits = al16(lw.ffn_norm) && plan_cluster(d, lw, ctx->sm_count, ctx->moe_kernels == 3, ca, smem);
+    if (!fits) {
+        if (ctx->moe_kernels == 3) return fail(STYX_EUNSUPPORTED, "cluster MoE block does not fit these dims / formats");
+        return 1;
+    }
+    fill_cluster(ca, ctx, d, lw, x, ids64, wts, ws, L);
+    if (partial) {
+        ca.partial = partial;
+        ca.quiet = 1;
+    }
+    CK(styx::launch_cluster(ca, lw.gate.qtype, lw.down.qtype, smem, st));
+    ctx->last_path = 6;
+    ctx->last_cluster = ca.C;
+    return STYX_OK;
+}
+
 // Argument checks shared by the MoE block entry points.
 static int check_block(styx_ctx *ctx, const styx_moe_dims *dims, const styx_moe_layer *lw, int layer, const float *x,
                        const int32_t *ids, void *workspace, uint64_t workspace_bytes, WsLayout &Lout) {
@@ -1116,7 +1244,9 @@ int styx_moe_block(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims,
         return moe_block_host_read(ctx, st, *dims, *lw, x, ids64, wts, ws, L);
     }
 
-    // the single cooperative kernel when the shape fits, else three kernels
+    // the cluster form when the shape fits, else the single cooperative
+    // kernel, else three kernels
+    if ((rc = try_cluster(ctx, st, *dims, *lw, x, ids64, wts, ws, L, nullptr)) <= 0) return rc;
     if (ctx->moe_kernels != 2) {
         styx::FusedArgs fa{};
         uint32_t smem = 0;
@@ -1155,7 +1285,7 @@ int styx_moe_blocks(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims
     styx::FusedArgs plan{};
     uint32_t smem = 0;
     const styx_moe_layer &l0 = layers[0];
-    bool linked = ctx->moe_layers != 0 && n_layers > 1 && ctx->moe_kernels != 2 &&
+    bool linked = ctx->moe_layers != 0 && n_layers > 1 && ctx->moe_kernels != 2 && ctx->moe_kernels != 3 &&
                   !(ctx->trace && ctx->sm_count > static_cast<int>(kTraceCtas));
     for (int i = 0; linked && i < n_layers; i++) {
         const styx_moe_layer &li = layers[i];
@@ -1227,8 +1357,12 @@ int styx_moe_block_ep(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *di
     int32_t *ids64 = ids + static_cast<size_t>(layer) * STYX_IDS_PER_LAYER;
     float *wts = weights_out ? weights_out : reinterpret_cast<float *>(ws + L.weights);
     const cudaStream_t st = S(stream);
-    // the single kernel with its partial-output epilogue when the shape fits
-    if (ctx->moe_kernels != 2 && !full_in_host(lw->gate) && !full_in_host(lw->up) && !full_in_host(lw->down)) {
+    // the cluster form or the single kernel, with their partial-output
+    // epilogues, when the shape fits
+    const bool in_hbm = !full_in_host(lw->gate) && !full_in_host(lw->up) && !full_in_host(lw->down);
+    if (in_hbm && (rc = try_cluster(ctx, st, *dims, *lw, const_cast<float *>(x), ids64, wts, ws, L, partial)) <= 0)
+        return rc;
+    if (ctx->moe_kernels != 2 && ctx->moe_kernels != 3 && in_hbm) {
         styx::FusedArgs fa{};
         uint32_t smem = 0;
         if (al16(lw->ffn_norm) && plan_fused(*dims, *lw, ctx->sm_count, fa, smem)) {
@@ -1666,7 +1800,7 @@ int styx_attn_decode(styx_ctx *ctx, styx_stream stream, const float *q, const fl
 
 namespace {
 struct AttnWs {
-    size_t cnt, xnorm, qkv, att, part, trace, total;
+    size_t cnt, xnorm, qkv, att, part, opart, ccnt, trace, total;
 };
 AttnWs attn_ws(const styx_attn_dims &d) {
     AttnWs w{};
@@ -1687,6 +1821,8 @@ AttnWs attn_ws(const styx_attn_dims &d) {
     uint64_t pb = 0;
     styx_attn_workspace_bytes(d.n_heads, d.head_dim, &pb);
     w.part = take(pb);
+    w.opart = take(static_cast<size_t>(d.n_kv_heads) * H * 4);   // cluster form: each cluster's o rows
+    w.ccnt = take(styx::kClusterMaxC * styx::kCntStride * 4);     // cluster form: row-block counters
     w.trace = take(kTraceCtas * styx::kAttnTraceStamps * 8);   // last: STYX_OPT_TRACE stamps
     w.total = o;
     return w;
@@ -1744,6 +1880,60 @@ bool plan_attn_fused(const styx_attn_dims &d, const styx_attn_layer &lw, int sms
 }
 }  // namespace
 
+namespace {
+// The cluster-form plan (attn_cluster.cu) for these dims / formats at n_t
+// cache rows; false when it does not apply.  One cluster of 16 CTAs per kv
+// head (8, 4, 2 when the device holds fewer of 16 at once); the Wo columns of
+// a cluster's heads are a whole number of blocks on 16-byte boundaries.
+bool plan_attn_cluster(const styx_attn_dims &d, const styx_attn_layer &lw, int sms, int n_t,
+                       styx::AttnClusterArgs &a, uint32_t &smem) {
+    const int H = d.n_embd, hd = d.head_dim, nh = d.n_heads, nkv = d.n_kv_heads;
+    if (hd != 128 || nh % nkv || H % 64 || H > 2048) return false;
+    const int gqa = nh / nkv, nq = gqa * hd;
+    const int qw = lw.wq.qtype, qv = lw.wv.qtype;
+    if (lw.wk.qtype != qw || lw.wo.qtype != qw || !styx::attn_cluster_supported(qw, qv)) return false;
+    if (!units_ok(qw, H) || !units_ok(qv, H) || !units_ok(qw, nq) || nq / 64 > 32) return false;
+    a.rb_q = static_cast<int>(row_bytes(qw, H));
+    a.rb_v = static_cast<int>(row_bytes(qv, H));
+    a.rb_o = static_cast<int>(row_bytes(qw, nh * hd));
+    const long long blk_o = row_bytes(qw, nq);
+    if (blk_o * nkv != a.rb_o || blk_o % 16 || a.rb_o % 16 || !al16(lw.wo.data)) return false;
+    for (int C = styx::kClusterMaxC; C >= 2; C >>= 1) {
+        if (gqa > C || nkv * C > sms) continue;
+        a.C = C;
+        a.tps = (n_t + C - 1) / C;
+        if (a.tps > 512) return false;
+        a.npre = std::min(a.tps, 48);
+        const int nqr = (nq + C - 1) / C, nkr = (hd + C - 1) / C, nor = (H + C - 1) / C;
+        const int hpw = std::max(1, 16 / gqa);
+        size_t o = styx::kAttnClusterHeader;
+        auto take = [&](size_t n) {
+            const size_t r = o;
+            o = a128(o + n);
+            return static_cast<uint32_t>(r);
+        };
+        a.off_x = take(static_cast<size_t>(H) * 4);
+        a.off_dig = take(3 * static_cast<size_t>(H) + H / 32 * 4);
+        a.off_q = take((static_cast<size_t>(nq) + 2 * hd) * 4);
+        a.off_rope = take(hd / 2 * 16);
+        a.off_sc = take((((static_cast<size_t>(a.tps) * gqa + 3) & ~size_t(3)) + 2 * gqa) * 4);
+        a.off_acc = take(static_cast<size_t>(hpw) * gqa * hd * 4);
+        a.off_mrecv = take(static_cast<size_t>(C) * 132 * 4);
+        a.off_att = take(static_cast<size_t>(nq) * 4);
+        a.off_adig = take(3 * static_cast<size_t>(nq) + nq / 32 * 4);
+        a.off_o = take(static_cast<size_t>(nor) * 4);
+        const size_t wqkv = static_cast<size_t>(nqr) * a.rb_q + static_cast<size_t>(nkr) * (a.rb_q + a.rb_v) + 96;
+        a.off_w = take(std::max(wqkv, static_cast<size_t>(nor) * static_cast<size_t>(blk_o)));
+        a.off_kv = take(2 * static_cast<size_t>(a.npre) * hd * 4);
+        if (o > 227 * 1024) continue;
+        if (styx::attn_cluster_max_active(qw, qv, C, static_cast<uint32_t>(o)) < nkv) continue;
+        smem = static_cast<uint32_t>(o);
+        return true;
+    }
+    return false;
+}
+}  // namespace
+
 int styx_attn_block(styx_ctx *ctx, styx_stream stream, const styx_attn_dims *dims, const styx_attn_layer *lw,
                     float *x, int pos, const int32_t *pos_dev, float *kcache, float *vcache, int n_ctx,
                     void *workspace, uint64_t workspace_bytes) {
@@ -1771,8 +1961,51 @@ int styx_attn_block(styx_ctx *ctx, styx_stream stream, const styx_attn_dims *dim
     NEED(extent_ok(x, static_cast<uint64_t>(H) * 4) && extent_ok(lw->attn_norm, static_cast<uint64_t>(H) * 4),
          "x / attn_norm smaller than n_embd");
     int rc;
-    // one cooperative kernel when the shape fits, else seven launches
-    if (ctx->attn_kernels != 2) {
+    // auto: one cooperative kernel when the shape fits, else the cluster form
+    // when it fits, else seven launches (on B200 the cooperative kernel is
+    // the faster of the two one-launch forms at the 30B-A3B shape)
+    styx::AttnFusedArgs fa{};
+    uint32_t fsmem = 0;
+    const bool fused_fits = ctx->attn_kernels == 0 && plan_attn_fused(d, *lw, ctx->sm_count, pos + 1, fa, fsmem);
+    if ((ctx->attn_kernels == 0 && !fused_fits) || ctx->attn_kernels == 3) {
+        styx::AttnClusterArgs a{};
+        uint32_t smem = 0;
+        const bool fits = al16(x) && al16(lw->attn_norm) && plan_attn_cluster(d, *lw, ctx->sm_count, pos + 1, a, smem);
+        if (!fits && ctx->attn_kernels == 3)
+            return fail(STYX_EUNSUPPORTED, "cluster attention does not fit these dims / formats");
+        if (fits) {
+            NEED(extent_ok(lw->wq.data, static_cast<uint64_t>(a.rb_q) * qd) &&
+                     extent_ok(lw->wk.data, static_cast<uint64_t>(a.rb_q) * kvd) &&
+                     extent_ok(lw->wv.data, static_cast<uint64_t>(a.rb_v) * kvd) &&
+                     extent_ok(lw->wo.data, static_cast<uint64_t>(a.rb_o) * H),
+                 "a weight matrix is smaller than its shape");
+            a.x = x;
+            a.attn_norm = lw->attn_norm;
+            a.eps = d.rms_eps;
+            a.wq = static_cast<const uint8_t *>(lw->wq.data);
+            a.wk = static_cast<const uint8_t *>(lw->wk.data);
+            a.wv = static_cast<const uint8_t *>(lw->wv.data);
+            a.wo = static_cast<const uint8_t *>(lw->wo.data);
+            a.H = H;
+            a.n_heads = d.n_heads;
+            a.n_kv = d.n_kv_heads;
+            a.q_norm = d.qk_norm ? lw->q_norm : nullptr;
+            a.k_norm = d.qk_norm ? lw->k_norm : nullptr;
+            a.theta_scale = std::pow(static_cast<double>(d.rope_base), -2.0 / static_cast<double>(hd));
+            a.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+            a.n_t = pos + 1;
+            a.kcache = kcache;
+            a.vcache = vcache;
+            a.opart = reinterpret_cast<float *>(ws + w.opart);
+            a.cnt = reinterpret_cast<unsigned *>(ws + w.ccnt);
+            a.err = ctx->d_err;
+            a.trace = ctx->trace ? reinterpret_cast<long long *>(ws + w.trace) : nullptr;
+            CK(styx::launch_attn_cluster(a, lw->wq.qtype, lw->wv.qtype, smem, S(stream)));
+            ctx->attn_last_path = 3;
+            return STYX_OK;
+        }
+    }
+    if (ctx->attn_kernels != 2 && ctx->attn_kernels != 3) {
         styx::AttnFusedArgs a{};
         uint32_t smem = 0;
         const bool fits = plan_attn_fused(d, *lw, ctx->sm_count, pos + 1, a, smem);

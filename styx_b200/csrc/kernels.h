@@ -297,6 +297,37 @@ int attn_fused_threads();
 cudaError_t launch_attn_fused(const AttnFusedArgs &a, int qw, int qv, int grid, uint32_t smem, bool coop,
                               cudaStream_t st);
 
+// The attention half of a decode layer as one launch of thread-block
+// clusters (attn_cluster.cu): one cluster of C CTAs per kv head, head_dim
+// 128.  The cluster computes its q heads, k and v rows, the attention of its
+// q heads over the cache rows (split over its CTAs, merged through
+// distributed shared memory), and its columns' share of Wo . att; the CTA
+// that completes a row block last over the n_kv clusters adds the shares in
+// cluster order into x.
+struct AttnClusterArgs {
+    float *x;                          // [H] in/out
+    const float *attn_norm;
+    float eps;
+    const uint8_t *wq, *wk, *wv, *wo;  // row-major blocks; q, k, o of one qtype, v of another
+    int rb_q, rb_v, rb_o;              // row bytes (k as q)
+    int H, n_heads, n_kv;
+    const float *q_norm, *k_norm;      // [128] or null
+    double theta_scale;
+    float scale;
+    int n_t;                           // cache rows read; the token's position is n_t - 1
+    float *kcache, *vcache;            // [n_ctx][n_kv * 128]
+    float *opart;                      // workspace [n_kv][H]: each cluster's share of the o rows
+    unsigned *cnt;                     // workspace: per row block (kCntStride apart) the clusters done; 0 between launches
+    int *err;
+    long long *trace;                  // STYX_OPT_TRACE: clock64 stamps [CTA][16], else null
+    int C, tps, npre;                  // CTAs per cluster, cache rows per CTA, of them prefetched into shared memory
+    uint32_t off_x, off_dig, off_q, off_rope, off_sc, off_acc, off_mrecv, off_att, off_adig, off_o, off_w, off_kv;
+};
+constexpr uint32_t kAttnClusterHeader = 128;   // shared-memory header bytes of the cluster form
+bool attn_cluster_supported(int qw, int qv);
+int attn_cluster_max_active(int qw, int qv, int C, uint32_t smem);
+cudaError_t launch_attn_cluster(const AttnClusterArgs &a, int qw, int qv, uint32_t smem, cudaStream_t st);
+
 constexpr int kAttnMaxSplits = 256;
 constexpr int kArgmaxCtas = 296;   // partial maxima of styx_argmax_f32
 size_t attn_smem_bytes(int gqa, int hd, int tps);
@@ -340,6 +371,48 @@ cudaError_t launch_fused_layers(const FusedLaunch &a, int qg, int qd, int grid, 
 bool fused_supported(int qg, int qd);
 int fused_block_threads();
 constexpr uint32_t kFusedHeader = 1792;
+
+// The MoE block as one launch of thread-block clusters (moe_cluster.cu): one
+// cluster of C CTAs per selected slot.  Every cluster routes the token itself
+// (its CTAs split the router rows and exchange the logits through
+// distributed shared memory), streams slot s's gate/up rows and down rows
+// split over its CTAs, exchanges h through distributed shared memory, and
+// writes slot s's down rows; the CTA that completes a row block last (one
+// counter per block) adds the k slots in slot order into x.
+struct ClusterArgs {
+    float *x;                // residual f32[H]: read, then += the block (unless partial)
+    const float *norm_w;
+    float eps;
+    const float *router;     // f32[E][H]
+    int E, H, F, k, renorm;
+    const uint32_t *remap, *pmap;
+    ExpSrc gate, up, down;
+    int32_t *ids64;
+    float *weights;
+    float *logits;           // debug views, written by cluster 0's first CTA (h: by every CTA, its rows)
+    float *xnorm;
+    float *h;                // [k][F]
+    float *y;                // workspace f32[k][H]: the down rows of each slot
+    unsigned *cnt;           // workspace: per row block (kCntStride apart) the slots done; 0 between launches
+    int *err;
+    long long *trace;        // optional: kTraceStamps clock64 stamps per CTA
+    float *partial;          // expert parallelism: w[s] * d[s][r] per slot instead of the combine
+    int quiet;
+    // plan
+    int C;                   // CTAs per cluster
+    int rb_g, rb_u, rb_d;
+    int units_g, gs_g, units_d, gs_d;
+    int ng, chg;             // gate/up chunks per CTA (<= 8) and row pairs per chunk
+    uint32_t off_lg, off_x, off_xd, off_hf, off_hd, off_y, off_gu, off_dn;   // shared-memory regions
+    uint32_t gu_stride, gu_up_off;
+};
+constexpr int kCntStride = 32;          // u32 words between the row-block counters (one 128-byte line each)
+constexpr int kClusterMaxC = 16;
+constexpr uint32_t kClusterHeader = 2048;
+bool cluster_supported(int qg, int qd);
+cudaError_t launch_cluster(const ClusterArgs &a, int qg, int qd, uint32_t smem, cudaStream_t st);
+// clusters of a launch that can be resident at once (0 if the query fails)
+int cluster_max_active(int qg, int qd, int C, uint32_t smem);
 constexpr int kTraceStamps = 32;   // phase stamps per CTA (STYX_OPT_TRACE)
 
 // shared-memory plan of the fused kernels (computed on the host)

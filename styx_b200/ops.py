@@ -52,11 +52,12 @@ class Context:
         return v.value
 
     def set_moe_kernels(self, mode: int) -> None:
-        """0 auto, 1 the single cooperative kernel, 2 three kernels."""
+        """0 auto, 1 the single cooperative kernel, 2 three kernels, 3 the cluster form."""
         self.set_option(_lib.OPT_MOE_KERNELS, mode)
 
     def last_moe_path(self) -> int:
-        """1 = single kernel, 2 = three kernels (the last styx_moe_block)."""
+        """1 = single kernel, 2 = three kernels, 3 = host-read form, 4 / 5 = single
+        kernel over several layers, 6 = cluster form (the last styx_moe_block[s])."""
         return self.get_option(_lib.OPT_MOE_LAST_PATH)
 
 

@@ -161,17 +161,22 @@ def _attn_layer(seed, H, n_heads, n_kv, hd, qts):
     return ws, an, qn, kn
 
 
-FUSED, SEPARATE = 0, 2
+# STYX_OPT_ATTN_KERNELS values and the LAST_PATH each gives for head_dim 128
+AUTO, FUSED, SEPARATE, CLUSTER = 0, 1, 2, 3
+PATH = {AUTO: 1, FUSED: 1, SEPARATE: 2, CLUSTER: 3}
 
 
-@pytest.mark.parametrize("form", [FUSED, SEPARATE], ids=["one-kernel", "seven-kernels"])
+@pytest.mark.parametrize("form", [AUTO, CLUSTER, SEPARATE], ids=["one-kernel", "cluster", "seven-kernels"])
 @pytest.mark.parametrize("H,n_heads,n_kv,hd,qk", [(2048, 32, 4, 128, True), (1024, 16, 4, 128, False),
                                                  (512, 8, 2, 64, False)])
 def test_attn_block_decodes_like_the_oracle(H, n_heads, n_kv, hd, qk, form):
     """Six tokens through one layer's attention half (the 30B shape: q/k/o
     q4_K, v q6_K), the caches filling up row by row; x and the caches after
-    every token against the oracle's layer.  Both forms: one cooperative
-    kernel (head_dim 128) and seven launches."""
+    every token against the oracle's layer.  Three forms: one cooperative
+    kernel (the default for head_dim 128), one launch of thread-block
+    clusters and seven launches."""
+    if hd != 128 and form == CLUSTER:
+        pytest.skip("the one-kernel forms take head_dim 128")
     qts = (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K, _lib.Q4_K)
     ws, an, qn, kn = _attn_layer(H + hd, H, n_heads, n_kv, hd, qts)
     eps, base, n_ctx = 1e-6, 1_000_000.0, 64
@@ -180,7 +185,7 @@ def test_attn_block_decodes_like_the_oracle(H, n_heads, n_kv, hd, qk, form):
     blk.ctx.set_option(_lib.OPT_ATTN_KERNELS, form)
     try:
         _decode_six(blk, H, n_heads, n_kv, hd, qk, ws, an, qn, kn, eps, base, n_ctx, kvd)
-        assert blk.last_path() == (1 if form == FUSED and hd == 128 else 2)
+        assert blk.last_path() == (PATH[form] if hd == 128 else 2)
     finally:
         blk.ctx.set_option(_lib.OPT_ATTN_KERNELS, 0)
 
@@ -227,23 +232,24 @@ def test_one_kernel_attention_at_long_context(pos):
     w = ops.AttnWeights(T(an), *[ops.DenseWeight(qt, T(raw)) for qt, raw in ws], q_norm=T(qn), k_norm=T(kn))
     outs = {}
     try:
-        for form in (FUSED, SEPARATE):
+        for form in (CLUSTER, FUSED, SEPARATE):
             blk.ctx.set_option(_lib.OPT_ATTN_KERNELS, form)
             kc, vc, x = T(kc0), T(vc0), T(x0)
             blk.forward(x, w, pos, T(np.array([pos], np.int32)), kc, vc, n_ctx)
             torch.cuda.synchronize()
             blk.ctx.check_device_error()
-            assert blk.last_path() == (1 if form == FUSED else 2)
+            assert blk.last_path() == PATH[form]
             outs[form] = (x.cpu().numpy(), kc.cpu().numpy()[pos], vc.cpu().numpy()[pos])
     finally:
         blk.ctx.set_option(_lib.OPT_ATTN_KERNELS, 0)
     okc, ovc = kc0.copy(), vc0.copy()
     exp = O.attn_block(x0, an, eps, n_heads, n_kv, hd, qn, kn, base, ws, pos, okc, ovc)
-    for form in (FUSED, SEPARATE):
+    for form in (CLUSTER, FUSED, SEPARATE):
         x, krow, vrow = outs[form]
         assert rel_to_max(x, exp) < 1e-4, form
         assert rel_to_max(krow, okc[pos]) < 1e-4 and rel_to_max(vrow, ovc[pos]) < 1e-4
     assert rel_to_max(outs[FUSED][0], outs[SEPARATE][0]) < 1e-5
+    assert rel_to_max(outs[CLUSTER][0], outs[SEPARATE][0]) < 1e-5
 
 
 def test_one_kernel_attention_split_launch_numbers_time_out_and_recover():
@@ -264,10 +270,14 @@ def test_one_kernel_attention_split_launch_numbers_time_out_and_recover():
     x0 = rng.normal(0, 1, H).astype(np.float32)
     blk.ctx.check_device_error()
     blk.workspace[0:8].view(torch.int64).fill_(blk.ctx.sm_count // 2)   # the launch counter
-    x = T(x0)
-    blk.forward(x, w, pos, T(np.array([pos], np.int32)), T(kc0), T(vc0), n_ctx)
-    torch.cuda.synchronize()
-    assert blk.last_path() == 1
+    blk.ctx.set_option(_lib.OPT_ATTN_KERNELS, FUSED)   # the form with grid-wide waits
+    try:
+        x = T(x0)
+        blk.forward(x, w, pos, T(np.array([pos], np.int32)), T(kc0), T(vc0), n_ctx)
+        torch.cuda.synchronize()
+        assert blk.last_path() == 1
+    finally:
+        blk.ctx.set_option(_lib.OPT_ATTN_KERNELS, 0)
     with pytest.raises(_lib.StyxError) as ei:
         blk.ctx.check_device_error()
     assert ei.value.code == _lib.STYX_ETIMEOUT
@@ -284,7 +294,7 @@ def test_one_kernel_attention_split_launch_numbers_time_out_and_recover():
 def test_attention_options_are_checked():
     c = ops.ctx(0)
     with pytest.raises(_lib.StyxError) as ei:
-        c.set_option(_lib.OPT_ATTN_KERNELS, 3)
+        c.set_option(_lib.OPT_ATTN_KERNELS, 4)
     assert ei.value.code == _lib.STYX_EINVAL
     with pytest.raises(_lib.StyxError):
         c.set_option(_lib.OPT_ATTN_LAST_PATH, 1)     # read only

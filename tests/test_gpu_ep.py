@@ -48,21 +48,24 @@ def _rank_layer(c, owned):
                                    (4096, 1536, 8, 4, (_lib.Q4_K, _lib.Q4_K, _lib.Q4_K))],
                          ids=["gate_up-kernel", "235B-like"])
 @pytest.mark.parametrize("R", [2, 3])
-@pytest.mark.parametrize("mode", [_lib.MOE_SPLIT, _lib.MOE_AUTO], ids=["three-kernel", "single-kernel"])
+@pytest.mark.parametrize("mode", [_lib.MOE_SPLIT, _lib.MOE_FUSED, _lib.MOE_AUTO],
+                         ids=["three-kernel", "single-kernel", "auto"])
 def test_ep_ranks_sum_to_single_device(shape, R, mode):
     H, F, E, k, qts = shape
+    if mode == _lib.MOE_FUSED and H != 1024:
+        pytest.skip("the single kernel does not take this shape")
     c = make_case(51, H, F, E, k, qts)
     ref = oracle_block(c)
     blk = ops.MoeBlock(ops.Dims(H, F, E, k), 0)
     blk.ctx.set_moe_kernels(mode)
-    want_path = 1 if (mode == _lib.MOE_AUTO and H == 1024) else 2
+    want_path = {2} if (mode == _lib.MOE_SPLIT or H != 1024) else ({1, 6} if mode == _lib.MOE_AUTO else {1})
     try:
         x1 = _t(c.x)
         ids1 = torch.full((64,), -7, dtype=torch.int32, device=DEV)
         blk.forward(x1, _full_layer(c), 0, ids1)
         torch.cuda.synchronize()
         blk.ctx.check_device_error()
-        assert blk.ctx.last_moe_path() == want_path
+        assert blk.ctx.last_moe_path() in want_path
         total = torch.zeros(k * H, dtype=torch.float32, device=DEV)
         for r in range(R):
             owned = [e for e in range(E) if e % R == r]
@@ -74,7 +77,7 @@ def test_ep_ranks_sum_to_single_device(shape, R, mode):
             blk.forward_ep(xr, lw, 0, ids, partial, weights_out=w)
             torch.cuda.synchronize()
             blk.ctx.check_device_error()           # experts held elsewhere are not errors
-            assert blk.ctx.last_moe_path() == want_path
+            assert blk.ctx.last_moe_path() in want_path
             assert torch.equal(xr, _t(c.x))          # x is read, not updated
             assert torch.equal(ids[:k], ids1[:k])    # every rank routes the same
             p = partial.view(k, H).cpu().numpy()

@@ -64,7 +64,7 @@ def _rank_main(rank, port, out_dir):
             full = ops.LayerWeights(ffn_norm=t(c.norm), router=t(c.router),
                                     gate=ops.Experts(c.qts[0], t(c.gate), sg), up=ops.Experts(c.qts[1], t(c.up), su),
                                     down=ops.Experts(c.qts[2], t(c.down), sd))
-            assert path == 1   # this shape runs the single kernel's expert-parallel form
+            assert path in (1, 6)   # the cluster form or the single kernel, with its expert-parallel epilogue
             x1 = t(c.x)
             blk.forward(x1, full, 0, torch.full((64,), -7, dtype=torch.int32, device=dev))
             torch.cuda.synchronize()

@@ -241,21 +241,33 @@ CASES = [
 ]
 
 
-# shapes the single cooperative kernel takes (the others run three kernels)
+# shapes the cluster form and the single cooperative kernel take (the others
+# run three kernels)
 FUSED_OK = {"cfg1-q8_0", "cfg2-shape-E16", "q5K-q5K-q5K", "k16"}
+MODES = [_lib.MOE_AUTO, _lib.MOE_FUSED, _lib.MOE_SPLIT]
+MODE_IDS = ["auto", "fused", "split"]
 
 
-@pytest.mark.parametrize("mode", [_lib.MOE_AUTO, _lib.MOE_SPLIT], ids=["auto", "split"])
+def want_path(mode, fits=True):
+    """The LAST_PATH values a block call may report: auto takes the cluster
+    form (6) where the device holds its k clusters at once, else the single
+    kernel (1); the single kernel when asked for; three kernels (2) for the
+    shapes neither takes."""
+    if mode == _lib.MOE_SPLIT or not fits:
+        return {2}
+    return {1, 6} if mode == _lib.MOE_AUTO else {1}
+
+
+@pytest.mark.parametrize("mode", MODES, ids=MODE_IDS)
 @pytest.mark.parametrize("name,seed,H,F,E,k,qts", CASES, ids=[c[0] for c in CASES])
 def test_moe_block_matches_oracle(name, seed, H, F, E, k, qts, mode):
+    if mode == _lib.MOE_FUSED and name not in FUSED_OK:
+        pytest.skip("the single kernel does not take this shape")
     c = make_case(seed, H, F, E, k, qts)
     ref = oracle_block(c)
     lw = _upload_layer(c)
     blk, x, ids, w = _run_block(c, lw, mode=mode)
-    if mode == _lib.MOE_SPLIT:
-        assert blk.path == 2
-    else:
-        assert blk.path == (1 if name in FUSED_OK else 2), blk.path
+    assert blk.path in want_path(mode, name in FUSED_OK), blk.path
     # routing: ids bit-exact when the top-k margin exceeds 1e-4
     logits = blk.view(1, E).cpu().numpy()
     assert rel_to_max(logits, ref["logits"]) < 1e-5
@@ -273,7 +285,7 @@ def test_moe_block_matches_oracle(name, seed, H, F, E, k, qts, mode):
     assert rel_to_max(dx, dref) < 1e-4
 
 
-@pytest.mark.parametrize("mode", [_lib.MOE_AUTO, _lib.MOE_SPLIT], ids=["auto", "split"])
+@pytest.mark.parametrize("mode", MODES, ids=MODE_IDS)
 def test_moe_block_layer_chain_reuses_workspace(mode):
     """Three layers chained through one workspace, twice: the cross-CTA
     counters reset themselves and every layer matches the oracle chain."""
@@ -298,7 +310,7 @@ def test_moe_block_layer_chain_reuses_workspace(mode):
         blk.ctx.set_moe_kernels(_lib.MOE_AUTO)
 
 
-@pytest.mark.parametrize("mode", [_lib.MOE_AUTO, _lib.MOE_SPLIT], ids=["auto", "split"])
+@pytest.mark.parametrize("mode", MODES, ids=MODE_IDS)
 def test_moe_block_placement_is_invariant(mode):
     """Placement changes speed, never results (README.md:29-30): the same
     layer with experts split over a hot buffer, an arena and the full
@@ -339,7 +351,7 @@ def test_moe_block_placement_is_invariant(mode):
     assert np.array_equal(x_pl.view(np.uint32), x_full.view(np.uint32))
 
 
-@pytest.mark.parametrize("mode", [_lib.MOE_AUTO, _lib.MOE_SPLIT], ids=["auto", "split"])
+@pytest.mark.parametrize("mode", MODES, ids=MODE_IDS)
 @pytest.mark.parametrize("H,F,E,top,second", [
     (1024, 512, 32, [29, 3, 17, 4], [30, 11]),
     (256, 256, 512, [300, 7, 511, 149], [450, 148]),   # E > SM count: several router rows per CTA
@@ -357,7 +369,7 @@ def test_moe_block_routing_ties(mode, H, F, E, top, second):
     ref = oracle_block(c)
     assert list(ref["ids64"][:6]) == sorted(top) + sorted(second)
     blk, x, ids, w = _run_block(c, _upload_layer(c), mode=mode)
-    assert blk.path == (1 if mode == _lib.MOE_AUTO else 2)
+    assert blk.path in want_path(mode)
     logits = blk.view(1, E).cpu().numpy()
     assert np.all(logits[top] == logits[top[0]]) and np.all(logits[second] == logits[second[0]])
     assert np.array_equal(id_rows(ids, c.k), id_rows(ref["ids64"], c.k))
