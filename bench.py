@@ -45,9 +45,31 @@ sys.path.insert(0, ROOT)
 METRIC = "decode tok/s (30B-A3B shape, q4_K) at 1/2/4/8 B200; MoE-layer % of HBM peak"
 H, F, E, K_TOP, N_LAYERS = 2048, 768, 128, 8, 48
 Q4_K, Q6_K = 12, 14
+QD = Q6_K                          # down projection format
 SG = (H // 256) * 144 * F          # gate / up slab bytes per expert
 SD = (F // 256) * 210 * H          # down slab bytes per expert
 ALG_BYTES_LAYER = K_TOP * (2 * SG + SD) + E * H * 4 + 3 * H * 4   # 25,550,848
+SHAPE = "cfg2"
+
+
+def set_shape(name: str) -> None:
+    """The MoE stack's shape: cfg2 (the 30B-A3B layer of configs[1] / [2],
+    48 layers, down q6_K) or cfg5 (configs[4]'s 235B-A22B layer: H 4096, F
+    1536, 128 experts top-8, every matrix q4_K, 94 layers)."""
+    global H, F, N_LAYERS, QD, SG, SD, ALG_BYTES_LAYER, SHAPE
+    if name == "cfg5":
+        H, F, N_LAYERS, QD = 4096, 1536, 94, Q4_K
+    SG = (H // 256) * 144 * F
+    SD = (F // 256) * (210 if QD == Q6_K else 144) * H
+    ALG_BYTES_LAYER = K_TOP * (2 * SG + SD) + E * H * 4 + 3 * H * 4
+    SHAPE = name
+
+
+def shape_desc() -> str:
+    qd = "q6_K" if QD == Q6_K else "q4_K"
+    return f"H{H} E{E} top{K_TOP} F{F}, gate/up q4_K, down {qd}"
+
+
 ZIPF_S, ZIPF_TAU, ZIPF_KAPPA = 1.1, 0.25, 4.0
 
 
@@ -150,7 +172,7 @@ def cpu_layer(seed: int = 0):
     for e in range(E):
         gate[e * SG:(e + 1) * SG] = O.quantize(Q4_K, rng.standard_normal((F, H), np.float32) * np.float32(0.02)).reshape(-1)
         up[e * SG:(e + 1) * SG] = O.quantize(Q4_K, rng.standard_normal((F, H), np.float32) * np.float32(0.02)).reshape(-1)
-        down[e * SD:(e + 1) * SD] = O.quantize(Q6_K, rng.standard_normal((H, F), np.float32) * np.float32(0.02)).reshape(-1)
+        down[e * SD:(e + 1) * SD] = O.quantize(QD, rng.standard_normal((H, F), np.float32) * np.float32(0.02)).reshape(-1)
     return router_host(0), np.ones(H, np.float32), gate, up, down
 
 
@@ -160,11 +182,11 @@ def time_cpu(budget_s: float, nthreads: int):
     from oracle import oracle as O
     router, norm, gate, up, down = cpu_layer()
     toks = token_bank(16)
-    O.moe_block_mt(toks[0], norm, 1e-6, router, K_TOP, True, (Q4_K, Q4_K, Q6_K), gate, up, down, F, nthreads)
+    O.moe_block_mt(toks[0], norm, 1e-6, router, K_TOP, True, (Q4_K, Q4_K, QD), gate, up, down, F, nthreads)
     t0 = time.perf_counter()
     reps = 0
     while True:
-        O.moe_block_mt(toks[reps % 16], norm, 1e-6, router, K_TOP, True, (Q4_K, Q4_K, Q6_K), gate, up, down, F,
+        O.moe_block_mt(toks[reps % 16], norm, 1e-6, router, K_TOP, True, (Q4_K, Q4_K, QD), gate, up, down, F,
                        nthreads)
         reps += 1
         el = time.perf_counter() - t0
@@ -241,11 +263,13 @@ def run_reference(args, rank: int) -> int:
 
 
 def workload_config(n: int):
-    return {"workload": "cfg2 MoE layer (H2048 E128 top8 F768, gate/up q4_K, down q6_K) stacked x48 "
-                        "(cfg3 MoE path), batch-1 decode, all experts resident",
+    name = "cfg2 MoE layer" if SHAPE == "cfg2" else "cfg5 (configs[4]) MoE layer"
+    return {"workload": f"{name} ({shape_desc()}) stacked x{N_LAYERS} (cfg3 MoE path), batch-1 decode, "
+                        "all experts resident",
             "n_layers": N_LAYERS, "n_embd": H, "n_expert": E, "n_expert_used": K_TOP, "n_ff": F,
             "global_batch": n, "parallelism": f"replicas x{n}" if n > 1 else "single",
-            "l2": "inputs larger than L2 (1.2 GB of expert slabs per token vs 126 MB L2)",
+            "l2": f"inputs larger than L2 ({N_LAYERS * K_TOP * (2 * SG + SD) / 1e9:.1f} GB of expert slabs per "
+                  "token vs 126 MB L2)",
             "router": "Zipf(1.1) popularity bias"}
 
 
@@ -260,7 +284,7 @@ def build_model(dev: int, n_layers: int, unique: int = 4):
     for u in range(min(unique, n_layers)):
         g = ops.synth_quant(Q4_K, E * F, H, 1000 + 3 * u, 0.02, device=dev)
         up = ops.synth_quant(Q4_K, E * F, H, 1001 + 3 * u, 0.02, device=dev)
-        dn = ops.synth_quant(Q6_K, E * H, F, 1002 + 3 * u, 0.02, device=dev)
+        dn = ops.synth_quant(QD, E * H, F, 1002 + 3 * u, 0.02, device=dev)
         base.append((g, up, dn))
     torch.cuda.synchronize()
     layers = []
@@ -272,7 +296,7 @@ def build_model(dev: int, n_layers: int, unique: int = 4):
             g, up, dn = (t.clone() for t in base[layer % len(base)])
         router = torch.from_numpy(router_host(layer)).to(d)
         layers.append(ops.LayerWeights(norm, router, ops.Experts(Q4_K, g, SG), ops.Experts(Q4_K, up, SG),
-                                       ops.Experts(Q6_K, dn, SD)))
+                                       ops.Experts(QD, dn, SD)))
     torch.cuda.synchronize()
     return layers
 
@@ -298,7 +322,7 @@ def ep_moe_layers(dev: int, n_layers: int, world: int, rank: int, unique: int = 
     for u in range(min(unique, n_layers)):
         base.append((ops.synth_quant(Q4_K, E * F, H, 1000 + 3 * u, 0.02, device=dev),
                      ops.synth_quant(Q4_K, E * F, H, 1001 + 3 * u, 0.02, device=dev),
-                     ops.synth_quant(Q6_K, E * H, F, 1002 + 3 * u, 0.02, device=dev)))
+                     ops.synth_quant(QD, E * H, F, 1002 + 3 * u, 0.02, device=dev)))
     torch.cuda.synchronize()
     norm = torch.ones(H, dtype=torch.float32, device=d)
 
@@ -310,7 +334,7 @@ def ep_moe_layers(dev: int, n_layers: int, world: int, rank: int, unique: int = 
         router = torch.from_numpy(router_host(layer)).to(d)
         layers.append(ops.LayerWeights(norm, router, ops.Experts(Q4_K, None, SG, hot=mine(g, SG)),
                                        ops.Experts(Q4_K, None, SG, hot=mine(up, SG)),
-                                       ops.Experts(Q6_K, None, SD, hot=mine(dn, SD)), remap=remap))
+                                       ops.Experts(QD, None, SD, hot=mine(dn, SD)), remap=remap))
     del base
     torch.cuda.synchronize()
     return layers
@@ -864,11 +888,12 @@ def run_batch(args, local: int) -> int:
     t_layer = ms_step / L * 1e-3
     achieved = alg / t_layer / 1e9
     line = {
-        "metric": f"decode tok/s at batch {B} (30B-A3B MoE stack, q4_K/q6_K experts)", "value": value,
+        "metric": f"decode tok/s at batch {B} ({'30B-A3B' if SHAPE == 'cfg2' else '235B-A22B (configs[4])'} MoE "
+                  f"stack, {'q4_K/q6_K' if QD == Q6_K else 'q4_K'} experts)", "value": value,
         "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16 tensor-core operands (dequantised q4_K/q6_K), f32 accumulate", "data": "synthetic",
-        "config": {"workload": f"batch {B}: the cfg3 stack ({L} MoE layers H{H} E{E} top{K_TOP} F{F}) for {B} "
+        "config": {"workload": f"batch {B}: the {SHAPE} MoE stack ({L} layers, {shape_desc()}) for {B} "
                                f"tokens per step, grouped expert GEMMs (tcgen05)", "global_batch": B,
                    "n_layers": L, "parallelism": "single",
                    "l2": "inputs larger than L2 (every layer's used experts stream from HBM)",
@@ -918,8 +943,17 @@ def main() -> int:
                          "tokens after its 512-token prompt)")
     ap.add_argument("--tokens", type=int, default=256, help="cfg4: timed decode tokens")
     ap.add_argument("--batch", type=int, default=8, help="batch: tokens per step (1..64)")
+    ap.add_argument("--shape", default="cfg2", choices=["cfg2", "cfg5"],
+                    help="cfg3 / batch workloads: the 30B-A3B MoE layer (cfg2, 48 layers) or configs[4]'s "
+                         "235B-A22B layer (cfg5: H 4096, F 1536, every matrix q4_K, 94 layers)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.shape != "cfg2":
+        if args.workload not in ("cfg3", "batch") or args.impl != "styx":
+            ap.error("--shape cfg5 applies to the device arm's --workload cfg3 and batch")
+        set_shape(args.shape)
+        if args.layers == 48:
+            args.layers = N_LAYERS
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

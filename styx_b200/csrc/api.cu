@@ -1010,7 +1010,8 @@ static bool plan_fused(const styx_moe_dims &d, const styx_moe_layer &lw, int sms
     const size_t a_route = static_cast<size_t>(H) * 4 + 3 * static_cast<size_t>(H) + H / 32 * 4;
     const size_t kF = static_cast<size_t>(k) * F;
     const size_t a_down = 3 * kF + kF / 32 * 4;
-    const size_t size_a = a128(std::max(a_route, a_down)) + a128(static_cast<size_t>(d.n_expert) * 4);
+    // (then the remap / pmap tables, then the logits, at the end of region A)
+    const size_t size_a = a128(std::max(a_route, a_down)) + 3 * a128(static_cast<size_t>(d.n_expert) * 4);
     // gate/up: kGuChunks chunks per CTA (each at most two slot segments of
     // gate rows and of up rows); every chunk of the CTA resident.  Fewer,
     // larger chunks issue fewer bulk copies from the one issuing warp

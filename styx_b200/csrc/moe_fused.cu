@@ -144,6 +144,8 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
     float *hsc = reinterpret_cast<float *>(hd3 + kF);
     float *dpart = reinterpret_cast<float *>(smem + p.off_part);
     float *lgs = dpart - ((E + 31) & ~31);                    // the logits, at the end of region A
+    uint32_t *smap = reinterpret_cast<uint32_t *>(lgs) - 2 * ((E + 31) & ~31);   // remap, pmap (before the logits)
+    const int Ep = (E + 31) & ~31;
     uint8_t *gubuf = smem + p.off_ring;
     uint8_t *dbuf = smem + p.off_down;
 
@@ -250,6 +252,12 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
             if (dt > kPollFreeCycles) __nanosleep(256);
         }
         __syncwarp();
+    }
+    // the id tables in shared memory, read while x travels: the slab
+    // sources of the picked experts then cost no global round trip
+    for (int i = tid; i < E; i += kFusedBlock) {
+        smap[i] = p.remap ? __ldg(p.remap + i) : kSkip;
+        smap[Ep + i] = p.pmap ? __ldg(p.pmap + i) : kSkip;
     }
     float *xown = wts + 16;   // this CTA's own rows of the raw x (<= 16), for the residual add
     for (int i = tid; i < H4; i += kFusedBlock) {
@@ -392,11 +400,11 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
         // lane s < k: slot s's slab sources and id rows
         int hi = -1, ai = -1, fi = -1;
         if (lane < k) {
-            const uint32_t hot = (e >= 0 && p.remap) ? p.remap[e] : kSkip;
+            const uint32_t hot = e >= 0 ? smap[e] : kSkip;
             if (hot != kSkip) {
                 hi = static_cast<int>(hot);
             } else {
-                const uint32_t am = (e >= 0 && p.pmap) ? p.pmap[e] : kSkip;
+                const uint32_t am = e >= 0 ? smap[Ep + e] : kSkip;
                 if (am != kSkip) ai = static_cast<int>(am);
                 else fi = e;
             }
