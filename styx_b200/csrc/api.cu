@@ -1644,7 +1644,7 @@ static int dense_gemv(styx_ctx *ctx, cudaStream_t st, int qtype, const void *a, 
     da.rb = static_cast<int>(rb);
     da.units = ncols / 64;
     da.gs = std::min(32, pow2ceil(da.units));
-    da.rc = 2 * 8 * (32 / da.gs);   // two rows per lane group per chunk
+    da.rc = 2 * styx::kWideConsumerWarps * (32 / da.gs);   // two rows per lane group per chunk
     da.slot_stride = static_cast<uint32_t>(a16(static_cast<size_t>(da.rc) * da.rb + 32));
     da.stage_bytes = da.slot_stride;
     const int grid = std::max(1, std::min(ctx->sm_count, (nrows + da.rc - 1) / da.rc));
@@ -1662,7 +1662,7 @@ static int dense_gemv(styx_ctx *ctx, cudaStream_t st, int qtype, const void *a, 
     const uint32_t smem = da.stage_off + static_cast<uint32_t>(nst) * da.stage_bytes;
     NEED(smem <= 227 * 1024, "dense GEMV needs %u bytes of shared memory", smem);
     da.err = ctx->d_err;
-    CK(styx::launch_down(da, qtype, grid, smem, st));
+    CK(styx::launch_down(da, qtype, grid, smem, st, true));
     return STYX_OK;
 }
 

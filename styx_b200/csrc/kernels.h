@@ -211,7 +211,8 @@ struct GatherArgs {
 // launchers (return the launch error)
 cudaError_t launch_route(const RouteArgs &a, cudaStream_t st);
 cudaError_t launch_gate_up(const GateUpArgs &a, int qtype, int grid, cudaStream_t st);
-cudaError_t launch_down(const DownArgs &a, int qtype, int grid, uint32_t smem, cudaStream_t st);
+// wide: 16 consumer warps (a dense GEMV) instead of 8
+cudaError_t launch_down(const DownArgs &a, int qtype, int grid, uint32_t smem, cudaStream_t st, bool wide = false);
 cudaError_t launch_matvec_id(const MatVecIdArgs &a, int qtype, cudaStream_t st);
 cudaError_t launch_rms_norm(const float *x, const float *w, float eps, int ncols, int nrows,
                             float *out, cudaStream_t st);
@@ -418,6 +419,7 @@ constexpr int kTraceStamps = 32;   // phase stamps per CTA (STYX_OPT_TRACE)
 // shared-memory plan of the fused kernels (computed on the host)
 int gate_up_smem(const GateUpArgs &a);
 constexpr int kConsumerWarps = 8;
+constexpr int kWideConsumerWarps = 16;
 constexpr int kFusedThreads = 32 * (kConsumerWarps + 1);
 
 }  // namespace styx

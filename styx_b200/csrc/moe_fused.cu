@@ -756,6 +756,10 @@ cudaError_t resident_fit(const void *kern, int threads, uint32_t smem, int grid)
     // kernel never finds it set lower
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
+    // every large kernel asks for the same (largest) shared-memory carveout,
+    // so consecutive launches of different kernels need no reconfiguration
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
     int occ = 0, sms = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
     if (e != cudaSuccess) return e;

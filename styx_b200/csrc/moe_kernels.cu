@@ -324,8 +324,11 @@ cudaError_t launch_gate_up(const GateUpArgs &a, int qtype, int grid, cudaStream_
 // CTA b owns output rows [H*b/G, H*(b+1)/G); a chunk is <= rc rows, copied
 // for every slot (k bulk copies).  h is turned into digits once per CTA.
 // moe_reduce_f32.comp:8-13: acc = sum_s w[s]*d[s][i] in slot order, x += acc.
-template <int QT>
-__global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
+// CW consumer warps after the producer warp: 8 for the MoE block's down
+// rows, 16 for a dense GEMV (one slot, long rows: more warps keep more
+// dot products in flight per scheduler).
+template <int QT, int CW>
+__global__ void __launch_bounds__(32 * (CW + 1), 1) k_down(const DownArgs p) {
     pdl_trigger();
     pdl_wait();
     extern __shared__ __align__(128) uint8_t smem[];
@@ -347,7 +350,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
     if (threadIdx.x == 0) {
         for (int i = 0; i < p.nst; i++) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kConsumerWarps);
+            mbar_init(&empty[i], CW);
         }
         fence_mbar_init();
     }
@@ -392,19 +395,19 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
 
     // consumers: h -> digits (shared), weights
     const int cw = warp - 1;
-    digits_vector<8, true>(p.h, kF, hd1, hd2, hd3, hsc, threadIdx.x - 32, kConsumerWarps * 32);
+    digits_vector<8, true>(p.h, kF, hd1, hd2, hd3, hsc, threadIdx.x - 32, CW * 32);
     if (cw == 0 && lane < p.k) wts[lane] = p.w[lane];
-    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
 
     const int rpw = 32 / p.gs;
     const int ug = lane & (p.gs - 1), grp = lane / p.gs;
     const bool active = ug < p.units;
     // warp -> (slot, row phase): k <= 8 slots share the 8 warps, k > 8 loop
-    const bool multi = p.k > kConsumerWarps;
-    const int nwps = multi ? 1 : kConsumerWarps / p.k;
+    const bool multi = p.k > CW;
+    const int nwps = multi ? 1 : CW / p.k;
     const int slot0 = multi ? cw : cw / nwps;
     const int sub = multi ? 0 : cw % nwps;
-    const int sstep = multi ? kConsumerWarps : 1 << 30;
+    const int sstep = multi ? CW : 1 << 30;
     // rows of at most 32 units: a lane's unit of h stays in registers; wider
     // rows (a dense GEMV over more than 2048 columns) reload it per unit
     const bool preload = p.units <= 32;
@@ -444,7 +447,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
                 if (ug == 0 && row < n) part[s * p.rc + row] = v;
             }
         }
-        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
         const int ct = threadIdx.x - 32;
         if (ok && ct < n) {
             if (p.partial) {   // per-slot contributions for a cross-device sum (expert parallelism)
@@ -461,24 +464,32 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_down(const DownArgs p) {
     }
 }
 
-template <int QT>
+template <int QT, int CW>
 static cudaError_t launch_down_t(const DownArgs &a, int grid, uint32_t smem, cudaStream_t st) {
-    static bool attr_done = false;
+    static bool attr_done = false;   // (the attributes are the same on every device)
     if (!attr_done) {
-        cudaFuncSetAttribute(k_down<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(k_down<QT, CW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(k_down<QT, CW>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
         attr_done = true;
     }
-    return launch_pdl(k_down<QT>, dim3(grid), dim3(kFusedThreads), smem, st, a);
+    return launch_pdl(k_down<QT, CW>, dim3(grid), dim3(32 * (CW + 1)), smem, st, a);
 }
 
-cudaError_t launch_down(const DownArgs &a, int qtype, int grid, uint32_t smem, cudaStream_t st) {
+template <int CW>
+static cudaError_t launch_down_w(const DownArgs &a, int qtype, int grid, uint32_t smem, cudaStream_t st) {
     switch (qtype) {
-    case STYX_Q4_K: return launch_down_t<STYX_Q4_K>(a, grid, smem, st);
-    case STYX_Q5_K: return launch_down_t<STYX_Q5_K>(a, grid, smem, st);
-    case STYX_Q6_K: return launch_down_t<STYX_Q6_K>(a, grid, smem, st);
-    case STYX_Q8_0: return launch_down_t<STYX_Q8_0>(a, grid, smem, st);
+    case STYX_Q4_K: return launch_down_t<STYX_Q4_K, CW>(a, grid, smem, st);
+    case STYX_Q5_K: return launch_down_t<STYX_Q5_K, CW>(a, grid, smem, st);
+    case STYX_Q6_K: return launch_down_t<STYX_Q6_K, CW>(a, grid, smem, st);
+    case STYX_Q8_0: return launch_down_t<STYX_Q8_0, CW>(a, grid, smem, st);
     default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_down(const DownArgs &a, int qtype, int grid, uint32_t smem, cudaStream_t st, bool wide) {
+    return wide ? launch_down_w<kWideConsumerWarps>(a, qtype, grid, smem, st)
+                : launch_down_w<kConsumerWarps>(a, qtype, grid, smem, st);
 }
 
 // ------------------------------------------------ generic id matvec
