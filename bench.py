@@ -711,7 +711,8 @@ def run_streaming(args, local: int) -> int:
     torch.cuda.synchronize()
     hist = zipf_hist(L)
     st = ExpertStreamer(ops.Dims(H, F, E, K_TOP), L, (Q4_K, Q4_K, Q6_K), (SG, SG, SD), host, hist, budget,
-                        device=local, repin_interval=128, repin_max=2, prefetch=True)
+                        device=local, repin_interval=128, repin_max=2, prefetch=not args.no_prefetch,
+                        prefetch_min_hit=args.prefetch_min_hit, prefetch_probe=16)
     norm = torch.ones(H, dtype=torch.float32, device=dev)
     routers = [torch.from_numpy(router_host(l)).to(dev) for l in range(L)]
     layers = [st.layer_weights(l, norm, routers[l]) for l in range(L)]
@@ -758,14 +759,19 @@ def run_streaming(args, local: int) -> int:
             "dtype": "int8-dp4a/f32 (q4_K,q6_K weights)", "data": "synthetic",
             "config": {"workload": "cfg4: cfg3 MoE stack, 6 GiB expert budget, Zipf(1.1) pinning histogram, "
                                    "repin every 128 tokens (max 2 per layer), copy-engine prefetch of the previous "
-                                   "token's cold experts", "n_layers": L, "budget_bytes": budget,
-                       "tokens": n},
+                                   "token's cold experts" + (
+                                       "" if args.no_prefetch else
+                                       f" while it pays (probe of 16 tokens after each repin; off below a "
+                                       f"{args.prefetch_min_hit:.0%} hit rate)"),
+                       "n_layers": L, "budget_bytes": budget, "tokens": n},
             "hud": hud,
             "streaming": {"copy_ms_per_tok": copy_ms, "exposed_wait_ms_per_tok": exposed,
                           "kernel_ms_per_tok": sum(kern_ms) / max(n, 1),
                           "overlap_pct": 100.0 * max(0.0, 1.0 - exposed / copy_ms) if copy_ms > 0 else None,
                           "hit_rate_pct": hud["hot_pct"],
-                          "bytes_streamed_per_tok": (hud["prefetched_MiB_per_tok"] + hud["inplace_MiB_per_tok"]) * 2 ** 20},
+                          "bytes_streamed_per_tok": (hud["prefetched_MiB_per_tok"] + hud["inplace_MiB_per_tok"]) * 2 ** 20,
+                          "host_link_GBs": (hud["prefetched_MiB_per_tok"] + hud["inplace_MiB_per_tok"]) * 2 ** 20 /
+                                           (sum(tok_ms) / n * 1e-3) / 1e9},
             "e2e": {"value": n / t_wall, "unit": "tok/s", "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": L * 256,
                     "wall_s": t_wall}}
     print(json.dumps(line), flush=True)
@@ -941,7 +947,10 @@ def main() -> int:
     ap.add_argument("--ctx", type=int, default=640,
                     help="decode: cache rows before the token (640: the mean over configs[2]'s 256 decode "
                          "tokens after its 512-token prompt)")
-    ap.add_argument("--tokens", type=int, default=256, help="cfg4: timed decode tokens")
+    ap.add_argument("--tokens", type=int, default=1024, help="cfg4: timed decode tokens (configs[3]: 1024)")
+    ap.add_argument("--prefetch-min-hit", type=float, default=0.25,
+                    help="cfg4: the prefetch stays on while at least this share of prefetched slabs is used (0: always)")
+    ap.add_argument("--no-prefetch", action="store_true", help="cfg4: no next-token prefetch")
     ap.add_argument("--batch", type=int, default=8, help="batch: tokens per step (1..64)")
     ap.add_argument("--shape", default="cfg2", choices=["cfg2", "cfg5"],
                     help="cfg3 / batch workloads: the 30B-A3B MoE layer (cfg2, 48 layers) or configs[4]'s "

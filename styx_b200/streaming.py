@@ -12,6 +12,15 @@ Online repinning (maybe_repin, moe.rs:1450-1505) and the HUD counters
 (last_hot_cold, generate_moe.rs:35-119) come from the residency module
 (include/styx_residency.h).
 
+The prefetch is adaptive.  Predicting the next token's cold experts from
+the previous token's rarely hits (the reference records the same, README's
+"next-token prefetch does not work" note), and every prefetched slab costs
+host-link bandwidth that the in-place reads of the same token need.  So the
+streamer measures the hit rate over a probe window of tokens and switches the
+prefetch off when fewer than `prefetch_min_hit` of the prefetched slabs were
+used; a repin (which changes what is cold) opens a new probe window.
+
+
 Placement never changes results: a slot reads the same bytes from the hot
 buffer, the arena or the host tensor.
 """
@@ -37,6 +46,8 @@ class StreamStats:
     inplace_reads: int = 0     # cold slots read in place from host memory
     prefetched_slabs: int = 0  # expert slab triples copied by the copy engine
     repin_swaps: int = 0
+    prefetch_tokens: int = 0   # tokens that issued a prefetch
+    prefetch_off_at: int = -1  # token at which the probe switched the prefetch off (-1: never)
     copy_ms: float = 0.0       # side-stream copy time (first gather start -> last end)
     wait_ms: float = 0.0       # main-stream time spent waiting for those copies
     token_ms: float = 0.0
@@ -52,13 +63,19 @@ class ExpertStreamer:
     of HBM for pinned slabs (MoeModel's expert budget)."""
 
     def __init__(self, dims: ops.Dims, n_layers: int, qtypes, slabs, host, hist, budget: int,
-                 device: int = 0, repin_interval: int = 0, repin_max: int = 2, prefetch: bool = True):
+                 device: int = 0, repin_interval: int = 0, repin_max: int = 2, prefetch: bool = True,
+                 prefetch_min_hit: float = 0.0, prefetch_probe: int = 16):
         self.dims, self.n_layers, self.qtypes, self.slabs = dims, n_layers, tuple(qtypes), tuple(slabs)
         self.E, self.k = dims.n_expert, dims.n_expert_used
         self.dev = f"cuda:{device}"
         self.device = device
         self.host = host
         self.repin_interval, self.repin_max, self.prefetch = repin_interval, repin_max, prefetch
+        # adaptive prefetch: probe window (tokens) and the hit rate that keeps it on (0: always on)
+        self.prefetch_min_hit, self.prefetch_probe = prefetch_min_hit, prefetch_probe
+        self._probe_left = prefetch_probe
+        self._probe_slabs = self._probe_hits = 0
+        self._prefetch_on = prefetch
         self.res = ops.Residency(n_layers, self.E, self.k, int(sum(slabs)))
         self.n_pinned = self.res.pin(hist[0], hist[1], hist[2], budget)
         cx = ops.ctx(device).handle
@@ -83,6 +100,8 @@ class ExpertStreamer:
         self.ev_copy0, self.ev_copy1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         self.stats = StreamStats(cold_by_layer=[0] * n_layers)
         self._issued = False
+        self._issued_pmap = False
+        self._last_prefetched = 0
         self._layer_objs = {}
         torch.cuda.synchronize(device)
 
@@ -108,14 +127,23 @@ class ExpertStreamer:
             if swaps:
                 self._apply_swaps(swaps)
                 self.stats.repin_swaps += len(swaps)
-        if not self.prefetch:
+                if self.prefetch and self.prefetch_min_hit > 0:   # what is cold changed: probe again
+                    self._prefetch_on = True
+                    self._probe_left = self.prefetch_probe
+                    self._probe_slabs = self._probe_hits = 0
+        if not self._prefetch_on:
+            if self._issued_pmap:   # the arena holds nothing this token: no slot may read it
+                self.pmap.fill_(-1)
+                self._issued_pmap = False
             return
         pmap, pf = self.res.prefetch_plan(prev_ids)
+        self._issued_pmap = True
         self.pmap.copy_(torch.from_numpy(pmap.view(np.int32)))   # before this token's kernels (same stream)
         cur = torch.cuda.current_stream(self.device)
         self.side.wait_stream(cur)          # the previous token no longer reads the arena, the pmap is in place
         self.ev_copy0.record(self.side)
         srcs = [None, None, None]
+        self._last_prefetched = 0
         for l in range(self.n_layers):
             ids = pf[l, : self.k]
             n = int((ids >= 0).sum())
@@ -124,9 +152,11 @@ class ExpertStreamer:
                 ops.gather_slabs_async(srcs, list(self.slabs), self.arena, list(self.slabs), ids.tolist(), l, self.k,
                                        stream=self.side, n_expert=self.E)
                 self.stats.prefetched_slabs += n
+                self._last_prefetched += n
             self.ev_layer[l].record(self.side)
         self.ev_copy1.record(self.side)
         self._issued = True
+        self.stats.prefetch_tokens += 1
 
     def wait_layer(self, l: int) -> None:
         """Order layer l's kernels after its prefetch copies."""
@@ -142,8 +172,16 @@ class ExpertStreamer:
         blk = ids.reshape(self.n_layers, 64)
         arena_rows = blk[:, 32:32 + self.k]
         full_rows = blk[:, 48:48 + self.k]
-        self.stats.prefetch_hits += int((arena_rows >= 0).sum())
+        hits = int((arena_rows >= 0).sum())
+        self.stats.prefetch_hits += hits
         self.stats.inplace_reads += int((full_rows >= 0).sum())
+        if self._issued and self.prefetch_min_hit > 0 and self._probe_left > 0:
+            self._probe_hits += hits
+            self._probe_slabs += self._last_prefetched
+            self._probe_left -= 1
+            if self._probe_left == 0 and self._probe_hits < self.prefetch_min_hit * max(self._probe_slabs, 1):
+                self._prefetch_on = False
+                self.stats.prefetch_off_at = self.stats.tokens
         for l in range(self.n_layers):
             self.stats.cold_by_layer[l] += int(cold[l])
         if self._issued:
@@ -172,4 +210,5 @@ class ExpertStreamer:
                 "prefetch_hits": s.prefetch_hits, "inplace_reads": s.inplace_reads,
                 "prefetched_MiB_per_tok": s.prefetched_slabs * slab3 / per_tok / 2 ** 20,
                 "inplace_MiB_per_tok": s.inplace_reads * slab3 / per_tok / 2 ** 20,
-                "repin_swaps": s.repin_swaps, "cold_by_layer": glyphs, "pinned_slabs": self.n_pinned}
+                "repin_swaps": s.repin_swaps, "cold_by_layer": glyphs, "pinned_slabs": self.n_pinned,
+                "prefetch_tokens": s.prefetch_tokens, "prefetch_off_at": s.prefetch_off_at}

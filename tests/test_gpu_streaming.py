@@ -87,3 +87,61 @@ def test_cold_tier_in_host_memory_with_prefetch():
     assert np.max(np.abs(x_st - x_dev)) <= 1e-5 * scale
     for h in hosts:
         h.free()
+
+
+@pytest.mark.parametrize("min_hit,want_tokens", [(0.0, 5), (1.01, 2)], ids=["always", "switched-off"])
+def test_streamer_prefetch_is_switched_off_when_it_does_not_pay(min_hit, want_tokens):
+    """The streamer's adaptive prefetch: with a hit rate that no probe can
+    reach, the prefetch runs for the probe window (2 tokens) and then stops;
+    results match the all-HBM ones every token, whatever the prefetch does."""
+    from styx_b200.streaming import ExpertStreamer
+    L, H, F, E, k = 2, 512, 256, 16, 4
+    cases = [make_case(90 + l, H, F, E, k, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K)) for l in range(L)]
+    slabs = cases[0].slabs
+    hbs = []
+    host = []
+    for c in cases:
+        trio = []
+        for a in (c.gate, c.up, c.down):
+            hb = _host(a)
+            hbs.append(hb)
+            trio.append(hb.tensor)
+        host.append(tuple(trio))
+    hist = (np.repeat(np.arange(L, dtype=np.int32), E), np.tile(np.arange(E, dtype=np.int32), L),
+            np.tile(np.arange(E, 0, -1).astype(np.uint64), L))
+    budget = 2 * L * int(sum(slabs))   # two experts of each layer in HBM
+    st = ExpertStreamer(ops.Dims(H, F, E, k), L, cases[0].qts, slabs, host, hist, budget, device=0,
+                        prefetch=True, prefetch_min_hit=min_hit, prefetch_probe=2)
+    layers = [st.layer_weights(l, _t(cases[l].norm), _t(cases[l].router)) for l in range(L)]
+    dev_layers = [ops.LayerWeights(_t(c.norm), _t(c.router), ops.Experts(c.qts[0], _t(c.gate), slabs[0]),
+                                   ops.Experts(c.qts[1], _t(c.up), slabs[1]), ops.Experts(c.qts[2], _t(c.down), slabs[2]))
+                  for c in cases]
+    blk = ops.MoeBlock(ops.Dims(H, F, E, k), 0)
+    rng = np.random.default_rng(5)
+    prev = None
+    try:
+        for t in range(6):
+            x0 = rng.normal(0, 1, H).astype(np.float32)
+            st.before_token(t, prev, layers)
+            x = _t(x0)
+            ids = torch.zeros(L * 64, dtype=torch.int32, device=DEV)
+            for l in range(L):
+                st.wait_layer(l)
+                blk.forward(x, layers[l], l, ids)
+            prev = ids.cpu().numpy()
+            st.after_token(prev)
+            xr = _t(x0)
+            ids_r = torch.zeros(L * 64, dtype=torch.int32, device=DEV)
+            for l in range(L):
+                blk.forward(xr, dev_layers[l], l, ids_r)
+            torch.cuda.synchronize()
+            blk.ctx.check_device_error()
+            a, b = x.cpu().numpy(), xr.cpu().numpy()   # host-read form against the all-HBM kernel
+            assert np.max(np.abs(a - b)) <= 1e-5 * np.max(np.abs(b)), t
+        hud = st.hud()
+        assert hud["prefetch_tokens"] == want_tokens
+        assert hud["prefetch_off_at"] == (-1 if min_hit == 0 else 3)
+    finally:
+        torch.cuda.synchronize()
+        for hb in hbs:
+            hb.free()
