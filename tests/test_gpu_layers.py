@@ -19,6 +19,12 @@ DEV = "cuda:0"
 GEN_OFFSET = 128
 SEPARATE, PERSISTENT, CHAIN = 0, 1, 2
 PATH = {CHAIN: 5, PERSISTENT: 4, SEPARATE: 1}
+
+
+def path_ok(mode, got):
+    """One call per layer takes the cluster form (6) where the device holds
+    its k clusters at once, else the single kernel (1)."""
+    return got in (1, 6) if mode == SEPARATE else got == PATH[mode]
 MODES = pytest.mark.parametrize("mode", [CHAIN, PERSISTENT], ids=["chain", "persistent"])
 
 
@@ -76,7 +82,7 @@ def _run_both(cases, first_layer, reps, lws, c0, n, k, one, many, total, exclusi
 def test_linked_layers_equal_one_call_per_layer_and_the_oracle(mode):
     cases = [make_case(90 + l, 1024, 512, 32, 8, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K)) for l in range(5)]
     many, x, _ = run_both(cases, first_layer=3, mode=mode)
-    assert many.ctx.last_moe_path() == PATH[mode]
+    assert path_ok(mode, many.ctx.last_moe_path())
     xr = cases[0].x.copy()
     for c in cases:
         xr = oracle_block(dataclasses.replace(c, x=xr))["x"]
@@ -89,7 +95,7 @@ def test_plain_launches_equal_cooperative_ones(mode):
     attribute give the same bits."""
     cases = [make_case(150 + l, 2048, 768, 128, 8, (_lib.Q4_K, _lib.Q4_K, _lib.Q6_K)) for l in range(3)]
     many, _, _ = run_both(cases, mode=mode, exclusive=1)
-    assert many.ctx.last_moe_path() == PATH[mode]
+    assert path_ok(mode, many.ctx.last_moe_path())
 
 
 @MODES
@@ -98,7 +104,7 @@ def test_more_layers_than_one_launch_holds(mode):
     cases = [make_case(200 + l, 512, 256, 8, 2, (_lib.Q8_0, _lib.Q8_0, _lib.Q8_0), sigma=0.01)
              for l in range(83)]
     many, _, _ = run_both(cases, reps=1, mode=mode)
-    assert many.ctx.last_moe_path() == PATH[mode]
+    assert path_ok(mode, many.ctx.last_moe_path())
 
 
 @MODES
@@ -109,7 +115,7 @@ def test_mixed_formats(mode):
              make_case(301, 1024, 512, 16, 4, (_lib.Q4_K, _lib.Q4_K, _lib.Q4_K)),
              make_case(302, 1024, 512, 16, 4, (_lib.Q5_K, _lib.Q5_K, _lib.Q5_K))]
     many, _, _ = run_both(cases, reps=1, mode=mode)
-    assert many.ctx.last_moe_path() == (5 if mode == CHAIN else 1)
+    assert path_ok(CHAIN if mode == CHAIN else SEPARATE, many.ctx.last_moe_path())
 
 
 def test_chained_layers_replayed_from_a_graph():
