@@ -419,6 +419,8 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
     model = decode_model(local, L, ctx, world, rank, allreduce)
     blk_ctx = model.moe.ctx
     blk_ctx.set_option(_lib.OPT_EXCLUSIVE, 0 if args.shared_device else 1)
+    blk_ctx.set_option(_lib.OPT_ATTN_KERNELS, args.attn_kernels)
+    blk_ctx.set_option(_lib.OPT_MOE_KERNELS, args.moe_kernels)
     lib, cx = _lib.lib(), blk_ctx.handle
     stream = torch.cuda.Stream(device=dev)
     sp = C.c_void_p(stream.cuda_stream)
@@ -952,6 +954,10 @@ def main() -> int:
                     help="cfg4: the prefetch stays on while at least this share of prefetched slabs is used (0: always)")
     ap.add_argument("--no-prefetch", action="store_true", help="cfg4: no next-token prefetch")
     ap.add_argument("--batch", type=int, default=8, help="batch: tokens per step (1..64)")
+    ap.add_argument("--moe-kernels", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="STYX_OPT_MOE_KERNELS: 0 auto, 1 single cooperative kernel, 2 three kernels, 3 cluster form")
+    ap.add_argument("--attn-kernels", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="decode: STYX_OPT_ATTN_KERNELS: 0 auto, 1 cooperative kernel, 2 seven kernels, 3 cluster form")
     ap.add_argument("--shape", default="cfg2", choices=["cfg2", "cfg5"],
                     help="cfg3 / batch workloads: the 30B-A3B MoE layer (cfg2, 48 layers) or configs[4]'s "
                          "235B-A22B layer (cfg5: H 4096, F 1536, every matrix q4_K, 94 layers)")
@@ -1001,6 +1007,7 @@ def main() -> int:
 
     blk.ctx.set_option(_lib.OPT_MOE_LAYERS, {"block": 0, "layers": 1, "chain": 2}[args.launch])
     blk.ctx.set_option(_lib.OPT_EXCLUSIVE, 0 if args.shared_device else 1)
+    blk.ctx.set_option(_lib.OPT_MOE_KERNELS, args.moe_kernels)
 
     def moe_layers():
         if args.launch != "block":
