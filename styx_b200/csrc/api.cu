@@ -1874,7 +1874,8 @@ bool plan_attn_fused(const styx_attn_dims &d, const styx_attn_layer &lw, int sms
     a.off_w1 = static_cast<uint32_t>(a128(a.off_f32 + static_cast<size_t>(dmax) * 4));
     a.off_w2 = static_cast<uint32_t>(a128(a.off_w1 + std::max(w1_rows, w1_attn)));
     a.off_kv = static_cast<uint32_t>(a128(a.off_w2 + w2));
-    const size_t total = a.off_kv + 2 * static_cast<size_t>(styx::kPreRows) * hd * 4;
+    a.off_rope = static_cast<uint32_t>(a128(a.off_kv + 2 * static_cast<size_t>(styx::kPreRows) * hd * 4));
+    const size_t total = a.off_rope + static_cast<size_t>(hd / 2) * 16;   // the RoPE table (double cos, sin)
     if (total > 227 * 1024) return false;
     smem = static_cast<uint32_t>(total);
     return true;

@@ -199,6 +199,20 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
         *s_tag = static_cast<uint32_t>(atomicAdd(p.gen, 1ull) / static_cast<unsigned long long>(G)) + 1u;
         *s_ok = 1;
     }
+    // the RoPE table of this token's position (theta_i = pos * theta_scale^i,
+    // in double) and the norm weights: neither depends on the previous grid,
+    // so they are ready before it ends (warps 2-3 and one float4 per thread)
+    double2 *rope_t = reinterpret_cast<double2 *>(smem + p.off_rope);   // [64] (cos, sin)
+    if (tid >= 64 && tid < 64 + kHD / 2) {
+        const int i = tid - 64;
+        const double th = static_cast<double>(p.n_t - 1) * pow(p.theta_scale, static_cast<double>(i));
+        double sn, cs;
+        sincos(th, &sn, &cs);
+        rope_t[i] = make_double2(cs, sn);
+    }
+    const int H4 = H >> 2;
+    float4 wn = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tid < H4) wn = __ldg(reinterpret_cast<const float4 *>(p.attn_norm) + tid);
     pdl_trigger();
     pdl_wait();
     __syncthreads();
@@ -222,19 +236,28 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
     cp_async_commit();
 
     // ------------------------------------------------ phase A: x -> RMSNorm -> digits
-    float ss = 0.f;
-    for (int i = tid; i < H; i += kAF) {
-        const float v = __ldcg(p.x + i);
-        fst[i] = v;
-        ss += v * v;
-    }
-    ss = af_block_sum(ss, red);
+    // (H <= 2048: at most one float4 of x per thread)
+    float4 xr = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tid < H4) xr = __ldcg(reinterpret_cast<const float4 *>(p.x) + tid);
+    const float ss = af_block_sum(xr.x * xr.x + xr.y * xr.y + xr.z * xr.z + xr.w * xr.w, red);
     const float scale = 1.0f / sqrtf(ss / static_cast<float>(H) + p.eps);
-    for (int i = tid; i < H; i += kAF) fst[i] = fst[i] * scale * p.attn_norm[i];
+    if (tid < H4)
+        reinterpret_cast<float4 *>(fst)[tid] = make_float4(xr.x * scale * wn.x, xr.y * scale * wn.y,
+                                                           xr.z * scale * wn.z, xr.w * scale * wn.w);
     __syncthreads();
-    {
+    {   // four groups' shuffle chains together
         const DigitsView dv{dg1, dg2, dg3, dsc};
-        for (int g = warp; g < (H >> 5); g += kAFWarps) digits_group_warp(fst[g * 32 + lane], lane, dv, g);
+        for (int g0 = warp; g0 < (H >> 5); g0 += 4 * kAFWarps) {
+            float v[4];
+            int gi[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int g = g0 + j * kAFWarps;
+                gi[j] = g < (H >> 5) ? g : -1;
+                v[j] = g < (H >> 5) ? fst[g * 32 + lane] : 0.f;
+            }
+            digits_groups_warp<4>(v, gi, lane, dv);
+        }
     }
     __syncthreads();
     AF_STAMP(2);
@@ -298,8 +321,8 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
         float *sq = reinterpret_cast<float *>(w1);                 // [gqa][128] q heads
         float *sk = sq + gqa * kHD;                                // [128] k (row pos)
         float *sv = sk + kHD;                                      // [128] v (row pos)
-        double2 *rope = reinterpret_cast<double2 *>(sv + kHD);     // [64] (cos, sin)
-        float *ssc = reinterpret_cast<float *>(rope + kHD / 2);    // [tps][gqa]
+        const double2 *rope = rope_t;                              // [64] (cos, sin), computed at entry
+        float *ssc = sv + 3 * kHD;                                 // [tps][gqa] (a table-sized gap after v)
         float *sml = ssc + p.tps * gqa;                            // [gqa][2]
         float *sacc = sml + ((2 * gqa + 3) & ~3);                  // [8][8][128]
         // wait for the gqa q heads, k head and v head of kvh (lanes of warp 0)
@@ -311,12 +334,6 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
             }
             fine = __all_sync(0xffffffffu, fine);
             if (lane == 0 && !fine) *s_ok = 0;
-        }
-        if (tid < kHD / 2) {   // RoPE table: theta_i = pos * theta_scale^i, in double
-            const double th = static_cast<double>(p.n_t - 1) * pow(p.theta_scale, static_cast<double>(tid));
-            double sn, cs;
-            sincos(th, &sn, &cs);
-            rope[tid] = make_double2(cs, sn);
         }
         __syncthreads();
         AF_STAMP(5);

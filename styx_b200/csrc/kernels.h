@@ -289,7 +289,7 @@ struct AttnFusedArgs {
     unsigned long long *gen, *head_cnt, *split_cnt, *att_cnt;   // zero at workspace init
     int *err;
     long long *trace;                  // STYX_OPT_TRACE: clock64 stamps [CTA][16], else null
-    uint32_t off_dig, off_f32, off_w1, off_w2, off_kv;
+    uint32_t off_dig, off_f32, off_w1, off_w2, off_kv, off_rope;
 };
 constexpr int kAttnTraceStamps = 16;
 constexpr int kPreRows = 32;   // cache rows of K and of V a CTA prefetches (async copies)

@@ -431,12 +431,25 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1) k_down(const DownArgs p) {
             const uint8_t *base = stages + static_cast<size_t>(st) * p.stage_bytes +
                                   static_cast<size_t>(s) * p.slot_stride +
                                   (src ? (reinterpret_cast<uintptr_t>(src + static_cast<size_t>(r0) * p.rb) & 15) : 0);
-            for (int t = sub * rpw; t < n; t += nwps * rpw) {
+            // two rows per lane group per pass when the unit's digits stay in
+            // registers: independent dot products in flight
+            for (int t = sub * rpw; preload && t < n; t += 2 * nwps * rpw) {
+                const int ra = t + grp, rb = t + nwps * rpw + grp;
+                float va = 0.f, vb = 0.f;
+                if (src && active && ra < n) va = unit_dot<QT>(base + static_cast<size_t>(ra) * p.rb, ug, x);
+                if (src && active && rb < n) vb = unit_dot<QT>(base + static_cast<size_t>(rb) * p.rb, ug, x);
+                __syncwarp();   // regroup the lanes after the row-bound branches
+                for (int o = p.gs >> 1; o; o >>= 1) {
+                    va += __shfl_xor_sync(0xffffffffu, va, o);
+                    vb += __shfl_xor_sync(0xffffffffu, vb, o);
+                }
+                if (ug == 0 && ra < n) part[s * p.rc + ra] = va;
+                if (ug == 0 && rb < n) part[s * p.rc + rb] = vb;
+            }
+            for (int t = sub * rpw; !preload && t < n; t += nwps * rpw) {
                 const int row = t + grp;
                 float v = 0.f;
-                if (preload) {
-                    if (src && active && row < n) v = unit_dot<QT>(base + static_cast<size_t>(row) * p.rb, ug, x);
-                } else if (src && row < n) {
+                if (src && row < n) {
                     for (int u = ug; u < p.units; u += p.gs) {
                         load_xunit<QT>(x, hd1 + s * p.F, hd2 + s * p.F, hd3 + s * p.F, hsc + s * (p.F >> 5), u);
                         v += unit_dot<QT>(base + static_cast<size_t>(row) * p.rb, u, x);
