@@ -474,30 +474,49 @@ __global__ void __launch_bounds__(kAF, 1) k_attn_fused(const __grid_constant__ A
         __syncthreads();
         AF_STAMP(8);
         const float *ml = p.part_ml + static_cast<size_t>(b) * S * 2;
-        float m = -INFINITY;
-        for (int s = tid; s < S; s += kAF) m = fmaxf(m, __ldcg(ml + 2 * s));
-        m = af_warp_max(m);
+        // every load of the merge in flight at once: thread s < S its split's
+        // (max, sum) pair (S <= kAttnMaxSplits < kAF), and thread (c, q) the
+        // partials of column c for splits q, q+4, .. (the first kMergeRegs
+        // of them into registers)
+        const float *acc = p.part_acc + static_cast<size_t>(b) * S * kHD;
+        const int c = tid & (kHD - 1), q = tid >> 7;
+        constexpr int kMergeRegs = 16;
+        float av[kMergeRegs];
+#pragma unroll
+        for (int i = 0; i < kMergeRegs; i++) {
+            const int s = q + (kAF / kHD) * i;
+            av[i] = s < S ? __ldcg(acc + static_cast<size_t>(s) * kHD + c) : 0.f;
+        }
+        float mv = -INFINITY, lv = 0.f;
+        if (tid < S) {
+            mv = __ldcg(ml + 2 * tid);
+            lv = __ldcg(ml + 2 * tid + 1);
+        }
+        const float m = af_warp_max(mv);
         if (lane == 0) red[warp] = m;
         __syncthreads();
         float M = -INFINITY;
         for (int i = 0; i < kAFWarps; i++) M = fmaxf(M, red[i]);
         __syncthreads();
         float l = 0.f;
-        for (int s = tid; s < S; s += kAF) {
-            const float ws = expf(__ldcg(ml + 2 * s) - M);
-            w[s] = ws;
-            l += ws * __ldcg(ml + 2 * s + 1);
+        if (tid < S) {
+            const float ws = expf(mv - M);
+            w[tid] = ws;
+            l += ws * lv;
         }
         const float L = af_block_sum(l, red);
         const float inv = 1.0f / L;
-        // column c = tid % 128 summed by four threads (splits q, q+4, ..),
-        // then the four partials in order
-        const float *acc = p.part_acc + static_cast<size_t>(b) * S * kHD;
+        // column c summed by four threads (splits q, q+4, ..), then the four
+        // partials in order
         {
-            const int c = tid & (kHD - 1), q = tid >> 7;
             float o = 0.f;
-#pragma unroll 4
-            for (int s = q; s < S; s += kAF / kHD) o += w[s] * __ldcg(acc + static_cast<size_t>(s) * kHD + c);
+#pragma unroll
+            for (int i = 0; i < kMergeRegs; i++) {
+                const int s = q + (kAF / kHD) * i;
+                if (s < S) o += w[s] * av[i];
+            }
+            for (int s = q + (kAF / kHD) * kMergeRegs; s < S; s += kAF / kHD)
+                o += w[s] * __ldcg(acc + static_cast<size_t>(s) * kHD + c);
             fst[q * kHD + c] = o;
         }
         __syncthreads();
