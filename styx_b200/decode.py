@@ -7,9 +7,13 @@ Per token: the embedding row (styx_get_rows), then per layer the attention
 half (styx_attn_block: RMSNorm, q/k/v, per-head norms, RoPE, the KV cache
 row, attention, o, residual) and the MoE block (styx_moe_block), then the
 output norm, the LM head GEMV and the greedy pick on the device
-(styx_argmax_f32).  The KV caches are allocated once for n_ctx positions
-(the reference grows them page by page, moe.rs:1802-1822; the result is the
-same).
+(styx_argmax_f32).  The KV caches hold n_ctx positions at most: allocated
+once (kv_page 0), or grown page by page as the reference does
+(moe.rs:501-503, 1802-1822: pages of KV_PAGE_TOKENS = 512 rows, every
+layer's caches reallocated one page larger and the filled rows copied over
+-- here a device-to-device copy on the stream instead of a host round trip);
+the attention reads the same rows either way, so the results are the same
+bits.
 
 Expert parallelism (`allreduce` given): every rank runs the whole step on
 the same token with the same dense weights, but holds only its own experts
@@ -54,16 +58,18 @@ class DecodeLayer:
 
 class DecodeModel:
     def __init__(self, hp: DecodeParams, embd: ops.DenseWeight, layers: list, output_norm: torch.Tensor,
-                 head: ops.DenseWeight, n_ctx: int, device: int = 0, allreduce=None):
+                 head: ops.DenseWeight, n_ctx: int, device: int = 0, allreduce=None, kv_page: int = 0):
         self.hp, self.embd, self.layers, self.output_norm, self.head = hp, embd, layers, output_norm, head
-        self.n_ctx = n_ctx
+        self.n_ctx = n_ctx            # n_ctx_max: positions the caches may grow to
+        self.kv_page = kv_page        # 0: allocated once for n_ctx rows; else rows per page
         dev = f"cuda:{device}"
         self.attn = ops.AttnBlock(hp.n_embd, hp.n_heads, hp.n_kv_heads, hp.head_dim, hp.qk_norm, hp.rms_eps,
                                   hp.rope_base, device)
         self.moe = ops.MoeBlock(ops.Dims(hp.n_embd, hp.n_ff, hp.n_expert, hp.n_expert_used, hp.norm_topk,
                                          hp.rms_eps), device)
         kv_dim = hp.n_kv_heads * hp.head_dim
-        self.kcache = torch.zeros(hp.n_layers, n_ctx, kv_dim, dtype=torch.float32, device=dev)
+        self.cap = min(n_ctx, kv_page) if kv_page > 0 else n_ctx   # rows the caches hold now
+        self.kcache = torch.zeros(hp.n_layers, self.cap, kv_dim, dtype=torch.float32, device=dev)
         self.vcache = torch.zeros_like(self.kcache)
         self.x = torch.empty(hp.n_embd, dtype=torch.float32, device=dev)
         self.xn = torch.empty_like(self.x)
@@ -78,6 +84,18 @@ class DecodeModel:
         self.allreduce = allreduce
         self.partial = torch.zeros(hp.n_expert_used * hp.n_embd, dtype=torch.float32, device=dev)
 
+    def _grow(self) -> None:
+        """One page more for every layer's K and V caches (moe.rs:1802-1822):
+        new buffers, the filled rows copied, the old ones released (on the
+        current stream, so the copy is ordered after every earlier step)."""
+        cap = min(self.n_ctx, self.cap + self.kv_page)
+        for name in ("kcache", "vcache"):
+            old = getattr(self, name)
+            new = torch.zeros(old.shape[0], cap, old.shape[2], dtype=old.dtype, device=old.device)
+            new[:, :self.cap].copy_(old)
+            setattr(self, name, new)
+        self.cap = cap
+
     def reset(self) -> None:
         self.n_past = 0
 
@@ -87,6 +105,8 @@ class DecodeModel:
         if self.n_past >= self.n_ctx:
             raise ValueError(f"KV caches full ({self.n_ctx})")
         with torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext():
+            if self.n_past >= self.cap:
+                self._grow()
             self.tok.fill_(token)
             self.pos.fill_(self.n_past)
         self.step(stream)
@@ -101,7 +121,7 @@ class DecodeModel:
         hp, pos = self.hp, self.n_past
         ops.get_rows(self.embd.qtype, self.embd.data, hp.n_vocab, hp.n_embd, self.tok, out=self.x, stream=stream)
         for li, ly in enumerate(self.layers):
-            self.attn.forward(self.x, ly.attn, pos, self.pos, self.kcache[li], self.vcache[li], self.n_ctx,
+            self.attn.forward(self.x, ly.attn, pos, self.pos, self.kcache[li], self.vcache[li], self.cap,
                               stream=stream)
             if self.allreduce is None:
                 self.moe.forward(self.x, ly.moe, li, self.ids, stream=stream)

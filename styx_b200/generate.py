@@ -2,7 +2,7 @@
 (crates/model/examples/generate_moe.rs) on the library's decode step.
 
     python -m styx_b200.generate MODEL.gguf --prompt 1,2,3 -n 32 [--ctx 4096]
-                                 [--experts-in-host] [--device 0]
+                                 [--kv-page 512] [--experts-in-host] [--device 0]
 
 Token ids in, token ids out (the reference example reads and prints ids the
 same way when no tokenizer is given); prefill and decode rates are printed
@@ -20,7 +20,9 @@ def main(argv=None) -> int:
     ap.add_argument("model")
     ap.add_argument("--prompt", required=True, help="comma-separated token ids")
     ap.add_argument("-n", "--n-predict", type=int, default=32)
-    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--ctx", type=int, default=4096, help="n_ctx_max: positions the KV caches may hold")
+    ap.add_argument("--kv-page", type=int, default=512,
+                    help="KV cache rows per page, grown on demand (moe.rs:501-503); 0 allocates --ctx rows at once")
     ap.add_argument("--experts-in-host", action="store_true",
                     help="expert tensors in pinned host memory, read in place")
     ap.add_argument("--device", type=int, default=0)
@@ -32,7 +34,7 @@ def main(argv=None) -> int:
     torch.cuda.set_device(args.device)
     prompt = [int(t) for t in args.prompt.split(",") if t.strip()]
     g = G.Gguf.open(args.model)
-    model, keep = G.load_decode_model(g, args.ctx, args.device, args.experts_in_host)
+    model, keep = G.load_decode_model(g, args.ctx, args.device, args.experts_in_host, kv_page=args.kv_page)
     g.close()
     t0 = time.perf_counter()
     for t in prompt:

@@ -444,12 +444,13 @@ def decode_params(g: Gguf):
                         g.has_tensor("blk.0.attn_q_norm.weight"))
 
 
-def load_decode_model(g: Gguf, n_ctx: int, device: int = 0, experts_in_host: bool = False):
+def load_decode_model(g: Gguf, n_ctx: int, device: int = 0, experts_in_host: bool = False, kv_page: int = 0):
     """A DecodeModel (styx_b200.decode) from a model file, as MoeModel::load
     uploads it (moe.rs:996-1108): token_embd (the embedding rows), per layer
     attn_norm, attn_q / attn_k / attn_v / attn_output, attn_q_norm /
     attn_k_norm when present and the MoE block's tensors, then output_norm
-    and output (the LM head).  Returns (model, host buffers to keep)."""
+    and output (the LM head).  kv_page > 0 grows the KV caches page by page
+    up to n_ctx (moe.rs:1802-1822).  Returns (model, host buffers to keep)."""
     import torch
 
     from . import ops
@@ -482,7 +483,7 @@ def load_decode_model(g: Gguf, n_ctx: int, device: int = 0, experts_in_host: boo
                                k_norm=f32(n("attn_k_norm"), hp.head_dim) if hp.qk_norm else None)
         layers.append(DecodeLayer(attn, moe))
     model = DecodeModel(hp, dense("token_embd.weight", hp.n_vocab, H), layers, f32("output_norm.weight", H),
-                        dense("output.weight", hp.n_vocab, H), n_ctx, device)
+                        dense("output.weight", hp.n_vocab, H), n_ctx, device, kv_page=kv_page)
     return model, keep
 
 

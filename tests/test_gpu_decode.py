@@ -27,7 +27,7 @@ def rel_to_max(got, exp):
     return float(np.max(np.abs(got - exp)) / max(np.max(np.abs(exp)), 1e-30))
 
 
-def gpu_model(m, n_ctx):
+def gpu_model(m, n_ctx, kv_page=0):
     hp = m.hp
     H, F, E = hp["n_embd"], hp["n_ff"], hp["n_expert"]
     layers = []
@@ -43,7 +43,7 @@ def gpu_model(m, n_ctx):
     p = DecodeParams(hp["n_layers"], H, hp["n_heads"], hp["n_kv_heads"], hp["head_dim"], F, E,
                      hp["n_expert_used"], hp["n_vocab"], hp["rms_eps"], hp["rope_base"])
     return DecodeModel(p, ops.DenseWeight(Q4_K, T(m.embd)), layers, T(m.output_norm),
-                       ops.DenseWeight(Q6_K, T(m.head)), n_ctx)
+                       ops.DenseWeight(Q6_K, T(m.head)), n_ctx, kv_page=kv_page)
 
 
 @pytest.mark.parametrize("seed,cfg", [(0, {}), (1, {}), (2, dict(hd=128, n_heads=8, n_kv=2))],
@@ -121,3 +121,25 @@ def test_argmax_total_order_last_of_equals():
     assert int(ops.argmax_f32(T(x)).item()) == 1
     x = np.array([np.inf, np.nan, 1.0], np.float32)
     assert int(ops.argmax_f32(T(x)).item()) == total_cmp_argmax_last(x) == 1
+
+
+@pytest.mark.parametrize("page", [4, 7])
+def test_paged_kv_cache_gives_the_same_bits(page):
+    """KV caches grown page by page (moe.rs:1802-1822: reallocated one page
+    larger, the filled rows copied) against caches allocated once: every
+    step's hidden state, logits and greedy pick are the same bits, across
+    several page boundaries."""
+    m = make_model(3, hd=128, n_heads=8, n_kv=2)
+    n_ctx, toks = 32, [5, 17, 99, 3, 250, 11, 42, 7, 8, 900, 1, 77, 64, 31, 2]
+    flat = gpu_model(m, n_ctx)
+    paged = gpu_model(m, n_ctx, kv_page=page)
+    assert paged.cap == page
+    for t in toks:
+        flat.forward_token(t)
+        paged.forward_token(t)
+        torch.cuda.synchronize()
+        assert np.array_equal(flat.x.cpu().numpy().view(np.uint32), paged.x.cpu().numpy().view(np.uint32))
+        assert np.array_equal(flat.logits.cpu().numpy().view(np.uint32), paged.logits.cpu().numpy().view(np.uint32))
+        assert int(flat.next.item()) == int(paged.next.item())
+    assert paged.cap == min(n_ctx, page * -(-len(toks) // page)) and paged.kcache.shape[1] == paged.cap
+    assert np.array_equal(paged.kcache.cpu().numpy(), flat.kcache[:, :paged.cap].cpu().numpy())
