@@ -9,8 +9,10 @@ norm, LM head (151,936 x 2048 q6_K), greedy pick -- with --ctx cache rows
 already filled, batch 1.  Every expert resident in HBM (18.8 GB); router
 rows carry a Zipf(1.1) popularity bias.  Synthetic data, generated on the
 device.  At N > 1 (torchrun) the same sequence runs with its experts split
-over the ranks (expert parallelism, e % N == rank) and one NCCL all-reduce
-of the k x H slot buffer per layer: strong scaling of one sequence.
+over the ranks (expert parallelism, e % N == rank) and one cross-rank sum
+of the k x H slot buffer per layer (--ep-comm p2p: one kernel that pushes
+the slots over NVLink peer memory and combines; nccl: an NCCL all-reduce):
+strong scaling of one sequence.
 
 `value`: tokens/s, device-timed with CUDA events (a CUDA graph at N = 1).
 `e2e`: a greedy chain through the C ABI with host buffers (token id in,
@@ -232,7 +234,7 @@ def run_reference(args, rank: int) -> int:
         sample = (f"per step one layer of the whole decode step (attention half at {ctx} cache rows, one thread; "
                   f"MoE block, {nth} threads) and 1/48 of the LM head ({head_rows} q6_K rows), i.e. 1/48 of a "
                   f"token; scaled to the token")
-        workload = decode_config(args.layers, ctx, int(os.environ.get("WORLD_SIZE", "1")))
+        workload = decode_config(args.layers, ctx, int(os.environ.get("WORLD_SIZE", "1")), args.ep_comm)
         metric = METRIC
     else:
         def step(i):
@@ -340,19 +342,21 @@ def ep_moe_layers(dev: int, n_layers: int, world: int, rank: int, unique: int = 
     return layers
 
 
-def decode_config(L: int, ctx: int, world: int) -> dict:
+def decode_config(L: int, ctx: int, world: int, comm: str = "p2p") -> dict:
     """The decode workload's config (both arms)."""
     return {"workload": f"whole decode step at the 30B-A3B shape (configs[2]): embedding row, {L} x "
                         f"(attention {N_HEADS}q/{N_KV}kv x {HD} + MoE block H{H} E{E} top{K_TOP} F{F}, "
                         f"gate/up q4_K, down q6_K), LM head {N_VOCAB} x {H} q6_K, greedy pick; batch 1; "
                         f"{ctx} cache rows before the token",
             "ctx": ctx, "global_batch": 1,
-            "parallelism": (f"expert-parallel x{world}: experts e % {world} == rank, one NCCL all-reduce "
-                            f"of the {K_TOP} x {H} slot buffer per layer" if world > 1 else "single"),
+            "parallelism": (f"expert-parallel x{world}: experts e % {world} == rank, per layer one cross-rank "
+                            f"sum of the {K_TOP} x {H} slot buffer ("
+                            + ("one kernel over NVLink peer memory" if comm == "p2p" else "NCCL all-reduce") + ")"
+                            if world > 1 else "single"),
             "l2": "inputs larger than L2 (%.2f GB read per token)" % (decode_bytes_per_token(L, ctx) / 1e9)}
 
 
-def decode_model(local: int, L: int, ctx: int, world: int, rank: int, allreduce=None):
+def decode_model(local: int, L: int, ctx: int, world: int, rank: int, allreduce=None, ep_comm=None):
     """The 30B-shaped decode model with random weights: attention q/k/o q4_K,
     v q6_K (four generated layer bases, copied to every layer), the MoE
     layers (every expert at world 1, this rank's experts under expert
@@ -380,7 +384,7 @@ def decode_model(local: int, L: int, ctx: int, world: int, rank: int, allreduce=
     embd = ops.DenseWeight(Q4_K, ops.synth_quant(Q4_K, N_VOCAB, H, 3000, 0.5, device=local))
     head = ops.DenseWeight(Q6_K, ops.synth_quant(Q6_K, N_VOCAB, H, 3001, 0.02, device=local))
     p = DecodeParams(L, H, N_HEADS, N_KV, HD, F, E, K_TOP, N_VOCAB)
-    model = DecodeModel(p, embd, layers, ones(H), head, ctx + 1, local, allreduce=allreduce)
+    model = DecodeModel(p, embd, layers, ones(H), head, ctx + 1, local, allreduce=allreduce, ep_comm=ep_comm)
     model.kcache[:, :ctx].copy_(ops.synth_f32(L * ctx * kvd, 4000, 0, 1.0, device=local).view(L, ctx, kvd))
     model.vcache[:, :ctx].copy_(ops.synth_f32(L * ctx * kvd, 4001, 0, 1.0, device=local).view(L, ctx, kvd))
     model.n_past = ctx
@@ -415,8 +419,13 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device(dev))
         pg = dist
     L, ctx = args.layers, args.ctx
-    allreduce = (lambda t: pg.all_reduce(t)) if pg else None
-    model = decode_model(local, L, ctx, world, rank, allreduce)
+    p2p = pg is not None and args.ep_comm == "p2p"
+    ep_comm = None
+    if p2p:   # the cross-rank sum and the combine as one kernel over NVLink peer memory
+        ep_comm = ops.EpComm(rank, world, K_TOP, H, local)
+        ep_comm.connect_with(pg)
+    allreduce = (lambda t: pg.all_reduce(t)) if pg and not p2p else None
+    model = decode_model(local, L, ctx, world, rank, allreduce, ep_comm)
     blk_ctx = model.moe.ctx
     blk_ctx.set_option(_lib.OPT_EXCLUSIVE, 0 if args.shared_device else 1)
     blk_ctx.set_option(_lib.OPT_ATTN_KERNELS, args.attn_kernels)
@@ -548,6 +557,10 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
                 model.moe.forward_ep(model.x, ly.moe, li, model.ids, model.partial, stream=stream)
 
         def allreduce_only():
+            if p2p:
+                for _ in range(L):
+                    ep_comm.combine(model.partial, model.x, stream=stream)
+                return
             with torch.cuda.stream(stream):
                 for _ in range(L):
                     pg.all_reduce(model.partial)
@@ -558,11 +571,14 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
         roof = {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
                 "frac": achieved / (peak * world), "peak_kind": peak_kind + f" x{world}",
                 "alg_bytes": ALG_BYTES_LAYER, "us_per_layer": t_layer * 1e6,
-                "unit_of_work": "one MoE layer over all ranks: styx_moe_block_ep on every rank + one all-reduce "
-                                "of the k x H slot buffer"}
+                "unit_of_work": "one MoE layer over all ranks: styx_moe_block_ep on every rank + the cross-rank "
+                                "sum of the k x H slot buffer" + (" and the combine (styx_ep_combine)" if p2p else "")}
         ep = {"moe_ep_us_per_layer": t_moe * 1e3, "allreduce_us_per_layer": t_ar * 1e3,
               "allreduce_bytes": K_TOP * H * 4, "limiter": "all-reduce latency" if t_ar > t_moe else
-              "the block's compute", "nccl_ranks": world}
+              "the block's compute", "ranks": world,
+              "collective": "styx_ep_combine: plain stores into the peers' inboxes over NVLink (CUDA IPC), "
+                            "release/acquire flags, the sum and the combine in one kernel" if p2p else
+                            "NCCL all-reduce (torch.distributed) + styx_moe_combine"}
     bytes_tok = decode_bytes_per_token(L, ctx)
     step_achieved = bytes_tok / (ms * 1e-3) / 1e9
     one_attn, one_moe = attn_path in (1, 3), moe_path in (1, 6)
@@ -577,7 +593,7 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
         "dtype": "int8-dp4a/f32 (q4_K,q6_K weights)",
         "data": "synthetic (random weights of the 30B-A3B shapes, random cache rows)",
-        "config": decode_config(L, ctx, world),
+        "config": decode_config(L, ctx, world, args.ep_comm),
         "kernels": {"launch": ("CUDA graph" if world == 1 else "eager (NCCL all-reduces between the kernels)") +
                               (", cooperative" if args.shared_device else
                                ", plain single kernels (STYX_OPT_EXCLUSIVE: the bench owns its GPU)"),
@@ -613,6 +629,9 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
     hout.free()
     if pg:
         pg.barrier()
+        if ep_comm is not None:
+            ep_comm.close()
+            pg.barrier()   # no rank unmaps an inbox a peer still writes
         pg.destroy_process_group()
     return 0
 
@@ -956,6 +975,9 @@ def main() -> int:
     ap.add_argument("--batch", type=int, default=8, help="batch: tokens per step (1..64)")
     ap.add_argument("--moe-kernels", type=int, default=0, choices=[0, 1, 2, 3],
                     help="STYX_OPT_MOE_KERNELS: 0 auto, 1 single cooperative kernel, 2 three kernels, 3 cluster form")
+    ap.add_argument("--ep-comm", default="p2p", choices=["p2p", "nccl"],
+                    help="decode at N > 1: the cross-rank sum + combine as one kernel over NVLink peer memory (p2p, "
+                         "styx_ep_combine) or an NCCL all-reduce + styx_moe_combine")
     ap.add_argument("--attn-kernels", type=int, default=0, choices=[0, 1, 2, 3],
                     help="decode: STYX_OPT_ATTN_KERNELS: 0 auto, 1 cooperative kernel, 2 seven kernels, 3 cluster form")
     ap.add_argument("--shape", default="cfg2", choices=["cfg2", "cfg5"],

@@ -1565,6 +1565,118 @@ int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial, fl
     return STYX_OK;
 }
 
+// ------------------------------------------------ cross-rank combine over peer memory
+struct styx_ep {
+    int dev = 0, rank = 0, world = 1, k = 0, H = 0;
+    uint8_t *base = nullptr;                      // this rank's inbox (two halves), then its flags
+    size_t flags_off = 0;
+    float *inbox[styx::kEpMaxRanks] = {};
+    unsigned long long *flags[styx::kEpMaxRanks] = {};
+    void *peer_base[styx::kEpMaxRanks] = {};      // the peers' mappings (closed by styx_ep_close)
+    bool connected = false;
+    unsigned long long gen = 0;                   // calls so far
+};
+static_assert(sizeof(cudaIpcMemHandle_t) == STYX_EP_HANDLE_BYTES, "IPC handle size");
+static_assert(styx::kEpMaxRanks == STYX_EP_MAX_RANKS, "rank limit");
+
+int styx_ep_open(styx_ctx *ctx, int rank, int world, int k, int n_embd, styx_ep **out, void *handle) {
+    ENTER(ctx);
+    NEED(out && handle, "null pointer");
+    NEED(world >= 1 && world <= STYX_EP_MAX_RANKS && rank >= 0 && rank < world, "rank %d of world %d (at most %d)",
+         rank, world, STYX_EP_MAX_RANKS);
+    NEED(k >= 1 && k <= STYX_MAX_TOPK && n_embd > 0 && n_embd % 4 == 0, "bad k %d / n_embd %d", k, n_embd);
+    styx_ep *ep = new styx_ep();
+    ep->dev = ctx->device;
+    ep->rank = rank;
+    ep->world = world;
+    ep->k = k;
+    ep->H = n_embd;
+    const int G = (n_embd + styx::kEpCols - 1) / styx::kEpCols;
+    const size_t inbox = 2 * static_cast<size_t>(world) * k * n_embd * 4;
+    ep->flags_off = a128(inbox);
+    const size_t total = ep->flags_off + static_cast<size_t>(world) * G * 8;
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, total);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, total);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();   // zeroed before any peer can map it
+    cudaIpcMemHandle_t h{};
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        delete ep;
+        return fail(STYX_ECUDA, "styx_ep_open: %s", cudaGetErrorString(e));
+    }
+    ep->base = static_cast<uint8_t *>(p);
+    ep->inbox[rank] = reinterpret_cast<float *>(ep->base);
+    ep->flags[rank] = reinterpret_cast<unsigned long long *>(ep->base + ep->flags_off);
+    memcpy(handle, &h, sizeof(h));
+    *out = ep;
+    return STYX_OK;
+}
+
+int styx_ep_connect(styx_ep *ep, const void *handles) {
+    NEED(ep && handles, "null pointer");
+    NEED(!ep->connected, "styx_ep_connect: already connected");
+    CK(cudaSetDevice(ep->dev));
+    const uint8_t *hb = static_cast<const uint8_t *>(handles);
+    for (int p = 0; p < ep->world; p++) {
+        if (p == ep->rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hb + static_cast<size_t>(p) * STYX_EP_HANDLE_BYTES, sizeof(h));
+        void *ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < p; q++)
+                if (ep->peer_base[q]) {
+                    cudaIpcCloseMemHandle(ep->peer_base[q]);
+                    ep->peer_base[q] = nullptr;
+                }
+            return fail(STYX_ECUDA, "styx_ep_connect: rank %d's inbox: %s", p, cudaGetErrorString(e));
+        }
+        ep->peer_base[p] = ptr;
+        ep->inbox[p] = static_cast<float *>(ptr);
+        ep->flags[p] = reinterpret_cast<unsigned long long *>(static_cast<uint8_t *>(ptr) + ep->flags_off);
+    }
+    ep->connected = true;
+    return STYX_OK;
+}
+
+int styx_ep_combine(styx_ctx *ctx, styx_ep *ep, styx_stream stream, const float *partial, float *x) {
+    ENTER(ctx);
+    NEED(ep && partial && x, "null pointer");
+    NEED(ep->connected, "styx_ep_combine before styx_ep_connect");
+    NEED(ep->dev == ctx->device, "styx_ep of device %d used with a context of device %d", ep->dev, ctx->device);
+    NEED(al16(partial), "partial must be 16-byte aligned");
+    NEED(extent_ok(partial, static_cast<uint64_t>(ep->k) * ep->H * 4) && extent_ok(x, static_cast<uint64_t>(ep->H) * 4),
+         "partial / x smaller than k * n_embd / n_embd");
+    styx::EpCombineArgs a{};
+    a.partial = partial;
+    a.x = x;
+    for (int p = 0; p < ep->world; p++) {
+        a.inbox[p] = ep->inbox[p];
+        a.flags[p] = ep->flags[p];
+    }
+    a.rank = ep->rank;
+    a.world = ep->world;
+    a.k = ep->k;
+    a.H = ep->H;
+    a.gen = ++ep->gen;
+    a.err = ctx->d_err;
+    CK(styx::launch_ep_combine(a, S(stream)));
+    return STYX_OK;
+}
+
+int styx_ep_close(styx_ep *ep) {
+    if (!ep) return STYX_OK;
+    cudaSetDevice(ep->dev);
+    cudaDeviceSynchronize();   // no combine of this rank still reads or writes the inboxes
+    for (int p = 0; p < ep->world; p++)
+        if (ep->peer_base[p]) cudaIpcCloseMemHandle(ep->peer_base[p]);
+    if (ep->base) cudaFree(ep->base);
+    delete ep;
+    return STYX_OK;
+}
+
 // ------------------------------------------------ MoE block, no allocation
 int styx_moe_block_noalloc(styx_ctx *ctx, styx_stream stream, const styx_moe_dims *dims, const styx_moe_layer *lw,
                            int layer, float *x, int32_t *ids, float *weights_out) {

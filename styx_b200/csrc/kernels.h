@@ -224,6 +224,19 @@ cudaError_t launch_swiglu(const float *g, const float *u, float *out, int n, cud
 cudaError_t launch_moe_reduce(const float *d, const float *w, float *x, int ne, int k,
                               cudaStream_t st);
 cudaError_t launch_combine_partial(const float *partial, float *x, int ne, int k, cudaStream_t st);
+// the cross-rank sum + combine over peer memory (styx_ep_combine, moe_kernels.cu)
+constexpr int kEpMaxRanks = 8;
+constexpr int kEpCols = 128;   // columns of x per CTA
+struct EpCombineArgs {
+    const float *partial;                         // this rank's f32[k][H]
+    float *x;                                     // [H], += the slot-ordered sum
+    float *inbox[kEpMaxRanks];                    // rank p's inbox [2][world][k][H] (this rank's own included)
+    unsigned long long *flags[kEpMaxRanks];       // rank p's flags [world][G]
+    int rank, world, k, H;
+    unsigned long long gen;                       // this call's generation: 1, 2, ...
+    int *err;
+};
+cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t st);
 cudaError_t launch_gather(const GatherArgs &a, cudaStream_t st);
 cudaError_t launch_synth_quant(int qtype, uint8_t *dst, uint64_t nrows, int ncols, uint64_t seed,
                                float sigma, cudaStream_t st);

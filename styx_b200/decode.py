@@ -15,12 +15,14 @@ layer's caches reallocated one page larger and the filled rows copied over
 the attention reads the same rows either way, so the results are the same
 bits.
 
-Expert parallelism (`allreduce` given): every rank runs the whole step on
-the same token with the same dense weights, but holds only its own experts
-(its layers' hot buffers, remap -> local slot); each MoE block writes its
-slot contributions (styx_moe_block_ep), `allreduce` sums them over the
-ranks in place on the stream, and styx_moe_combine adds the slot-ordered
-sum into x -- bit-identical to one device holding every expert.
+Expert parallelism (`allreduce` or `ep_comm` given): every rank runs the
+whole step on the same token with the same dense weights, but holds only
+its own experts (its layers' hot buffers, remap -> local slot); each MoE
+block writes its slot contributions (styx_moe_block_ep), `allreduce` sums
+them over the ranks in place on the stream and styx_moe_combine adds the
+slot-ordered sum into x, or `ep_comm` (ops.EpComm) does both as one kernel
+over NVLink peer memory -- either way bit-identical to one device holding
+every expert.
 """
 from __future__ import annotations
 
@@ -58,7 +60,8 @@ class DecodeLayer:
 
 class DecodeModel:
     def __init__(self, hp: DecodeParams, embd: ops.DenseWeight, layers: list, output_norm: torch.Tensor,
-                 head: ops.DenseWeight, n_ctx: int, device: int = 0, allreduce=None, kv_page: int = 0):
+                 head: ops.DenseWeight, n_ctx: int, device: int = 0, allreduce=None, kv_page: int = 0,
+                 ep_comm=None):
         self.hp, self.embd, self.layers, self.output_norm, self.head = hp, embd, layers, output_norm, head
         self.n_ctx = n_ctx            # n_ctx_max: positions the caches may grow to
         self.kv_page = kv_page        # 0: allocated once for n_ctx rows; else rows per page
@@ -82,6 +85,8 @@ class DecodeModel:
         # expert parallelism: a callable summing a tensor over the ranks in
         # place, on the current stream (e.g. torch.distributed.all_reduce)
         self.allreduce = allreduce
+        # or: an ops.EpComm (the sum and the combine as one kernel over NVLink peer memory)
+        self.ep_comm = ep_comm
         self.partial = torch.zeros(hp.n_expert_used * hp.n_embd, dtype=torch.float32, device=dev)
 
     def _grow(self) -> None:
@@ -123,7 +128,10 @@ class DecodeModel:
         for li, ly in enumerate(self.layers):
             self.attn.forward(self.x, ly.attn, pos, self.pos, self.kcache[li], self.vcache[li], self.cap,
                               stream=stream)
-            if self.allreduce is None:
+            if self.ep_comm is not None:
+                self.moe.forward_ep(self.x, ly.moe, li, self.ids, self.partial, stream=stream)
+                self.ep_comm.combine(self.partial, self.x, stream=stream)
+            elif self.allreduce is None:
                 self.moe.forward(self.x, ly.moe, li, self.ids, stream=stream)
             else:
                 self.moe.forward_ep(self.x, ly.moe, li, self.ids, self.partial, stream=stream)

@@ -325,6 +325,48 @@ class MoeBlock:
         return self.workspace[off: off + 4 * n].view(torch.float32)
 
 
+class EpComm:
+    """styx_ep: the cross-rank sum of the expert-parallel slot buffer and the
+    combine into x, as one kernel over NVLink peer memory (no library
+    collective).  Every rank opens one, the ranks exchange handles (any host
+    channel: `connect_with` uses torch.distributed), then every rank calls
+    `combine` once per layer in the same order."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, rank: int, world: int, k: int, n_embd: int, device: int = 0):
+        self.ctx = ctx(device)
+        self.handle = C.c_void_p()
+        self._local = (C.c_uint8 * self.HANDLE_BYTES)()
+        check(lib().styx_ep_open(self.ctx.handle, rank, world, k, n_embd, C.byref(self.handle), self._local))
+        self.rank, self.world = rank, world
+
+    def local_handle(self) -> bytes:
+        return bytes(self._local)
+
+    def connect(self, handles) -> None:
+        """handles: every rank's local_handle(), in rank order."""
+        buf = b"".join(handles)
+        assert len(buf) == self.world * self.HANDLE_BYTES
+        check(lib().styx_ep_connect(self.handle, buf))
+
+    def connect_with(self, dist) -> None:
+        """Exchanges the handles over a torch.distributed process group."""
+        got = [None] * self.world
+        dist.all_gather_object(got, self.local_handle())
+        self.connect(got)
+
+    def combine(self, partial: torch.Tensor, x: torch.Tensor, stream=None) -> torch.Tensor:
+        """x += the slot-ordered sum over the ranks of their partials."""
+        check(lib().styx_ep_combine(self.ctx.handle, self.handle, _stream(stream), _ptr(partial), _ptr(x)))
+        return x
+
+    def close(self) -> None:
+        if self.handle:
+            check(lib().styx_ep_close(self.handle))
+            self.handle = C.c_void_p()
+
+
 class MoeBatch:
     """The MoE block of a batch of up to 64 tokens of one layer
     (styx_moe_block_batch: grouped expert GEMMs on the tensor cores)."""
