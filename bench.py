@@ -399,9 +399,11 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
     sequence; at N > 1 its experts are split over the ranks (expert
     parallelism: every rank runs the step on the same token, holds the
     experts e % N == rank, and one NCCL all-reduce per layer sums the slot
-    contributions), so the scaling is strong.  At N = 1 the token is a CUDA
-    graph recorded through the C ABI; at N > 1 the step runs eagerly (its
-    all-reduces go through torch.distributed)."""
+    contributions), so the scaling is strong.  The token is a CUDA graph
+    recorded through the C ABI at N = 1 and, with the peer-memory combine
+    (--ep-comm p2p: only this library's kernels), at N > 1 too; with
+    --ep-comm nccl the step runs eagerly (its all-reduces go through
+    torch.distributed)."""
     import ctypes as C
     import zlib
 
@@ -443,7 +445,7 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
     blk_ctx.check_device_error(stream)
     attn_path, moe_path = model.attn.last_path(), blk_ctx.last_moe_path()
     graph = None
-    if world == 1:
+    if world == 1 or p2p:
         graph = C.c_void_p()
         _lib.check(lib.styx_graph_begin(cx, sp))
         model.step(stream)
@@ -564,8 +566,26 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
             with torch.cuda.stream(stream):
                 for _ in range(L):
                     pg.all_reduce(model.partial)
-        t_moe = timed(moe_ep_only, reps) / L
-        t_ar = timed(allreduce_only, reps) / L
+        def as_graph(fn):
+            # p2p: the pieces as recorded graphs, as the step runs them
+            if not p2p:
+                return fn, None
+            g = C.c_void_p()
+            _lib.check(lib.styx_graph_begin(cx, sp))
+            fn()
+            _lib.check(lib.styx_graph_end(cx, sp, C.byref(g)))
+            return (lambda: _lib.check(lib.styx_graph_launch(cx, g, sp))), g
+
+        graphs = []
+        f_moe, g = as_graph(moe_ep_only)
+        graphs.append(g)
+        f_ar, g = as_graph(allreduce_only)
+        graphs.append(g)
+        t_moe = timed(f_moe, reps) / L
+        t_ar = timed(f_ar, reps) / L
+        for g in graphs:
+            if g is not None:
+                _lib.check(lib.styx_graph_destroy(cx, g))
         t_layer = (t_moe + t_ar) * 1e-3
         achieved = ALG_BYTES_LAYER / t_layer / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
@@ -594,7 +614,7 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
         "dtype": "int8-dp4a/f32 (q4_K,q6_K weights)",
         "data": "synthetic (random weights of the 30B-A3B shapes, random cache rows)",
         "config": decode_config(L, ctx, world, args.ep_comm),
-        "kernels": {"launch": ("CUDA graph" if world == 1 else "eager (NCCL all-reduces between the kernels)") +
+        "kernels": {"launch": ("CUDA graph" if world == 1 or p2p else "eager (NCCL all-reduces between the kernels)") +
                               (", cooperative" if args.shared_device else
                                ", plain single kernels (STYX_OPT_EXCLUSIVE: the bench owns its GPU)"),
                     "attention": attn_form, "moe": moe_form},

@@ -389,7 +389,9 @@ int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial,
  * x[i], ranks then slots in order: with one non-zero contributor per slot
  * the result equals the single-device block bit for bit, as the NCCL form
  * does.  Every rank must call it once per layer, in the same order; calls on
- * one styx_ep must not overlap on the GPU (one stream).  No multicast, no
+ * one styx_ep must not overlap on the GPU (one stream).  The call's
+ * generation is a counter in the rank's own memory (advanced by the call's
+ * last CTA), so a launch recorded once can be replayed.  No multicast, no
  * library collective.  styx_ep_close synchronises the device, unmaps the
  * peers and frees the inbox: call it on every rank after a barrier. */
 #define STYX_EP_HANDLE_BYTES 64

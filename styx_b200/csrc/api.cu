@@ -1574,7 +1574,6 @@ struct styx_ep {
     unsigned long long *flags[styx::kEpMaxRanks] = {};
     void *peer_base[styx::kEpMaxRanks] = {};      // the peers' mappings (closed by styx_ep_close)
     bool connected = false;
-    unsigned long long gen = 0;                   // calls so far
 };
 static_assert(sizeof(cudaIpcMemHandle_t) == STYX_EP_HANDLE_BYTES, "IPC handle size");
 static_assert(styx::kEpMaxRanks == STYX_EP_MAX_RANKS, "rank limit");
@@ -1594,7 +1593,8 @@ int styx_ep_open(styx_ctx *ctx, int rank, int world, int k, int n_embd, styx_ep 
     const int G = (n_embd + styx::kEpCols - 1) / styx::kEpCols;
     const size_t inbox = 2 * static_cast<size_t>(world) * k * n_embd * 4;
     ep->flags_off = a128(inbox);
-    const size_t total = ep->flags_off + static_cast<size_t>(world) * G * 8;
+    // then the flags, then this rank's call counter (u64) and the CTAs done of the current call (u32)
+    const size_t total = ep->flags_off + static_cast<size_t>(world) * G * 8 + 16;
     void *p = nullptr;
     cudaError_t e = cudaMalloc(&p, total);
     if (e == cudaSuccess) e = cudaMemset(p, 0, total);
@@ -1660,7 +1660,9 @@ int styx_ep_combine(styx_ctx *ctx, styx_ep *ep, styx_stream stream, const float 
     a.world = ep->world;
     a.k = ep->k;
     a.H = ep->H;
-    a.gen = ++ep->gen;
+    const int G = (ep->H + styx::kEpCols - 1) / styx::kEpCols;
+    a.calls = reinterpret_cast<unsigned long long *>(ep->flags[ep->rank] + static_cast<size_t>(ep->world) * G);
+    a.done = reinterpret_cast<unsigned *>(a.calls + 1);
     a.err = ctx->d_err;
     CK(styx::launch_ep_combine(a, S(stream)));
     return STYX_OK;

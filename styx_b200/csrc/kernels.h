@@ -233,7 +233,11 @@ struct EpCombineArgs {
     float *inbox[kEpMaxRanks];                    // rank p's inbox [2][world][k][H] (this rank's own included)
     unsigned long long *flags[kEpMaxRanks];       // rank p's flags [world][G]
     int rank, world, k, H;
-    unsigned long long gen;                       // this call's generation: 1, 2, ...
+    // this rank's call counter (calls completed; this call's generation is
+    // *calls + 1) and the CTAs of the current call that have finished: both
+    // in this rank's memory, so that a recorded graph replays correctly
+    unsigned long long *calls;
+    unsigned *done;
     int *err;
 };
 cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t st);

@@ -705,6 +705,9 @@ cudaError_t launch_combine_partial(const float *partial, float *x, int ne, int k
 // slots in order.  The inbox has two halves, by the parity of the call's
 // generation: a peer one call ahead writes the other half, and it cannot
 // get two calls ahead before this rank has pushed (hence summed) this one.
+// The generation is this rank's count of completed calls + 1, read by every
+// CTA at entry and advanced by the CTA that finishes the call last, so the
+// launch carries no per-call argument and a recorded graph replays as well.
 __device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -722,9 +725,11 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpCombineArgs a
     const int b = blockIdx.x, G = gridDim.x, tid = threadIdx.x;
     const int c0 = b * kEpCols, nc = min(kEpCols, a.H - c0);
     const int H4 = a.H >> 2, c04 = c0 >> 2, nc4 = nc >> 2;
+    // (the previous call on this stream has ended: its counter update is visible)
+    const unsigned long long gen = __ldcg(a.calls) + 1ull;
     const size_t row = static_cast<size_t>(a.k) * a.H;                      // one rank's row of an inbox half
     const size_t half = static_cast<size_t>(a.world) * row;
-    const size_t mine = (a.gen & 1ull) * half + static_cast<size_t>(a.rank) * row;   // our row, this call's half
+    const size_t mine = (gen & 1ull) * half + static_cast<size_t>(a.rank) * row;   // our row, this call's half
     // 1. push
     for (int i = tid; i < a.k * nc4; i += kEpThreads) {
         const int s = i / nc4, j = i - s * nc4;
@@ -737,13 +742,13 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpCombineArgs a
     // 2. this CTA's columns of this call are in every peer's inbox
     if (tid < a.world && tid != a.rank) {
         __threadfence_system();
-        st_release_sys(a.flags[tid] + static_cast<size_t>(a.rank) * G + b, a.gen);
+        st_release_sys(a.flags[tid] + static_cast<size_t>(a.rank) * G + b, gen);
     }
     // 3. every peer's columns of this call are in ours (bounded wait)
     if (tid < a.world && tid != a.rank) {
         const unsigned long long *f = a.flags[a.rank] + static_cast<size_t>(tid) * G + b;
         const long long t0 = clock64();
-        while (ld_acquire_sys(f) < a.gen) {
+        while (ld_acquire_sys(f) < gen) {
             const long long dt = clock64() - t0;
             if (dt > kSpinCycles) {
                 atomicExch(a.err, kErrWaitRoute);
@@ -754,7 +759,7 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpCombineArgs a
     }
     __syncthreads();
     // 4. the slot-ordered sum (one non-zero rank per slot: exact in any order)
-    const float *box = a.inbox[a.rank] + (a.gen & 1ull) * half;
+    const float *box = a.inbox[a.rank] + (gen & 1ull) * half;
     for (int j = tid; j < nc; j += kEpThreads) {
         const int c = c0 + j;
         float acc = 0.f;
@@ -766,6 +771,17 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpCombineArgs a
             acc = __fadd_rn(acc, v);
         }
         a.x[c] = __fadd_rn(a.x[c], acc);
+    }
+    // 5. the last CTA of the call advances the generation (no CTA of this
+    // call reads it again)
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(a.done, 1u) == static_cast<unsigned>(G - 1)) {
+            *a.done = 0u;
+            *a.calls = gen;
+            __threadfence();
+        }
     }
 }
 

@@ -4,8 +4,12 @@ inbox, plain stores, release / acquire flags at system scope, no library
 collective).  One process per GPU (world size 2); the handles travel over a
 gloo process group.  Three layers in a row (both inbox halves, and a rank a
 call ahead of the other) must each equal the single-device styx_moe_block
-bit for bit.  Skipped with fewer than two GPUs.
+bit for bit.  The same three layers recorded once as a CUDA graph and
+replayed twice (the call generation lives in device memory, so a replay
+runs with fresh generations) must give the same bits again.  Skipped with
+fewer than two GPUs.
 """
+import ctypes as C
 import datetime
 import os
 import socket
@@ -65,6 +69,27 @@ def _rank_main(rank, port, out_dir):
         torch.cuda.synchronize()
         blk.ctx.check_device_error()
         np.save(os.path.join(out_dir, f"x{rank}.npy"), x.cpu().numpy())
+        # the same layers as one recorded graph, replayed twice from the same input
+        lib, cx = _lib.lib(), blk.ctx.handle
+        stream = torch.cuda.Stream(device=dev)
+        sp = C.c_void_p(stream.cuda_stream)
+        x0, xg = t(cases[0].x), torch.empty_like(x)
+        graph = C.c_void_p()
+        _lib.check(lib.styx_graph_begin(cx, sp))
+        for l, lw in enumerate(lws):
+            blk.forward_ep(xg, lw, l, ids, partial, stream=stream)
+            ep.combine(partial, xg, stream=stream)
+        _lib.check(lib.styx_graph_end(cx, sp, C.byref(graph)))
+        try:
+            for rep in range(2):
+                with torch.cuda.stream(stream):
+                    xg.copy_(x0)
+                _lib.check(lib.styx_graph_launch(cx, graph, sp))
+                stream.synchronize()
+                blk.ctx.check_device_error(stream)
+                np.save(os.path.join(out_dir, f"g{rank}_{rep}.npy"), xg.cpu().numpy())
+        finally:
+            _lib.check(lib.styx_graph_destroy(cx, graph))
         if rank == 0:   # the single-device blocks with every expert
             x1 = t(cases[0].x)
             for l, c in enumerate(cases):
@@ -90,3 +115,6 @@ def test_ep_over_peer_memory_matches_single_device(tmp_path):
     for r in range(WORLD):
         x = np.load(tmp_path / f"x{r}.npy")
         assert np.array_equal(x.view(np.uint32), single.view(np.uint32)), r
+        for rep in range(2):
+            g = np.load(tmp_path / f"g{r}_{rep}.npy")
+            assert np.array_equal(g.view(np.uint32), single.view(np.uint32)), (r, rep)
