@@ -10,9 +10,10 @@ already filled, batch 1.  Every expert resident in HBM (18.8 GB); router
 rows carry a Zipf(1.1) popularity bias.  Synthetic data, generated on the
 device.  At N > 1 (torchrun) the same sequence runs with its experts split
 over the ranks (expert parallelism, e % N == rank) and one cross-rank sum
-of the k x H slot buffer per layer (--ep-comm p2p: one kernel that pushes
-the slots over NVLink peer memory and combines; nccl: an NCCL all-reduce):
-strong scaling of one sequence.
+of the k x H slot buffer per layer (--ep-comm fused, the default: the
+block's own kernel pushes its rows over NVLink peer memory and adds the
+ranks' sum into x; p2p: one kernel after the block does the exchange and
+the combine; nccl: an NCCL all-reduce): strong scaling of one sequence.
 
 `value`: tokens/s, device-timed with CUDA events (a CUDA graph at N = 1).
 `e2e`: a greedy chain through the C ABI with host buffers (token id in,
@@ -342,7 +343,7 @@ def ep_moe_layers(dev: int, n_layers: int, world: int, rank: int, unique: int = 
     return layers
 
 
-def decode_config(L: int, ctx: int, world: int, comm: str = "p2p") -> dict:
+def decode_config(L: int, ctx: int, world: int, comm: str = "fused") -> dict:
     """The decode workload's config (both arms)."""
     return {"workload": f"whole decode step at the 30B-A3B shape (configs[2]): embedding row, {L} x "
                         f"(attention {N_HEADS}q/{N_KV}kv x {HD} + MoE block H{H} E{E} top{K_TOP} F{F}, "
@@ -351,12 +352,15 @@ def decode_config(L: int, ctx: int, world: int, comm: str = "p2p") -> dict:
             "ctx": ctx, "global_batch": 1,
             "parallelism": (f"expert-parallel x{world}: experts e % {world} == rank, per layer one cross-rank "
                             f"sum of the {K_TOP} x {H} slot buffer ("
-                            + ("one kernel over NVLink peer memory" if comm == "p2p" else "NCCL all-reduce") + ")"
+                            + {"fused": "over NVLink peer memory, inside the block's kernel",
+                               "p2p": "one kernel over NVLink peer memory",
+                               "nccl": "NCCL all-reduce"}[comm] + ")"
                             if world > 1 else "single"),
             "l2": "inputs larger than L2 (%.2f GB read per token)" % (decode_bytes_per_token(L, ctx) / 1e9)}
 
 
-def decode_model(local: int, L: int, ctx: int, world: int, rank: int, allreduce=None, ep_comm=None):
+def decode_model(local: int, L: int, ctx: int, world: int, rank: int, allreduce=None, ep_comm=None,
+                 ep_fused: bool = True):
     """The 30B-shaped decode model with random weights: attention q/k/o q4_K,
     v q6_K (four generated layer bases, copied to every layer), the MoE
     layers (every expert at world 1, this rank's experts under expert
@@ -384,7 +388,8 @@ def decode_model(local: int, L: int, ctx: int, world: int, rank: int, allreduce=
     embd = ops.DenseWeight(Q4_K, ops.synth_quant(Q4_K, N_VOCAB, H, 3000, 0.5, device=local))
     head = ops.DenseWeight(Q6_K, ops.synth_quant(Q6_K, N_VOCAB, H, 3001, 0.02, device=local))
     p = DecodeParams(L, H, N_HEADS, N_KV, HD, F, E, K_TOP, N_VOCAB)
-    model = DecodeModel(p, embd, layers, ones(H), head, ctx + 1, local, allreduce=allreduce, ep_comm=ep_comm)
+    model = DecodeModel(p, embd, layers, ones(H), head, ctx + 1, local, allreduce=allreduce, ep_comm=ep_comm,
+                        ep_fused=ep_fused)
     model.kcache[:, :ctx].copy_(ops.synth_f32(L * ctx * kvd, 4000, 0, 1.0, device=local).view(L, ctx, kvd))
     model.vcache[:, :ctx].copy_(ops.synth_f32(L * ctx * kvd, 4001, 0, 1.0, device=local).view(L, ctx, kvd))
     model.n_past = ctx
@@ -401,7 +406,7 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
     experts e % N == rank, and one NCCL all-reduce per layer sums the slot
     contributions), so the scaling is strong.  The token is a CUDA graph
     recorded through the C ABI at N = 1 and, with the peer-memory combine
-    (--ep-comm p2p: only this library's kernels), at N > 1 too; with
+    (--ep-comm fused / p2p: only this library's kernels), at N > 1 too; with
     --ep-comm nccl the step runs eagerly (its all-reduces go through
     torch.distributed)."""
     import ctypes as C
@@ -421,13 +426,13 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device(dev))
         pg = dist
     L, ctx = args.layers, args.ctx
-    p2p = pg is not None and args.ep_comm == "p2p"
+    p2p = pg is not None and args.ep_comm in ("fused", "p2p")
     ep_comm = None
     if p2p:   # the cross-rank sum and the combine as one kernel over NVLink peer memory
         ep_comm = ops.EpComm(rank, world, K_TOP, H, local)
         ep_comm.connect_with(pg)
     allreduce = (lambda t: pg.all_reduce(t)) if pg and not p2p else None
-    model = decode_model(local, L, ctx, world, rank, allreduce, ep_comm)
+    model = decode_model(local, L, ctx, world, rank, allreduce, ep_comm, args.ep_comm == "fused")
     blk_ctx = model.moe.ctx
     blk_ctx.set_option(_lib.OPT_EXCLUSIVE, 0 if args.shared_device else 1)
     blk_ctx.set_option(_lib.OPT_ATTN_KERNELS, args.attn_kernels)
@@ -554,6 +559,8 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
                 "peak_kind": peak_kind, "alg_bytes": ALG_BYTES_LAYER, "us_per_layer": t_layer * 1e6,
                 "unit_of_work": "one MoE block (one k_moe_fused launch), timed as 48 blocks in a graph in this run"}
     else:
+        fused = args.ep_comm == "fused"
+
         def moe_ep_only():
             for li, ly in enumerate(model.layers):
                 model.moe.forward_ep(model.x, ly.moe, li, model.ids, model.partial, stream=stream)
@@ -566,8 +573,13 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
             with torch.cuda.stream(stream):
                 for _ in range(L):
                     pg.all_reduce(model.partial)
+
+        def ep_blocks():
+            for li, ly in enumerate(model.layers):
+                ep_comm.moe_block(model.moe, model.x, ly.moe, li, model.ids, stream=stream)
+
         def as_graph(fn):
-            # p2p: the pieces as recorded graphs, as the step runs them
+            # fused / p2p: the pieces as recorded graphs, as the step runs them
             if not p2p:
                 return fn, None
             g = C.c_void_p()
@@ -579,30 +591,43 @@ def run_decode(args, local: int, rank: int, world: int) -> int:
         graphs = []
         f_moe, g = as_graph(moe_ep_only)
         graphs.append(g)
-        f_ar, g = as_graph(allreduce_only)
+        f_ar, g = as_graph(ep_blocks if fused else allreduce_only)
         graphs.append(g)
         t_moe = timed(f_moe, reps) / L
         t_ar = timed(f_ar, reps) / L
         for g in graphs:
             if g is not None:
                 _lib.check(lib.styx_graph_destroy(cx, g))
-        t_layer = (t_moe + t_ar) * 1e-3
+        if fused:   # t_ar timed the block and its exchange together
+            t_layer = t_ar * 1e-3
+            t_ar = t_ar - t_moe
+        else:
+            t_layer = (t_moe + t_ar) * 1e-3
         achieved = ALG_BYTES_LAYER / t_layer / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
                 "frac": achieved / (peak * world), "peak_kind": peak_kind + f" x{world}",
                 "alg_bytes": ALG_BYTES_LAYER, "us_per_layer": t_layer * 1e6,
-                "unit_of_work": "one MoE layer over all ranks: styx_moe_block_ep on every rank + the cross-rank "
-                                "sum of the k x H slot buffer" + (" and the combine (styx_ep_combine)" if p2p else "")}
+                "unit_of_work": "one MoE layer over all ranks: " + (
+                    "styx_ep_moe_block on every rank (the block with the exchange and the combine as its "
+                    "epilogue: one k_moe_fused launch)" if fused else
+                    "styx_moe_block_ep on every rank + the cross-rank sum of the k x H slot buffer" +
+                    (" and the combine (styx_ep_combine)" if p2p else ""))}
         ep = {"moe_ep_us_per_layer": t_moe * 1e3, "allreduce_us_per_layer": t_ar * 1e3,
               "allreduce_bytes": K_TOP * H * 4, "limiter": "all-reduce latency" if t_ar > t_moe else
               "the block's compute", "ranks": world,
-              "collective": "styx_ep_combine: plain stores into the peers' inboxes over NVLink (CUDA IPC), "
-                            "release/acquire flags, the sum and the combine in one kernel" if p2p else
-                            "NCCL all-reduce (torch.distributed) + styx_moe_combine"}
+              "collective": {"fused": "styx_ep_moe_block: each CTA of the block's kernel stores its rows of every "
+                                      "slot into the peers' inboxes over NVLink (CUDA IPC), release adds / acquire "
+                                      "loads of arrival counters, the ranks' sum added into x in the same kernel "
+                                      "(allreduce_us_per_layer: the block with its exchange minus the block alone)",
+                             "p2p": "styx_ep_combine: plain stores into the peers' inboxes over NVLink (CUDA IPC), "
+                                    "release adds / acquire loads of arrival counters, the sum and the combine in "
+                                    "one kernel after the block",
+                             "nccl": "NCCL all-reduce (torch.distributed) + styx_moe_combine"}[args.ep_comm]}
     bytes_tok = decode_bytes_per_token(L, ctx)
     step_achieved = bytes_tok / (ms * 1e-3) / 1e9
     one_attn, one_moe = attn_path in (1, 3), moe_path in (1, 6)
-    launches = 1 + L * ((1 if one_attn else 8) + (1 if one_moe else 3) + (1 if world > 1 else 0)) + 3
+    ep_launch = 1 if world > 1 and not (args.ep_comm == "fused" and moe_path == 1) else 0
+    launches = 1 + L * ((1 if one_attn else 8) + (1 if one_moe else 3) + ep_launch) + 3
     attn_form = {1: "one cooperative kernel per layer", 3: "one launch of thread-block clusters per layer "
                  "(a cluster per kv head)"}.get(attn_path, "eight kernels per layer")
     moe_form = {1: "single cooperative kernel per layer", 6: "one launch of thread-block clusters per layer "
@@ -995,9 +1020,10 @@ def main() -> int:
     ap.add_argument("--batch", type=int, default=8, help="batch: tokens per step (1..64)")
     ap.add_argument("--moe-kernels", type=int, default=0, choices=[0, 1, 2, 3],
                     help="STYX_OPT_MOE_KERNELS: 0 auto, 1 single cooperative kernel, 2 three kernels, 3 cluster form")
-    ap.add_argument("--ep-comm", default="p2p", choices=["p2p", "nccl"],
-                    help="decode at N > 1: the cross-rank sum + combine as one kernel over NVLink peer memory (p2p, "
-                         "styx_ep_combine) or an NCCL all-reduce + styx_moe_combine")
+    ap.add_argument("--ep-comm", default="fused", choices=["fused", "p2p", "nccl"],
+                    help="decode at N > 1: the exchange over NVLink peer memory inside the block's kernel (fused, "
+                         "styx_ep_moe_block), as one kernel after it (p2p, styx_ep_combine), or an NCCL all-reduce "
+                         "+ styx_moe_combine")
     ap.add_argument("--attn-kernels", type=int, default=0, choices=[0, 1, 2, 3],
                     help="decode: STYX_OPT_ATTN_KERNELS: 0 auto, 1 cooperative kernel, 2 seven kernels, 3 cluster form")
     ap.add_argument("--shape", default="cfg2", choices=["cfg2", "cfg5"],

@@ -374,32 +374,48 @@ int styx_moe_block_batch(styx_ctx *ctx, styx_stream stream,
 int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial,
                      float *x, int ne, int k);
 
-/* The cross-rank sum and the combine as one kernel over NVLink peer memory
- * (no counterpart in the reference: it replaces "all-reduce partial, then
+/* The cross-rank sum and the combine over NVLink peer memory (no
+ * counterpart in the reference: it replaces "all-reduce partial, then
  * styx_moe_combine" for the ranks of one node).  Each rank owns an inbox of
- * 2 x world x k x n_embd floats (two halves, by call parity) and world x G
- * generation flags in its own device memory; styx_ep_open allocates it and
- * returns its CUDA IPC handle (STYX_EP_HANDLE_BYTES), the caller gathers
- * every rank's handle (e.g. with torch.distributed) and passes them, in
- * rank order, to styx_ep_connect, which maps the peers' inboxes.
- * styx_ep_combine then pushes this rank's partial into every peer's inbox
- * with plain stores over NVLink, raises its flags there (release, system
- * scope), waits (bounded: STYX_ETIMEOUT after about a second) for every
- * peer's flags of this call, and adds sum_s (sum_r partial_r[s][i]) into
- * x[i], ranks then slots in order: with one non-zero contributor per slot
- * the result equals the single-device block bit for bit, as the NCCL form
- * does.  Every rank must call it once per layer, in the same order; calls on
- * one styx_ep must not overlap on the GPU (one stream).  The call's
- * generation is a counter in the rank's own memory (advanced by the call's
- * last CTA), so a launch recorded once can be replayed.  No multicast, no
- * library collective.  styx_ep_close synchronises the device, unmaps the
- * peers and frees the inbox: call it on every rank after a barrier. */
+ * 2 x world x k x n_embd floats (two halves, by call parity) and arrival
+ * counters (one per sending rank) in its own device memory; styx_ep_open
+ * allocates them and returns their CUDA IPC handle (STYX_EP_HANDLE_BYTES),
+ * the caller gathers every rank's handle (e.g. with torch.distributed) and
+ * passes them, in rank order, to styx_ep_connect, which maps the peers'.
+ *
+ * styx_ep_combine (one kernel) pushes this rank's partial into every peer's
+ * inbox with plain stores over NVLink, adds the rows it pushed to its
+ * counter in every peer (release, system scope), waits (bounded:
+ * STYX_ETIMEOUT after about a second) until every peer's counter shows the
+ * whole call, and adds sum_s (sum_r partial_r[s][i]) into x[i], ranks then
+ * slots in order: with one non-zero contributor per slot the result equals
+ * the single-device block bit for bit, as the NCCL form does.
+ *
+ * styx_ep_moe_block is styx_moe_block_ep + styx_ep_combine in one call: x
+ * ends as the single-device styx_moe_block leaves it, bit for bit.  Where
+ * the single-kernel form fits (STYX_OPT_MOE_KERNELS 0 or 1) the exchange is
+ * that kernel's epilogue -- each CTA pushes its own rows of every slot as
+ * soon as they are computed, and adds the ranks' sum of the same rows into
+ * x -- so the block and the exchange are one launch; otherwise the block's
+ * partial goes through styx_ep_combine (workspace as for styx_moe_block_ep,
+ * plus k x n_embd floats held by the styx_ep).
+ *
+ * Every rank must make the same calls on one styx_ep (either entry point,
+ * once per layer) in the same order; calls on one styx_ep must not overlap
+ * on the GPU (one stream).  The call's generation is a counter in the
+ * rank's own memory (advanced by the call's last CTA), so a launch recorded
+ * once can be replayed.  No multicast, no library collective, no load from
+ * a peer's memory.  styx_ep_close synchronises the device, unmaps the peers
+ * and frees the inbox: call it on every rank after a barrier. */
 #define STYX_EP_HANDLE_BYTES 64
 #define STYX_EP_MAX_RANKS 8
 typedef struct styx_ep styx_ep;
 int styx_ep_open(styx_ctx *ctx, int rank, int world, int k, int n_embd, styx_ep **out, void *handle);
 int styx_ep_connect(styx_ep *ep, const void *handles);
 int styx_ep_combine(styx_ctx *ctx, styx_ep *ep, styx_stream stream, const float *partial, float *x);
+int styx_ep_moe_block(styx_ctx *ctx, styx_ep *ep, styx_stream stream, const styx_moe_dims *dims,
+                      const styx_moe_layer *lw, int layer, float *x, int32_t *ids, float *weights_out,
+                      void *workspace, uint64_t workspace_bytes);
 int styx_ep_close(styx_ep *ep);
 
 /* styx_moe_block without a caller workspace; it has no counterpart in the

@@ -126,6 +126,8 @@ _SIGS = {
     "styx_ep_open": (_i, [_vp, _i, _i, _i, _i, C.POINTER(_vp), _vp]),
     "styx_ep_connect": (_i, [_vp, _vp]),
     "styx_ep_combine": (_i, [_vp, _vp, _vp, _vp, _vp]),
+    "styx_ep_moe_block": (_i, [_vp, _vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp, _vp, _vp,
+                               _u64]),
     "styx_ep_close": (_i, [_vp]),
     "styx_moe_batch_workspace_bytes": (_i, [C.POINTER(MoeDims), _i, C.POINTER(C.c_uint64)]),
     "styx_moe_block_batch": (_i, [_vp, _vp, C.POINTER(MoeDims), C.POINTER(MoeLayer), _i, _vp, _vp, _vp, _vp,

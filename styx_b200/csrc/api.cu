@@ -418,6 +418,7 @@ int styx_check_device_error(styx_ctx *ctx, styx_stream stream) {
         CK(cudaStreamSynchronize(S(stream)));
         if (h == 4) return fail(STYX_EINVAL, "a kernel skipped an out-of-range expert id / hot index / arena slot");
         if (h == 5) return fail(STYX_EINVAL, "a kernel skipped a KV cache row outside [0, n_ctx)");
+        if (h == 6) return fail(STYX_ETIMEOUT, "expert parallelism: a peer rank's rows did not arrive (bounded wait gave up)");
         return fail(STYX_ETIMEOUT, "device-side bounded wait gave up (code %d)", h);
     }
     return STYX_OK;
@@ -1566,17 +1567,30 @@ int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial, fl
 }
 
 // ------------------------------------------------ cross-rank combine over peer memory
+// One device allocation per rank, mapped by every peer: the inbox (two
+// halves of world x k x H f32), then (ctl_off) the arrival counters
+// u64[kEpMaxRanks], the call counter (u64) and the CTAs done of the current
+// call (u32); then, read only by this rank, the EpPeers table the kernels
+// take and the partial buffer styx_ep_moe_block uses when the block does not
+// run as the single kernel.
 struct styx_ep {
     int dev = 0, rank = 0, world = 1, k = 0, H = 0;
-    uint8_t *base = nullptr;                      // this rank's inbox (two halves), then its flags
-    size_t flags_off = 0;
-    float *inbox[styx::kEpMaxRanks] = {};
-    unsigned long long *flags[styx::kEpMaxRanks] = {};
+    uint8_t *base = nullptr;
+    size_t ctl_off = 0, peers_off = 0, partial_off = 0;
+    styx::EpPeers peers{};                        // host copy of the table
+    styx::EpPeers *d_peers = nullptr;             // device copy (in base)
     void *peer_base[styx::kEpMaxRanks] = {};      // the peers' mappings (closed by styx_ep_close)
     bool connected = false;
 };
 static_assert(sizeof(cudaIpcMemHandle_t) == STYX_EP_HANDLE_BYTES, "IPC handle size");
 static_assert(styx::kEpMaxRanks == STYX_EP_MAX_RANKS, "rank limit");
+
+namespace {
+void ep_bind(styx_ep *ep, int p, uint8_t *b) {
+    ep->peers.inbox[p] = reinterpret_cast<float *>(b);
+    ep->peers.cnt[p] = reinterpret_cast<unsigned long long *>(b + ep->ctl_off);
+}
+}  // namespace
 
 int styx_ep_open(styx_ctx *ctx, int rank, int world, int k, int n_embd, styx_ep **out, void *handle) {
     ENTER(ctx);
@@ -1590,11 +1604,10 @@ int styx_ep_open(styx_ctx *ctx, int rank, int world, int k, int n_embd, styx_ep 
     ep->world = world;
     ep->k = k;
     ep->H = n_embd;
-    const int G = (n_embd + styx::kEpCols - 1) / styx::kEpCols;
-    const size_t inbox = 2 * static_cast<size_t>(world) * k * n_embd * 4;
-    ep->flags_off = a128(inbox);
-    // then the flags, then this rank's call counter (u64) and the CTAs done of the current call (u32)
-    const size_t total = ep->flags_off + static_cast<size_t>(world) * G * 8 + 16;
+    ep->ctl_off = a128(2 * static_cast<size_t>(world) * k * n_embd * 4);
+    ep->peers_off = ep->ctl_off + 128;
+    ep->partial_off = a128(ep->peers_off + sizeof(styx::EpPeers));
+    const size_t total = ep->partial_off + static_cast<size_t>(k) * n_embd * 4;
     void *p = nullptr;
     cudaError_t e = cudaMalloc(&p, total);
     if (e == cudaSuccess) e = cudaMemset(p, 0, total);
@@ -1607,8 +1620,14 @@ int styx_ep_open(styx_ctx *ctx, int rank, int world, int k, int n_embd, styx_ep 
         return fail(STYX_ECUDA, "styx_ep_open: %s", cudaGetErrorString(e));
     }
     ep->base = static_cast<uint8_t *>(p);
-    ep->inbox[rank] = reinterpret_cast<float *>(ep->base);
-    ep->flags[rank] = reinterpret_cast<unsigned long long *>(ep->base + ep->flags_off);
+    ep->d_peers = reinterpret_cast<styx::EpPeers *>(ep->base + ep->peers_off);
+    ep_bind(ep, rank, ep->base);
+    ep->peers.calls = ep->peers.cnt[rank] + styx::kEpMaxRanks;
+    ep->peers.done = reinterpret_cast<unsigned *>(ep->peers.calls + 1);
+    ep->peers.rank = rank;
+    ep->peers.world = world;
+    ep->peers.k = k;
+    ep->peers.H = n_embd;
     memcpy(handle, &h, sizeof(h));
     *out = ep;
     return STYX_OK;
@@ -1634,44 +1653,83 @@ int styx_ep_connect(styx_ep *ep, const void *handles) {
             return fail(STYX_ECUDA, "styx_ep_connect: rank %d's inbox: %s", p, cudaGetErrorString(e));
         }
         ep->peer_base[p] = ptr;
-        ep->inbox[p] = static_cast<float *>(ptr);
-        ep->flags[p] = reinterpret_cast<unsigned long long *>(static_cast<uint8_t *>(ptr) + ep->flags_off);
+        ep_bind(ep, p, static_cast<uint8_t *>(ptr));
     }
+    CK(cudaMemcpy(ep->d_peers, &ep->peers, sizeof(styx::EpPeers), cudaMemcpyHostToDevice));
     ep->connected = true;
     return STYX_OK;
 }
 
+namespace {
+int ep_check(styx_ctx *ctx, styx_ep *ep) {
+    NEED(ep, "null styx_ep");
+    NEED(ep->connected, "styx_ep used before styx_ep_connect");
+    NEED(ep->dev == ctx->device, "styx_ep of device %d used with a context of device %d", ep->dev, ctx->device);
+    return STYX_OK;
+}
+}  // namespace
+
 int styx_ep_combine(styx_ctx *ctx, styx_ep *ep, styx_stream stream, const float *partial, float *x) {
     ENTER(ctx);
-    NEED(ep && partial && x, "null pointer");
-    NEED(ep->connected, "styx_ep_combine before styx_ep_connect");
-    NEED(ep->dev == ctx->device, "styx_ep of device %d used with a context of device %d", ep->dev, ctx->device);
+    int rc = ep_check(ctx, ep);
+    if (rc) return rc;
+    NEED(partial && x, "null pointer");
     NEED(al16(partial), "partial must be 16-byte aligned");
     NEED(extent_ok(partial, static_cast<uint64_t>(ep->k) * ep->H * 4) && extent_ok(x, static_cast<uint64_t>(ep->H) * 4),
          "partial / x smaller than k * n_embd / n_embd");
     styx::EpCombineArgs a{};
     a.partial = partial;
     a.x = x;
-    for (int p = 0; p < ep->world; p++) {
-        a.inbox[p] = ep->inbox[p];
-        a.flags[p] = ep->flags[p];
-    }
-    a.rank = ep->rank;
-    a.world = ep->world;
-    a.k = ep->k;
+    a.ep = ep->d_peers;
     a.H = ep->H;
-    const int G = (ep->H + styx::kEpCols - 1) / styx::kEpCols;
-    a.calls = reinterpret_cast<unsigned long long *>(ep->flags[ep->rank] + static_cast<size_t>(ep->world) * G);
-    a.done = reinterpret_cast<unsigned *>(a.calls + 1);
     a.err = ctx->d_err;
     CK(styx::launch_ep_combine(a, S(stream)));
     return STYX_OK;
 }
 
+int styx_ep_moe_block(styx_ctx *ctx, styx_ep *ep, styx_stream stream, const styx_moe_dims *dims,
+                      const styx_moe_layer *lw, int layer, float *x, int32_t *ids, float *weights_out, void *workspace,
+                      uint64_t workspace_bytes) {
+    ENTER(ctx);
+    int rc = ep_check(ctx, ep);
+    if (rc) return rc;
+    WsLayout L;
+    if ((rc = check_block(ctx, dims, lw, layer, x, ids, workspace, workspace_bytes, L))) return rc;
+    NEED(dims->n_expert_used == ep->k && dims->n_embd == ep->H, "styx_ep opened for k %d / n_embd %d, dims say %d / %d",
+         ep->k, ep->H, dims->n_expert_used, dims->n_embd);
+    const bool in_hbm = !full_in_host(lw->gate) && !full_in_host(lw->up) && !full_in_host(lw->down);
+    if (in_hbm && (ctx->moe_kernels == 0 || ctx->moe_kernels == 1)) {
+        styx::FusedArgs fa{};
+        uint32_t smem = 0;
+        if (al16(lw->ffn_norm) && plan_fused(*dims, *lw, ctx->sm_count, fa, smem) && ctx->sm_count <= dims->n_embd) {
+            NEED(!ctx->trace || ctx->sm_count <= static_cast<int>(kTraceCtas), "too many CTAs to trace");
+            uint8_t *ws = static_cast<uint8_t *>(workspace);
+            int32_t *ids64 = ids + static_cast<size_t>(layer) * STYX_IDS_PER_LAYER;
+            float *wts = weights_out ? weights_out : reinterpret_cast<float *>(ws + L.weights);
+            fill_fused(fa, ctx, *dims, *lw, x, ids64, wts, ws, L);
+            fa.ep = ep->d_peers;
+            fa.quiet = 1;
+            const styx::LayerLink alone{0, false, false, true, nullptr, nullptr, nullptr};
+            CK(styx::launch_fused(fa, alone, lw->gate.qtype, lw->down.qtype, ctx->sm_count, smem, !ctx->exclusive,
+                                  S(stream)));
+            ctx->last_path = 1;
+            return STYX_OK;
+        }
+    }
+    float *partial = reinterpret_cast<float *>(ep->base + ep->partial_off);
+    if ((rc = styx_moe_block_ep(ctx, stream, dims, lw, layer, x, ids, weights_out, partial, workspace,
+                                workspace_bytes)))
+        return rc;
+    const int path = ctx->last_path;
+    rc = styx_ep_combine(ctx, ep, stream, partial, x);
+    ctx->last_path = path;
+    return rc;
+}
+
 int styx_ep_close(styx_ep *ep) {
     if (!ep) return STYX_OK;
     cudaSetDevice(ep->dev);
-    cudaDeviceSynchronize();   // no combine of this rank still reads or writes the inboxes
+    cudaDeviceSynchronize();   // no call of this rank still reads or writes the inboxes
     for (int p = 0; p < ep->world; p++)
         if (ep->peer_base[p]) cudaIpcCloseMemHandle(ep->peer_base[p]);
     if (ep->base) cudaFree(ep->base);

@@ -27,6 +27,7 @@ enum : int {
     kErrWaitRoute = 3,   // route: last-block handoff failed
     kErrBadId = 4,       // an expert id / hot index / arena slot out of range
     kErrBadPos = 5,      // a token position outside the KV caches
+    kErrWaitPeer = 6,    // expert parallelism: a peer rank's rows of the call did not arrive
 };
 
 // ~1 s at the B200's 1.9 GHz SM clock

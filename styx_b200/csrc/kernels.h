@@ -70,6 +70,22 @@ struct DownArgs {
 };
 
 // the single-kernel MoE block (moe_fused.cu)
+// Expert parallelism over NVLink peer memory (styx_ep): every rank's inbox
+// ([2][world][k][H] f32: a half per call parity, a row per sending rank) and
+// every rank's arrival counters (u64[kEpMaxRanks]: rows of x received from
+// each sender, summed over the calls, so that after call g every sender has
+// added g * H), this rank's call counter (calls completed) and the CTAs of
+// the current call that have finished.  Lives in device memory (one copy per
+// rank, written once when the ranks connect).
+constexpr int kEpMaxRanks = 8;
+struct EpPeers {
+    float *inbox[kEpMaxRanks];
+    unsigned long long *cnt[kEpMaxRanks];
+    unsigned long long *calls;
+    unsigned *done;
+    int rank, world, k, H;
+};
+
 struct FusedArgs {
     float *x;
     const float *norm_w;
@@ -94,6 +110,10 @@ struct FusedArgs {
     // writes partial[s][r] = w[s] * d[s][r] instead of adding into x, and a
     // slot whose expert has no source here is another rank's (contributes 0)
     float *partial;
+    // expert parallelism over peer memory (single-layer launches, partial
+    // unset): each slot's weighted rows go to every peer's inbox, and the
+    // ranks' sum is added into x by the CTA that owns the rows
+    const EpPeers *ep;
     int quiet;
     // shared-memory plan (every chunk of a CTA is resident at once)
     uint32_t off_a, off_part, off_ring, off_down;
@@ -225,19 +245,12 @@ cudaError_t launch_moe_reduce(const float *d, const float *w, float *x, int ne, 
                               cudaStream_t st);
 cudaError_t launch_combine_partial(const float *partial, float *x, int ne, int k, cudaStream_t st);
 // the cross-rank sum + combine over peer memory (styx_ep_combine, moe_kernels.cu)
-constexpr int kEpMaxRanks = 8;
 constexpr int kEpCols = 128;   // columns of x per CTA
 struct EpCombineArgs {
     const float *partial;                         // this rank's f32[k][H]
     float *x;                                     // [H], += the slot-ordered sum
-    float *inbox[kEpMaxRanks];                    // rank p's inbox [2][world][k][H] (this rank's own included)
-    unsigned long long *flags[kEpMaxRanks];       // rank p's flags [world][G]
-    int rank, world, k, H;
-    // this rank's call counter (calls completed; this call's generation is
-    // *calls + 1) and the CTAs of the current call that have finished: both
-    // in this rank's memory, so that a recorded graph replays correctly
-    unsigned long long *calls;
-    unsigned *done;
+    const EpPeers *ep;                            // the ranks' inboxes and counters (device memory)
+    int H;
     int *err;
 };
 cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t st);

@@ -17,6 +17,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "ep_sync.cuh"
 #include "qdot.cuh"
 
 namespace styx {
@@ -697,92 +698,51 @@ cudaError_t launch_combine_partial(const float *partial, float *x, int ne, int k
 }
 
 // ------------------------------------------------ cross-rank sum + combine over peer memory
-// CTA b owns columns [kEpCols b, kEpCols (b+1)) of every slot.  It pushes
-// this rank's values of them into row `rank` of every peer's inbox (plain
-// stores over NVLink), raises flag [rank][b] in every peer (release, system
-// scope), waits for flag [p][b] of every peer p in its own flags (acquire,
-// bounded), and adds sum_s (sum_p partial_p[s][c]) into x[c], ranks then
-// slots in order.  The inbox has two halves, by the parity of the call's
-// generation: a peer one call ahead writes the other half, and it cannot
-// get two calls ahead before this rank has pushed (hence summed) this one.
-// The generation is this rank's count of completed calls + 1, read by every
-// CTA at entry and advanced by the CTA that finishes the call last, so the
-// launch carries no per-call argument and a recorded graph replays as well.
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
 constexpr int kEpThreads = 256;
 
+// CTA b owns columns [kEpCols b, kEpCols (b+1)) of every slot: it stores
+// this rank's values of them into row `rank` of every peer's inbox, adds
+// its column count to this rank's counter in every peer, waits until every
+// peer's counter here shows the whole call, and adds sum_s (sum_p
+// partial_p[s][c]) into x[c], ranks then slots in order (ep_sync.cuh).
 __global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpCombineArgs a) {
     pdl_trigger();
     pdl_wait();
+    const EpPeers &ep = *a.ep;
     const int b = blockIdx.x, G = gridDim.x, tid = threadIdx.x;
     const int c0 = b * kEpCols, nc = min(kEpCols, a.H - c0);
     const int H4 = a.H >> 2, c04 = c0 >> 2, nc4 = nc >> 2;
-    // (the previous call on this stream has ended: its counter update is visible)
-    const unsigned long long gen = __ldcg(a.calls) + 1ull;
-    const size_t row = static_cast<size_t>(a.k) * a.H;                      // one rank's row of an inbox half
-    const size_t half = static_cast<size_t>(a.world) * row;
-    const size_t mine = (gen & 1ull) * half + static_cast<size_t>(a.rank) * row;   // our row, this call's half
+    const int rank = ep.rank, world = ep.world, k = ep.k;
+    const unsigned long long gen = ep_generation(ep);
     // 1. push
-    for (int i = tid; i < a.k * nc4; i += kEpThreads) {
+    const size_t mine4 = ep_index(ep, gen, rank, 0, 0) >> 2;
+    for (int i = tid; i < k * nc4; i += kEpThreads) {
         const int s = i / nc4, j = i - s * nc4;
         const size_t o4 = static_cast<size_t>(s) * H4 + c04 + j;
         const float4 v = reinterpret_cast<const float4 *>(a.partial)[o4];
-        for (int p = 0; p < a.world; p++)
-            if (p != a.rank) reinterpret_cast<float4 *>(a.inbox[p] + mine)[o4] = v;
+        for (int p = 0; p < world; p++)
+            if (p != rank) reinterpret_cast<float4 *>(ep.inbox[p])[mine4 + o4] = v;
     }
     __syncthreads();
-    // 2. this CTA's columns of this call are in every peer's inbox
-    if (tid < a.world && tid != a.rank) {
-        __threadfence_system();
-        st_release_sys(a.flags[tid] + static_cast<size_t>(a.rank) * G + b, gen);
-    }
-    // 3. every peer's columns of this call are in ours (bounded wait)
-    if (tid < a.world && tid != a.rank) {
-        const unsigned long long *f = a.flags[a.rank] + static_cast<size_t>(tid) * G + b;
-        const long long t0 = clock64();
-        while (ld_acquire_sys(f) < gen) {
-            const long long dt = clock64() - t0;
-            if (dt > kSpinCycles) {
-                atomicExch(a.err, kErrWaitRoute);
-                break;
-            }
-            if (dt > 100000) __nanosleep(256);
-        }
-    }
+    // 2. publish this CTA's columns, wait for every peer's whole call
+    ep_signal_and_wait(ep, gen, nc, a.err);
     __syncthreads();
-    // 4. the slot-ordered sum (one non-zero rank per slot: exact in any order)
-    const float *box = a.inbox[a.rank] + (gen & 1ull) * half;
+    // 3. the slot-ordered sum (one non-zero rank per slot: exact in any order)
+    const float *box = ep.inbox[rank];
     for (int j = tid; j < nc; j += kEpThreads) {
         const int c = c0 + j;
         float acc = 0.f;
-        for (int s = 0; s < a.k; s++) {
-            const size_t o = static_cast<size_t>(s) * a.H + c;
+        for (int s = 0; s < k; s++) {
             float v = 0.f;
-            for (int p = 0; p < a.world; p++)
-                v = __fadd_rn(v, p == a.rank ? a.partial[o] : __ldcg(box + static_cast<size_t>(p) * row + o));
+            for (int p = 0; p < world; p++)
+                v = __fadd_rn(v, p == rank ? a.partial[static_cast<size_t>(s) * a.H + c]
+                                           : __ldcg(box + ep_index(ep, gen, p, s, c)));
             acc = __fadd_rn(acc, v);
         }
         a.x[c] = __fadd_rn(a.x[c], acc);
     }
-    // 5. the last CTA of the call advances the generation (no CTA of this
-    // call reads it again)
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        if (atomicAdd(a.done, 1u) == static_cast<unsigned>(G - 1)) {
-            *a.done = 0u;
-            *a.calls = gen;
-            __threadfence();
-        }
-    }
+    // 4. the last CTA of the call advances the generation
+    ep_call_done(ep, gen, G);
 }
 
 cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t st) {

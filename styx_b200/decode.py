@@ -20,9 +20,10 @@ whole step on the same token with the same dense weights, but holds only
 its own experts (its layers' hot buffers, remap -> local slot); each MoE
 block writes its slot contributions (styx_moe_block_ep), `allreduce` sums
 them over the ranks in place on the stream and styx_moe_combine adds the
-slot-ordered sum into x, or `ep_comm` (ops.EpComm) does both as one kernel
-over NVLink peer memory -- either way bit-identical to one device holding
-every expert.
+slot-ordered sum into x, or `ep_comm` (ops.EpComm) does the exchange over
+NVLink peer memory -- by default inside the block's own kernel
+(styx_ep_moe_block), else as one kernel after it -- either way bit-identical
+to one device holding every expert.
 """
 from __future__ import annotations
 
@@ -61,7 +62,7 @@ class DecodeLayer:
 class DecodeModel:
     def __init__(self, hp: DecodeParams, embd: ops.DenseWeight, layers: list, output_norm: torch.Tensor,
                  head: ops.DenseWeight, n_ctx: int, device: int = 0, allreduce=None, kv_page: int = 0,
-                 ep_comm=None):
+                 ep_comm=None, ep_fused: bool = True):
         self.hp, self.embd, self.layers, self.output_norm, self.head = hp, embd, layers, output_norm, head
         self.n_ctx = n_ctx            # n_ctx_max: positions the caches may grow to
         self.kv_page = kv_page        # 0: allocated once for n_ctx rows; else rows per page
@@ -85,8 +86,12 @@ class DecodeModel:
         # expert parallelism: a callable summing a tensor over the ranks in
         # place, on the current stream (e.g. torch.distributed.all_reduce)
         self.allreduce = allreduce
-        # or: an ops.EpComm (the sum and the combine as one kernel over NVLink peer memory)
+        # or: an ops.EpComm (the exchange over NVLink peer memory): with
+        # ep_fused the block and the exchange in one call (styx_ep_moe_block:
+        # one kernel where the single-kernel form fits), else the block's
+        # partial then styx_ep_combine
         self.ep_comm = ep_comm
+        self.ep_fused = ep_fused
         self.partial = torch.zeros(hp.n_expert_used * hp.n_embd, dtype=torch.float32, device=dev)
 
     def _grow(self) -> None:
@@ -128,7 +133,9 @@ class DecodeModel:
         for li, ly in enumerate(self.layers):
             self.attn.forward(self.x, ly.attn, pos, self.pos, self.kcache[li], self.vcache[li], self.cap,
                               stream=stream)
-            if self.ep_comm is not None:
+            if self.ep_comm is not None and self.ep_fused:
+                self.ep_comm.moe_block(self.moe, self.x, ly.moe, li, self.ids, stream=stream)
+            elif self.ep_comm is not None:
                 self.moe.forward_ep(self.x, ly.moe, li, self.ids, self.partial, stream=stream)
                 self.ep_comm.combine(self.partial, self.x, stream=stream)
             elif self.allreduce is None:

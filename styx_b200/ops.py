@@ -330,7 +330,7 @@ class EpComm:
     combine into x, as one kernel over NVLink peer memory (no library
     collective).  Every rank opens one, the ranks exchange handles (any host
     channel: `connect_with` uses torch.distributed), then every rank calls
-    `combine` once per layer in the same order."""
+    `combine` (or `moe_block`) once per layer in the same order."""
 
     HANDLE_BYTES = 64
 
@@ -359,6 +359,17 @@ class EpComm:
     def combine(self, partial: torch.Tensor, x: torch.Tensor, stream=None) -> torch.Tensor:
         """x += the slot-ordered sum over the ranks of their partials."""
         check(lib().styx_ep_combine(self.ctx.handle, self.handle, _stream(stream), _ptr(partial), _ptr(x)))
+        return x
+
+    def moe_block(self, blk: "MoeBlock", x: torch.Tensor, layer_w: LayerWeights, layer: int, ids: torch.Tensor,
+                  weights_out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        """The whole expert-parallel MoE block (styx_ep_moe_block): x ends
+        as the single-device block leaves it.  Where the single kernel fits,
+        the exchange is its epilogue (one launch per layer)."""
+        st = layer_w.struct()
+        check(lib().styx_ep_moe_block(blk.ctx.handle, self.handle, _stream(stream), C.byref(blk._dims), C.byref(st),
+                                      layer, _ptr(x), _ptr(ids), _ptr(weights_out), _ptr(blk.workspace),
+                                      blk.ws_bytes))
         return x
 
     def close(self) -> None:

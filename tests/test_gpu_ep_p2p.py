@@ -1,13 +1,15 @@
-"""Expert parallelism with the cross-rank sum and the combine as one kernel
-over NVLink peer memory (styx_ep_*: CUDA IPC mappings of every rank's
-inbox, plain stores, release / acquire flags at system scope, no library
-collective).  One process per GPU (world size 2); the handles travel over a
-gloo process group.  Three layers in a row (both inbox halves, and a rank a
-call ahead of the other) must each equal the single-device styx_moe_block
-bit for bit.  The same three layers recorded once as a CUDA graph and
-replayed twice (the call generation lives in device memory, so a replay
-runs with fresh generations) must give the same bits again.  Skipped with
-fewer than two GPUs.
+"""Expert parallelism with the exchange over NVLink peer memory (styx_ep_*:
+CUDA IPC mappings of every rank's inbox, plain stores, release adds /
+acquire loads of arrival counters at system scope, no library collective),
+in both forms: styx_ep_moe_block (the exchange as the single kernel's
+epilogue) and styx_moe_block_ep + styx_ep_combine (the exchange as a kernel
+of its own).  One process per GPU (world size 2); the handles travel over a
+gloo process group.  Three layers in a row (both inbox halves, a rank a call
+ahead of the other) must each equal the single-device styx_moe_block bit for
+bit: in the combine form, in the fused form, and alternating the two.  The
+fused layers recorded once as a CUDA graph and replayed twice (the call
+generation lives in device memory) must give the same bits again.  Skipped
+with fewer than two GPUs.
 """
 import ctypes as C
 import datetime
@@ -58,18 +60,25 @@ def _rank_main(rank, port, out_dir):
                                     up=ex(c.qts[1], c.up, su), down=ex(c.qts[2], c.down, sd), remap=t(remap))
         lws = [ep_layer(c) for c in cases]
         blk = ops.MoeBlock(ops.Dims(H, F, E, k), rank)
+        blk.ctx.set_option(_lib.OPT_MOE_KERNELS, 1)   # the single kernel, as the reference below
         ep = ops.EpComm(rank, WORLD, k, H, rank)
         ep.connect_with(dist)
-        x = t(cases[0].x)
         ids = torch.full((LAYERS * 64,), -7, dtype=torch.int32, device=dev)
         partial = torch.empty(k * H, dtype=torch.float32, device=dev)
-        for l, lw in enumerate(lws):   # one stream, no host sync between the layers
-            blk.forward_ep(x, lw, l, ids, partial)
-            ep.combine(partial, x)
-        torch.cuda.synchronize()
-        blk.ctx.check_device_error()
-        np.save(os.path.join(out_dir, f"x{rank}.npy"), x.cpu().numpy())
-        # the same layers as one recorded graph, replayed twice from the same input
+        for name, fused in (("combine", [False] * LAYERS), ("fused", [True] * LAYERS),
+                            ("mixed", [l % 2 == 0 for l in range(LAYERS)])):
+            x = t(cases[0].x)
+            for l, lw in enumerate(lws):   # one stream, no host sync between the layers
+                if fused[l]:
+                    ep.moe_block(blk, x, lw, l, ids)
+                    assert blk.ctx.last_moe_path() == 1
+                else:
+                    blk.forward_ep(x, lw, l, ids, partial)
+                    ep.combine(partial, x)
+            torch.cuda.synchronize()
+            blk.ctx.check_device_error()
+            np.save(os.path.join(out_dir, f"{name}{rank}.npy"), x.cpu().numpy())
+        # the fused layers as one recorded graph, replayed twice from the same input
         lib, cx = _lib.lib(), blk.ctx.handle
         stream = torch.cuda.Stream(device=dev)
         sp = C.c_void_p(stream.cuda_stream)
@@ -77,8 +86,7 @@ def _rank_main(rank, port, out_dir):
         graph = C.c_void_p()
         _lib.check(lib.styx_graph_begin(cx, sp))
         for l, lw in enumerate(lws):
-            blk.forward_ep(xg, lw, l, ids, partial, stream=stream)
-            ep.combine(partial, xg, stream=stream)
+            ep.moe_block(blk, xg, lw, l, ids, stream=stream)
         _lib.check(lib.styx_graph_end(cx, sp, C.byref(graph)))
         try:
             for rep in range(2):
@@ -87,7 +95,7 @@ def _rank_main(rank, port, out_dir):
                 _lib.check(lib.styx_graph_launch(cx, graph, sp))
                 stream.synchronize()
                 blk.ctx.check_device_error(stream)
-                np.save(os.path.join(out_dir, f"g{rank}_{rep}.npy"), xg.cpu().numpy())
+                np.save(os.path.join(out_dir, f"graph{rank}_{rep}.npy"), xg.cpu().numpy())
         finally:
             _lib.check(lib.styx_graph_destroy(cx, graph))
         if rank == 0:   # the single-device blocks with every expert
@@ -111,10 +119,8 @@ def _rank_main(rank, port, out_dir):
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
 def test_ep_over_peer_memory_matches_single_device(tmp_path):
     mp.start_processes(_rank_main, args=(_free_port(), str(tmp_path)), nprocs=WORLD, start_method="spawn")
-    single = np.load(tmp_path / "single.npy")
+    single = np.load(tmp_path / "single.npy").view(np.uint32)
     for r in range(WORLD):
-        x = np.load(tmp_path / f"x{r}.npy")
-        assert np.array_equal(x.view(np.uint32), single.view(np.uint32)), r
-        for rep in range(2):
-            g = np.load(tmp_path / f"g{r}_{rep}.npy")
-            assert np.array_equal(g.view(np.uint32), single.view(np.uint32)), (r, rep)
+        for name in ("combine", "fused", "mixed", "graph_0", "graph_1"):
+            f = tmp_path / (f"graph{r}_{name[-1]}.npy" if name.startswith("graph") else f"{name}{r}.npy")
+            assert np.array_equal(np.load(f).view(np.uint32), single), (r, name)
