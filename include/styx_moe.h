@@ -377,19 +377,20 @@ int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial,
 /* The cross-rank sum and the combine over NVLink peer memory (no
  * counterpart in the reference: it replaces "all-reduce partial, then
  * styx_moe_combine" for the ranks of one node).  Each rank owns an inbox of
- * 2 x world x k x n_embd floats (two halves, by call parity) and arrival
- * counters (one per sending rank) in its own device memory; styx_ep_open
- * allocates them and returns their CUDA IPC handle (STYX_EP_HANDLE_BYTES),
- * the caller gathers every rank's handle (e.g. with torch.distributed) and
- * passes them, in rank order, to styx_ep_connect, which maps the peers'.
+ * 2 x world x k x n_embd 8-byte words (two halves, by call parity) in its
+ * own device memory; styx_ep_open allocates it and returns its CUDA IPC
+ * handle (STYX_EP_HANDLE_BYTES), the caller gathers every rank's handle
+ * (e.g. with torch.distributed) and passes them, in rank order, to
+ * styx_ep_connect, which maps the peers'.
  *
- * styx_ep_combine (one kernel) pushes this rank's partial into every peer's
- * inbox with plain stores over NVLink, adds the rows it pushed to its
- * counter in every peer (release, system scope), waits (bounded:
- * STYX_ETIMEOUT after about a second) until every peer's counter shows the
- * whole call, and adds sum_s (sum_r partial_r[s][i]) into x[i], ranks then
- * slots in order: with one non-zero contributor per slot the result equals
- * the single-device block bit for bit, as the NCCL form does.
+ * styx_ep_combine (one kernel) sends each value of this rank's partial to
+ * every peer's inbox over NVLink as one word tagged with the call's
+ * generation (an 8-byte store is atomic, so a word with this call's tag
+ * holds this call's value: no fence or flag), waits (bounded: STYX_ETIMEOUT
+ * after about a second) for the peers' words of its columns in its own
+ * inbox, and adds sum_s (sum_r partial_r[s][i]) into x[i], ranks then slots
+ * in order: with one non-zero contributor per slot the result equals the
+ * single-device block bit for bit, as the NCCL form does.
  *
  * styx_ep_moe_block is styx_moe_block_ep + styx_ep_combine in one call: x
  * ends as the single-device styx_moe_block leaves it, bit for bit.  Where

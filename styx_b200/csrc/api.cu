@@ -1568,11 +1568,10 @@ int styx_moe_combine(styx_ctx *ctx, styx_stream stream, const float *partial, fl
 
 // ------------------------------------------------ cross-rank combine over peer memory
 // One device allocation per rank, mapped by every peer: the inbox (two
-// halves of world x k x H f32), then (ctl_off) the arrival counters
-// u64[kEpMaxRanks], the call counter (u64) and the CTAs done of the current
-// call (u32); then, read only by this rank, the EpPeers table the kernels
-// take and the partial buffer styx_ep_moe_block uses when the block does not
-// run as the single kernel.
+// halves of world x k x H tagged 8-byte words), then (ctl_off) the call
+// counter (u64) and the CTAs done of the current call (u32); then, read only
+// by this rank, the EpPeers table the kernels take and the partial buffer
+// styx_ep_moe_block uses when the block does not run as the single kernel.
 struct styx_ep {
     int dev = 0, rank = 0, world = 1, k = 0, H = 0;
     uint8_t *base = nullptr;
@@ -1586,10 +1585,7 @@ static_assert(sizeof(cudaIpcMemHandle_t) == STYX_EP_HANDLE_BYTES, "IPC handle si
 static_assert(styx::kEpMaxRanks == STYX_EP_MAX_RANKS, "rank limit");
 
 namespace {
-void ep_bind(styx_ep *ep, int p, uint8_t *b) {
-    ep->peers.inbox[p] = reinterpret_cast<float *>(b);
-    ep->peers.cnt[p] = reinterpret_cast<unsigned long long *>(b + ep->ctl_off);
-}
+void ep_bind(styx_ep *ep, int p, uint8_t *b) { ep->peers.inbox[p] = reinterpret_cast<unsigned long long *>(b); }
 }  // namespace
 
 int styx_ep_open(styx_ctx *ctx, int rank, int world, int k, int n_embd, styx_ep **out, void *handle) {
@@ -1604,7 +1600,7 @@ int styx_ep_open(styx_ctx *ctx, int rank, int world, int k, int n_embd, styx_ep 
     ep->world = world;
     ep->k = k;
     ep->H = n_embd;
-    ep->ctl_off = a128(2 * static_cast<size_t>(world) * k * n_embd * 4);
+    ep->ctl_off = a128(2 * static_cast<size_t>(world) * k * n_embd * 8);
     ep->peers_off = ep->ctl_off + 128;
     ep->partial_off = a128(ep->peers_off + sizeof(styx::EpPeers));
     const size_t total = ep->partial_off + static_cast<size_t>(k) * n_embd * 4;
@@ -1622,7 +1618,7 @@ int styx_ep_open(styx_ctx *ctx, int rank, int world, int k, int n_embd, styx_ep 
     ep->base = static_cast<uint8_t *>(p);
     ep->d_peers = reinterpret_cast<styx::EpPeers *>(ep->base + ep->peers_off);
     ep_bind(ep, rank, ep->base);
-    ep->peers.calls = ep->peers.cnt[rank] + styx::kEpMaxRanks;
+    ep->peers.calls = reinterpret_cast<unsigned long long *>(ep->base + ep->ctl_off);
     ep->peers.done = reinterpret_cast<unsigned *>(ep->peers.calls + 1);
     ep->peers.rank = rank;
     ep->peers.world = world;

@@ -1,24 +1,27 @@
 // Expert parallelism over NVLink peer memory: the device side of styx_ep.
 //
 // Every rank holds the slot rows of its own experts, weighted (w[s] * d[s][r];
-// exactly 0 for another rank's slots).  A call moves them with plain stores
-// into row `rank` of every peer's inbox, in the half picked by the parity of
-// the call's generation, and then adds, per CTA, the rows it pushed to the
-// sender's counter in each peer (a release add at system scope after a
-// system fence).  A receiver waits (bounded) until every peer's counter has
-// reached gen * H -- every row of the call -- and sums, per column, the ranks
-// then the slots, in slot order, into x.  Each slot has one non-zero
-// contributor, so the sum equals the single-device block bit for bit.
+// exactly 0 for another rank's slots).  A call sends each value as one
+// 8-byte word -- the f32 bits in the low half, the call's generation (low
+// 32 bits) in the high half -- with a relaxed system-scope store into row
+// `rank` of every peer's inbox, in the half picked by the parity of the
+// generation.  An aligned 8-byte store is single-copy atomic, so a receiver
+// that reads its own word with a relaxed system-scope load and finds this
+// call's generation there has the value as well: no fence, no flag and no
+// counter on the path (the low-latency form of a tagged-word exchange).  It
+// then sums, per column, the ranks then the slots, in slot order, into x.
+// Each slot has one non-zero contributor, so the sum equals the
+// single-device block bit for bit.
 //
 // The generation is this rank's count of completed calls + 1, read from its
 // own memory after the grid dependency and advanced by the CTA that ends the
 // call last, so a launch carries no per-call value and a recorded graph
 // replays correctly.  A peer can be one call ahead (it writes the other
-// half) but not two: its next push needs this rank's push of the call it is
-// in.  Counters only grow, and every add of a call precedes every add of the
-// sender's next call (its kernels are stream-ordered), so a counter at
-// gen * H or above means every row of call gen has landed.
-// Nothing here loads another GPU's memory: peers are only stored to.
+// half) but not two: its next words need this rank's words of the call it is
+// in.  A word left from two calls back carries another generation.  Every
+// wait is bounded; a wait that gives up sets the error word, and the
+// thread's later waits of the call are skipped.  Nothing here loads another
+// GPU's memory: peers are only stored to.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -28,14 +31,36 @@
 
 namespace styx {
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+__device__ __forceinline__ void ep_put(unsigned long long *p, unsigned tag, float v) {
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long *p) {
     unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
-__device__ __forceinline__ void red_add_release_sys(unsigned long long *p, unsigned long long v) {
-    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// The value of word p once it carries `tag`; `live` false: a wait of this
+// thread already gave up in this call (returns 0 without waiting).
+__device__ __forceinline__ float ep_get(const unsigned long long *p, unsigned tag, bool &live, int *err) {
+    unsigned long long w = ld_relaxed_sys(p);
+    if (static_cast<unsigned>(w >> 32) != tag) {
+        if (!live) return 0.f;
+        const long long t0 = clock64();
+        do {
+            const long long dt = clock64() - t0;
+            if (dt > kSpinCycles) {
+                atomicExch(err, kErrWaitPeer);
+                live = false;
+                return 0.f;
+            }
+            if (dt > 100000) __nanosleep(256);
+            w = ld_relaxed_sys(p);
+        } while (static_cast<unsigned>(w >> 32) != tag);
+    }
+    return __uint_as_float(static_cast<unsigned>(w));
 }
 
 // the generation of the call in progress (after the grid dependency)
@@ -43,34 +68,8 @@ __device__ __forceinline__ unsigned long long ep_generation(const EpPeers &ep) {
     return __ldcg(ep.calls) + 1ull;
 }
 
-// After the CTA's stores to the peers (and a __syncthreads): thread p (p !=
-// rank, p < world) publishes the CTA's `rows` to peer p, then waits until
-// peer p's counter here shows every row of call `gen`.  Returns false (and
-// sets the error word) if a wait gave up.
-__device__ __forceinline__ bool ep_signal_and_wait(const EpPeers &ep, unsigned long long gen, int rows, int *err) {
-    const int t = threadIdx.x;
-    bool fine = true;
-    if (t < ep.world && t != ep.rank) {
-        __threadfence_system();
-        red_add_release_sys(ep.cnt[t] + ep.rank, static_cast<unsigned long long>(rows));
-        const unsigned long long want = gen * static_cast<unsigned long long>(ep.H);
-        const unsigned long long *c = ep.cnt[ep.rank] + t;
-        const long long t0 = clock64();
-        while (ld_acquire_sys(c) < want) {
-            const long long dt = clock64() - t0;
-            if (dt > kSpinCycles) {
-                atomicExch(err, kErrWaitPeer);
-                fine = false;
-                break;
-            }
-            if (dt > 100000) __nanosleep(256);
-        }
-    }
-    return fine;
-}
-
-// After every thread of the CTA has read the generation: the CTA that ends
-// the call last advances this rank's call counter.
+// After a __syncthreads that follows every read of the generation in the
+// CTA: the CTA that ends the call last advances this rank's call counter.
 __device__ __forceinline__ void ep_call_done(const EpPeers &ep, unsigned long long gen, int ctas) {
     if (threadIdx.x == 0) {
         __threadfence();
@@ -83,7 +82,7 @@ __device__ __forceinline__ void ep_call_done(const EpPeers &ep, unsigned long lo
     }
 }
 
-// the inbox element of (sending rank p, slot s, column c) in the half of `gen`
+// the inbox word of (sending rank p, slot s, column c) in the half of `gen`
 __device__ __forceinline__ size_t ep_index(const EpPeers &ep, unsigned long long gen, int p, int s, int c) {
     const size_t row = static_cast<size_t>(ep.k) * ep.H;
     return (gen & 1ull) * static_cast<size_t>(ep.world) * row + static_cast<size_t>(p) * row +

@@ -71,16 +71,13 @@ struct DownArgs {
 
 // the single-kernel MoE block (moe_fused.cu)
 // Expert parallelism over NVLink peer memory (styx_ep): every rank's inbox
-// ([2][world][k][H] f32: a half per call parity, a row per sending rank) and
-// every rank's arrival counters (u64[kEpMaxRanks]: rows of x received from
-// each sender, summed over the calls, so that after call g every sender has
-// added g * H), this rank's call counter (calls completed) and the CTAs of
-// the current call that have finished.  Lives in device memory (one copy per
-// rank, written once when the ranks connect).
+// ([2][world][k][H] tagged words: f32 bits | call generation << 32; a half
+// per call parity, a row per sending rank), this rank's call counter (calls
+// completed) and the CTAs of the current call that have finished.  Lives in
+// device memory (one copy per rank, written once when the ranks connect).
 constexpr int kEpMaxRanks = 8;
 struct EpPeers {
-    float *inbox[kEpMaxRanks];
-    unsigned long long *cnt[kEpMaxRanks];
+    unsigned long long *inbox[kEpMaxRanks];
     unsigned long long *calls;
     unsigned *done;
     int rank, world, k, H;
@@ -249,7 +246,7 @@ constexpr int kEpCols = 128;   // columns of x per CTA
 struct EpCombineArgs {
     const float *partial;                         // this rank's f32[k][H]
     float *x;                                     // [H], += the slot-ordered sum
-    const EpPeers *ep;                            // the ranks' inboxes and counters (device memory)
+    const EpPeers *ep;                            // the ranks' inboxes, this rank's call counter (device memory)
     int H;
     int *err;
 };

@@ -669,34 +669,34 @@ __device__ __forceinline__ void fused_layer(uint8_t *smem) {
         STYX_STAMP(13);
         if (p.ep) {
             // expert parallelism over peer memory (ep_sync.cuh): this CTA's
-            // weighted rows of every slot to every peer, then the ranks' sum
-            // of the same rows added into x here
+            // weighted rows of every slot to every peer as tagged words, then
+            // the ranks' sum of the same rows, as the peers' words arrive,
+            // added into x here
             const EpPeers &ep = *p.ep;
             const unsigned long long gen = ep_generation(ep);
+            const unsigned tag = static_cast<unsigned>(gen);
             if (tid < n) {
-                const size_t mine = ep_index(ep, gen, ep.rank, 0, dbeg + tid);
+                const int c = dbeg + tid;
                 for (int s = 0; s < k; s++) {
                     const float v = ok ? __fmul_rn(wts[s], dpart[s * p.rc + tid]) : 0.f;
                     dpart[s * p.rc + tid] = v;
+                    const size_t o = ep_index(ep, gen, ep.rank, s, c);
                     for (int q = 0; q < ep.world; q++)
-                        if (q != ep.rank) ep.inbox[q][mine + static_cast<size_t>(s) * H] = v;
+                        if (q != ep.rank) ep_put(ep.inbox[q] + o, tag, v);
                 }
-            }
-            __syncthreads();
-            ep_signal_and_wait(ep, gen, n, p.err);   // (gave up: the error word says so)
-            __syncthreads();
-            if (tid < n) {
-                const float *box = ep.inbox[ep.rank];
+                const unsigned long long *box = ep.inbox[ep.rank];
+                bool live = true;
                 float acc = 0.f;
                 for (int s = 0; s < k; s++) {
                     float v = 0.f;
                     for (int q = 0; q < ep.world; q++)
                         v = __fadd_rn(v, q == ep.rank ? dpart[s * p.rc + tid]
-                                                      : __ldcg(box + ep_index(ep, gen, q, s, dbeg + tid)));
+                                                      : ep_get(box + ep_index(ep, gen, q, s, c), tag, live, p.err));
                     acc = __fadd_rn(acc, v);
                 }
-                p.x[dbeg + tid] = __fadd_rn(p.x[dbeg + tid], acc);
+                p.x[c] = __fadd_rn(p.x[c], acc);
             }
+            __syncthreads();
             ep_call_done(ep, gen, G);
         } else if (tid < n && p.partial) {
             // expert parallelism: each slot's weighted rows; the ranks' sum

@@ -700,35 +700,32 @@ cudaError_t launch_combine_partial(const float *partial, float *x, int ne, int k
 // ------------------------------------------------ cross-rank sum + combine over peer memory
 constexpr int kEpThreads = 256;
 
-// CTA b owns columns [kEpCols b, kEpCols (b+1)) of every slot: it stores
-// this rank's values of them into row `rank` of every peer's inbox, adds
-// its column count to this rank's counter in every peer, waits until every
-// peer's counter here shows the whole call, and adds sum_s (sum_p
-// partial_p[s][c]) into x[c], ranks then slots in order (ep_sync.cuh).
+// CTA b owns columns [kEpCols b, kEpCols (b+1)) of every slot: it sends
+// this rank's values of them as tagged words into row `rank` of every
+// peer's inbox, then each thread waits for its columns' words of every peer
+// and adds sum_s (sum_p partial_p[s][c]) into x[c], ranks then slots in
+// order (ep_sync.cuh).
 __global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpCombineArgs a) {
     pdl_trigger();
     pdl_wait();
     const EpPeers &ep = *a.ep;
     const int b = blockIdx.x, G = gridDim.x, tid = threadIdx.x;
     const int c0 = b * kEpCols, nc = min(kEpCols, a.H - c0);
-    const int H4 = a.H >> 2, c04 = c0 >> 2, nc4 = nc >> 2;
     const int rank = ep.rank, world = ep.world, k = ep.k;
     const unsigned long long gen = ep_generation(ep);
-    // 1. push
-    const size_t mine4 = ep_index(ep, gen, rank, 0, 0) >> 2;
-    for (int i = tid; i < k * nc4; i += kEpThreads) {
-        const int s = i / nc4, j = i - s * nc4;
-        const size_t o4 = static_cast<size_t>(s) * H4 + c04 + j;
-        const float4 v = reinterpret_cast<const float4 *>(a.partial)[o4];
+    const unsigned tag = static_cast<unsigned>(gen);
+    // 1. send
+    for (int i = tid; i < k * nc; i += kEpThreads) {
+        const int s = i / nc, c = c0 + (i - s * nc);
+        const float v = a.partial[static_cast<size_t>(s) * a.H + c];
+        const size_t o = ep_index(ep, gen, rank, s, c);
         for (int p = 0; p < world; p++)
-            if (p != rank) reinterpret_cast<float4 *>(ep.inbox[p])[mine4 + o4] = v;
+            if (p != rank) ep_put(ep.inbox[p] + o, tag, v);
     }
-    __syncthreads();
-    // 2. publish this CTA's columns, wait for every peer's whole call
-    ep_signal_and_wait(ep, gen, nc, a.err);
-    __syncthreads();
-    // 3. the slot-ordered sum (one non-zero rank per slot: exact in any order)
-    const float *box = ep.inbox[rank];
+    // 2. the slot-ordered sum as the peers' words arrive (one non-zero rank
+    // per slot: exact in any order)
+    const unsigned long long *box = ep.inbox[rank];
+    bool live = true;
     for (int j = tid; j < nc; j += kEpThreads) {
         const int c = c0 + j;
         float acc = 0.f;
@@ -736,12 +733,13 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpCombineArgs a
             float v = 0.f;
             for (int p = 0; p < world; p++)
                 v = __fadd_rn(v, p == rank ? a.partial[static_cast<size_t>(s) * a.H + c]
-                                           : __ldcg(box + ep_index(ep, gen, p, s, c)));
+                                           : ep_get(box + ep_index(ep, gen, p, s, c), tag, live, a.err));
             acc = __fadd_rn(acc, v);
         }
         a.x[c] = __fadd_rn(a.x[c], acc);
     }
-    // 4. the last CTA of the call advances the generation
+    // 3. the last CTA of the call advances the generation
+    __syncthreads();
     ep_call_done(ep, gen, G);
 }
 
