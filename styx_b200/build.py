@@ -26,7 +26,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
 # per-source extra flags: the synthetic quantiser must round like the C oracle
 EXTRA = {"synth.cu": ["-fmad=false"]}
 SOURCES = ["moe_kernels.cu", "moe_fused.cu", "moe_cluster.cu", "batch.cu", "attn.cu", "attn_fused.cu", "attn_cluster.cu", "synth.cu", "api.cu", "residency.cpp", "gguf.cpp"]
-HEADERS = ["common.cuh", "qdot.cuh", "kernels.h", "moe_common.cuh", "cluster.cuh"]
+HEADERS = ["common.cuh", "qdot.cuh", "kernels.h", "moe_common.cuh", "cluster.cuh", "ep_sync.cuh"]
 
 
 def nvcc() -> str:
